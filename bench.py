@@ -1,0 +1,393 @@
+"""Benchmark of the hot path: MiniCPM-4 backbone decode on B200 (BASELINE.json config 2 at N=1).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step is one decode step of the 0.5B-shaped bf16 stack (24 layers, hidden 1024, 16/2 heads,
+FFN 4096) at batch 1, for a request whose 512-position prefill ran first; positions advance from
+512 each step. `value` is decode tokens/s over all ranks, timed with CUDA events on the runtime's
+stream with inputs resident in HBM; `e2e` is the same through the C-ABI step with host buffers
+(tg_decoder_step_rows: host-to-device copy of x and the placement, device-to-host read of the
+output, every step). The weights (717 MB) are far larger than the 126 MB L2, so no flush is
+needed between steps.
+
+Under torchrun (N > 1) each rank holds a full replica and decodes its own request (the path
+shards by request: no collective on the data path); the job's time is the max over ranks.
+
+`--impl reference` times the reference's CPU path for the same workload: tgtts-v4 itself cannot
+run here (Rust toolchain absent; its GPU path is Vulkan), so it is the C restatement under
+oracle/, on all host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PREFILL = 512
+CAPACITY = 1024
+METRIC = "LM decode tokens/s (0.5B-shaped bf16 backbone, batch 1, position 512+)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extras", action="store_true", help="skip the prefill/GEMM side measurements")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    return ap.parse_args()
+
+
+def dist_init(n):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class Clocks:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def stream_ctx(ctx):
+    import torch
+
+    return torch.cuda.ExternalStream(ctx.stream, device=f"cuda:{ctx.device}")
+
+
+def run_ours(args, rank, world, local):
+    import torch
+
+    import __graft_entry__ as entry
+
+    pkg = entry.load_package()
+    from tgtts_v4_b200 import synthetic as syn
+
+    torch.cuda.set_device(local)
+    ctx = pkg.Context(local)
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=CAPACITY)
+    weights = syn.make_weights(cfg, seed=0, as_bits=True)
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16")
+    dec.load(weights)
+    pre = pkg.Prefill(dec, max_rows=PREFILL)
+    x0 = syn.make_inputs(PREFILL, cfg.hidden, seed=1 + rank, bf16=True)
+    pre_out = pre.run(0, x0)
+    stream = stream_ctx(ctx)
+    H = cfg.hidden
+
+    # ---- value: device-resident decode steps, CUDA events on the runtime's stream ----
+    x_dev = torch.from_numpy(pre_out[-1:].copy()).to(f"cuda:{local}")
+    out_dev = torch.empty_like(x_dev)
+    torch.cuda.synchronize()
+
+    def positions(i):
+        return PREFILL + (i % (CAPACITY - PREFILL))
+
+    for i in range(args.warmup):
+        dec.step_device([positions(i)], x_dev.data_ptr(), out_dev.data_ptr())
+    ctx.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        e0.record(stream)
+        for i in range(args.steps):
+            dec.step_device([positions(args.warmup + i)], x_dev.data_ptr(), out_dev.data_ptr())
+        e1.record(stream)
+        e1.synchronize()
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    ms_max = max_over_ranks(ms, world)
+    ms_per_step = ms_max / args.steps
+    value = world * args.steps / (ms_max / 1e3)
+
+    # ---- e2e: the C-ABI step with host buffers, every step's copies inside the timed region ----
+    x_host = pre_out[-1:].copy()
+    for i in range(min(args.warmup, 5)):
+        dec.step_rows([pkg.Row(positions(i), 0)], x_host)
+    barrier(world)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        dec.step_rows([pkg.Row(positions(args.warmup + i), 0)], x_host)
+    t_e2e = time.perf_counter() - t0
+    t_e2e = max_over_ranks(t_e2e, world)
+    e2e = world * args.steps / t_e2e
+
+    result = None
+    extras = {}
+    if rank == 0:
+        hbm, tc, peak_kind = peaks()
+        # ---- roofline of the dominant kernel, live: a timed decoder's per-dispatch times ----
+        tdec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16", timed=True)
+        tdec.load(weights)
+        per = {}
+        for i in range(30):
+            tdec.step(PREFILL + i, pre_out[-1])
+            if i >= 5:
+                for label, ns in tdec.timings():
+                    per.setdefault(label, []).append(ns)
+        total = {k: sum(v) / len(v) for k, v in per.items()}
+        step_ns = sum(total.values())
+        # Algorithmic bytes per launch of gate_up: its weight rows 2 I H bf16, plus the f32 input
+        # row and the bf16 output row (negligible).
+        gate_up_bytes = 2 * cfg.inner * cfg.hidden * 2 + cfg.hidden * 4 + cfg.inner * 2
+        per_launch_ns = total["gate_up"] / shape.layers
+        achieved = gate_up_bytes / per_launch_ns  # bytes/ns = GB/s
+        roof = {"kernel": "gemv_gate_up (fused RMSNorm + gate/up GEMV + SiLU-mul)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_source": peak_kind,
+                "bytes_per_launch": gate_up_bytes, "launch_us": round(per_launch_ns / 1e3, 3),
+                "traffic": None}
+        step_bytes = shape.weight_bytes(2) + shape.cache_bytes(PREFILL + 15, 2)
+        extras["step_hbm"] = {"bytes": step_bytes, "ms": round(ms_per_step, 4),
+                              "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
+                              "frac": round(step_bytes / (ms_per_step * 1e6) / hbm, 4)}
+        extras["dispatch_share"] = {k: round(v / step_ns, 4) for k, v in sorted(total.items(), key=lambda kv: -kv[1])}
+        tdec.close()
+        if not args.no_extras:
+            extras.update(side_measurements(pkg, syn, ctx, torch, tc, peak_kind, weights))
+        cpu = None if args.no_cpu else cpu_baseline(syn, shape, weights)
+        c = clocks.summary()
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights seed 0 (numpy PCG64), N(0,1) bf16 embeddings",
+            "config": {"workload": "config 2: 0.5B-shaped bf16 backbone, 512-position prefill then "
+                                   "decode at batch 1, one request per GPU",
+                       "layers": 24, "hidden": 1024, "heads": "16q/2kv", "head_dim": 64, "ffn": 4096,
+                       "batch": 1, "positions": f"{PREFILL}..", "parallelism": f"replicas x{world}",
+                       "l2": "weights 717 MB > 126 MB L2 each step; no flush"},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 4 + 4,
+                    "d2h_bytes_per_step": H * 4},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "gpu_launches": (6 * shape.layers + 1) * args.steps,
+            "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
+            "extras": extras,
+        }
+    pre.close()
+    dec.close()
+    ctx.close()
+    return result
+
+
+def side_measurements(pkg, syn, ctx, torch, tc_peak, peak_kind, weights):
+    """Prefill throughput (config 2's 512-position prefill, and config 4's 16 x 2048) and the
+    tcgen05 GEMM's tensor-core fraction on config 4's gate/up projection."""
+    out = {}
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=2048)
+    dec = pkg.Decoder(ctx, shape, rows=16, slots=16, dtype="bf16")
+    dec.load(weights)
+    rows = 16 * 2048
+    pre = pkg.Prefill(dec, max_rows=rows, timed=True)
+    x = torch.randn(rows, cfg.hidden, device=f"cuda:{ctx.device}").to(torch.bfloat16).float()
+    o = torch.empty_like(x)
+    runs = [(0, 2048, s) for s in range(16)]
+    pre.run_batch_device(runs, x.data_ptr(), o.data_ptr())
+    ctx.synchronize()
+    times, per = [], {}
+    for _ in range(3):
+        pre.run_batch_device(runs, x.data_ptr(), o.data_ptr())
+        ctx.synchronize()
+        times.append(pre.elapsed_ns())
+        for label, ns in pre.timings():
+            per[label] = per.get(label, 0.0) + ns / 3
+    ns = min(times)
+    gemm_flops = 2 * rows * 14_942_208 * 24
+    gemm_ns = sum(v for k, v in per.items() if k.endswith("_proj"))
+    gu_ns = per.get("gate_up_proj", 0.0)
+    gu_flops = 2 * rows * 8192 * 1024 * 24
+    out["prefill_c4"] = {"rows": rows, "tokens_per_s": round(rows / (ns / 1e9), 1), "ms": round(ns / 1e6, 3),
+                         "gemm_tflops": round(gemm_flops / gemm_ns / 1e3, 1),
+                         "gemm_frac_of_peak": round(gemm_flops / gemm_ns / 1e3 / tc_peak, 4),
+                         "gate_up_gemm_tflops": round(gu_flops / gu_ns / 1e3, 1),
+                         "peak_tflops": tc_peak, "peak_source": peak_kind,
+                         "share": {k: round(v / sum(per.values()), 4) for k, v in sorted(per.items(), key=lambda kv: -kv[1])}}
+    pre.close()
+    dec.close()
+    return out
+
+
+def cpu_baseline(syn, shape, weights, seconds=10.0, max_steps=64):
+    """The CPU oracle on this host's cores: decode steps at batch 1 from position 512 over a KV
+    cache filled with N(0,1) values (a step's cost does not depend on the cache's values)."""
+    import oracle
+
+    threads = os.cpu_count() or 1
+    stack = oracle.OracleStack(shape, syn.as_f32(weights), threads=threads)
+    rng = np.random.default_rng(9)
+    for l in range(shape.layers):
+        stack.k_cache[l][:] = rng.standard_normal(stack.k_cache[l].shape, dtype=np.float32)
+        stack.v_cache[l][:] = rng.standard_normal(stack.v_cache[l].shape, dtype=np.float32)
+    x = rng.standard_normal((1, shape.hidden), dtype=np.float32)
+    stack.decode_step([(PREFILL, 0)], x)
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_steps and time.perf_counter() - t0 < seconds:
+        x = stack.decode_step([(PREFILL + 1 + n, 0)], x)
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": round(n / dt, 3), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} decode steps at batch 1 from position {PREFILL + 1} (f32 oracle, "
+                      f"{shape.layers} layers), {dt:.1f} s"}
+
+
+def run_reference(args, rank, world, local):
+    if rank != 0:
+        return None
+    import __graft_entry__ as entry
+
+    entry.load_package()
+    from tgtts_v4_b200 import synthetic as syn
+
+    import oracle
+
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=CAPACITY)
+    weights = syn.make_weights(cfg, seed=0)
+    threads = os.cpu_count() or 1
+    stack = oracle.OracleStack(shape, weights, threads=threads)
+    rng = np.random.default_rng(9)
+    for l in range(shape.layers):
+        stack.k_cache[l][:] = rng.standard_normal(stack.k_cache[l].shape, dtype=np.float32)
+        stack.v_cache[l][:] = rng.standard_normal(stack.v_cache[l].shape, dtype=np.float32)
+    x = rng.standard_normal((1, shape.hidden), dtype=np.float32)
+    for i in range(args.warmup):
+        x = stack.decode_step([(PREFILL + (i % 256), 0)], x)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        x = stack.decode_step([(PREFILL + ((args.warmup + i) % 256), 0)], x)
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    sample = (f"{args.steps} decode steps at batch 1 from position {PREFILL} over a 512-position "
+              f"cache, f32, all {threads} host threads")
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt * 1e3 / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config 2: 0.5B-shaped backbone decode at batch 1 from position 512",
+                       "parallelism": "CPU, rank 0"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "tgtts-v4 cannot run here (Rust toolchain absent; GPU path is Vulkan): "
+                    "the reference arm is the C restatement of its CPU f32 model (oracle/)"}
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_init(args.gpus)
+    if args.impl == "reference":
+        res = run_reference(args, rank, world, local)
+    else:
+        res = run_ours(args, rank, world, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res))
+        sys.stdout.flush()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

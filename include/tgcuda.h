@@ -1,0 +1,275 @@
+/*
+ * tgcuda: the B200 (sm_100a) runtime and kernels for the MiniCPM-4 stack that tgtts-v4's `graph`
+ * crate drives, behind a plain C ABI. It replaces the `vulkan` crate (crates/vulkan/src/lib.rs:50-60)
+ * as the layer under `graph::step::Step`, and the GLSL/MLIR kernels of kernels/glsl and
+ * kernels/gpu, for the decode step (crates/graph/src/decode.rs) and the prefill
+ * (crates/graph/src/prefill.rs).
+ *
+ * Every function returns a tg_status; on failure, tg_last_error() holds a message for the calling
+ * thread. Shape and size violations are refused before anything is launched. Nothing here
+ * falls back to the CPU: without a usable CUDA device, tg_ctx_create fails.
+ *
+ * Element types: the residual stream, norms' gains, RoPE tables, partial attention sums and every
+ * host-facing hidden state are f32. The storage type of a stack (tg_dtype) is that of its weights,
+ * KV cache and of the vectors its projections multiply (q, attention output, SiLU output, normed
+ * inputs): f32 or bf16, always with f32 accumulation.
+ */
+#ifndef TGCUDA_H
+#define TGCUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TGCUDA_ABI_VERSION 1u
+
+/* graph::Error / vulkan::Error (crates/graph/src/lib.rs:41-59, crates/vulkan/src/error.rs:3-40),
+ * as status codes. */
+typedef enum {
+    TG_OK = 0,
+    TG_EINVAL = 1,     /* a null handle or pointer, an unknown name or kernel */
+    TG_ESHAPE = 2,     /* graph::Error::Shape: shapes or placements the kernels cannot run */
+    TG_ECUDA = 3,      /* vulkan::Error::Vk: a CUDA call failed */
+    TG_ENOMEM = 4,     /* vulkan::Error::NoMemoryType: an allocation failed */
+    TG_ETIMEOUT = 5,   /* a wait ran past its deadline (crates/vulkan/src/context.rs:119-136) */
+    TG_ENOTFINITE = 6, /* graph::Error::NotFinite */
+    TG_EKERNEL = 7,    /* a kernel reported an error word (a bounded wait that gave up) */
+    TG_ENODEVICE = 8   /* vulkan::Error::NoDevice */
+} tg_status;
+
+/* vulkan::Residence (crates/vulkan/src/memory.rs): where a buffer lives. */
+typedef enum {
+    TG_RES_DEVICE = 0,   /* HBM, for the GPU alone; the host reaches it by copies */
+    TG_RES_UPLOAD = 1,   /* pinned host memory the host writes and the GPU reads */
+    TG_RES_READBACK = 2  /* pinned host memory the GPU writes and the host reads */
+} tg_residence;
+
+typedef enum { TG_F32 = 0, TG_BF16 = 1 } tg_dtype;
+
+typedef struct tg_ctx tg_ctx;
+typedef struct tg_mem tg_mem;
+typedef struct tg_program tg_program;
+typedef struct tg_decoder tg_decoder;
+typedef struct tg_prefill tg_prefill;
+
+/* The message of the calling thread's last failure, or "" (never NULL). */
+const char *tg_last_error(void);
+uint32_t tg_abi_version(void);
+
+/* ---- Context (crates/vulkan/src/context.rs:198-240) ------------------------------------- */
+
+/* A context on CUDA device `device`, with its own stream. Fails with TG_ENODEVICE when there is
+ * no such device or it is not an sm_100 part. */
+int tg_ctx_create(int device, tg_ctx **out);
+int tg_ctx_destroy(tg_ctx *ctx);
+/* Waits for all work on the context's stream, polling until `timeout_ns` (0: no limit). */
+int tg_ctx_synchronize(tg_ctx *ctx, uint64_t timeout_ns);
+/* The device's name and SM count. */
+int tg_ctx_info(tg_ctx *ctx, char *name, size_t name_bytes, int *sm_count);
+/* The context's CUDA stream (a cudaStream_t), on which every program of the context runs: callers
+ * time them with events recorded on it. */
+void *tg_ctx_stream(tg_ctx *ctx);
+
+/* ---- Memory (Context::memory_in / buffer_in, crates/vulkan/src/context.rs:487-495) -------- */
+
+int tg_mem_alloc(tg_ctx *ctx, uint64_t bytes, tg_residence residence, tg_mem **out);
+int tg_mem_free(tg_mem *mem);
+uint64_t tg_mem_size(const tg_mem *mem);
+/* The buffer's address for the GPU (a device pointer, or the mapped address of pinned memory). */
+void *tg_mem_device_ptr(const tg_mem *mem);
+/* Buffer::write_at / read_at (crates/vulkan/src/memory.rs:518-548): synchronous. */
+int tg_mem_write(tg_mem *mem, uint64_t offset, const void *src, uint64_t bytes);
+int tg_mem_read(tg_mem *mem, uint64_t offset, void *dst, uint64_t bytes);
+int tg_mem_fill(tg_mem *mem, uint64_t offset, uint32_t word, uint64_t bytes);
+
+/* Recording::copy_in / copy_out (crates/vulkan/src/recording.rs:522-532): copies of byte ranges
+ * between two buffers on the GPU, in order, on the context's stream; waits for them. */
+typedef struct {
+    uint64_t src_offset, dst_offset, bytes;
+} tg_region;
+int tg_copy_regions(tg_ctx *ctx, tg_mem *src, tg_mem *dst, const tg_region *regions, size_t n);
+
+/* ---- Kernel table (crates/graph/src/kernels.rs:104-161, crates/graph/src/prefill.rs:32-131) --
+ * Each kernel takes its bindings in the order listed and a params struct. A dispatch whose
+ * bindings are too small for what its params say it reaches is refused (Kernels::check,
+ * crates/graph/src/kernels.rs:232-263). "T" is the params' dtype. */
+typedef enum {
+    /* x f32 [rows][hidden], gain f32 [hidden] -> out f32 [rows][hidden]           rmsnorm.comp */
+    TG_KERNEL_RMSNORM = 0,
+    /* x f32 [rows][hidden], gain f32, W T [(heads+2kv)hd][hidden], cos f32, sin f32,
+     * at u32 [2 rows] -> q T [rows][heads][hd], k cache T, v cache T            gemv_qkv_rope.comp */
+    TG_KERNEL_GEMV_QKV_ROPE = 1,
+    /* q T, k cache T, v cache T, at u32 -> partial_o f32 [rows][heads][chunks][hd],
+     * partial_ml f32 [rows][heads][chunks][2]                                  attention_split.comp */
+    TG_KERNEL_ATTENTION_SPLIT = 2,
+    /* at u32, partial_o f32, partial_ml f32 -> out T [rows][heads hd]        attention_combine.comp */
+    TG_KERNEL_ATTENTION_COMBINE = 3,
+    /* x T [rows][k], W T [n][k], residual f32 [rows][n] -> out f32 [rows][n]  gemv_residual.comp */
+    TG_KERNEL_GEMV_RESIDUAL = 4,
+    /* x f32 [rows][hidden], gain f32, W T [2 inner][hidden] -> out T [rows][inner] gemv_gate_up.comp */
+    TG_KERNEL_GEMV_GATE_UP = 5,
+    /* data u32 -> out u32 (one word per block)                                  stream_read.comp */
+    TG_KERNEL_STREAM_READ = 6,
+    /* at u32 [2 rows], x f32, gain f32 -> out T                                   norm_rows.comp */
+    TG_KERNEL_NORM_ROWS = 7,
+    /* at u32, c f32 [rows][hidden], residual f32, gain f32 -> sum f32, normed (T, or f32 when
+     * params.normed_f32)                                                      add_norm_rows.comp */
+    TG_KERNEL_ADD_NORM_ROWS = 8,
+    /* at u32, c f32 [rows][(heads+2kv)hd], cos f32, sin f32 -> q T, k cache T, v cache T
+     *                                                                             rope_rows.comp */
+    TG_KERNEL_ROPE_ROWS = 9,
+    /* at u32, q T [rows][heads][hd], k cache T, v cache T -> out T           attention_rows.comp */
+    TG_KERNEL_ATTENTION_ROWS = 10,
+    /* at u32, c f32 [rows][2 inner] -> out T [rows][inner]                     silu_mul_rows.comp */
+    TG_KERNEL_SILU_MUL_ROWS = 11,
+    /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32) */
+    TG_KERNEL_GEMM = 12,
+    TG_KERNEL_COUNT = 13
+} tg_kernel_id;
+
+/* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the
+ * residual scale BASELINE's configs use; 1.0 reproduces tgtts-v4). `rows` is the rows a
+ * dispatch covers and `slots` the cache's slots. */
+typedef struct {
+    uint32_t dtype; /* tg_dtype */
+    uint32_t hidden, inner, heads, kv_heads, head_dim, capacity;
+    uint32_t rows, slots;
+    float eps, residual_scale;
+    uint32_t rope;       /* 0: q and k are not rotated */
+    uint32_t normed_f32; /* ADD_NORM_ROWS: normed is f32 (the final norm) rather than T */
+    uint32_t m, n, k;    /* GEMM, GEMV_RESIDUAL (n outputs of k), STREAM_READ (k words) */
+} tg_params;
+
+typedef struct {
+    tg_mem *mem;
+    uint64_t offset, bytes;
+} tg_binding;
+
+/* vulkan::Dispatch (crates/vulkan/src/recording.rs:33-87); the grid is derived from the params. */
+typedef struct {
+    uint32_t kernel; /* tg_kernel_id */
+    const tg_params *params;
+    const tg_binding *bindings;
+    uint32_t n_bindings;
+    const char *label; /* for timings; may be NULL */
+} tg_dispatch;
+
+/* Context::dispatch (crates/vulkan/src/context.rs:520): runs one dispatch, waits, and gives its
+ * GPU time in ns (may be NULL). */
+int tg_dispatch_once(tg_ctx *ctx, const tg_dispatch *d, double *ns);
+
+/* ---- Programs (Context::record / Recording, crates/vulkan/src/recording.rs:161-260, :599-760).
+ * A program is a chain of dispatches, checked once and captured into one CUDA graph, run as
+ * often as needed. `timed` adds an event between dispatches for per-dispatch times. */
+int tg_program_create(tg_ctx *ctx, const tg_dispatch *dispatches, size_t n, int timed,
+                      tg_program **out);
+int tg_program_destroy(tg_program *p);
+/* Recording::start_program: launches the graph and returns without waiting. */
+int tg_program_start(tg_program *p);
+/* Submission::wait: polls until the run ends or `timeout_ns` passes (TG_ETIMEOUT; the run stays
+ * pending and is waited for again before the next start). 0: no limit. */
+int tg_program_wait(tg_program *p, uint64_t timeout_ns);
+/* The last run's GPU time, and with `timed`, each dispatch's (n = dispatch count). */
+int tg_program_elapsed_ns(tg_program *p, double *ns);
+int tg_program_timings(tg_program *p, double *ns, size_t n);
+
+/* ---- The stack: shape, placement, decoder, prefill (crates/graph/src/decode.rs,
+ * crates/graph/src/prefill.rs) --------------------------------------------------------------- */
+
+/* decode.rs:66-83 `Shape`, plus `residual_scale`. rope_factors: head_dim/2 LongRoPE divisors, or
+ * NULL for all 1 (plain RoPE). */
+typedef struct {
+    uint32_t hidden, inner, heads, kv_heads, head_dim, layers, capacity;
+    float eps, rope_theta, residual_scale;
+    uint32_t rope;
+    const double *rope_factors;
+} tg_shape;
+
+/* Shape::weight_bytes / cache_bytes (decode.rs:127-141) at `bytes_per_weight` (2 for f16/bf16). */
+uint64_t tg_shape_weight_bytes(const tg_shape *s, uint32_t bytes_per_weight);
+uint64_t tg_shape_cache_bytes(const tg_shape *s, uint32_t position, uint32_t bytes_per_value);
+/* Shape::rope_tables (decode.rs:143-168): [capacity][head_dim/2] each, computed in f32. */
+int tg_shape_rope_tables(const tg_shape *s, float *cos_out, float *sin_out);
+
+/* decode.rs:230-235 `Row`: a position of a cache slot, or spare (position = TG_SPARE). */
+#define TG_SPARE 0xffffffffu
+typedef struct {
+    uint32_t position, slot;
+} tg_row;
+
+/* Batch::placement (decode.rs:198-227): the words for `n_rows` rows of a batch of `slots` slots
+ * (positions, then slots when slots > 1; spare rows TG_SPARE). Refuses two rows in one slot and
+ * places past the capacity or slots (TG_ESHAPE). `words` holds 2 n_rows. */
+int tg_batch_placement(uint32_t n_rows, uint32_t slots, const tg_row *rows, uint32_t capacity,
+                       uint32_t *words, uint32_t *n_words);
+
+/* Decoder::with_batch (decode.rs:790-806): the decode step of `s` for a batch of `rows` rows
+ * in a cache of `slots` slots, recorded once, with zero weights until loaded. */
+int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, uint32_t slots,
+                      tg_dtype dtype, int timed, tg_decoder **out);
+int tg_decoder_destroy(tg_decoder *d);
+/* Decoder::load (decode.rs:808-820, load_stack :740-776): one weight by its upstream name
+ * ("layers.{l}.self_attn.{q,k,v,o}_proj.weight", "layers.{l}.mlp.{gate,up,down}_proj.weight",
+ * "layers.{l}.{input,post_attention}_layernorm.weight", "norm.weight"), from host f32
+ * (src_dtype TG_F32) or bf16 bits (TG_BF16), converted to the decoder's dtype (RNE). q/k/v and
+ * gate/up are joined along their rows as load_stack joins them. */
+int tg_decoder_load(tg_decoder *d, const char *name, const void *src, uint64_t count,
+                    tg_dtype src_dtype);
+/* Decoder::step_rows (decode.rs:849-853): x [rows][hidden] f32 in, out [rows][hidden] f32 out;
+ * a spare row's output is meaningless. */
+int tg_decoder_step_rows(tg_decoder *d, const tg_row *rows, const float *x, float *out);
+/* Decoder::set_rows / start / output (decode.rs:857-872), for callers that overlap host work. */
+int tg_decoder_set_rows(tg_decoder *d, const tg_row *rows, const float *x);
+int tg_decoder_start(tg_decoder *d);
+int tg_decoder_wait(tg_decoder *d, uint64_t timeout_ns);
+int tg_decoder_output(tg_decoder *d, float *out);
+/* Device-resident step for callers whose inputs are already on the GPU: placement words (as
+ * tg_batch_placement gives) from the host, x and out device pointers of [rows][hidden] f32. */
+int tg_decoder_step_device(tg_decoder *d, const uint32_t *words, const float *x_dev,
+                           float *out_dev);
+/* Decoder::timings: the last step's GPU time, and per dispatch when created timed. */
+int tg_decoder_elapsed_ns(tg_decoder *d, double *ns);
+int tg_decoder_timings(tg_decoder *d, double *ns, size_t n, size_t *n_dispatches);
+/* The recorded dispatches' count and labels (decode.rs:935-951: 6 per layer and the final norm). */
+int tg_decoder_dispatch_label(tg_decoder *d, size_t i, char *label, size_t label_bytes);
+/* Copies positions [first, first+count) of a slot's keys (kind 0) or values (1) of a layer to the
+ * host as f32 [kv_heads][count][head_dim]. */
+int tg_decoder_read_cache(tg_decoder *d, uint32_t layer, uint32_t slot, uint32_t kind,
+                          uint32_t first, uint32_t count, float *out);
+/* Recording::copy_out / copy_in of KV ranges (crates/graph/src/step.rs:295-339,
+ * crates/graph/src/prompt.rs:587-633): moves positions [0, count) of slot `from` to slot `to`
+ * in every layer, on the GPU. */
+int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, uint32_t count);
+/* The weight bytes one step reads at this dtype (Shape::weight_bytes at its element size). */
+uint64_t tg_decoder_weight_bytes(const tg_decoder *d);
+
+/* Prefill::new (prefill.rs:431-461): programs over the decoder's weights, tables and cache for up
+ * to `max_rows` rows at once. */
+int tg_prefill_create(tg_decoder *d, uint32_t max_rows, int timed, tg_prefill **out);
+int tg_prefill_destroy(tg_prefill *p);
+/* Prefill::run (prefill.rs:473-503): x [len][hidden] f32 of positions start..start+len-1 into
+ * `slot`, out [len][hidden] f32 after the final norm. Longer runs than max_rows go in pieces. */
+int tg_prefill_run(tg_prefill *p, uint32_t start, uint32_t slot, const float *x, uint32_t len,
+                   float *out);
+/* Several runs at once, each in its own slot, rows packed in order (each run's rows start on a
+ * multiple of 64 inside the launch): the batched prefill of BASELINE config 4. */
+typedef struct {
+    uint32_t start, len, slot;
+} tg_run;
+int tg_prefill_run_batch(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x,
+                         float *out);
+/* Device-resident variant: x_dev/out_dev are device pointers [sum len][hidden] f32. */
+int tg_prefill_run_batch_device(tg_prefill *p, const tg_run *runs, uint32_t n_runs,
+                                const float *x_dev, float *out_dev);
+int tg_prefill_elapsed_ns(tg_prefill *p, double *ns);
+int tg_prefill_timings(tg_prefill *p, double *ns, size_t n, size_t *n_dispatches);
+int tg_prefill_dispatch_label(tg_prefill *p, size_t i, char *label, size_t label_bytes);
+uint32_t tg_prefill_max_rows(const tg_prefill *p);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

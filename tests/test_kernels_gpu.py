@@ -1,0 +1,89 @@
+"""Single kernels of the table on the GPU, dispatched through the C ABI (tg_dispatch_once),
+against f64 references; and the dispatch checks that refuse a binding too small for its params."""
+
+import numpy as np
+import pytest
+
+from conftest import distance
+
+pytestmark = pytest.mark.gpu
+
+
+def _mem(pkg, ctx, a):
+    a = np.ascontiguousarray(a)
+    m = pkg.Memory(ctx, max(a.nbytes, 16))
+    m.write(a)
+    return m
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 1280, 1024), (384, 1024, 4096), (200, 192, 256),
+                                   (128, 128, 128), (512, 8192, 1024)])
+def test_tcgen05_gemm_matches_f64(pkg, ctx, syn, m, n, k):
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((n, k), dtype=np.float32) * 0.02
+    ab, bb = syn.bf16_bits(a), syn.bf16_bits(b)
+    ma, mb = _mem(pkg, ctx, ab), _mem(pkg, ctx, bb)
+    mc = pkg.Memory(ctx, m * n * 4)
+    shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "bf16", rows=m, m=m, n=n, k=k)
+    pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, ab.nbytes), (mb, 0, bb.nbytes), (mc, 0, m * n * 4)])
+    got = mc.read(np.float32, m * n).reshape(m, n)
+    af, bf = syn.bf16_to_f32(ab).astype(np.float64), syn.bf16_to_f32(bb).astype(np.float64)
+    want = af @ bf.T
+    # An f32 sum of k products is within k unit roundoffs of the sum of their magnitudes.
+    bound = k * 2.0**-24 * (np.abs(af) @ np.abs(bf).T) + 1e-30
+    assert np.all(np.abs(got - want) <= bound), float(np.max(np.abs(got - want) / bound))
+    # A defect the bound catches: one k-step of 16 left out.
+    short = af[:, 16:] @ bf[:, 16:].T
+    assert np.mean(np.abs(short - want) > bound) > 0.5
+
+
+def test_simt_gemm_f32(pkg, ctx):
+    rng = np.random.default_rng(1)
+    m, n, k = 100, 72, 48
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((n, k), dtype=np.float32)
+    ma, mb, mc = _mem(pkg, ctx, a), _mem(pkg, ctx, b), pkg.Memory(ctx, m * n * 4)
+    shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "f32", rows=m, m=m, n=n, k=k)
+    pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, a.nbytes), (mb, 0, b.nbytes), (mc, 0, m * n * 4)])
+    got = mc.read(np.float32, m * n).reshape(m, n)
+    np.testing.assert_allclose(got, a.astype(np.float64) @ b.T.astype(np.float64), atol=1e-4)
+
+
+def test_a_binding_smaller_than_its_reach_is_refused(pkg, ctx):
+    shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "f32", rows=2)
+    x, g, out = pkg.Memory(ctx, 2 * 256 * 4), pkg.Memory(ctx, 256 * 4), pkg.Memory(ctx, 256 * 4)
+    with pytest.raises(pkg.ShapeError):
+        pkg.dispatch_once(ctx, "rmsnorm", p, [(x, 0, 2 * 256 * 4), (g, 0, 256 * 4), (out, 0, 256 * 4)])
+    with pytest.raises(pkg.InvalidError):
+        pkg.dispatch_once(ctx, "rmsnorm", p, [(x, 0, 2 * 256 * 4), (g, 0, 256 * 4)])
+
+
+def test_rmsnorm_kernel(pkg, ctx):
+    import oracle
+
+    rng = np.random.default_rng(2)
+    rows, h = 5, 1024
+    x = rng.standard_normal((rows, h), dtype=np.float32) * 3
+    g = (1 + 0.25 * rng.standard_normal(h)).astype(np.float32)
+    mx, mg, mo = _mem(pkg, ctx, x), _mem(pkg, ctx, g), pkg.Memory(ctx, x.nbytes)
+    shape = pkg.Shape(hidden=h, inner=1024, heads=16, kv_heads=2, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "f32", rows=rows)
+    pkg.dispatch_once(ctx, "rmsnorm", p, [(mx, 0, x.nbytes), (mg, 0, g.nbytes), (mo, 0, x.nbytes)])
+    got = mo.read(np.float32, rows * h).reshape(rows, h)
+    want = np.stack([oracle.rmsnorm(x[i], g, 1e-5) for i in range(rows)])
+    assert distance(got, want)[0] < 1e-5
+
+
+def test_stream_read_reads_every_word(pkg, ctx):
+    words = np.arange(1 << 20, dtype=np.uint32) * np.uint32(2654435761)
+    m = _mem(pkg, ctx, words)
+    out = pkg.Memory(ctx, 148 * 8 * 4 * 4)
+    shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "f32", rows=0, k=words.size, n=ctx.sm_count * 8)
+    pkg.dispatch_once(ctx, "stream_read", p, [(m, 0, words.nbytes), (out, 0, ctx.sm_count * 8 * 4)])
+    got = out.read(np.uint32, ctx.sm_count * 8)
+    assert np.bitwise_xor.reduce(got) == np.bitwise_xor.reduce(words)

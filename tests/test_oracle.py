@@ -1,0 +1,163 @@
+"""The CPU oracle pinned to tgtts-v4's own known answers and cross-checked against an independent
+numpy restatement. No GPU."""
+
+import json
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle import ref_numpy
+from conftest import distance
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def test_rms_layernorm_matches_the_reference_fixture():
+    # crates/testkit/tests/testkit.rs:57-68 and fixtures/testkit.py:16-18: upstream's
+    # rms_layernorm([[3, 4]], [1, 2], eps 0) = [3/sqrt(12.5), 8/sqrt(12.5)] within 1e-6.
+    fix = json.loads((GOLDEN / "reference_testkit.json").read_text())["rms_layernorm"]
+    got = oracle.rmsnorm(np.array([3.0, 4.0]), np.array([1.0, 2.0]), 0.0)
+    want = np.array(fix["out"][0], np.float32)
+    rms = math.sqrt(12.5)
+    for g, w in zip(got, [3 / rms, 8 / rms]):
+        assert abs(g - w) <= 1e-6 + 1e-6 * abs(w)
+    assert np.max(np.abs(got - want)) <= 1e-6
+    np.testing.assert_allclose(ref_numpy.rmsnorm([3.0, 4.0], [1.0, 2.0], 0.0), want, atol=1e-6)
+
+
+def test_bf16_rounding_matches_the_bytes_torch_stored(syn):
+    # crates/testkit/tests/testkit.rs:45-55: bf16 [1.0, -2.5, 0.1, 3.14159] as torch rounds it.
+    fix = json.loads((GOLDEN / "reference_testkit.json").read_text())["bf16"]
+    bits = syn.bf16_bits(np.array(fix["values"], np.float32))
+    assert list(bits.astype("<u2").tobytes()) == fix["bytes"]
+    # Ties go to even: 1 + 2^-8 sits halfway between 1 and 1 + 2^-7.
+    assert syn.bf16_bits(np.array([1 + 2**-8], np.float32))[0] == 0x3F80
+    assert syn.bf16_bits(np.array([1 + 3 * 2**-8], np.float32))[0] == 0x3F82
+
+
+@pytest.mark.parametrize("tables", ["oracle", "numpy"])
+def test_rope_tables_start_at_the_identity_and_turn_at_each_rate(tables):
+    # crates/graph/src/decode.rs:1232-1242: position 0 is the identity; position 1, frequency 0
+    # is one radian.
+    fn = oracle.rope_tables if tables == "oracle" else ref_numpy.rope_tables
+    cos, sin = fn(128, 64, 10000.0)
+    assert cos.shape == (64, 64)
+    assert np.all(cos[0] == 1.0) and np.all(sin[0] == 0.0)
+    assert cos[1, 0] == np.float32(math.cos(1.0))
+    assert sin[1, 0] == np.float32(math.sin(1.0))
+
+
+def test_rope_tables_follow_longrope_factors():
+    cos, sin = oracle.rope_tables(8, 16, 10000.0, [0.99, 1.6, 3.4, 8.9])
+    cn, sn = ref_numpy.rope_tables(8, 16, 10000.0, [0.99, 1.6, 3.4, 8.9])
+    np.testing.assert_allclose(cos, cn, atol=2e-7)
+    np.testing.assert_allclose(sin, sn, atol=2e-7)
+
+
+def _tiny_shape(pkg, **kw):
+    base = dict(hidden=64, inner=96, heads=4, kv_heads=2, head_dim=16, layers=2, capacity=32,
+                eps=1e-5, rope_theta=10000.0, residual_scale=0.7)
+    base.update(kw)
+    return pkg.Shape(**base)
+
+
+def _weights(shape, seed=0, zero=False):
+    rng = np.random.default_rng(seed)
+    h, i, d = shape.hidden, shape.inner, shape.head_dim
+    w = {}
+    for l in range(shape.layers):
+        shapes = {"self_attn.q_proj": (shape.heads * d, h), "self_attn.k_proj": (shape.kv_heads * d, h),
+                  "self_attn.v_proj": (shape.kv_heads * d, h), "self_attn.o_proj": (h, shape.heads * d),
+                  "mlp.gate_proj": (i, h), "mlp.up_proj": (i, h), "mlp.down_proj": (h, i)}
+        for n, s in shapes.items():
+            w[f"layers.{l}.{n}.weight"] = np.zeros(s, np.float32) if zero else rng.standard_normal(s, dtype=np.float32) * 0.1
+        for g in ("input_layernorm", "post_attention_layernorm"):
+            w[f"layers.{l}.{g}.weight"] = np.zeros(h, np.float32) if zero else (1 + 0.1 * rng.standard_normal(h)).astype(np.float32)
+    w["norm.weight"] = np.zeros(h, np.float32) if zero else (1 + 0.1 * rng.standard_normal(h)).astype(np.float32)
+    return w
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_oracle_decode_matches_the_numpy_restatement(pkg, rope):
+    shape = _tiny_shape(pkg, rope=rope)
+    w = _weights(shape)
+    c = oracle.OracleStack(shape, w, slots=3, threads=3)
+    n = ref_numpy.NumpyStack(shape, w, slots=3)
+    rng = np.random.default_rng(5)
+    # Rows in slots 2 and 0 advance together, with a spare row between them.
+    for t in range(6):
+        rows = [(t, 2), None, (t + 3, 0)] if t < 5 else [(t, 2), None, None]
+        x = rng.standard_normal((3, shape.hidden)).astype(np.float32)
+        got = c.decode_step(rows, x)
+        want = n.decode_step(rows, x)
+        assert distance(got, want)[0] < 1e-4
+        assert np.all(got[1] == 0)
+
+
+def test_oracle_prefill_matches_numpy_and_equals_its_decode_steps_bit_for_bit(pkg):
+    shape = _tiny_shape(pkg)
+    w = _weights(shape, seed=3)
+    x = np.random.default_rng(7).standard_normal((9, shape.hidden)).astype(np.float32)
+    a = oracle.OracleStack(shape, w, threads=4)
+    pre = a.prefill(0, x[:5])
+    pre2 = a.prefill(5, x[5:])  # a second piece goes on from the first's cache
+    n = ref_numpy.NumpyStack(shape, w)
+    want = np.concatenate([n.prefill(0, x[:5]), n.prefill(5, x[5:])])
+    assert distance(np.concatenate([pre, pre2]), want)[0] < 1e-4
+    b = oracle.OracleStack(shape, w, threads=1)
+    steps = np.concatenate([b.decode_step([(t, 0)], x[t][None]) for t in range(9)])
+    assert np.array_equal(steps, np.concatenate([pre, pre2]))
+    for l in range(shape.layers):
+        assert np.array_equal(a.k_cache[l], b.k_cache[l]) and np.array_equal(a.v_cache[l], b.v_cache[l])
+
+
+def test_oracle_is_the_same_at_any_thread_count(pkg):
+    shape = _tiny_shape(pkg)
+    w = _weights(shape, seed=4)
+    x = np.random.default_rng(1).standard_normal((7, shape.hidden)).astype(np.float32)
+    outs = [oracle.OracleStack(shape, w, threads=t).prefill(0, x) for t in (1, 2, 5)]
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+
+
+def test_zero_weights_give_zero(pkg):
+    # crates/graph/tests/prefill.rs:303-319: a stack of zero weights gives zero outputs.
+    shape = _tiny_shape(pkg)
+    out = oracle.OracleStack(shape, _weights(shape, zero=True)).prefill(0, np.ones((4, shape.hidden), np.float32))
+    assert np.all(out == 0)
+
+
+def test_refused_shapes(pkg):
+    shape = _tiny_shape(pkg)
+    stack = oracle.OracleStack(shape, _weights(shape))
+    with pytest.raises(ValueError):
+        stack.prefill(30, np.zeros((5, shape.hidden), np.float32))  # past the capacity
+
+
+def test_gemm_sums_each_product_in_k_order():
+    # kernels/gpu/cpu_oracle.py:276-286: C = A B^T with each sum sequential in K.
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((5, 37)).astype(np.float32)
+    b = rng.standard_normal((7, 37)).astype(np.float32)
+    c = oracle.gemm_abt(a, b, threads=2)
+    seq = np.zeros((5, 7), np.float32)
+    for k in range(37):
+        seq = (seq + a[:, k][:, None] * b[:, k][None, :]).astype(np.float32)
+    np.testing.assert_allclose(c, seq, rtol=0, atol=1e-5)
+    np.testing.assert_allclose(c, a.astype(np.float64) @ b.T.astype(np.float64), atol=1e-4)
+
+
+def test_oracle_reproduces_its_committed_outputs_for_config_1(pkg, syn):
+    gold = np.load(GOLDEN / "oracle_tiny.npz")
+    cfg = syn.TINY
+    shape = syn.shape_of(cfg, capacity=64)
+    stack = oracle.OracleStack(shape, syn.make_weights(cfg, seed=0), threads=2)
+    x = syn.make_inputs(32, cfg.hidden, seed=1)
+    pre = stack.prefill(0, x)
+    np.testing.assert_allclose(pre, gold["prefill"], atol=1e-5)
+    h = pre[-1]
+    for t in range(16):
+        h = stack.decode_step([(32 + t, 0)], h[None])[0]
+        np.testing.assert_allclose(h, gold["decode"][t], atol=1e-5)

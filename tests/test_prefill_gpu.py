@@ -1,0 +1,101 @@
+"""The prefill on the GPU against the oracle: runs in pieces, several runs at once, zero weights,
+and the refusals (crates/graph/tests/prefill.rs:278-363)."""
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import distance
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_prefill_in_pieces_matches_one_run_and_the_oracle(pkg, ctx, syn, dtype):
+    cfg = syn.TINY if dtype == "f32" else syn.S05B
+    shape = syn.shape_of(cfg, capacity=512, layers=2)
+    w = syn.make_weights(cfg, seed=0, layers=2, jitter_gains=True)
+    x = syn.make_inputs(300, cfg.hidden, seed=2, bf16=dtype == "bf16")
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype=dtype)
+    dec.load(w)
+    whole = pkg.Prefill(dec, max_rows=384).run(0, x)
+    small = pkg.Prefill(dec, max_rows=128)
+    pieces = small.run(0, x)  # three pieces of at most 128
+    assert small.max_rows() == 128
+    ref = oracle.OracleStack(shape, w)
+    want = ref.prefill(0, x)
+    tol = 2e-4 if dtype == "f32" else 2e-2
+    for got in (whole, pieces):
+        m, _, cos = distance(got, want)
+        assert m <= tol and cos >= 0.9999, (m, cos)
+    # The cache after the run in pieces holds the oracle's keys and values.
+    kc = dec.read_cache(1, 0, "k", 0, 300)
+    assert distance(kc, ref.k_cache[1][0, :, :300])[0] <= (1e-4 if dtype == "f32" else 2e-2)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_runs_prefilled_together_match_each_run_alone(pkg, ctx, syn, dtype):
+    cfg = syn.TINY if dtype == "f32" else syn.S05B
+    shape = syn.shape_of(cfg, capacity=256, layers=2)
+    w = syn.make_weights(cfg, seed=1, layers=2)
+    runs = [(0, 70, 0), (0, 130, 1), (5, 33, 2)]
+    x = syn.make_inputs(sum(r[1] for r in runs), cfg.hidden, seed=5, bf16=dtype == "bf16")
+    dec = pkg.Decoder(ctx, shape, rows=3, slots=3, dtype=dtype)
+    dec.load(w)
+    pre = pkg.Prefill(dec, max_rows=512)
+    # The third run goes on from a 5-position prefix in its slot.
+    pre.run(0, syn.make_inputs(5, cfg.hidden, seed=6), slot=2)
+    together = pre.run_batch(runs, x)
+    alone_dec = pkg.Decoder(ctx, shape, rows=1, slots=3, dtype=dtype)
+    alone_dec.load(w)
+    alone_pre = pkg.Prefill(alone_dec, max_rows=512)
+    alone_pre.run(0, syn.make_inputs(5, cfg.hidden, seed=6), slot=2)
+    row = 0
+    for start, n, slot in runs:
+        alone = alone_pre.run(start, x[row:row + n], slot=slot)
+        assert np.array_equal(together[row:row + n], alone), (start, n, slot)
+        row += n
+
+
+def test_zero_weights_give_zero(pkg, ctx, syn):
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=128, layers=2)
+    w = {k: np.zeros_like(v) for k, v in syn.make_weights(cfg, layers=2).items()}
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16")
+    dec.load(w)
+    out = pkg.Prefill(dec, max_rows=128).run(0, np.ones((40, cfg.hidden), np.float32))
+    assert np.all(out == 0)
+
+
+def test_refused_runs(pkg, ctx, syn):
+    cfg = syn.TINY
+    shape = syn.shape_of(cfg, capacity=64, layers=1)
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype="f32")
+    pre = pkg.Prefill(dec, max_rows=128)
+    with pytest.raises(pkg.ShapeError):
+        pre.run(60, np.zeros((8, cfg.hidden), np.float32))  # past the capacity
+    with pytest.raises(pkg.ShapeError):
+        pre.run(0, np.zeros((8, cfg.hidden), np.float32), slot=1)  # no such slot
+    with pytest.raises(pkg.ShapeError):
+        pre.run(0, np.zeros(cfg.hidden + 1, np.float32))
+
+
+def test_config2_full_stack_prefill_512_and_decode(pkg, ctx, syn):
+    """BASELINE config 2 at full depth: 24 layers, a 512-position bf16 prefill, then decode steps."""
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=1024)
+    w = syn.make_weights(cfg, seed=0)
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16")
+    dec.load(w)
+    pre = pkg.Prefill(dec, max_rows=512)
+    ref = oracle.OracleStack(shape, w)
+    x = syn.make_inputs(512, cfg.hidden, seed=1, bf16=True)
+    got, want = pre.run(0, x), ref.prefill(0, x)
+    m, _, cos = distance(got, want)
+    assert m <= 2e-2 and cos >= 0.9999, (m, cos)
+    h, hr = got[-1], want[-1]
+    for t in range(4):
+        h = dec.step(512 + t, h)[0]
+        hr = ref.decode_step([(512 + t, 0)], hr[None])[0]
+        m, _, cos = distance(h, hr)
+        assert m <= 2e-2 and cos >= 0.9999, (t, m, cos)

@@ -1,0 +1,338 @@
+// The prefill's projection GEMM, C[m][n] = A[m][k] B[n][k]^T with f32 accumulation
+// (kernels/gpu/gemm.mlir:14-29; a linear layer: A the activations, B the weights as a checkpoint
+// lays them out, both K-major).
+//
+// bf16: a tcgen05 kernel. Each block computes a 128 x BN tile of C. One thread streams A and B
+// tiles of 64 columns of K into a ring of shared-memory stages with TMA (128-byte swizzle, no
+// multicast), one thread issues tcgen05.mma into a TMEM accumulator (M = 128, N = BN, K = 16 per
+// instruction) and releases each stage with tcgen05.commit, and all four warps read the
+// accumulator back with tcgen05.ld for the epilogue. Every wait on an mbarrier is bounded: past
+// its limit the kernel sets the context's error word and runs to its end.
+//
+// f32: a SIMT kernel, each sum sequential in k.
+#include <cuda.h>
+
+#include "tg_common.cuh"
+#include "tg_internal.h"
+
+namespace tg {
+
+// ---- f32 SIMT ---------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(256)
+    gemm_f32_kernel(int M, int N, int K, const float *__restrict__ A, const float *__restrict__ B,
+                    float *__restrict__ C) {
+    __shared__ float As[16][64 + 4];
+    __shared__ float Bs[16][64 + 4];
+    const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+    const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += 16) {
+        for (int i = threadIdx.x; i < 64 * 16; i += 256) {
+            const int r = i / 16, kk = i % 16;
+            As[kk][r] = (m0 + r < M && k0 + kk < K) ? A[(size_t)(m0 + r) * K + k0 + kk] : 0.0f;
+            Bs[kk][r] = (n0 + r < N && k0 + kk < K) ? B[(size_t)(n0 + r) * K + k0 + kk] : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < 16; kk++) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                a[i] = As[kk][ty * 4 + i];
+                b[i] = Bs[kk][tx * 4 + i];
+            }
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const int n = n0 + tx * 4 + j;
+            if (n < N) C[(size_t)m * N + n] = acc[i][j];
+        }
+    }
+}
+
+// ---- tcgen05 bf16 ------------------------------------------------------------------------------
+
+constexpr int TC_BM = 128, TC_BK = 64, TC_STAGES = 4, TC_THREADS = 128;
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB per stage
+
+TG_DEVICE uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+TG_DEVICE uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+TG_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+TG_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+TG_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase of parity `parity` of `bar` to complete, for at most 2 s (1 ms once the
+// block has given up on a wait). Past that it records ERR_WAIT_TIMEOUT and returns, so that the
+// kernel always ends.
+TG_DEVICE void mbar_wait(uint32_t bar, uint32_t parity, uint32_t *err, volatile int *gave_up) {
+    if (mbar_try_wait(bar, parity)) return;
+    const uint64_t limit = *gave_up ? 1000000ull : 2000000000ull;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > limit) {
+            *gave_up = 1;
+            atomicExch(err, ERR_WAIT_TIMEOUT);
+            return;
+        }
+    }
+}
+
+TG_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// The shared-memory matrix descriptor of a K-major tile with 128-byte rows in the 128-byte
+// swizzle TMA writes: start address, leading byte offset 16 (unused for this layout), stride
+// byte offset 1024 between groups of 8 rows, descriptor version 1, swizzle mode 2 (128 B).
+TG_DEVICE uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3fff) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// The instruction descriptor of kind::f16 with bf16 A and B (both K-major), f32 D, M x N.
+__host__ __device__ constexpr uint32_t bf16_idesc(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+TG_DEVICE void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+TG_DEVICE void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+TG_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+TG_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 16 consecutive f32 columns of this warp's 32 TMEM lanes: lane i of the warp gets row
+// (warp % 4) * 32 + i.
+TG_DEVICE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+template <int BN>
+struct TcLayout {
+    static constexpr int B_BYTES = BN * TC_BK * 2;
+    static constexpr int STAGE = TC_A_BYTES + B_BYTES;
+    static constexpr int BARRIERS = TC_STAGES * STAGE;  // offset of the mbarriers
+    static constexpr int SMEM = BARRIERS + 256 + 1024;  // + barriers + alignment slack
+};
+
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   float *__restrict__ C, int M, int N, int K, uint32_t *err) {
+    using L = TcLayout<BN>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t base = smem_u32(smem);
+    const uint32_t bars = base + L::BARRIERS;
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (TC_STAGES + s); };
+    const uint32_t done = bars + 8u * (2 * TC_STAGES);
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::BARRIERS + 8 * (2 * TC_STAGES + 1));
+    __shared__ int gave_up;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
+    const int nk = K / TC_BK;
+
+    if (threadIdx.x == 0) {
+        gave_up = 0;
+        for (int s = 0; s < TC_STAGES; s++) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)BN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // Producer: stage kb of A and B into slot kb % STAGES once the MMAs have released it.
+        int issued = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % TC_STAGES;
+            mbar_wait(empty(s), ((kb / TC_STAGES) & 1) ^ 1, err, &gave_up);
+            mbar_arrive_expect_tx(full(s), L::STAGE);
+            tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
+            tma_load_2d(base + s * L::STAGE + TC_A_BYTES, &map_b, kb * TC_BK, n0, full(s));
+            issued = kb + 1;
+        }
+        // Every copy this thread started has landed before the block can end.
+        for (int kb = issued > TC_STAGES ? issued - TC_STAGES : 0; kb < issued; kb++)
+            mbar_wait(full(kb % TC_STAGES), (kb / TC_STAGES) & 1, err, &gave_up);
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer: four K = 16 steps per stage, accumulating after the first.
+        constexpr uint32_t idesc = bf16_idesc(TC_BM, BN);
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % TC_STAGES;
+            mbar_wait(full(s), (kb / TC_STAGES) & 1, err, &gave_up);
+            tc_fence_after();
+            const uint32_t a_addr = base + s * L::STAGE;
+            const uint32_t b_addr = a_addr + TC_A_BYTES;
+#pragma unroll
+            for (int k = 0; k < TC_BK / 16; k++) {
+                tc_mma(tmem, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+            }
+            tc_commit(empty(s));
+        }
+        tc_commit(done);
+    }
+    __syncwarp();
+
+    // Epilogue: row m0 + 32 warp + lane, BN columns from TMEM, 16 at a time.
+    mbar_wait(done, 0, err, &gave_up);
+    tc_fence_after();
+    const int row = m0 + warp * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(lane_base + c0, v);
+        if (row < M && n0 + c0 < N) {
+            float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+#pragma unroll
+            for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN)
+                     : "memory");
+    }
+}
+
+// ---- host -------------------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void *p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// A 2-D map over a row-major [rows][k] bf16 matrix, boxes of 64 columns x `box_rows` rows in the
+// 128-byte swizzle.
+static bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {k, rows};
+    cuuint64_t strides[1] = {k * 2};
+    cuuint32_t box[2] = {TC_BK, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN>
+static cudaError_t launch_tc(const void *a, const void *b, float *c, int M, int N, int K, uint32_t *err,
+                             cudaStream_t s) {
+    CUtensorMap ma, mb;
+    if (!make_map(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map(&mb, b, (uint64_t)N, (uint64_t)K, BN))
+        return cudaErrorInvalidValue;
+    auto kern = gemm_tc_kernel<BN>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<BN>::SMEM);
+    if (e != cudaSuccess) return e;
+    dim3 grid(N / BN, (M + TC_BM - 1) / TC_BM);
+    kern<<<grid, TC_THREADS, TcLayout<BN>::SMEM, s>>>(ma, mb, c, M, N, K, err);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c, uint32_t *err,
+                        cudaStream_t s) {
+    const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
+    if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
+    if (p.dtype != TG_BF16) {
+        dim3 grid((N + 63) / 64, (M + 63) / 64);
+        gemm_f32_kernel<<<grid, 256, 0, s>>>(M, N, K, (const float *)a, (const float *)b, c);
+        return cudaGetLastError();
+    }
+    if (K % TC_BK != 0) return cudaErrorInvalidValue;
+    if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s);
+    if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s);
+    if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s);
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace tg

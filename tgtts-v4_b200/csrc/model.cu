@@ -1,0 +1,785 @@
+// The MiniCPM-4 stack over the runtime: its shape and byte model (crates/graph/src/decode.rs:66-168),
+// placements (decode.rs:171-235), the decode step recorded once per batch (decode.rs:457-736,
+// :778-913) and the prefill programs over the decoder's weights and cache (prefill.rs:181-504).
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+
+#include "tg_common.cuh"
+#include "tg_internal.h"
+
+using namespace tg;
+
+// ---- shape ----------------------------------------------------------------------------------------
+
+extern "C" uint64_t tg_shape_weight_bytes(const tg_shape *s, uint32_t bytes_per_weight) {
+    if (!s) return 0;
+    const uint64_t h = s->hidden, i = s->inner, d = s->head_dim;
+    const uint64_t qkv = (uint64_t)(s->heads + 2 * s->kv_heads) * d * h;
+    const uint64_t layer = qkv + (uint64_t)s->heads * d * h + 2 * i * h + i * h + 2 * h;
+    return (uint64_t)bytes_per_weight * ((uint64_t)s->layers * layer + h);
+}
+
+extern "C" uint64_t tg_shape_cache_bytes(const tg_shape *s, uint32_t position, uint32_t bytes_per_value) {
+    if (!s) return 0;
+    const uint64_t read = std::min<uint64_t>((uint64_t)position + 1, s->capacity);
+    return (uint64_t)s->layers * 2 * s->kv_heads * read * s->head_dim * bytes_per_value;
+}
+
+static void rope_tables(const tg_shape &s, const double *factors, float *cs, float *sn) {
+    const uint32_t half = s.head_dim / 2;
+    for (uint32_t i = 0; i < half; i++) {
+        // 1 / theta^(2i / dim) and 1 / factor in f32, then t * rate * inv (decode.rs:146-168).
+        const float inv = 1.0f / powf(s.rope_theta, (float)(2 * i) / (float)s.head_dim);
+        const float rate = 1.0f / (float)(factors ? factors[i] : 1.0);
+        for (uint32_t t = 0; t < s.capacity; t++) {
+            const float f = (float)t * rate * inv;
+            cs[(size_t)t * half + i] = cosf(f);
+            sn[(size_t)t * half + i] = sinf(f);
+        }
+    }
+}
+
+extern "C" int tg_shape_rope_tables(const tg_shape *s, float *cs, float *sn) {
+    if (!s || !cs || !sn) return fail(TG_EINVAL, "tg_shape_rope_tables: null argument");
+    rope_tables(*s, s->rope_factors, cs, sn);
+    return TG_OK;
+}
+
+extern "C" int tg_batch_placement(uint32_t n_rows, uint32_t slots, const tg_row *rows, uint32_t capacity,
+                                  uint32_t *words, uint32_t *n_words) {
+    if ((n_rows && (!rows || !words)) || slots == 0) return fail(TG_EINVAL, "tg_batch_placement: null argument");
+    const uint32_t nw = slots > 1 ? 2 * n_rows : n_rows;
+    for (uint32_t i = 0; i < nw; i++) words[i] = TG_SPARE;
+    std::vector<bool> taken(slots, false);
+    for (uint32_t b = 0; b < n_rows; b++) {
+        const tg_row r = rows[b];
+        if (r.position == TG_SPARE) continue;
+        if (r.position >= capacity || r.slot >= slots || taken[r.slot])
+            return fail(TG_ESHAPE, "row %u at position %u of %u in slot %u of %u, taken: %s", b, r.position, capacity,
+                        r.slot, slots, r.slot < slots && taken[r.slot] ? "true" : "false");
+        taken[r.slot] = true;
+        words[b] = r.position;
+        if (slots > 1) words[n_rows + b] = r.slot;
+    }
+    if (n_words) *n_words = nw;
+    return TG_OK;
+}
+
+// ---- decoder --------------------------------------------------------------------------------------
+
+namespace {
+
+struct Owned {
+    tg_mem *m = nullptr;
+    ~Owned() { tg_mem_free(m); }
+    int alloc(tg_ctx *ctx, uint64_t bytes, tg_residence r = TG_RES_DEVICE) { return tg_mem_alloc(ctx, bytes, r, &m); }
+    char *ptr() const { return static_cast<char *>(m->ptr); }
+    char *host() const { return static_cast<char *>(m->host); }
+};
+
+uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
+
+struct LayerOffsets {
+    uint64_t qkv, o, gate_up, down, in_norm, post_norm;
+};
+
+}  // namespace
+
+struct tg_decoder {
+    tg_ctx *ctx = nullptr;
+    tg_shape shape{};
+    std::vector<double> factors;
+    uint32_t rows = 0, slots = 0;
+    tg_dtype dtype = TG_F32;
+    bool timed = false;
+    uint64_t esize = 4;
+    // Weights: every layer's projections (storage type) and gains (f32), then the final gain.
+    Owned weights;
+    std::vector<LayerOffsets> layer;
+    uint64_t final_norm = 0;
+    Owned cos, sin, kcache, vcache;  // caches: [layers][slots][kv][capacity][hd]
+    uint64_t cache_layer = 0;        // bytes of one layer's cache
+    // Activations of the step, [rows][...].
+    Owned x_in, h, mid, out, q, att, mlp, po, pml, words;
+    Owned stage_x, stage_words, stage_out;  // pinned host staging
+    Program prog;
+    std::vector<Launch> launches;
+
+    uint64_t width() const { return (uint64_t)(shape.heads + 2 * shape.kv_heads) * shape.head_dim; }
+    uint64_t attn() const { return (uint64_t)shape.heads * shape.head_dim; }
+    tg_params params() const {
+        tg_params p{};
+        p.dtype = dtype;
+        p.hidden = shape.hidden;
+        p.inner = shape.inner;
+        p.heads = shape.heads;
+        p.kv_heads = shape.kv_heads;
+        p.head_dim = shape.head_dim;
+        p.capacity = shape.capacity;
+        p.rows = rows;
+        p.slots = slots;
+        p.eps = shape.eps;
+        p.residual_scale = shape.residual_scale;
+        p.rope = shape.rope;
+        return p;
+    }
+    char *w(uint64_t off) const { return weights.ptr() + off; }
+    char *kc(uint32_t l) const { return kcache.ptr() + l * cache_layer; }
+    char *vc(uint32_t l) const { return vcache.ptr() + l * cache_layer; }
+};
+
+static int check_shape(const tg_shape &s, tg_dtype dtype) {
+    const uint32_t vec = dtype == TG_BF16 ? 256 : 128;
+    if (dtype != TG_F32 && dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %d", (int)dtype);
+    if (s.layers == 0 || s.hidden == 0 || s.inner == 0 || s.heads == 0 || s.kv_heads == 0)
+        return fail(TG_ESHAPE, "an empty shape");
+    if (s.hidden % vec || s.inner % vec || (s.heads * s.head_dim) % vec)
+        return fail(TG_ESHAPE, "%u hidden, %u inner and %u attention columns in steps of %u", s.hidden, s.inner,
+                    s.heads * s.head_dim, vec);
+    if (s.heads % s.kv_heads || (s.head_dim != 64 && s.head_dim != 128))
+        return fail(TG_ESHAPE, "%u heads over %u of %u", s.heads, s.kv_heads, s.head_dim);
+    if (s.capacity == 0 || s.capacity % ATTN_CHUNK)
+        return fail(TG_ESHAPE, "a cache of %u positions (a multiple of %u)", s.capacity, ATTN_CHUNK);
+    if (!(s.eps >= 0.0f) || !std::isfinite(s.residual_scale)) return fail(TG_ESHAPE, "eps %g, residual scale %g", s.eps, s.residual_scale);
+    return TG_OK;
+}
+
+#define TG_TRY(x)                 \
+    do {                          \
+        const int st_ = (x);      \
+        if (st_) return st_;      \
+    } while (0)
+
+static void push(std::vector<Launch> &v, uint32_t kernel, const tg_params &p, const char *label,
+                 std::initializer_list<std::pair<void *, uint64_t>> b) {
+    Launch l;
+    l.kernel = kernel;
+    l.p = p;
+    l.label = label;
+    for (auto &x : b) {
+        l.ptr.push_back(x.first);
+        l.bytes.push_back(x.second);
+    }
+    v.push_back(std::move(l));
+}
+
+// decode_batch_graph (decode.rs:457-736): per layer qkv_rope, attention_split, attention_combine,
+// o_proj (+ residual), gate_up (+ norm, SiLU), down_proj (+ residual); then the final norm.
+static void decode_launches(tg_decoder &d) {
+    const tg_params base = d.params();
+    const uint64_t T = d.esize, F = 4, R = d.rows;
+    const tg_shape &s = d.shape;
+    const uint64_t H = s.hidden, I = s.inner, hd = s.head_dim, heads = s.heads;
+    const uint64_t chunks = s.capacity / ATTN_CHUNK;
+    const uint64_t words = (d.slots > 1 ? 2 : 1) * R * 4;
+    const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
+    d.launches.clear();
+    for (uint32_t l = 0; l < s.layers; l++) {
+        const LayerOffsets &o = d.layer[l];
+        char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
+        push(d.launches, TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
+             {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
+              {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * T},
+              {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
+        push(d.launches, TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
+             {{d.q.ptr(), R * d.attn() * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
+              {d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
+              {d.pml.ptr(), R * heads * chunks * 2 * F}});
+        push(d.launches, TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
+             {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
+              {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.att.ptr(), R * d.attn() * T}});
+        tg_params po = base;
+        po.n = (uint32_t)H;
+        po.k = (uint32_t)d.attn();
+        push(d.launches, TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
+             {{d.att.ptr(), R * d.attn() * T}, {d.w(o.o), H * d.attn() * T}, {in, R * H * F}, {d.mid.ptr(), R * H * F}});
+        push(d.launches, TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
+             {{d.mid.ptr(), R * H * F}, {d.w(o.post_norm), H * F}, {d.w(o.gate_up), 2 * I * H * T},
+              {d.mlp.ptr(), R * I * T}});
+        tg_params pd = base;
+        pd.n = (uint32_t)H;
+        pd.k = (uint32_t)I;
+        push(d.launches, TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
+             {{d.mlp.ptr(), R * I * T}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
+    }
+    push(d.launches, TG_KERNEL_RMSNORM, base, "final_norm",
+         {{d.h.ptr(), R * H * F}, {d.w(d.final_norm), H * F}, {d.out.ptr(), R * H * F}});
+}
+
+extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, uint32_t slots, tg_dtype dtype,
+                                 int timed, tg_decoder **out) {
+    if (!ctx || !s || !out) return fail(TG_EINVAL, "tg_decoder_create: null argument");
+    *out = nullptr;
+    TG_TRY(check_shape(*s, dtype));
+    if (rows == 0 || rows > slots) return fail(TG_ESHAPE, "%u rows in %u slots", rows, slots);
+    TG_CUDA(cudaSetDevice(ctx->device));
+    std::unique_ptr<tg_decoder> d(new tg_decoder());
+    d->ctx = ctx;
+    d->shape = *s;
+    if (s->rope_factors) d->factors.assign(s->rope_factors, s->rope_factors + s->head_dim / 2);
+    d->shape.rope_factors = nullptr;
+    d->rows = rows;
+    d->slots = slots;
+    d->dtype = dtype;
+    d->timed = timed != 0;
+    d->esize = dtype == TG_BF16 ? 2 : 4;
+    const uint64_t T = d->esize, F = 4, H = s->hidden, I = s->inner;
+    uint64_t off = 0;
+    for (uint32_t l = 0; l < s->layers; l++) {
+        LayerOffsets o;
+        o.qkv = off;
+        off = align256(off + d->width() * H * T);
+        o.o = off;
+        off = align256(off + H * d->attn() * T);
+        o.gate_up = off;
+        off = align256(off + 2 * I * H * T);
+        o.down = off;
+        off = align256(off + H * I * T);
+        o.in_norm = off;
+        off = align256(off + H * F);
+        o.post_norm = off;
+        off = align256(off + H * F);
+        d->layer.push_back(o);
+    }
+    d->final_norm = off;
+    off = align256(off + H * F);
+    TG_TRY(d->weights.alloc(ctx, off));
+    const uint64_t table = (uint64_t)s->capacity * (s->head_dim / 2) * F;
+    TG_TRY(d->cos.alloc(ctx, table));
+    TG_TRY(d->sin.alloc(ctx, table));
+    {
+        std::vector<float> cs(table / 4), sn(table / 4);
+        rope_tables(d->shape, d->factors.empty() ? nullptr : d->factors.data(), cs.data(), sn.data());
+        TG_TRY(tg_mem_write(d->cos.m, 0, cs.data(), table));
+        TG_TRY(tg_mem_write(d->sin.m, 0, sn.data(), table));
+    }
+    d->cache_layer = align256((uint64_t)slots * s->kv_heads * s->capacity * s->head_dim * T);
+    TG_TRY(d->kcache.alloc(ctx, d->cache_layer * s->layers));
+    TG_TRY(d->vcache.alloc(ctx, d->cache_layer * s->layers));
+    const uint64_t R = rows, chunks = s->capacity / ATTN_CHUNK;
+    TG_TRY(d->x_in.alloc(ctx, R * H * F));
+    TG_TRY(d->h.alloc(ctx, R * H * F));
+    TG_TRY(d->mid.alloc(ctx, R * H * F));
+    TG_TRY(d->out.alloc(ctx, R * H * F));
+    TG_TRY(d->q.alloc(ctx, R * d->attn() * T));
+    TG_TRY(d->att.alloc(ctx, R * d->attn() * T));
+    TG_TRY(d->mlp.alloc(ctx, R * I * T));
+    TG_TRY(d->po.alloc(ctx, R * s->heads * chunks * s->head_dim * F));
+    TG_TRY(d->pml.alloc(ctx, R * s->heads * chunks * 2 * F));
+    TG_TRY(d->words.alloc(ctx, 2 * R * 4));
+    TG_TRY(d->stage_x.alloc(ctx, R * H * F, TG_RES_UPLOAD));
+    TG_TRY(d->stage_words.alloc(ctx, 2 * R * 4, TG_RES_UPLOAD));
+    TG_TRY(d->stage_out.alloc(ctx, R * H * F, TG_RES_READBACK));
+    TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
+    decode_launches(*d);
+    TG_TRY(program_build(ctx, d->launches, d->timed, d->prog));
+    *out = d.release();
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_destroy(tg_decoder *d) {
+    if (!d) return TG_OK;
+    cudaSetDevice(d->ctx->device);
+    if (d->prog.pending) program_wait(d->prog, 0);
+    program_release(d->prog);
+    delete d;
+    return TG_OK;
+}
+
+__global__ void to_bf16_kernel(const float *__restrict__ src, bf16 *__restrict__ dst, uint64_t n) {
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+// Writes `count` values from the host into the weight arena at `off`, in the decoder's storage
+// type (`as_f32` forces f32, for gains): f32 to bf16 rounds to nearest even on the GPU
+// (__float2bfloat16_rn); bf16 to f32 widens exactly.
+static int write_values(tg_decoder *d, uint64_t off, const void *src, uint64_t count, tg_dtype src_dtype, bool as_f32) {
+    const bool dst_bf16 = !as_f32 && d->dtype == TG_BF16;
+    const uint64_t dst_bytes = count * (dst_bf16 ? 2 : 4);
+    if (off + dst_bytes > tg_mem_size(d->weights.m)) return fail(TG_ESHAPE, "a weight past its arena");
+    if (src_dtype == TG_BF16 && dst_bf16) return tg_mem_write(d->weights.m, off, src, dst_bytes);
+    std::vector<float> f32;
+    const float *vals = static_cast<const float *>(src);
+    if (src_dtype == TG_BF16) {
+        f32.resize(count);
+        const uint16_t *b = static_cast<const uint16_t *>(src);
+        for (uint64_t i = 0; i < count; i++) {
+            const uint32_t bits = (uint32_t)b[i] << 16;
+            memcpy(&f32[i], &bits, 4);
+        }
+        vals = f32.data();
+    }
+    if (!dst_bf16) return tg_mem_write(d->weights.m, off, vals, dst_bytes);
+    Owned tmp;
+    TG_TRY(tmp.alloc(d->ctx, count * 4));
+    TG_TRY(tg_mem_write(tmp.m, 0, vals, count * 4));
+    to_bf16_kernel<<<d->ctx->sm_count * 4, 256, 0, d->ctx->stream>>>(
+        reinterpret_cast<const float *>(tmp.ptr()), reinterpret_cast<bf16 *>(d->w(off)), count);
+    TG_CUDA(cudaGetLastError());
+    return tg_ctx_synchronize(d->ctx, 0);
+}
+
+extern "C" int tg_decoder_load(tg_decoder *d, const char *name, const void *src, uint64_t count, tg_dtype src_dtype) {
+    if (!d || !name || !src) return fail(TG_EINVAL, "tg_decoder_load: null argument");
+    if (src_dtype != TG_F32 && src_dtype != TG_BF16) return fail(TG_EINVAL, "source dtype %d", (int)src_dtype);
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    const tg_shape &s = d->shape;
+    const uint64_t H = s.hidden, I = s.inner, hd = s.head_dim, T = d->esize;
+    auto want = [&](uint64_t n) -> int {
+        if (count != n) return fail(TG_ESHAPE, "%s: %llu values, not %llu", name, (unsigned long long)count, (unsigned long long)n);
+        return TG_OK;
+    };
+    if (!strcmp(name, "norm.weight")) {
+        TG_TRY(want(H));
+        return write_values(d, d->final_norm, src, count, src_dtype, true);
+    }
+    unsigned l = 0;
+    char rest[128] = {0};
+    if (sscanf(name, "layers.%u.%127s", &l, rest) != 2 || l >= s.layers)
+        return fail(TG_EINVAL, "no weight %s in a stack of %u layers", name, s.layers);
+    const LayerOffsets &o = d->layer[l];
+    const std::string r = rest;
+    // load_stack's joins: qkv = rows[q; k; v], gate_up = rows[gate; up] (decode.rs:764-775).
+    if (r == "self_attn.q_proj.weight") {
+        TG_TRY(want(s.heads * hd * H));
+        return write_values(d, o.qkv, src, count, src_dtype, false);
+    }
+    if (r == "self_attn.k_proj.weight") {
+        TG_TRY(want(s.kv_heads * hd * H));
+        return write_values(d, o.qkv + s.heads * hd * H * T, src, count, src_dtype, false);
+    }
+    if (r == "self_attn.v_proj.weight") {
+        TG_TRY(want(s.kv_heads * hd * H));
+        return write_values(d, o.qkv + (s.heads + s.kv_heads) * hd * H * T, src, count, src_dtype, false);
+    }
+    if (r == "self_attn.o_proj.weight") {
+        TG_TRY(want(H * s.heads * hd));
+        return write_values(d, o.o, src, count, src_dtype, false);
+    }
+    if (r == "mlp.gate_proj.weight") {
+        TG_TRY(want(I * H));
+        return write_values(d, o.gate_up, src, count, src_dtype, false);
+    }
+    if (r == "mlp.up_proj.weight") {
+        TG_TRY(want(I * H));
+        return write_values(d, o.gate_up + I * H * T, src, count, src_dtype, false);
+    }
+    if (r == "mlp.down_proj.weight") {
+        TG_TRY(want(H * I));
+        return write_values(d, o.down, src, count, src_dtype, false);
+    }
+    if (r == "input_layernorm.weight") {
+        TG_TRY(want(H));
+        return write_values(d, o.in_norm, src, count, src_dtype, true);
+    }
+    if (r == "post_attention_layernorm.weight") {
+        TG_TRY(want(H));
+        return write_values(d, o.post_norm, src, count, src_dtype, true);
+    }
+    return fail(TG_EINVAL, "no weight %s", name);
+}
+
+static int set_words(tg_decoder *d, const tg_row *rows) {
+    uint32_t n = 0;
+    TG_TRY(tg_batch_placement(d->rows, d->slots, rows, d->shape.capacity,
+                              reinterpret_cast<uint32_t *>(d->stage_words.host()), &n));
+    TG_CUDA(cudaMemcpyAsync(d->words.ptr(), d->stage_words.ptr(), (uint64_t)n * 4, cudaMemcpyDefault, d->ctx->stream));
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_set_rows(tg_decoder *d, const tg_row *rows, const float *x) {
+    if (!d || !rows || !x) return fail(TG_EINVAL, "tg_decoder_set_rows: null argument");
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    const uint64_t bytes = (uint64_t)d->rows * d->shape.hidden * 4;
+    memcpy(d->stage_x.host(), x, bytes);
+    TG_TRY(set_words(d, rows));
+    TG_CUDA(cudaMemcpyAsync(d->x_in.ptr(), d->stage_x.ptr(), bytes, cudaMemcpyDefault, d->ctx->stream));
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_start(tg_decoder *d) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    std::lock_guard<std::mutex> lock(d->ctx->mu);
+    return program_start(d->prog);
+}
+
+extern "C" int tg_decoder_wait(tg_decoder *d, uint64_t timeout_ns) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    return program_wait(d->prog, timeout_ns);
+}
+
+extern "C" int tg_decoder_output(tg_decoder *d, float *out) {
+    if (!d || !out) return fail(TG_EINVAL, "tg_decoder_output: null argument");
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    const uint64_t bytes = (uint64_t)d->rows * d->shape.hidden * 4;
+    TG_CUDA(cudaMemcpyAsync(d->stage_out.ptr(), d->out.ptr(), bytes, cudaMemcpyDefault, d->ctx->stream));
+    TG_CUDA(cudaStreamSynchronize(d->ctx->stream));
+    memcpy(out, d->stage_out.host(), bytes);
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_step_rows(tg_decoder *d, const tg_row *rows, const float *x, float *out) {
+    TG_TRY(tg_decoder_set_rows(d, rows, x));
+    TG_TRY(tg_decoder_start(d));
+    TG_TRY(tg_decoder_wait(d, 60ull * 1000000000ull));
+    return tg_decoder_output(d, out);
+}
+
+extern "C" int tg_decoder_step_device(tg_decoder *d, const uint32_t *words, const float *x_dev, float *out_dev) {
+    if (!d || !words || !x_dev || !out_dev) return fail(TG_EINVAL, "tg_decoder_step_device: null argument");
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    const uint32_t nw = d->slots > 1 ? 2 * d->rows : d->rows;
+    memcpy(d->stage_words.host(), words, (uint64_t)nw * 4);
+    const uint64_t bytes = (uint64_t)d->rows * d->shape.hidden * 4;
+    std::lock_guard<std::mutex> lock(d->ctx->mu);
+    TG_CUDA(cudaMemcpyAsync(d->words.ptr(), d->stage_words.ptr(), (uint64_t)nw * 4, cudaMemcpyDefault, d->ctx->stream));
+    TG_CUDA(cudaMemcpyAsync(d->x_in.ptr(), x_dev, bytes, cudaMemcpyDeviceToDevice, d->ctx->stream));
+    TG_TRY(program_start(d->prog));
+    TG_CUDA(cudaMemcpyAsync(out_dev, d->out.ptr(), bytes, cudaMemcpyDeviceToDevice, d->ctx->stream));
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_elapsed_ns(tg_decoder *d, double *ns) {
+    if (!d || !ns) return fail(TG_EINVAL, "null argument");
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    *ns = program_elapsed_ns(d->prog);
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_timings(tg_decoder *d, double *ns, size_t n, size_t *n_dispatches) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    if (n_dispatches) *n_dispatches = d->launches.size();
+    if (!ns) return TG_OK;
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    return program_timings(d->prog, ns, n);
+}
+
+extern "C" int tg_decoder_dispatch_label(tg_decoder *d, size_t i, char *label, size_t label_bytes) {
+    if (!d || !label) return fail(TG_EINVAL, "null argument");
+    if (i >= d->launches.size()) return fail(TG_EINVAL, "dispatch %zu of %zu", i, d->launches.size());
+    snprintf(label, label_bytes, "%s", d->launches[i].label.c_str());
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_read_cache(tg_decoder *d, uint32_t layer, uint32_t slot, uint32_t kind, uint32_t first,
+                                     uint32_t count, float *out) {
+    if (!d || !out) return fail(TG_EINVAL, "null argument");
+    const tg_shape &s = d->shape;
+    if (layer >= s.layers || slot >= d->slots || kind > 1 || first > s.capacity || count > s.capacity - first)
+        return fail(TG_ESHAPE, "cache layer %u slot %u kind %u positions %u+%u", layer, slot, kind, first, count);
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    const uint64_t hd = s.head_dim, T = d->esize;
+    std::vector<uint8_t> raw((uint64_t)count * hd * T);
+    tg_mem *m = kind == 0 ? d->kcache.m : d->vcache.m;
+    for (uint32_t kv = 0; kv < s.kv_heads; kv++) {
+        const uint64_t off = layer * d->cache_layer + ((((uint64_t)slot * s.kv_heads + kv) * s.capacity + first) * hd) * T;
+        TG_TRY(tg_mem_read(m, off, raw.data(), raw.size()));
+        float *o = out + (uint64_t)kv * count * hd;
+        for (uint64_t i = 0; i < (uint64_t)count * hd; i++) {
+            if (T == 4) {
+                memcpy(&o[i], &raw[i * 4], 4);
+            } else {
+                uint16_t b;
+                memcpy(&b, &raw[i * 2], 2);
+                const uint32_t bits = (uint32_t)b << 16;
+                memcpy(&o[i], &bits, 4);
+            }
+        }
+    }
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, uint32_t count) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    const tg_shape &s = d->shape;
+    if (from >= d->slots || to >= d->slots || count > s.capacity)
+        return fail(TG_ESHAPE, "copy of %u positions from slot %u to %u of %u", count, from, to, d->slots);
+    if (from == to || count == 0) return TG_OK;
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    const uint64_t hd = s.head_dim, T = d->esize;
+    std::vector<tg_region> regions;
+    for (uint32_t l = 0; l < s.layers; l++)
+        for (uint32_t kv = 0; kv < s.kv_heads; kv++) {
+            const uint64_t a = l * d->cache_layer + (((uint64_t)from * s.kv_heads + kv) * s.capacity) * hd * T;
+            const uint64_t b = l * d->cache_layer + (((uint64_t)to * s.kv_heads + kv) * s.capacity) * hd * T;
+            regions.push_back({a, b, (uint64_t)count * hd * T});
+        }
+    TG_TRY(tg_copy_regions(d->ctx, d->kcache.m, d->kcache.m, regions.data(), regions.size()));
+    return tg_copy_regions(d->ctx, d->vcache.m, d->vcache.m, regions.data(), regions.size());
+}
+
+extern "C" uint64_t tg_decoder_weight_bytes(const tg_decoder *d) {
+    return d ? tg_shape_weight_bytes(&d->shape, (uint32_t)d->esize) : 0;
+}
+
+extern "C" void *tg_ctx_stream(tg_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+// ---- prefill ----------------------------------------------------------------------------------------
+
+struct tg_prefill {
+    tg_decoder *d = nullptr;
+    uint32_t max_rows = 0;  // a multiple of 128
+    bool timed = false;
+    Owned words, x_in, h, mid, normed, qkv, q, att, proj, gu, mlp, out;
+    Owned stage_x, stage_words, stage_out;
+    std::map<uint32_t, Program> programs;  // by rows, a multiple of 128
+    std::map<uint32_t, std::vector<std::string>> labels;
+    Program *last = nullptr;
+};
+
+// prefill_graph / append_prefill (prefill.rs:181-413): the first input norm, then per layer the
+// q/k/v GEMM, rope_rows, attention_rows, the o GEMM, add_norm_rows, the gate/up GEMM,
+// silu_mul_rows, the down GEMM and add_norm_rows with the next gain (the final norm's after the
+// last layer).
+static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
+    tg_decoder &d = *p.d;
+    const tg_shape &s = d.shape;
+    tg_params base = d.params();
+    base.rows = rows;
+    const uint64_t T = d.esize, F = 4, R = rows, H = s.hidden, I = s.inner, hd = s.head_dim;
+    const uint64_t W = d.width(), A = d.attn();
+    const uint64_t words = (d.slots > 1 ? 2 : 1) * R * 4;
+    const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
+    std::vector<Launch> v;
+    push(v, TG_KERNEL_NORM_ROWS, base, "input_norm",
+         {{p.words.ptr(), words}, {p.x_in.ptr(), R * H * F}, {d.w(d.layer[0].in_norm), H * F}, {p.normed.ptr(), R * H * T}});
+    auto gemm = [&](const char *label, void *a, void *b, void *c, uint64_t n, uint64_t k) {
+        tg_params g = base;
+        g.m = rows;
+        g.n = (uint32_t)n;
+        g.k = (uint32_t)k;
+        push(v, TG_KERNEL_GEMM, g, label, {{a, R * k * T}, {b, n * k * T}, {c, R * n * F}});
+    };
+    for (uint32_t l = 0; l < s.layers; l++) {
+        const LayerOffsets &o = d.layer[l];
+        char *in = l == 0 ? p.x_in.ptr() : p.h.ptr();
+        gemm("qkv_proj", p.normed.ptr(), d.w(o.qkv), p.qkv.ptr(), W, H);
+        push(v, TG_KERNEL_ROPE_ROWS, base, "rope_rows",
+             {{p.words.ptr(), words}, {p.qkv.ptr(), R * W * F}, {d.cos.ptr(), table}, {d.sin.ptr(), table},
+              {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
+        push(v, TG_KERNEL_ATTENTION_ROWS, base, "attention_rows",
+             {{p.words.ptr(), words}, {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
+              {p.att.ptr(), R * A * T}});
+        gemm("o_proj", p.att.ptr(), d.w(o.o), p.proj.ptr(), H, A);
+        push(v, TG_KERNEL_ADD_NORM_ROWS, base, "add_norm_rows",
+             {{p.words.ptr(), words}, {p.proj.ptr(), R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
+              {p.mid.ptr(), R * H * F}, {p.normed.ptr(), R * H * T}});
+        gemm("gate_up_proj", p.normed.ptr(), d.w(o.gate_up), p.gu.ptr(), 2 * I, H);
+        push(v, TG_KERNEL_SILU_MUL_ROWS, base, "silu_mul_rows",
+             {{p.words.ptr(), words}, {p.gu.ptr(), R * 2 * I * F}, {p.mlp.ptr(), R * I * T}});
+        gemm("down_proj", p.mlp.ptr(), d.w(o.down), p.proj.ptr(), H, I);
+        const bool last = l + 1 == s.layers;
+        tg_params an = base;
+        an.normed_f32 = last ? 1 : 0;
+        push(v, TG_KERNEL_ADD_NORM_ROWS, an, "add_norm_rows",
+             {{p.words.ptr(), words}, {p.proj.ptr(), R * H * F}, {p.mid.ptr(), R * H * F},
+              {d.w(last ? d.final_norm : d.layer[l + 1].in_norm), H * F}, {p.h.ptr(), R * H * F},
+              {last ? p.out.ptr() : p.normed.ptr(), R * H * (last ? F : T)}});
+    }
+    return v;
+}
+
+extern "C" int tg_prefill_create(tg_decoder *d, uint32_t max_rows, int timed, tg_prefill **out) {
+    if (!d || !out) return fail(TG_EINVAL, "tg_prefill_create: null argument");
+    *out = nullptr;
+    if (max_rows == 0 || max_rows > (1u << 20)) return fail(TG_ESHAPE, "programs of up to %u rows", max_rows);
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    std::unique_ptr<tg_prefill> p(new tg_prefill());
+    p->d = d;
+    p->timed = timed != 0;
+    p->max_rows = (max_rows + 127) / 128 * 128;
+    const tg_shape &s = d->shape;
+    const uint64_t R = p->max_rows, T = d->esize, F = 4, H = s.hidden, I = s.inner;
+    tg_ctx *ctx = d->ctx;
+    TG_TRY(p->words.alloc(ctx, 2 * R * 4));
+    TG_TRY(p->x_in.alloc(ctx, R * H * F));
+    TG_TRY(p->h.alloc(ctx, R * H * F));
+    TG_TRY(p->mid.alloc(ctx, R * H * F));
+    TG_TRY(p->normed.alloc(ctx, R * H * T));
+    TG_TRY(p->qkv.alloc(ctx, R * d->width() * F));
+    TG_TRY(p->q.alloc(ctx, R * d->attn() * T));
+    TG_TRY(p->att.alloc(ctx, R * d->attn() * T));
+    TG_TRY(p->proj.alloc(ctx, R * H * F));
+    TG_TRY(p->gu.alloc(ctx, R * 2 * I * F));
+    TG_TRY(p->mlp.alloc(ctx, R * I * T));
+    TG_TRY(p->out.alloc(ctx, R * H * F));
+    TG_TRY(p->stage_x.alloc(ctx, R * H * F, TG_RES_UPLOAD));
+    TG_TRY(p->stage_words.alloc(ctx, 2 * R * 4, TG_RES_UPLOAD));
+    TG_TRY(p->stage_out.alloc(ctx, R * H * F, TG_RES_READBACK));
+    *out = p.release();
+    return TG_OK;
+}
+
+extern "C" int tg_prefill_destroy(tg_prefill *p) {
+    if (!p) return TG_OK;
+    cudaSetDevice(p->d->ctx->device);
+    for (auto &kv : p->programs) {
+        if (kv.second.pending) program_wait(kv.second, 0);
+        program_release(kv.second);
+    }
+    delete p;
+    return TG_OK;
+}
+
+static int program_for(tg_prefill *p, uint32_t rows, Program **out) {
+    auto it = p->programs.find(rows);
+    if (it == p->programs.end()) {
+        Program prog;
+        const int st = program_build(p->d->ctx, prefill_launches(*p, rows), p->timed, prog);
+        if (st) {
+            program_release(prog);
+            return st;
+        }
+        it = p->programs.emplace(rows, prog).first;
+    }
+    *out = &it->second;
+    return TG_OK;
+}
+
+// Lays `runs` out as rows of one launch: each run's rows start on a multiple of PREFILL_TILE
+// (padding rows between are spare). Fills the words (positions, then slots, at the bucket's
+// stride) and returns the rows used and each run's first row.
+static int layout_runs(tg_prefill *p, const tg_run *runs, uint32_t n_runs, uint32_t &used,
+                       std::vector<uint32_t> &first) {
+    const tg_shape &s = p->d->shape;
+    std::vector<bool> slot_taken(p->d->slots, false);
+    uint32_t row = 0;
+    first.clear();
+    for (uint32_t i = 0; i < n_runs; i++) {
+        const tg_run &r = runs[i];
+        if (r.len == 0 || (uint64_t)r.start + r.len > s.capacity || r.slot >= p->d->slots || slot_taken[r.slot])
+            return fail(TG_ESHAPE, "run %u: %u positions from %u in slot %u of %u in a cache of %u", i, r.len, r.start,
+                        r.slot, p->d->slots, s.capacity);
+        slot_taken[r.slot] = true;
+        row = (row + PREFILL_TILE - 1) / PREFILL_TILE * PREFILL_TILE;
+        first.push_back(row);
+        row += r.len;
+        if (row > p->max_rows) return fail(TG_ESHAPE, "runs of %u rows in a prefill of at most %u", row, p->max_rows);
+    }
+    used = row;
+    return TG_OK;
+}
+
+static int run_rows(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x, bool x_on_device,
+                    float *out, bool out_on_device) {
+    tg_decoder *d = p->d;
+    tg_ctx *ctx = d->ctx;
+    const uint64_t H = d->shape.hidden, F = 4;
+    uint32_t used = 0;
+    std::vector<uint32_t> first;
+    TG_TRY(layout_runs(p, runs, n_runs, used, first));
+    const uint32_t rows = (used + 127) / 128 * 128;
+    Program *prog = nullptr;
+    TG_TRY(program_for(p, rows, &prog));
+    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    for (auto &kv : p->programs)
+        if (kv.second.pending) TG_TRY(program_wait(kv.second, 0));
+    uint32_t *w = reinterpret_cast<uint32_t *>(p->stage_words.host());
+    for (uint32_t i = 0; i < 2 * rows; i++) w[i] = TG_SPARE;
+    for (uint32_t i = 0; i < n_runs; i++)
+        for (uint32_t j = 0; j < runs[i].len; j++) {
+            w[first[i] + j] = runs[i].start + j;
+            w[rows + first[i] + j] = runs[i].slot;
+        }
+    std::lock_guard<std::mutex> lock(ctx->mu);
+    TG_CUDA(cudaMemcpyAsync(p->words.ptr(), p->stage_words.ptr(), (uint64_t)2 * rows * 4, cudaMemcpyDefault, ctx->stream));
+    uint64_t src_row = 0;
+    for (uint32_t i = 0; i < n_runs; i++) {
+        const uint64_t bytes = (uint64_t)runs[i].len * H * F;
+        char *dst = p->x_in.ptr() + (uint64_t)first[i] * H * F;
+        if (x_on_device) {
+            TG_CUDA(cudaMemcpyAsync(dst, x + src_row * H, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+        } else {
+            memcpy(p->stage_x.host() + (uint64_t)first[i] * H * F, x + src_row * H, bytes);
+            TG_CUDA(cudaMemcpyAsync(dst, p->stage_x.ptr() + (uint64_t)first[i] * H * F, bytes, cudaMemcpyDefault, ctx->stream));
+        }
+        src_row += runs[i].len;
+    }
+    TG_TRY(program_start(*prog));
+    p->last = prog;
+    src_row = 0;
+    for (uint32_t i = 0; i < n_runs; i++) {
+        const uint64_t bytes = (uint64_t)runs[i].len * H * F;
+        const char *src = p->out.ptr() + (uint64_t)first[i] * H * F;
+        if (out_on_device) {
+            TG_CUDA(cudaMemcpyAsync(out + src_row * H, src, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+        } else {
+            TG_CUDA(cudaMemcpyAsync(p->stage_out.ptr() + (uint64_t)first[i] * H * F, src, bytes, cudaMemcpyDefault, ctx->stream));
+        }
+        src_row += runs[i].len;
+    }
+    if (out_on_device) return TG_OK;
+    TG_TRY(program_wait(*prog, 600ull * 1000000000ull));
+    TG_CUDA(cudaStreamSynchronize(ctx->stream));
+    src_row = 0;
+    for (uint32_t i = 0; i < n_runs; i++) {
+        memcpy(out + src_row * H, p->stage_out.host() + (uint64_t)first[i] * H * F, (uint64_t)runs[i].len * H * F);
+        src_row += runs[i].len;
+    }
+    return TG_OK;
+}
+
+extern "C" int tg_prefill_run(tg_prefill *p, uint32_t start, uint32_t slot, const float *x, uint32_t len, float *out) {
+    if (!p || !x || !out) return fail(TG_EINVAL, "tg_prefill_run: null argument");
+    const tg_shape &s = p->d->shape;
+    if (len == 0 || (uint64_t)start + len > s.capacity || slot >= p->d->slots)
+        return fail(TG_ESHAPE, "%u positions from %u in slot %u of a cache of %u", len, start, slot, s.capacity);
+    TG_CUDA(cudaSetDevice(p->d->ctx->device));
+    // A run of more than max_rows positions runs in pieces (prefill.rs:487-502).
+    for (uint32_t done = 0; done < len;) {
+        const uint32_t n = std::min(len - done, p->max_rows);
+        const tg_run r = {start + done, n, slot};
+        TG_TRY(run_rows(p, &r, 1, x + (uint64_t)done * s.hidden, false, out + (uint64_t)done * s.hidden, false));
+        done += n;
+    }
+    return TG_OK;
+}
+
+extern "C" int tg_prefill_run_batch(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x, float *out) {
+    if (!p || !runs || !n_runs || !x || !out) return fail(TG_EINVAL, "tg_prefill_run_batch: null argument");
+    TG_CUDA(cudaSetDevice(p->d->ctx->device));
+    return run_rows(p, runs, n_runs, x, false, out, false);
+}
+
+extern "C" int tg_prefill_run_batch_device(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x_dev,
+                                           float *out_dev) {
+    if (!p || !runs || !n_runs || !x_dev || !out_dev) return fail(TG_EINVAL, "tg_prefill_run_batch_device: null argument");
+    TG_CUDA(cudaSetDevice(p->d->ctx->device));
+    return run_rows(p, runs, n_runs, x_dev, true, out_dev, true);
+}
+
+extern "C" int tg_prefill_elapsed_ns(tg_prefill *p, double *ns) {
+    if (!p || !ns || !p->last) return fail(TG_EINVAL, "no prefill has run");
+    if (p->last->pending) TG_TRY(program_wait(*p->last, 0));
+    *ns = program_elapsed_ns(*p->last);
+    return TG_OK;
+}
+
+extern "C" int tg_prefill_timings(tg_prefill *p, double *ns, size_t n, size_t *n_dispatches) {
+    if (!p || !p->last) return fail(TG_EINVAL, "no prefill has run");
+    if (n_dispatches) *n_dispatches = p->last->labels.size();
+    if (!ns) return TG_OK;
+    if (p->last->pending) TG_TRY(program_wait(*p->last, 0));
+    return program_timings(*p->last, ns, n);
+}
+
+extern "C" int tg_prefill_dispatch_label(tg_prefill *p, size_t i, char *label, size_t label_bytes) {
+    if (!p || !label || !p->last) return fail(TG_EINVAL, "no prefill has run");
+    if (i >= p->last->labels.size()) return fail(TG_EINVAL, "dispatch %zu of %zu", i, p->last->labels.size());
+    snprintf(label, label_bytes, "%s", p->last->labels[i].c_str());
+    return TG_OK;
+}
+
+extern "C" uint32_t tg_prefill_max_rows(const tg_prefill *p) { return p ? p->max_rows : 0; }

@@ -1,0 +1,132 @@
+// Device-side building blocks shared by every kernel: the storage types, 16-byte vector loads,
+// and the fixed reduction orders that make a row's result independent of the batch it runs in
+// (tgtts-v4's invariant, crates/graph/src/decode.rs:8-11, kernels/glsl/gemv.glsl:1-5).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define TG_DEVICE __device__ __forceinline__
+
+namespace tg {
+
+using bf16 = __nv_bfloat16;
+
+// Error words a kernel may set in the context's error buffer (read by the host after a wait).
+enum : uint32_t {
+    ERR_NONE = 0,
+    ERR_WAIT_TIMEOUT = 1,  // a bounded spin on an mbarrier gave up
+    ERR_BAD_INDEX = 2,     // a placement word pointed outside its buffer and was skipped
+};
+
+// One 16-byte load of storage type T: 4 f32 or 8 bf16, widened to f32.
+template <typename T>
+struct Vec;
+template <>
+struct Vec<float> {
+    static constexpr int N = 4;
+    using Raw = float4;
+    static TG_DEVICE void unpack(const Raw &r, float (&f)[N]) {
+        f[0] = r.x;
+        f[1] = r.y;
+        f[2] = r.z;
+        f[3] = r.w;
+    }
+};
+template <>
+struct Vec<bf16> {
+    static constexpr int N = 8;
+    using Raw = uint4;
+    static TG_DEVICE void unpack(const Raw &r, float (&f)[N]) {
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            f[2 * i] = __uint_as_float(w[i] << 16);
+            f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+    }
+};
+
+template <typename T>
+TG_DEVICE float to_f32(T v);
+template <>
+TG_DEVICE float to_f32<float>(float v) { return v; }
+template <>
+TG_DEVICE float to_f32<bf16>(bf16 v) { return __bfloat162float(v); }
+
+// Rounds to the storage type, to nearest even (the only rounding points are where a tensor is
+// stored, kernels/glsl/common.glsl:1-7).
+template <typename T>
+TG_DEVICE T from_f32(float v);
+template <>
+TG_DEVICE float from_f32<float>(float v) { return v; }
+template <>
+TG_DEVICE bf16 from_f32<bf16>(float v) { return __float2bfloat16_rn(v); }
+
+// A read-only 16-byte load through the non-coherent path.
+template <typename R>
+TG_DEVICE R ldg16(const R *p) { return __ldg(p); }
+
+// Streaming variant for weights that are read once per step.
+TG_DEVICE uint4 ld_stream(const uint4 *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+TG_DEVICE float4 ld_stream(const float4 *p) {
+    float4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+// Warp sum by the xor butterfly 16, 8, 4, 2, 1: every lane ends with the same bits, and the order
+// depends on nothing but the lane values.
+TG_DEVICE float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+TG_DEVICE float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// The canonical RMSNorm scale of one f32 row of k values (k a multiple of 128), taken by one warp:
+// lane l sums the squares of float4 chunks l, l + 32, ... in order (one fused multiply-add per
+// value), then the butterfly joins the lanes. Every kernel that norms a row calls this, so a row's
+// scale is the same bits wherever and beside whatever it is computed. 1 / sqrt(mean + eps) as
+// kernels/glsl/norm.glsl:29 (IEEE division and square root).
+TG_DEVICE float warp_rms_scale(const float *row, int k, float eps) {
+    const int lane = threadIdx.x & 31;
+    const float4 *v = reinterpret_cast<const float4 *>(row);
+    float s = 0.0f;
+    for (int c = lane; c < k / 4; c += 32) {
+        float4 q = v[c];
+        s = __fmaf_rn(q.x, q.x, s);
+        s = __fmaf_rn(q.y, q.y, s);
+        s = __fmaf_rn(q.z, q.z, s);
+        s = __fmaf_rn(q.w, q.w, s);
+    }
+    s = warp_sum(s);
+    return 1.0f / sqrtf(__fdiv_rn(s, (float)k) + eps);
+}
+
+TG_DEVICE float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
+
+// Placement words (crates/graph/src/decode.rs:198-227, kernels/glsl/batch.glsl:9-14): positions
+// of `rows` rows, then their slots when slots > 1. A row placed past the capacity or the slots is
+// spare: it writes no cache and attends to nothing.
+TG_DEVICE bool placed(const uint32_t *at, int rows, int b, uint32_t capacity, uint32_t slots,
+                      uint32_t &pos, uint32_t &slot) {
+    pos = at[b];
+    slot = slots > 1 ? at[rows + b] : 0u;
+    return pos < capacity && slot < slots;
+}
+
+}  // namespace tg

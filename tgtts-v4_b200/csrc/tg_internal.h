@@ -1,0 +1,126 @@
+// Host-side internals shared by the runtime, the kernel table and the model: the handle types
+// behind the C ABI, per-thread error messages, and the launch interface every kernel implements.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "tgcuda.h"
+
+struct tg_ctx {
+    int device = 0;
+    int sm_count = 0;
+    int cc_major = 0, cc_minor = 0;
+    char name[256] = {0};
+    cudaStream_t stream = nullptr;
+    // One error word the kernels may set (tg::ERR_*), in mapped pinned memory so the host reads
+    // it after a wait without a copy.
+    uint32_t *err_host = nullptr;
+    uint32_t *err_dev = nullptr;
+    std::mutex mu;  // submission is behind a mutex (crates/vulkan/src/recording.rs:622-628)
+};
+
+struct tg_mem {
+    tg_ctx *ctx = nullptr;
+    void *ptr = nullptr;  // device pointer, or the mapped device address of pinned memory
+    void *host = nullptr; // pinned host address for UPLOAD / READBACK
+    uint64_t bytes = 0;
+    tg_residence residence = TG_RES_DEVICE;
+};
+
+namespace tg {
+
+// Records `msg` as the calling thread's last error and returns `status`.
+int fail(int status, const char *fmt, ...);
+int cuda_fail(cudaError_t e, const char *what);
+void clear_error();
+
+#define TG_CUDA(call)                                             \
+    do {                                                          \
+        cudaError_t e_ = (call);                                  \
+        if (e_ != cudaSuccess) return ::tg::cuda_fail(e_, #call); \
+    } while (0)
+
+// One dispatch resolved to device pointers, as the kernel table launches it.
+struct Launch {
+    uint32_t kernel = 0;
+    tg_params p{};
+    std::vector<void *> ptr;
+    std::vector<uint64_t> bytes;
+    std::string label;
+};
+
+// The kernel table: checks a dispatch's params against its bindings' sizes (what each binding
+// must hold for the grid the params give), then launches it on `stream`.
+int check_launch(const Launch &l);
+int enqueue_launch(const Launch &l, uint32_t *err_dev, cudaStream_t stream, int sm_count);
+
+// A captured chain of launches (a CUDA graph) with optional events between them.
+struct Program {
+    tg_ctx *ctx = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<cudaEvent_t> events;  // [n + 1] when timed, else [2]
+    std::vector<std::string> labels;
+    bool timed = false;
+    bool pending = false;
+};
+
+// Captures `launches` (plus any host-to-device copies `pre` issues first) into a graph on the
+// context's stream. `pre` may be empty.
+int program_build(tg_ctx *ctx, const std::vector<Launch> &launches, bool timed, Program &out);
+int program_start(Program &p);
+int program_wait(Program &p, uint64_t timeout_ns);
+void program_release(Program &p);
+double program_elapsed_ns(Program &p);
+int program_timings(Program &p, double *ns, size_t n);
+
+// Polls `ev` until it completes or `timeout_ns` passes (0: no limit).
+int wait_event(cudaEvent_t ev, uint64_t timeout_ns);
+// Reads and clears the context's kernel error word; TG_EKERNEL when it was set.
+int take_kernel_error(tg_ctx *ctx);
+
+// Kernel launchers, one per family (kernels_decode.cu, kernels_prefill.cu, gemm_sm100.cu).
+cudaError_t launch_rmsnorm(const tg_params &p, const float *x, const float *g, float *out,
+                           cudaStream_t s);
+cudaError_t launch_gemv_qkv_rope(const tg_params &p, const float *x, const float *g,
+                                 const void *w, const float *cos, const float *sin,
+                                 const uint32_t *at, void *q, void *kc, void *vc, cudaStream_t s);
+cudaError_t launch_attention_split(const tg_params &p, const void *q, const void *kc,
+                                   const void *vc, const uint32_t *at, float *po, float *pml,
+                                   cudaStream_t s);
+cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, const float *po,
+                                     const float *pml, void *out, cudaStream_t s);
+cudaError_t launch_gemv_residual(const tg_params &p, const void *x, const void *w,
+                                 const float *res, float *out, cudaStream_t s);
+cudaError_t launch_gemv_gate_up(const tg_params &p, const float *x, const float *g,
+                                const void *w, void *out, cudaStream_t s);
+cudaError_t launch_stream_read(const tg_params &p, const uint32_t *data, uint32_t *out,
+                               cudaStream_t s, int sm_count);
+cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
+                             const float *g, void *out, cudaStream_t s);
+cudaError_t launch_add_norm_rows(const tg_params &p, const uint32_t *at, const float *c,
+                                 const float *res, const float *g, float *sum, void *normed,
+                                 cudaStream_t s);
+cudaError_t launch_rope_rows(const tg_params &p, const uint32_t *at, const float *c,
+                             const float *cos, const float *sin, void *q, void *kc, void *vc,
+                             cudaStream_t s);
+cudaError_t launch_attention_rows(const tg_params &p, const uint32_t *at, const void *q,
+                                  const void *kc, const void *vc, void *out, cudaStream_t s);
+cudaError_t launch_silu_mul_rows(const tg_params &p, const uint32_t *at, const float *c,
+                                 void *out, cudaStream_t s);
+// C[m][n] = A[m][k] B[n][k]^T in f32. bf16 operands run on tcgen05 (TMA-fed, TMEM accumulator);
+// f32 operands on a SIMT kernel. Returns cudaErrorInvalidValue for shapes it does not tile.
+cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c,
+                        uint32_t *err, cudaStream_t s);
+// The decode constants: positions per attention chunk.
+constexpr uint32_t ATTN_CHUNK = 64;
+// The rows of a prefill attention tile; each run starts on a multiple of it.
+constexpr uint32_t PREFILL_TILE = 64;
+
+}  // namespace tg
