@@ -10,9 +10,10 @@
  * falls back to the CPU: without a usable CUDA device, tg_ctx_create fails.
  *
  * Element types: the residual stream, norms' gains, RoPE tables, partial attention sums and every
- * host-facing hidden state are f32. The storage type of a stack (tg_dtype) is that of its weights,
- * KV cache and of the vectors its projections multiply (q, attention output, SiLU output, normed
- * inputs): f32 or bf16, always with f32 accumulation.
+ * host-facing hidden state are f32, and so is every activation of the decode step (q, attention
+ * output, SiLU output). The storage type of a stack (tg_dtype) is that of its weights and KV
+ * cache, and of the prefill's GEMM operands (normed inputs, q, attention output, SiLU output):
+ * f32 or bf16, always with f32 accumulation.
  */
 #ifndef TGCUDA_H
 #define TGCUDA_H
@@ -100,16 +101,17 @@ typedef enum {
     /* x f32 [rows][hidden], gain f32 [hidden] -> out f32 [rows][hidden]           rmsnorm.comp */
     TG_KERNEL_RMSNORM = 0,
     /* x f32 [rows][hidden], gain f32, W T [(heads+2kv)hd][hidden], cos f32, sin f32,
-     * at u32 [2 rows] -> q T [rows][heads][hd], k cache T, v cache T            gemv_qkv_rope.comp */
+     * at u32 [2 rows] -> q f32 [rows][heads][hd], k cache T, v cache T          gemv_qkv_rope.comp */
     TG_KERNEL_GEMV_QKV_ROPE = 1,
-    /* q T, k cache T, v cache T, at u32 -> partial_o f32 [rows][heads][chunks][hd],
+    /* q f32, k cache T, v cache T, at u32 -> partial_o f32 [rows][heads][chunks][hd],
      * partial_ml f32 [rows][heads][chunks][2]                                  attention_split.comp */
     TG_KERNEL_ATTENTION_SPLIT = 2,
-    /* at u32, partial_o f32, partial_ml f32 -> out T [rows][heads hd]        attention_combine.comp */
+    /* at u32, partial_o f32, partial_ml f32 -> out f32 [rows][heads hd]      attention_combine.comp */
     TG_KERNEL_ATTENTION_COMBINE = 3,
-    /* x T [rows][k], W T [n][k], residual f32 [rows][n] -> out f32 [rows][n]  gemv_residual.comp */
+    /* x f32 [rows][k], W T [n][k], residual f32 [rows][n] -> out f32 [rows][n] gemv_residual.comp */
     TG_KERNEL_GEMV_RESIDUAL = 4,
-    /* x f32 [rows][hidden], gain f32, W T [2 inner][hidden] -> out T [rows][inner] gemv_gate_up.comp */
+    /* x f32 [rows][hidden], gain f32, W T [2 inner][hidden] -> out f32 [rows][inner]
+     *                                                                            gemv_gate_up.comp */
     TG_KERNEL_GEMV_GATE_UP = 5,
     /* data u32 -> out u32 (one word per block)                                  stream_read.comp */
     TG_KERNEL_STREAM_READ = 6,

@@ -480,6 +480,57 @@ def dispatch_once(ctx: Context, kernel: str, p: TgParams,
     return ns.value
 
 
+class Program:
+    """A chain of kernel-table dispatches captured once into a CUDA graph (vulkan::Recording):
+    `dispatches` are (kernel name, params, [(buffer, offset, bytes)], label)."""
+
+    def __init__(self, ctx: Context, dispatches, timed: bool = False):
+        self.ctx = ctx
+        keep = []
+        arr = (TgDispatch * len(dispatches))()
+        for i, (kernel, p, bindings, label) in enumerate(dispatches):
+            b = (TgBinding * len(bindings))(*[TgBinding(m.handle, o, n) for m, o, n in bindings])
+            pp = ctypes.pointer(p)
+            lab = label.encode()
+            keep += [b, pp, lab]
+            arr[i] = TgDispatch(KERNELS[kernel], pp, b, len(bindings), lab)
+        h = ctypes.c_void_p()
+        check(library().tg_program_create(ctx.handle, arr, len(dispatches), int(timed), ctypes.byref(h)))
+        self.handle = h
+        self.n = len(dispatches)
+
+    def start(self) -> None:
+        check(library().tg_program_start(self.handle))
+
+    def wait(self, timeout_ns: int = 0) -> None:
+        check(library().tg_program_wait(self.handle, timeout_ns))
+
+    def run(self) -> None:
+        self.start()
+        self.wait()
+
+    def elapsed_ns(self) -> float:
+        ns = ctypes.c_double()
+        check(library().tg_program_elapsed_ns(self.handle, ctypes.byref(ns)))
+        return ns.value
+
+    def timings(self) -> list[float]:
+        ns = (ctypes.c_double * self.n)()
+        check(library().tg_program_timings(self.handle, ns, self.n))
+        return list(ns)
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            library().tg_program_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 # ---- decoder (decode.rs:778-913) ---------------------------------------------------------------------
 
 WEIGHT_NAMES = ("self_attn.q_proj.weight", "self_attn.k_proj.weight", "self_attn.v_proj.weight",

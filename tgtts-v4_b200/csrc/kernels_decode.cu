@@ -15,59 +15,103 @@ namespace tg {
 
 constexpr int GEMV_WARPS = 4;
 constexpr int GEMV_THREADS = GEMV_WARPS * 32;
-// Vectors each lane loads before it multiplies, per row it takes.
-constexpr int GEMV_AHEAD = 4;
 
-// Writes rows b0 .. b0 + NB - 1 of x ([rows][k] f32) into xs ([NB][k] T), each normed by RMSNorm
-// with gain g when g is given, rows past `rows` as zero (kernels/glsl/norm.glsl:47-53: x times its
-// scale times the gain, rounded once to the storage type).
+// Programmatic dependent launch: a kernel lets the next one start as soon as all of its blocks
+// are running (launch_dependents), and waits for the one before it to finish and its writes to
+// land (wait) only where it first reads what that one wrote. The GEMVs load their weights -
+// constants - before the wait, so the weight stream runs across kernel boundaries. Every block
+// waits before it ends, so a kernel never finishes ahead of the one before it. Both are no-ops
+// in a launch without the programmatic attribute.
+TG_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+TG_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The vectors of the batch a GEMV block multiplies are staged in shared memory in f32 (the
+// decode step keeps every activation in f32; only weights and the KV cache are in the storage
+// type). For 8-wide bf16 weight vectors, element e of vector j of row b sits at
+// xs[b][e / 4][4 j + e % 4], so that a warp's float4 reads of one half are consecutive.
+template <typename T>
+struct Stage {
+    static constexpr int V = Vec<T>::N;
+    static TG_DEVICE int index(int k, int b, int i) {  // element i of row b
+        if constexpr (V == 4) return b * k + i;
+        const int j = i / 8, e = i % 8;
+        return b * k + (e / 4) * (k / 2) + 4 * j + (e % 4);
+    }
+    // The V floats of vector j of row b.
+    static TG_DEVICE void load(const float *xs, int k, int b, int j, float (&x)[V]) {
+        const float4 a = reinterpret_cast<const float4 *>(xs + (size_t)b * k)[j];
+        x[0] = a.x;
+        x[1] = a.y;
+        x[2] = a.z;
+        x[3] = a.w;
+        if constexpr (V == 8) {
+            const float4 c = reinterpret_cast<const float4 *>(xs + (size_t)b * k + k / 2)[j];
+            x[4] = c.x;
+            x[5] = c.y;
+            x[6] = c.z;
+            x[7] = c.w;
+        }
+    }
+};
+
+// Writes rows b0 .. b0 + NB - 1 of x ([rows][k] f32) into xs, each normed by RMSNorm with gain g
+// when g is given (kernels/glsl/norm.glsl:47-53: x times its scale times the gain), rows past
+// `rows` as zero.
 template <typename T, int NB>
-__device__ void stage_normed(const float *__restrict__ x, const float *__restrict__ g, int rows,
-                             int b0, int k, float eps, T *xs) {
+__device__ void stage_rows(const float *__restrict__ x, const float *__restrict__ g, int rows,
+                           int b0, int k, float eps, float *xs) {
     __shared__ float scales[NB];
     const int warp = threadIdx.x >> 5;
-    for (int b = warp; b < NB; b += GEMV_WARPS) {
-        float sc = 0.0f;
-        if (b0 + b < rows) sc = warp_rms_scale(x + (size_t)(b0 + b) * k, k, eps);
-        if ((threadIdx.x & 31) == 0) scales[b] = sc;
+    if (g) {
+        for (int b = warp; b < NB; b += GEMV_WARPS) {
+            float sc = 0.0f;
+            if (b0 + b < rows) sc = warp_rms_scale(x + (size_t)(b0 + b) * k, k, eps);
+            if ((threadIdx.x & 31) == 0) scales[b] = sc;
+        }
+        __syncthreads();
     }
-    __syncthreads();
     const int quads = k / 4;
     for (int i = threadIdx.x; i < NB * quads; i += blockDim.x) {
         const int b = i / quads, c = i % quads;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
         if (b0 + b < rows) v = reinterpret_cast<const float4 *>(x + (size_t)(b0 + b) * k)[c];
-        const float4 gg = reinterpret_cast<const float4 *>(g)[c];
-        const float s = scales[b];
-        T *o = xs + (size_t)b * k + 4 * c;
-        o[0] = from_f32<T>(v.x * s * gg.x);
-        o[1] = from_f32<T>(v.y * s * gg.y);
-        o[2] = from_f32<T>(v.z * s * gg.z);
-        o[3] = from_f32<T>(v.w * s * gg.w);
+        if (g) {
+            const float4 gg = reinterpret_cast<const float4 *>(g)[c];
+            const float s = scales[b];
+            v = make_float4(v.x * s * gg.x, v.y * s * gg.y, v.z * s * gg.z, v.w * s * gg.w);
+        }
+        // Four consecutive elements 4c .. 4c + 3 stay together in either layout.
+        *reinterpret_cast<float4 *>(xs + Stage<T>::index(k, b, 4 * c)) = v;
     }
     __syncthreads();
 }
 
-// Writes rows b0 .. b0 + NB - 1 of x ([rows][k] T) into xs as they are.
-template <typename T, int NB>
-__device__ void stage_plain(const T *__restrict__ x, int rows, int b0, int k, T *xs) {
+// The first AHEAD vectors of each of a warp's rows, loaded before the kernel waits on the one
+// before it.
+template <typename T, int R, int AHEAD>
+struct Prefetch {
+    typename Vec<T>::Raw v[AHEAD][R];
+};
+
+template <typename T, int R, int AHEAD>
+TG_DEVICE void prefetch_rows(const T *__restrict__ w, const int (&rows)[R], int k, Prefetch<T, R, AHEAD> &pf) {
     using Raw = typename Vec<T>::Raw;
-    constexpr int V = Vec<T>::N;
-    const int nvec = k / V;
-    for (int i = threadIdx.x; i < NB * nvec; i += blockDim.x) {
-        const int b = i / nvec, j = i % nvec;
-        Raw v{};
-        if (b0 + b < rows) v = reinterpret_cast<const Raw *>(x + (size_t)(b0 + b) * k)[j];
-        reinterpret_cast<Raw *>(xs + (size_t)b * k)[j] = v;
+    const int lane = threadIdx.x & 31, nvec = k / Vec<T>::N;
+#pragma unroll
+    for (int t = 0; t < AHEAD; t++) {
+        const int j = t * 32 + lane;
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            pf.v[t][r] = j < nvec ? ld_stream(reinterpret_cast<const Raw *>(w + (size_t)rows[r] * k) + j) : Raw{};
     }
-    __syncthreads();
 }
 
-// acc[b][r] = W[rows[r]] . xs[b] for the warp, each lane's share in the fixed order above
-// (summed over lanes by the caller).
-template <typename T, int NB, int R>
-__device__ __forceinline__ void dot_rows(const T *__restrict__ w, const int (&rows)[R], int k,
-                                         const T *xs, float (&acc)[NB][R]) {
+// acc[b][r] = W[rows[r]] . xs[b] for the warp: lane l takes the 16-byte vectors l, l + 32, ... of
+// each row in order, each element by one fused multiply-add (the lanes are joined by the caller).
+// The first AHEAD steps come from `pf`; the rest are loaded AHEAD steps at a time.
+template <typename T, int NB, int R, int AHEAD>
+TG_DEVICE void dot_rows(const T *__restrict__ w, const int (&rows)[R], int k, const float *xs,
+                        const Prefetch<T, R, AHEAD> &pf, float (&acc)[NB][R]) {
     using VT = Vec<T>;
     using Raw = typename VT::Raw;
     constexpr int V = VT::N;
@@ -77,21 +121,24 @@ __device__ __forceinline__ void dot_rows(const T *__restrict__ w, const int (&ro
     for (int b = 0; b < NB; b++)
 #pragma unroll
         for (int r = 0; r < R; r++) acc[b][r] = 0.0f;
-    for (int j0 = 0; j0 < nvec; j0 += 32 * GEMV_AHEAD) {
-        Raw wv[GEMV_AHEAD][R];
+    for (int j0 = 0; j0 < nvec; j0 += 32 * AHEAD) {
+        Raw wv[AHEAD][R];
+        if (j0 == 0) {
 #pragma unroll
-        for (int t = 0; t < GEMV_AHEAD; t++) {
-            const int j = j0 + t * 32 + lane;
+            for (int t = 0; t < AHEAD; t++)
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                if (j < nvec)
-                    wv[t][r] = ld_stream(reinterpret_cast<const Raw *>(w + (size_t)rows[r] * k) + j);
-                else
-                    wv[t][r] = Raw{};
+                for (int r = 0; r < R; r++) wv[t][r] = pf.v[t][r];
+        } else {
+#pragma unroll
+            for (int t = 0; t < AHEAD; t++) {
+                const int j = j0 + t * 32 + lane;
+#pragma unroll
+                for (int r = 0; r < R; r++)
+                    wv[t][r] = j < nvec ? ld_stream(reinterpret_cast<const Raw *>(w + (size_t)rows[r] * k) + j) : Raw{};
             }
         }
 #pragma unroll
-        for (int t = 0; t < GEMV_AHEAD; t++) {
+        for (int t = 0; t < AHEAD; t++) {
             const int j = j0 + t * 32 + lane;
             if (j >= nvec) break;
             float wf[R][V];
@@ -100,7 +147,7 @@ __device__ __forceinline__ void dot_rows(const T *__restrict__ w, const int (&ro
 #pragma unroll
             for (int b = 0; b < NB; b++) {
                 float xf[V];
-                VT::unpack(reinterpret_cast<const Raw *>(xs + (size_t)b * k)[j], xf);
+                Stage<T>::load(xs, k, b, j, xf);
 #pragma unroll
                 for (int r = 0; r < R; r++)
 #pragma unroll
@@ -119,28 +166,36 @@ __device__ __forceinline__ float pick(const float (&v)[NB], int i) {
     return out;
 }
 
+constexpr int AHEAD_PAIRS = 4;  // vectors per row loaded ahead by the two-row GEMVs
+constexpr int AHEAD_ROW = 8;    // and by the one-row GEMV
+
 // gemv_qkv_rope.comp:51-107: q, k, v = W RMSNorm(x); q and k rotated at the row's position; k, v
 // into the row's slot there. A warp takes the pair of rows (i, i + hd/2) of one head, the pair
-// RoPE turns together. Grid: [pairs / GEMV_WARPS, ceil(rows / NB)].
+// RoPE turns together. q is kept in f32. Grid: [pairs / GEMV_WARPS, ceil(rows / NB)].
 template <typename T, int NB>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_qkv_rope_kernel(tg_params p, const float *__restrict__ x, const float *__restrict__ g,
                          const T *__restrict__ w, const float *__restrict__ cosv,
                          const float *__restrict__ sinv, const uint32_t *__restrict__ at,
-                         T *__restrict__ q, T *__restrict__ kc, T *__restrict__ vc) {
+                         float *__restrict__ q, T *__restrict__ kc, T *__restrict__ vc) {
     extern __shared__ __align__(16) unsigned char smem[];
-    T *xs = reinterpret_cast<T *>(smem);
+    float *xs = reinterpret_cast<float *>(smem);
+    pdl_launch_dependents();
     const int k = p.hidden, hd = p.head_dim, half = hd / 2;
     const int heads = p.heads, kvh = p.kv_heads;
     const int b0 = blockIdx.y * NB;
-    stage_normed<T, NB>(x, g, p.rows, b0, k, p.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pair = blockIdx.x * GEMV_WARPS + warp;
-    if (pair >= (heads + 2 * kvh) * half) return;
+    const bool active = pair < (heads + 2 * kvh) * half;
     const int head = pair / half, i = pair % half;
-    const int rows[2] = {head * hd + i, head * hd + i + half};
+    const int rows[2] = {active ? head * hd + i : 0, active ? head * hd + i + half : 0};
+    Prefetch<T, 2, AHEAD_PAIRS> pf;
+    prefetch_rows<T, 2, AHEAD_PAIRS>(w, rows, k, pf);
+    pdl_wait();
+    stage_rows<T, NB>(x, g, p.rows, b0, k, p.eps, xs);
+    if (!active) return;
     float acc[NB][2];
-    dot_rows<T, NB, 2>(w, rows, k, xs, acc);
+    dot_rows<T, NB, 2, AHEAD_PAIRS>(w, rows, k, xs, pf, acc);
     float a[NB], c[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) {
@@ -168,8 +223,8 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     }
     if (head < heads) {
         const size_t to = ((size_t)b * heads + head) * hd + i;
-        q[to] = from_f32<T>(ra);
-        q[to + half] = from_f32<T>(rc);
+        q[to] = ra;
+        q[to + half] = rc;
     } else {
         const size_t to = (((size_t)slot * kvh + (head - heads)) * p.capacity + pos) * hd + i;
         kc[to] = from_f32<T>(ra);
@@ -177,22 +232,27 @@ __global__ void __launch_bounds__(GEMV_THREADS)
     }
 }
 
-// gemv_residual.comp:28-45: out = residual + s W x, a warp to an output row.
+// gemv_residual.comp:28-45: out = residual + s W x, a warp to an output row; x in f32.
 template <typename T, int NB>
 __global__ void __launch_bounds__(GEMV_THREADS)
-    gemv_residual_kernel(tg_params p, const T *__restrict__ x, const T *__restrict__ w,
+    gemv_residual_kernel(tg_params p, const float *__restrict__ x, const T *__restrict__ w,
                          const float *__restrict__ res, float *__restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];
-    T *xs = reinterpret_cast<T *>(smem);
+    float *xs = reinterpret_cast<float *>(smem);
+    pdl_launch_dependents();
     const int k = p.k, n = p.n;
     const int b0 = blockIdx.y * NB;
-    stage_plain<T, NB>(x, p.rows, b0, k, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row = blockIdx.x * GEMV_WARPS + warp;
-    if (row >= n) return;
-    const int rows[1] = {row};
+    const bool active = row < n;
+    const int rows[1] = {active ? row : 0};
+    Prefetch<T, 1, AHEAD_ROW> pf;
+    prefetch_rows<T, 1, AHEAD_ROW>(w, rows, k, pf);
+    pdl_wait();
+    stage_rows<T, NB>(x, nullptr, p.rows, b0, k, 0.0f, xs);
+    if (!active) return;
     float acc[NB][1];
-    dot_rows<T, NB, 1>(w, rows, k, xs, acc);
+    dot_rows<T, NB, 1, AHEAD_ROW>(w, rows, k, xs, pf, acc);
     float y[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) y[b] = warp_sum(acc[b][0]);
@@ -202,22 +262,27 @@ __global__ void __launch_bounds__(GEMV_THREADS)
 }
 
 // gemv_gate_up.comp:31-52: RMSNorm(x) with the post-attention gain, then gate row i and up row i
-// (rows i and inner + i of W) by one warp, out = SiLU(gate) up.
+// (rows i and inner + i of W) by one warp, out = SiLU(gate) up, in f32.
 template <typename T, int NB>
 __global__ void __launch_bounds__(GEMV_THREADS)
     gemv_gate_up_kernel(tg_params p, const float *__restrict__ x, const float *__restrict__ g,
-                        const T *__restrict__ w, T *__restrict__ out) {
+                        const T *__restrict__ w, float *__restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem[];
-    T *xs = reinterpret_cast<T *>(smem);
+    float *xs = reinterpret_cast<float *>(smem);
+    pdl_launch_dependents();
     const int k = p.hidden, inner = p.inner;
     const int b0 = blockIdx.y * NB;
-    stage_normed<T, NB>(x, g, p.rows, b0, k, p.eps, xs);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i = blockIdx.x * GEMV_WARPS + warp;
-    if (i >= inner) return;
-    const int rows[2] = {i, inner + i};
+    const bool active = i < inner;
+    const int rows[2] = {active ? i : 0, active ? inner + i : 0};
+    Prefetch<T, 2, AHEAD_PAIRS> pf;
+    prefetch_rows<T, 2, AHEAD_PAIRS>(w, rows, k, pf);
+    pdl_wait();
+    stage_rows<T, NB>(x, g, p.rows, b0, k, p.eps, xs);
+    if (!active) return;
     float acc[NB][2];
-    dot_rows<T, NB, 2>(w, rows, k, xs, acc);
+    dot_rows<T, NB, 2, AHEAD_PAIRS>(w, rows, k, xs, pf, acc);
     float gate[NB], up[NB];
 #pragma unroll
     for (int b = 0; b < NB; b++) {
@@ -225,13 +290,15 @@ __global__ void __launch_bounds__(GEMV_THREADS)
         up[b] = warp_sum(acc[b][1]);
     }
     if (lane >= NB || b0 + lane >= (int)p.rows) return;
-    out[(size_t)(b0 + lane) * inner + i] = from_f32<T>(silu_mul(pick<NB>(gate, lane), pick<NB>(up, lane)));
+    out[(size_t)(b0 + lane) * inner + i] = silu_mul(pick<NB>(gate, lane), pick<NB>(up, lane));
 }
 
 // rmsnorm.comp: out = RMSNorm(x) g per row, a warp to a row, in f32.
 __global__ void __launch_bounds__(128)
     rmsnorm_kernel(tg_params p, const float *__restrict__ x, const float *__restrict__ g,
                    float *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= (int)p.rows) return;
     const int k = p.hidden;
@@ -248,10 +315,12 @@ __global__ void __launch_bounds__(128)
 // attention_split.comp:52-112: block (c, h, b) scores the GROUP query heads that kv head h serves
 // against ATTN_CHUNK positions from c ATTN_CHUNK of row b's slot, masked past the row's position,
 // and writes each head's chunk softmax unnormalised with its maximum and sum. A chunk that starts
-// past the position writes nothing, nor does a spare row.
+// past the position writes nothing, nor does a spare row. The keys and values before the row's
+// position were written by earlier steps, so they are loaded before waiting on qkv_rope; the
+// position's own, and q, after.
 template <typename T>
 __global__ void __launch_bounds__(128)
-    attention_split_kernel(tg_params p, const T *__restrict__ q, const T *__restrict__ kc,
+    attention_split_kernel(tg_params p, const float *__restrict__ q, const T *__restrict__ kc,
                            const T *__restrict__ vc, const uint32_t *__restrict__ at,
                            float *__restrict__ po, float *__restrict__ pml) {
     constexpr int C = ATTN_CHUNK;
@@ -259,35 +328,34 @@ __global__ void __launch_bounds__(128)
     using Raw = typename VT::Raw;
     constexpr int V = VT::N;
     extern __shared__ __align__(16) unsigned char smem[];
+    pdl_launch_dependents();
     const int hd = p.head_dim, heads = p.heads, kvh = p.kv_heads, group = heads / kvh;
     const int c = blockIdx.x, kv = blockIdx.y, b = blockIdx.z;
     const int start = c * C;
     uint32_t pos, slot;
-    if (!placed(at, p.rows, b, p.capacity, p.slots, pos, slot) || start > (int)pos) return;
+    if (!placed(at, p.rows, b, p.capacity, p.slots, pos, slot) || start > (int)pos) {
+        pdl_wait();
+        return;
+    }
     float *qs = reinterpret_cast<float *>(smem);   // [group][hd]
     float *ks = qs + group * hd;                   // [C][hd + 1]
     float *vs = ks + C * (hd + 1);                 // [C][hd]
     float *ps = vs + C * hd;                       // [group][C]
     const int tid = threadIdx.x;
     const int first_head = kv * group;
-    {
-        const Raw *src = reinterpret_cast<const Raw *>(q + ((size_t)b * heads + first_head) * hd);
-        for (int i = tid; i < group * hd / V; i += blockDim.x) {
-            float f[V];
-            VT::unpack(src[i], f);
-#pragma unroll
-            for (int e = 0; e < V; e++) qs[i * V + e] = f[e];
-        }
-    }
-    {
-        const size_t base = (((size_t)slot * kvh + kv) * p.capacity + start) * hd;
-        const Raw *ksrc = reinterpret_cast<const Raw *>(kc + base);
-        const Raw *vsrc = reinterpret_cast<const Raw *>(vc + base);
-        const int per_row = hd / V;
+    const size_t base = (((size_t)slot * kvh + kv) * p.capacity + start) * hd;
+    const Raw *ksrc = reinterpret_cast<const Raw *>(kc + base);
+    const Raw *vsrc = reinterpret_cast<const Raw *>(vc + base);
+    const int per_row = hd / V;
+    // pass 0: positions before the row's (earlier steps wrote them); pass 1: the row's own.
+    for (int pass = 0; pass < 2; pass++) {
+        if (pass == 1) pdl_wait();
         for (int i = tid; i < C * per_row; i += blockDim.x) {
             const int pp = i / per_row, j = i % per_row;
+            const int at_pos = start + pp;
+            if ((pass == 0) != (at_pos < (int)pos)) continue;
             float kf[V], vf[V];
-            if (start + pp <= (int)pos) {
+            if (at_pos <= (int)pos) {
                 VT::unpack(ksrc[i], kf);
                 VT::unpack(vsrc[i], vf);
             } else {
@@ -300,6 +368,10 @@ __global__ void __launch_bounds__(128)
                 vs[pp * hd + j * V + e] = vf[e];
             }
         }
+    }
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(q + ((size_t)b * heads + first_head) * hd);
+        for (int i = tid; i < group * hd / 4; i += blockDim.x) reinterpret_cast<float4 *>(qs)[i] = src[i];
     }
     __syncthreads();
     const float scale = 1.0f / sqrtf((float)hd);
@@ -341,12 +413,13 @@ __global__ void __launch_bounds__(128)
 }
 
 // attention_combine.comp:29-58: joins chunks 0 .. pos / ATTN_CHUNK of each (row, head) in order:
-// their largest maximum, the rescaled sums, and the division.
-template <typename T>
+// their largest maximum, the rescaled sums, and the division; out in f32.
 __global__ void __launch_bounds__(128)
     attention_combine_kernel(tg_params p, const uint32_t *__restrict__ at,
                              const float *__restrict__ po, const float *__restrict__ pml,
-                             T *__restrict__ out) {
+                             float *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int h = blockIdx.x, b = blockIdx.y, hd = p.head_dim;
     uint32_t pos, slot;
     if (!placed(at, p.rows, b, p.capacity, p.slots, pos, slot)) return;
@@ -361,7 +434,7 @@ __global__ void __launch_bounds__(128)
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
         float acc = 0.0f;
         for (int c = 0; c < n; c++) acc = __fmaf_rn(o[(size_t)c * hd + d], expf(ml[2 * c] - m), acc);
-        out[((size_t)b * p.heads + h) * hd + d] = from_f32<T>(__fdiv_rn(acc, total));
+        out[((size_t)b * p.heads + h) * hd + d] = __fdiv_rn(acc, total);
     }
 }
 
@@ -400,7 +473,7 @@ __global__ void __launch_bounds__(256) stream_read_kernel(const uint4 *__restric
 
 // The rows of a batch a GEMV block takes: up to 8, fewer when their vectors of k would not fit in
 // `limit` bytes of shared memory. What a block takes never changes what is summed.
-static int rows_per_block(uint32_t rows, uint32_t k, size_t elem, size_t limit = 160 * 1024) {
+static int rows_per_block(uint32_t rows, uint32_t k, size_t elem = 4, size_t limit = 160 * 1024) {
     int nb = 8;
     while (nb > 1 && ((uint32_t)nb / 2 >= rows || nb * k * elem > limit)) nb /= 2;
     return nb;
@@ -410,6 +483,24 @@ template <typename F>
 static cudaError_t with_smem(F kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return cudaSuccess;
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+// Launches `kern` with the programmatic-stream-serialization attribute, so that in a stream (or a
+// graph captured from one) it may start while the kernel before it finishes (see pdl_wait).
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 #define TG_DISPATCH_NB(NB_VAR, ...)                           \
@@ -424,17 +515,18 @@ template <typename T>
 static cudaError_t qkv_rope_t(const tg_params &p, const float *x, const float *g, const void *w,
                               const float *cs, const float *sn, const uint32_t *at, void *q,
                               void *kc, void *vc, cudaStream_t s) {
-    const int nb = rows_per_block(p.rows, p.hidden, sizeof(T));
+    const int nb = rows_per_block(p.rows, p.hidden);
     const uint32_t pairs = (p.heads + 2 * p.kv_heads) * p.head_dim / 2;
     dim3 grid((pairs + GEMV_WARPS - 1) / GEMV_WARPS, (p.rows + nb - 1) / nb);
     cudaError_t e = cudaSuccess;
     TG_DISPATCH_NB(nb, {
-        const size_t smem = (size_t)NB * p.hidden * sizeof(T);
+        const size_t smem = (size_t)NB * p.hidden * 4;
         auto kern = gemv_qkv_rope_kernel<T, NB>;
         if ((e = with_smem(kern, smem)) != cudaSuccess) return e;
-        kern<<<grid, GEMV_THREADS, smem, s>>>(p, x, g, (const T *)w, cs, sn, at, (T *)q, (T *)kc, (T *)vc);
+        e = launch_pdl(kern, grid, dim3(GEMV_THREADS), smem, s, p, x, g, (const T *)w, cs, sn, at, (float *)q,
+                       (T *)kc, (T *)vc);
     });
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_gemv_qkv_rope(const tg_params &p, const float *x, const float *g,
@@ -447,16 +539,16 @@ cudaError_t launch_gemv_qkv_rope(const tg_params &p, const float *x, const float
 template <typename T>
 static cudaError_t residual_t(const tg_params &p, const void *x, const void *w, const float *res,
                               float *out, cudaStream_t s) {
-    const int nb = rows_per_block(p.rows, p.k, sizeof(T));
+    const int nb = rows_per_block(p.rows, p.k);
     dim3 grid((p.n + GEMV_WARPS - 1) / GEMV_WARPS, (p.rows + nb - 1) / nb);
     cudaError_t e = cudaSuccess;
     TG_DISPATCH_NB(nb, {
-        const size_t smem = (size_t)NB * p.k * sizeof(T);
+        const size_t smem = (size_t)NB * p.k * 4;
         auto kern = gemv_residual_kernel<T, NB>;
         if ((e = with_smem(kern, smem)) != cudaSuccess) return e;
-        kern<<<grid, GEMV_THREADS, smem, s>>>(p, (const T *)x, (const T *)w, res, out);
+        e = launch_pdl(kern, grid, dim3(GEMV_THREADS), smem, s, p, (const float *)x, (const T *)w, res, out);
     });
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_gemv_residual(const tg_params &p, const void *x, const void *w,
@@ -468,16 +560,16 @@ cudaError_t launch_gemv_residual(const tg_params &p, const void *x, const void *
 template <typename T>
 static cudaError_t gate_up_t(const tg_params &p, const float *x, const float *g, const void *w,
                              void *out, cudaStream_t s) {
-    const int nb = rows_per_block(p.rows, p.hidden, sizeof(T));
+    const int nb = rows_per_block(p.rows, p.hidden);
     dim3 grid((p.inner + GEMV_WARPS - 1) / GEMV_WARPS, (p.rows + nb - 1) / nb);
     cudaError_t e = cudaSuccess;
     TG_DISPATCH_NB(nb, {
-        const size_t smem = (size_t)NB * p.hidden * sizeof(T);
+        const size_t smem = (size_t)NB * p.hidden * 4;
         auto kern = gemv_gate_up_kernel<T, NB>;
         if ((e = with_smem(kern, smem)) != cudaSuccess) return e;
-        kern<<<grid, GEMV_THREADS, smem, s>>>(p, x, g, (const T *)w, (T *)out);
+        e = launch_pdl(kern, grid, dim3(GEMV_THREADS), smem, s, p, x, g, (const T *)w, (float *)out);
     });
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_gemv_gate_up(const tg_params &p, const float *x, const float *g,
@@ -488,8 +580,7 @@ cudaError_t launch_gemv_gate_up(const tg_params &p, const float *x, const float 
 
 cudaError_t launch_rmsnorm(const tg_params &p, const float *x, const float *g, float *out,
                            cudaStream_t s) {
-    rmsnorm_kernel<<<(p.rows + 3) / 4, 128, 0, s>>>(p, x, g, out);
-    return cudaGetLastError();
+    return launch_pdl(rmsnorm_kernel, dim3((p.rows + 3) / 4), dim3(128), 0, s, p, x, g, out);
 }
 
 static size_t split_smem(const tg_params &p) {
@@ -505,8 +596,7 @@ static cudaError_t split_t(const tg_params &p, const void *q, const void *kc, co
     cudaError_t e = with_smem(kern, smem);
     if (e != cudaSuccess) return e;
     dim3 grid(p.capacity / ATTN_CHUNK, p.kv_heads, p.rows);
-    kern<<<grid, 128, smem, s>>>(p, (const T *)q, (const T *)kc, (const T *)vc, at, po, pml);
-    return cudaGetLastError();
+    return launch_pdl(kern, grid, dim3(128), smem, s, p, (const float *)q, (const T *)kc, (const T *)vc, at, po, pml);
 }
 
 cudaError_t launch_attention_split(const tg_params &p, const void *q, const void *kc,
@@ -520,11 +610,7 @@ cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, con
                                      const float *pml, void *out, cudaStream_t s) {
     dim3 grid(p.heads, p.rows);
     const int threads = p.head_dim < 128 ? p.head_dim : 128;
-    if (p.dtype == TG_BF16)
-        attention_combine_kernel<bf16><<<grid, threads, 0, s>>>(p, at, po, pml, (bf16 *)out);
-    else
-        attention_combine_kernel<float><<<grid, threads, 0, s>>>(p, at, po, pml, (float *)out);
-    return cudaGetLastError();
+    return launch_pdl(attention_combine_kernel, grid, dim3(threads), 0, s, p, at, po, pml, (float *)out);
 }
 
 cudaError_t launch_stream_read(const tg_params &p, const uint32_t *data, uint32_t *out,

@@ -184,28 +184,28 @@ static void decode_launches(tg_decoder &d) {
         char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
         push(d.launches, TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
              {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
-              {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * T},
+              {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * F},
               {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
         push(d.launches, TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
-             {{d.q.ptr(), R * d.attn() * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
+             {{d.q.ptr(), R * d.attn() * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}});
         push(d.launches, TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
              {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
-              {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.att.ptr(), R * d.attn() * T}});
+              {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.att.ptr(), R * d.attn() * F}});
         tg_params po = base;
         po.n = (uint32_t)H;
         po.k = (uint32_t)d.attn();
         push(d.launches, TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
-             {{d.att.ptr(), R * d.attn() * T}, {d.w(o.o), H * d.attn() * T}, {in, R * H * F}, {d.mid.ptr(), R * H * F}});
+             {{d.att.ptr(), R * d.attn() * F}, {d.w(o.o), H * d.attn() * T}, {in, R * H * F}, {d.mid.ptr(), R * H * F}});
         push(d.launches, TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
              {{d.mid.ptr(), R * H * F}, {d.w(o.post_norm), H * F}, {d.w(o.gate_up), 2 * I * H * T},
-              {d.mlp.ptr(), R * I * T}});
+              {d.mlp.ptr(), R * I * F}});
         tg_params pd = base;
         pd.n = (uint32_t)H;
         pd.k = (uint32_t)I;
         push(d.launches, TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
-             {{d.mlp.ptr(), R * I * T}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
+             {{d.mlp.ptr(), R * I * F}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
     }
     push(d.launches, TG_KERNEL_RMSNORM, base, "final_norm",
          {{d.h.ptr(), R * H * F}, {d.w(d.final_norm), H * F}, {d.out.ptr(), R * H * F}});
@@ -266,9 +266,9 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(d->h.alloc(ctx, R * H * F));
     TG_TRY(d->mid.alloc(ctx, R * H * F));
     TG_TRY(d->out.alloc(ctx, R * H * F));
-    TG_TRY(d->q.alloc(ctx, R * d->attn() * T));
-    TG_TRY(d->att.alloc(ctx, R * d->attn() * T));
-    TG_TRY(d->mlp.alloc(ctx, R * I * T));
+    TG_TRY(d->q.alloc(ctx, R * d->attn() * F));
+    TG_TRY(d->att.alloc(ctx, R * d->attn() * F));
+    TG_TRY(d->mlp.alloc(ctx, R * I * F));
     TG_TRY(d->po.alloc(ctx, R * s->heads * chunks * s->head_dim * F));
     TG_TRY(d->pml.alloc(ctx, R * s->heads * chunks * 2 * F));
     TG_TRY(d->words.alloc(ctx, 2 * R * 4));

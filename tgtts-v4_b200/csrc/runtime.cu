@@ -84,24 +84,24 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             break;
         case TG_KERNEL_GEMV_QKV_ROPE:
             out = {{"x", rows * H * F}, {"gain", H * F}, {"W", width * H * T}, {"cos", table},
-                   {"sin", table}, {"at", words}, {"q", rows * attn * T}, {"k_cache", cache},
+                   {"sin", table}, {"at", words}, {"q", rows * attn * F}, {"k_cache", cache},
                    {"v_cache", cache}};
             break;
         case TG_KERNEL_ATTENTION_SPLIT:
-            out = {{"q", rows * attn * T}, {"k_cache", cache}, {"v_cache", cache}, {"at", words},
+            out = {{"q", rows * attn * F}, {"k_cache", cache}, {"v_cache", cache}, {"at", words},
                    {"partial_o", rows * heads * chunks * hd * F},
                    {"partial_ml", rows * heads * chunks * 2 * F}};
             break;
         case TG_KERNEL_ATTENTION_COMBINE:
             out = {{"at", words}, {"partial_o", rows * heads * chunks * hd * F},
-                   {"partial_ml", rows * heads * chunks * 2 * F}, {"out", rows * attn * T}};
+                   {"partial_ml", rows * heads * chunks * 2 * F}, {"out", rows * attn * F}};
             break;
         case TG_KERNEL_GEMV_RESIDUAL:
-            out = {{"x", rows * p.k * T}, {"W", (uint64_t)p.n * p.k * T}, {"residual", rows * p.n * F},
+            out = {{"x", rows * p.k * F}, {"W", (uint64_t)p.n * p.k * T}, {"residual", rows * p.n * F},
                    {"out", rows * p.n * F}};
             break;
         case TG_KERNEL_GEMV_GATE_UP:
-            out = {{"x", rows * H * F}, {"gain", H * F}, {"W", 2 * I * H * T}, {"out", rows * I * T}};
+            out = {{"x", rows * H * F}, {"gain", H * F}, {"W", 2 * I * H * T}, {"out", rows * I * F}};
             break;
         case TG_KERNEL_STREAM_READ:
             out = {{"data", (uint64_t)p.k * 4}, {"out", (uint64_t)p.n * 4}};
@@ -272,12 +272,17 @@ int program_build(tg_ctx *ctx, const std::vector<Launch> &launches, bool timed, 
         return cuda_fail(e, "cudaStreamBeginCapture");
     }
     int st = TG_OK;
-    cudaEventRecord(out.events[0], cap);
+    // External event nodes, so that the host can query and time them after each launch.
+    auto record = [&](cudaEvent_t ev) {
+        const cudaError_t r = cudaEventRecordWithFlags(ev, cap, cudaEventRecordExternal);
+        if (r != cudaSuccess && st == TG_OK) st = cuda_fail(r, "cudaEventRecordWithFlags");
+    };
+    record(out.events[0]);
     for (size_t i = 0; i < launches.size() && st == TG_OK; i++) {
         st = enqueue_launch(launches[i], ctx->err_dev, cap, ctx->sm_count);
-        if (timed) cudaEventRecord(out.events[i + 1], cap);
+        if (timed) record(out.events[i + 1]);
     }
-    if (!timed) cudaEventRecord(out.events[1], cap);
+    if (!timed) record(out.events[1]);
     cudaGraph_t graph = nullptr;
     e = cudaStreamEndCapture(cap, &graph);
     cudaStreamDestroy(cap);
