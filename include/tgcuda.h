@@ -271,6 +271,23 @@ int tg_prefill_timings(tg_prefill *p, double *ns, size_t n, size_t *n_dispatches
 int tg_prefill_dispatch_label(tg_prefill *p, size_t i, char *label, size_t label_bytes);
 uint32_t tg_prefill_max_rows(const tg_prefill *p);
 
+/* ---- Decode attention without allocation -------------------------------------------------------
+ * No counterpart in tgtts-v4. For callers that cannot allocate device memory themselves or let a
+ * library do it (an engine that owns every byte of HBM through its own pool, or code recording a
+ * CUDA graph, where an allocation would break the capture): attention_split + attention_combine of
+ * the decode step (TG_KERNEL_ATTENTION_SPLIT / _COMBINE, same params and results) with their
+ * partial sums kept in a fixed array inside the library, TG_NOALLOC_SCRATCH_BYTES per device,
+ * instead of a buffer the caller passes. It allocates nothing. The caller passes q (f32
+ * [rows][heads][hd]), the caches (storage type), the placement words and out (f32
+ * [rows][heads hd]), all device pointers, and a cudaStream_t (NULL: the legacy stream); the work
+ * is enqueued there and not waited for. Refuses (TG_ESHAPE) a shape whose partials,
+ * rows x heads x capacity/64 x (head_dim + 2) f32, do not fit. The first call on a device looks the
+ * array up for that device (and may load the library's module there): make it before any stream
+ * capture. All calls on a device share the array, so calls that overlap on the GPU race. */
+#define TG_NOALLOC_SCRATCH_BYTES (4u << 20)
+int tg_attention_decode_noalloc(const tg_params *p, const float *q, const void *k_cache,
+                                const void *v_cache, const uint32_t *at, float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -189,6 +189,7 @@ SIGNATURES = {
     "tg_prefill_timings": (_I, [_P, _DP, _SZ, ctypes.POINTER(_SZ)]),
     "tg_prefill_dispatch_label": (_I, [_P, _SZ, ctypes.c_char_p, _SZ]),
     "tg_prefill_max_rows": (_U32, [_P]),
+    "tg_attention_decode_noalloc": (_I, [ctypes.POINTER(TgParams), _P, _P, _P, _P, _P, _P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -529,6 +530,16 @@ class Program:
             self.close()
         except Exception:
             pass
+
+
+def attention_decode_noalloc(p: TgParams, q_ptr: int, k_ptr: int, v_ptr: int, at_ptr: int,
+                             out_ptr: int, stream: int = 0) -> None:
+    """Decode attention (split + combine) with its partials in the library's fixed scratch array:
+    nothing is allocated. All pointers are device addresses; the work is enqueued on `stream`."""
+    check(library().tg_attention_decode_noalloc(ctypes.byref(p), ctypes.c_void_p(q_ptr),
+                                                ctypes.c_void_p(k_ptr), ctypes.c_void_p(v_ptr),
+                                                ctypes.c_void_p(at_ptr), ctypes.c_void_p(out_ptr),
+                                                ctypes.c_void_p(stream)))
 
 
 # ---- decoder (decode.rs:778-913) ---------------------------------------------------------------------
