@@ -129,7 +129,11 @@ typedef enum {
     TG_KERNEL_SILU_MUL_ROWS = 11,
     /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32) */
     TG_KERNEL_GEMM = 12,
-    TG_KERNEL_COUNT = 13
+    /* q f32, k cache T, v cache T, at u32 -> out f32 [rows][heads hd]: ATTENTION_SPLIT and
+     * ATTENTION_COMBINE in one dispatch, a thread-block cluster per (row, kv head) whose blocks
+     * keep their chunks' partials in shared memory; the same results bit for bit */
+    TG_KERNEL_ATTENTION_DECODE = 13,
+    TG_KERNEL_COUNT = 14
 } tg_kernel_id;
 
 /* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the
@@ -235,7 +239,8 @@ int tg_decoder_step_device(tg_decoder *d, const uint32_t *words, const float *x_
 /* Decoder::timings: the last step's GPU time, and per dispatch when created timed. */
 int tg_decoder_elapsed_ns(tg_decoder *d, double *ns);
 int tg_decoder_timings(tg_decoder *d, double *ns, size_t n, size_t *n_dispatches);
-/* The recorded dispatches' count and labels (decode.rs:935-951: 6 per layer and the final norm). */
+/* The recorded dispatches' count and labels (decode.rs:935-951: 6 per layer and the final norm;
+ * one, "decode_step", when the step is the persistent launch). */
 int tg_decoder_dispatch_label(tg_decoder *d, size_t i, char *label, size_t label_bytes);
 /* Copies positions [first, first+count) of a slot's keys (kind 0) or values (1) of a layer to the
  * host as f32 [kv_heads][count][head_dim]. */
@@ -245,6 +250,14 @@ int tg_decoder_read_cache(tg_decoder *d, uint32_t layer, uint32_t slot, uint32_t
  * crates/graph/src/prompt.rs:587-633): moves positions [0, count) of slot `from` to slot `to`
  * in every layer, on the GPU. */
 int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, uint32_t count);
+/* Decoder::retuned (decode.rs:874-890): records the step again over the same weights and cache, as
+ * one persistent launch (persistent != 0; batches of up to 2 rows) or as six kernels a layer, timed
+ * per dispatch when `timed`. Both give the same results bit for bit. A new decoder starts recorded
+ * as kernels. TG_ESHAPE when the persistent step does not take the decoder (it is then left
+ * recorded as kernels). */
+int tg_decoder_retune(tg_decoder *d, int persistent, int timed);
+/* 1 when the decoder's step is the persistent launch. */
+int tg_decoder_persistent(const tg_decoder *d);
 /* The weight bytes one step reads at this dtype (Shape::weight_bytes at its element size). */
 uint64_t tg_decoder_weight_bytes(const tg_decoder *d);
 

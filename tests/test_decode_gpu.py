@@ -95,6 +95,13 @@ def test_a_row_comes_out_bit_for_bit_as_it_does_alone(pkg, ctx, syn, dtype):
         return np.stack(outs)  # [steps][requests][hidden]
 
     alone = {r: run(1, 1, [r])[:, 0] for r in (0, 5, 17, 63)}
+    # Alone again on the persistent step: the same bits as on the kernels.
+    for r in (0, 17):
+        dec = pkg.Decoder(ctx, shape, rows=1, slots=1, dtype=dtype).retuned(True)
+        dec.load(w)
+        for t in range(steps):
+            assert np.array_equal(dec.step_rows([pkg.Row(start[r] + t, 0)], xs[t, r][None])[0], alone[r][t])
+        dec.close()
     for rows in (3, 8, 64):
         requests = list(range(rows)) if rows == 64 else [0, 5, 17][:rows] + list(range(20, 20 + rows - 3))
         batched = run(rows, rows, requests)
@@ -174,3 +181,45 @@ def test_timed_steps_label_six_dispatches_a_layer(pkg, ctx, syn):
     assert [l for l, _ in t[:6]] == ["qkv_rope", "attention_split", "attention_combine", "o_proj",
                                      "gate_up", "down_proj"]
     assert t[-1][0] == "final_norm" and all(ns > 0 for _, ns in t)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_the_persistent_step_gives_the_kernel_steps_bits(pkg, ctx, syn, dtype):
+    """One persistent launch per step and six kernels a layer (Decoder::retuned) take the same sums
+    in the same order: every live row comes out bit for bit the same, spare rows included."""
+    cfg = syn.TINY if dtype == "f32" else syn.S05B
+    shape = syn.shape_of(cfg, capacity=256, layers=3)
+    w = syn.make_weights(cfg, seed=0, layers=3, jitter_gains=True)
+    outs, caches = {}, {}
+    for persistent in (True, False):
+        dec = pkg.Decoder(ctx, shape, rows=2, slots=2, dtype=dtype)
+        dec.load(w)
+        dec.retuned(persistent)
+        assert dec.persistent == persistent
+        pkg.Prefill(dec, max_rows=128).run(0, syn.make_inputs(70, cfg.hidden, seed=3), slot=1)
+        rng = np.random.default_rng(4)
+        res = []
+        for t in range(5):
+            x = rng.standard_normal((2, cfg.hidden), dtype=np.float32)
+            rows = [pkg.Row(t, 0), pkg.Row(70 + t, 1)] if t < 4 else [None, pkg.Row(74, 1)]
+            res.append(dec.step_rows(rows, x))
+        outs[persistent] = res
+        caches[persistent] = [dec.read_cache(l, s_, k, 0, 75) for l in range(3) for s_ in range(2) for k in "kv"]
+        dec.close()
+    for t, (a, b) in enumerate(zip(outs[True], outs[False])):
+        assert np.array_equal(a[1], b[1]), t
+        if t < 4:
+            assert np.array_equal(a[0], b[0]), t
+    for a, b in zip(caches[True], caches[False]):
+        assert np.array_equal(a, b)
+
+
+def test_the_persistent_step_takes_small_batches_only(pkg, ctx, syn):
+    shape = syn.shape_of(syn.S05B, capacity=1024, layers=1)
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16")
+    assert not dec.persistent
+    assert dec.retuned(True).persistent
+    assert dec.labels() == ["decode_step"]
+    assert not dec.retuned(False).persistent and len(dec.labels()) == 7
+    with pytest.raises(pkg.ShapeError):
+        pkg.Decoder(ctx, shape, rows=3, slots=3, dtype="bf16").retuned(True)

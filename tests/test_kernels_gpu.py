@@ -87,3 +87,46 @@ def test_stream_read_reads_every_word(pkg, ctx):
     pkg.dispatch_once(ctx, "stream_read", p, [(m, 0, words.nbytes), (out, 0, ctx.sm_count * 8 * 4)])
     got = out.read(np.uint32, ctx.sm_count * 8)
     assert np.bitwise_xor.reduce(got) == np.bitwise_xor.reduce(words)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_fused_decode_attention_equals_split_and_combine(pkg, ctx, syn, dtype):
+    rows, cap = 5, 256
+    shape = pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=1, capacity=cap)
+    rng = np.random.default_rng(9)
+    hd, heads, kv = 64, 16, 2
+    q = rng.standard_normal((rows, heads, hd), dtype=np.float32)
+    k = rng.standard_normal((rows, kv, cap, hd), dtype=np.float32)
+    v = rng.standard_normal((rows, kv, cap, hd), dtype=np.float32)
+    if dtype == "bf16":
+        k, v = syn.bf16_bits(k), syn.bf16_bits(v)
+    words = np.array([0, 63, 64, 0xFFFFFFFF, 255] + list(range(rows)), np.uint32)
+    mq, mk, mv, mat = _mem(pkg, ctx, q), _mem(pkg, ctx, k), _mem(pkg, ctx, v), _mem(pkg, ctx, words)
+    chunks = cap // 64
+    po = pkg.Memory(ctx, rows * heads * chunks * hd * 4)
+    pml = pkg.Memory(ctx, rows * heads * chunks * 2 * 4)
+    n = rows * heads * hd
+    outs = []
+    for _ in range(2):
+        a, b = pkg.Memory(ctx, n * 4), pkg.Memory(ctx, n * 4)
+        a.write(np.zeros(n, np.float32))
+        b.write(np.zeros(n, np.float32))
+        p = pkg.params(shape, dtype, rows=rows, slots=rows)
+        common = [(mq, 0, q.nbytes), (mk, 0, k.nbytes), (mv, 0, v.nbytes), (mat, 0, words.nbytes),
+                  (po, 0, po.nbytes), (pml, 0, pml.nbytes)]
+        pkg.dispatch_once(ctx, "attention_split", p, common)
+        pkg.dispatch_once(ctx, "attention_combine", p, [(mat, 0, words.nbytes), (po, 0, po.nbytes),
+                                                        (pml, 0, pml.nbytes), (a, 0, n * 4)])
+        pkg.dispatch_once(ctx, "attention_decode", p, common[:4] + [(b, 0, n * 4)])
+        outs.append((a.read(np.float32, n), b.read(np.float32, n)))
+    for split_combine, fused in outs:
+        assert np.array_equal(split_combine, fused)
+    # Against softmax attention in f64 for a live row (row 2 at position 64, slot 2).
+    kf = syn.bf16_to_f32(k) if dtype == "bf16" else k
+    vf = syn.bf16_to_f32(v) if dtype == "bf16" else v
+    got = outs[0][1].reshape(rows, heads, hd)
+    for h in (0, 9):
+        s = kf[2, h // 8, :65].astype(np.float64) @ q[2, h].astype(np.float64) / 8.0
+        e = np.exp(s - s.max())
+        want = (e / e.sum()) @ vf[2, h // 8, :65].astype(np.float64)
+        assert np.max(np.abs(got[2, h] - want)) < 1e-5

@@ -93,7 +93,7 @@ RES_DEVICE, RES_UPLOAD, RES_READBACK = 0, 1, 2
 KERNELS = {
     "rmsnorm": 0, "gemv_qkv_rope": 1, "attention_split": 2, "attention_combine": 3,
     "gemv_residual": 4, "gemv_gate_up": 5, "stream_read": 6, "norm_rows": 7, "add_norm_rows": 8,
-    "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12,
+    "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12, "attention_decode": 13,
 }
 
 
@@ -180,6 +180,8 @@ SIGNATURES = {
     "tg_decoder_read_cache": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _FP]),
     "tg_decoder_copy_slot": (_I, [_P, _U32, _U32, _U32]),
     "tg_decoder_weight_bytes": (_U64, [_P]),
+    "tg_decoder_retune": (_I, [_P, _I, _I]),
+    "tg_decoder_persistent": (_I, [_P]),
     "tg_prefill_create": (_I, [_P, _U32, _I, ctypes.POINTER(_P)]),
     "tg_prefill_destroy": (_I, [_P]),
     "tg_prefill_run": (_I, [_P, _U32, _U32, _FP, _U32, _FP]),
@@ -661,6 +663,16 @@ class Decoder:
 
     def weight_bytes(self) -> int:
         return int(library().tg_decoder_weight_bytes(self.handle))
+
+    def retuned(self, persistent: bool, timed: bool = False) -> "Decoder":
+        """Decoder::retuned (decode.rs:874-890): the step recorded again, as one persistent launch
+        or as six kernels a layer (the same results bit for bit), over the same weights and cache."""
+        check(library().tg_decoder_retune(self.handle, int(persistent), int(timed)))
+        return self
+
+    @property
+    def persistent(self) -> bool:
+        return bool(library().tg_decoder_persistent(self.handle))
 
     def _x(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)

@@ -66,34 +66,6 @@ __global__ void __launch_bounds__(256)
 constexpr int TC_BM = 128, TC_BK = 64, TC_STAGES = 4, TC_THREADS = 128;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB per stage
 
-TG_DEVICE uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-TG_DEVICE uint64_t globaltimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-TG_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-TG_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-
-TG_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.b32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
 
 // Waits for the phase of parity `parity` of `bar` to complete, for at most 2 s (1 ms once the
 // block has given up on a wait). Past that it records ERR_WAIT_TIMEOUT and returns, so that the

@@ -105,7 +105,9 @@ struct tg_decoder {
     Owned cos, sin, kcache, vcache;  // caches: [layers][slots][kv][capacity][hd]
     uint64_t cache_layer = 0;        // bytes of one layer's cache
     // Activations of the step, [rows][...].
-    Owned x_in, h, mid, out, q, att, mlp, po, pml, words;
+    Owned x_in, h, mid, out, q, att, mlp, words;
+    Owned po, pml, psync, offs;  // the persistent step's attention partials, barrier words, weight offsets
+    bool persistent = false;     // the step is one persistent launch (rows <= 2), else six kernels a layer
     Owned stage_x, stage_words, stage_out;  // pinned host staging
     Program prog;
     std::vector<Launch> launches;
@@ -172,6 +174,36 @@ static void push(std::vector<Launch> &v, uint32_t kernel, const tg_params &p, co
 // o_proj (+ residual), gate_up (+ norm, SiLU), down_proj (+ residual); then the final norm.
 static void decode_launches(tg_decoder &d) {
     const tg_params base = d.params();
+    if (d.persistent) {
+        Launch l;
+        l.kernel = KERNEL_DECODE_STEP;
+        l.p = base;
+        l.label = "decode_step";
+        DecodeStep &st = l.step;
+        st.p = base;
+        st.layers = (int)d.shape.layers;
+        st.weights = reinterpret_cast<const unsigned char *>(d.weights.ptr());
+        st.offs = reinterpret_cast<const uint64_t *>(d.offs.ptr());
+        st.final_norm = d.final_norm;
+        st.cosv = reinterpret_cast<const float *>(d.cos.ptr());
+        st.sinv = reinterpret_cast<const float *>(d.sin.ptr());
+        st.at = reinterpret_cast<const uint32_t *>(d.words.ptr());
+        st.x_in = reinterpret_cast<const float *>(d.x_in.ptr());
+        st.h = reinterpret_cast<float *>(d.h.ptr());
+        st.mid = reinterpret_cast<float *>(d.mid.ptr());
+        st.mlp = reinterpret_cast<float *>(d.mlp.ptr());
+        st.q = reinterpret_cast<float *>(d.q.ptr());
+        st.out = reinterpret_cast<float *>(d.out.ptr());
+        st.po = reinterpret_cast<float *>(d.po.ptr());
+        st.pml = reinterpret_cast<float *>(d.pml.ptr());
+        st.kcache = reinterpret_cast<unsigned char *>(d.kcache.ptr());
+        st.vcache = reinterpret_cast<unsigned char *>(d.vcache.ptr());
+        st.cache_layer = d.cache_layer;
+        st.sync = reinterpret_cast<uint32_t *>(d.psync.ptr());
+        st.err = d.ctx->err_dev;
+        d.launches.assign(1, l);
+        return;
+    }
     const uint64_t T = d.esize, F = 4, R = d.rows;
     const tg_shape &s = d.shape;
     const uint64_t H = s.hidden, I = s.inner, hd = s.head_dim, heads = s.heads;
@@ -210,6 +242,8 @@ static void decode_launches(tg_decoder &d) {
     push(d.launches, TG_KERNEL_RMSNORM, base, "final_norm",
          {{d.h.ptr(), R * H * F}, {d.w(d.final_norm), H * F}, {d.out.ptr(), R * H * F}});
 }
+
+static int record_step(tg_decoder &d, bool persistent);
 
 extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, uint32_t slots, tg_dtype dtype,
                                  int timed, tg_decoder **out) {
@@ -269,18 +303,58 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(d->q.alloc(ctx, R * d->attn() * F));
     TG_TRY(d->att.alloc(ctx, R * d->attn() * F));
     TG_TRY(d->mlp.alloc(ctx, R * I * F));
+    TG_TRY(d->words.alloc(ctx, 2 * R * 4));
     TG_TRY(d->po.alloc(ctx, R * s->heads * chunks * s->head_dim * F));
     TG_TRY(d->pml.alloc(ctx, R * s->heads * chunks * 2 * F));
-    TG_TRY(d->words.alloc(ctx, 2 * R * 4));
+    TG_TRY(d->psync.alloc(ctx, 256));
+    {
+        std::vector<uint64_t> offs;
+        for (const LayerOffsets &o : d->layer) {
+            for (uint64_t v : {o.qkv, o.o, o.gate_up, o.down, o.in_norm, o.post_norm}) offs.push_back(v);
+        }
+        TG_TRY(d->offs.alloc(ctx, offs.size() * 8));
+        TG_TRY(tg_mem_write(d->offs.m, 0, offs.data(), offs.size() * 8));
+    }
     TG_TRY(d->stage_x.alloc(ctx, R * H * F, TG_RES_UPLOAD));
     TG_TRY(d->stage_words.alloc(ctx, 2 * R * 4, TG_RES_UPLOAD));
     TG_TRY(d->stage_out.alloc(ctx, R * H * F, TG_RES_READBACK));
     TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
-    decode_launches(*d);
-    TG_TRY(program_build(ctx, d->launches, d->timed, d->prog));
+    // Six kernels a layer by default: at batch 1 on B200 they take ~690 us a step against the
+    // persistent launch's ~970 us (tg_decoder_retune selects either).
+    TG_TRY(record_step(*d, false));
     *out = d.release();
     return TG_OK;
 }
+
+// Records the step as one persistent launch or as six kernels a layer. A persistent recording the
+// device or shape does not take falls back to the kernels (the same results bit for bit).
+static int record_step(tg_decoder &d, bool persistent) {
+    if (d.prog.pending) TG_TRY(program_wait(d.prog, 0));
+    program_release(d.prog);
+    d.prog = Program();
+    d.persistent = persistent;
+    decode_launches(d);
+    int st = program_build(d.ctx, d.launches, d.timed, d.prog);
+    if (st != TG_OK && persistent) {
+        program_release(d.prog);
+        d.prog = Program();
+        d.persistent = false;
+        decode_launches(d);
+        st = program_build(d.ctx, d.launches, d.timed, d.prog);
+    }
+    return st;
+}
+
+extern "C" int tg_decoder_retune(tg_decoder *d, int persistent, int timed) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    d->timed = timed != 0;
+    TG_TRY(record_step(*d, persistent != 0));
+    if (persistent && !d->persistent) return fail(TG_ESHAPE, "this decoder's batch or shape has no persistent step");
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_persistent(const tg_decoder *d) { return d && d->persistent ? 1 : 0; }
 
 extern "C" int tg_decoder_destroy(tg_decoder *d) {
     if (!d) return TG_OK;

@@ -128,6 +128,10 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
                    {"c", (uint64_t)p.m * p.n * F}};
             break;
+        case TG_KERNEL_ATTENTION_DECODE:
+            out = {{"q", rows * attn * F}, {"k_cache", cache}, {"v_cache", cache}, {"at", words},
+                   {"out", rows * attn * F}};
+            break;
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
@@ -138,7 +142,7 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm"};
+        "silu_mul_rows", "gemm", "attention_decode"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
 }
 
@@ -169,6 +173,7 @@ static int check_shape(const Launch &l) {
             break;
         case TG_KERNEL_ATTENTION_SPLIT:
         case TG_KERNEL_ATTENTION_COMBINE:
+        case TG_KERNEL_ATTENTION_DECODE:
         case TG_KERNEL_ROPE_ROWS:
         case TG_KERNEL_ATTENTION_ROWS:
             if (!heads_ok()) return fail(TG_ESHAPE, "%s: %u heads over %u of %u, capacity %u (multiple of %u)", kernel_name(l.kernel), p.heads, p.kv_heads, p.head_dim, p.capacity, ATTN_CHUNK);
@@ -194,6 +199,7 @@ static int check_shape(const Launch &l) {
 }
 
 int check_launch(const Launch &l) {
+    if (l.kernel == KERNEL_DECODE_STEP) return TG_OK;  // recorded by the decoder over its own buffers
     int st = check_shape(l);
     if (st) return st;
     std::vector<Need> need;
@@ -220,11 +226,11 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
     cudaError_t e = cudaSuccess;
     switch (l.kernel) {
         case TG_KERNEL_RMSNORM: e = launch_rmsnorm(p, F(0), F(1), F(2), s); break;
-        case TG_KERNEL_GEMV_QKV_ROPE: e = launch_gemv_qkv_rope(p, F(0), F(1), b[2], F(3), F(4), U(5), b[6], b[7], b[8], s); break;
+        case TG_KERNEL_GEMV_QKV_ROPE: e = launch_gemv_qkv_rope(p, F(0), F(1), b[2], F(3), F(4), U(5), b[6], b[7], b[8], err, s); break;
         case TG_KERNEL_ATTENTION_SPLIT: e = launch_attention_split(p, b[0], b[1], b[2], U(3), F(4), F(5), s); break;
         case TG_KERNEL_ATTENTION_COMBINE: e = launch_attention_combine(p, U(0), F(1), F(2), b[3], s); break;
-        case TG_KERNEL_GEMV_RESIDUAL: e = launch_gemv_residual(p, b[0], b[1], F(2), F(3), s); break;
-        case TG_KERNEL_GEMV_GATE_UP: e = launch_gemv_gate_up(p, F(0), F(1), b[2], b[3], s); break;
+        case TG_KERNEL_GEMV_RESIDUAL: e = launch_gemv_residual(p, b[0], b[1], F(2), F(3), err, s); break;
+        case TG_KERNEL_GEMV_GATE_UP: e = launch_gemv_gate_up(p, F(0), F(1), b[2], b[3], err, s); break;
         case TG_KERNEL_STREAM_READ: e = launch_stream_read(p, U(0), U(1), s, sm_count); break;
         case TG_KERNEL_NORM_ROWS: e = launch_norm_rows(p, U(0), F(1), F(2), b[3], s); break;
         case TG_KERNEL_ADD_NORM_ROWS: e = launch_add_norm_rows(p, U(0), F(1), F(2), F(3), F(4), b[5], s); break;
@@ -232,9 +238,14 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case TG_KERNEL_ATTENTION_ROWS: e = launch_attention_rows(p, U(0), b[1], b[2], b[3], b[4], s); break;
         case TG_KERNEL_SILU_MUL_ROWS: e = launch_silu_mul_rows(p, U(0), F(1), b[2], s); break;
         case TG_KERNEL_GEMM: e = launch_gemm(p, b[0], b[1], F(2), err, s); break;
+        case TG_KERNEL_ATTENTION_DECODE: e = launch_attention_decode(p, b[0], b[1], b[2], U(3), b[4], s); break;
+        case KERNEL_DECODE_STEP: e = launch_decode_step(l.step, sm_count, s); break;
         default: return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
-    if (e != cudaSuccess) return fail(TG_ECUDA, "launching %s (%s): %s", kernel_name(l.kernel), l.label.c_str(), cudaGetErrorString(e));
+    if (e != cudaSuccess)
+        return fail(e == cudaErrorNotSupported ? TG_ESHAPE : TG_ECUDA, "launching %s (%s): %s",
+                    l.kernel == KERNEL_DECODE_STEP ? "decode_step" : kernel_name(l.kernel), l.label.c_str(),
+                    cudaGetErrorString(e));
     return TG_OK;
 }
 
@@ -415,7 +426,11 @@ extern "C" int tg_mem_alloc(tg_ctx *ctx, uint64_t bytes, tg_residence residence,
     cudaError_t e;
     if (residence == TG_RES_DEVICE) {
         e = cudaMalloc(&m->ptr, bytes);
-        if (e == cudaSuccess) e = cudaMemset(m->ptr, 0, bytes);
+        // Zeroed on the context's stream, which every later copy and launch of the context uses:
+        // the stream does not wait for the legacy default stream, so a cudaMemset there could
+        // land after a write that follows it.
+        if (e == cudaSuccess) e = cudaMemsetAsync(m->ptr, 0, bytes, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     } else if (residence == TG_RES_UPLOAD || residence == TG_RES_READBACK) {
         e = cudaHostAlloc(&m->host, bytes, cudaHostAllocMapped);
         if (e == cudaSuccess) e = cudaHostGetDevicePointer(&m->ptr, m->host, 0);

@@ -129,4 +129,70 @@ TG_DEVICE bool placed(const uint32_t *at, int rows, int b, uint32_t capacity, ui
     return pos < capacity && slot < slots;
 }
 
+// ---- mbarriers, bulk copies, programmatic dependent launch (sm_90+) ------------------------------
+
+TG_DEVICE uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+TG_DEVICE uint64_t globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+TG_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+TG_DEVICE void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+TG_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+TG_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Waits for the phase of parity `parity` of `bar` to complete, for at most `limit_ns`. Past that it
+// records ERR_WAIT_TIMEOUT in `err` and returns false, so that the kernel always ends.
+TG_DEVICE bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint32_t *err, uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer() - t0 > limit_ns) {
+            if (err) atomicExch(err, ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// A 1-D bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global to
+// this block's shared memory, completing on mbarrier `bar` (no multicast).
+TG_DEVICE void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+// Programmatic dependent launch: a kernel lets the next one start as soon as all of its blocks
+// are running (launch_dependents), and waits for the one before it to finish and its writes to
+// land (wait) only where it first reads what that one wrote. Every block waits before it ends,
+// so that a kernel never finishes ahead of the one before it. Both are no-ops in a launch
+// without the programmatic attribute.
+TG_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+TG_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace tg

@@ -46,6 +46,25 @@ void clear_error();
         if (e_ != cudaSuccess) return ::tg::cuda_fail(e_, #call); \
     } while (0)
 
+// The persistent decode step: everything it reads and writes (a decoder's buffers).
+struct DecodeStep {
+    tg_params p;
+    int layers;
+    const unsigned char *weights;
+    const uint64_t *offs;  // device [layers][6]: qkv, o, gate_up, down, input norm, post norm
+    uint64_t final_norm;
+    const float *cosv, *sinv;
+    const uint32_t *at;
+    const float *x_in;
+    float *h, *mid, *mlp, *q, *out, *po, *pml;
+    unsigned char *kcache, *vcache;
+    uint64_t cache_layer;
+    uint32_t *sync;  // 8 bytes, zeroed by the launch
+    uint32_t *err;
+};
+// Kernel ids past the table's, for launches the library records itself.
+constexpr uint32_t KERNEL_DECODE_STEP = 1000;  // the persistent decode step (DecodeStep)
+
 // One dispatch resolved to device pointers, as the kernel table launches it.
 struct Launch {
     uint32_t kernel = 0;
@@ -53,6 +72,7 @@ struct Launch {
     std::vector<void *> ptr;
     std::vector<uint64_t> bytes;
     std::string label;
+    DecodeStep step{};  // KERNEL_DECODE_STEP only
 };
 
 // The kernel table: checks a dispatch's params against its bindings' sizes (what each binding
@@ -90,16 +110,20 @@ cudaError_t launch_rmsnorm(const tg_params &p, const float *x, const float *g, f
                            cudaStream_t s);
 cudaError_t launch_gemv_qkv_rope(const tg_params &p, const float *x, const float *g,
                                  const void *w, const float *cos, const float *sin,
-                                 const uint32_t *at, void *q, void *kc, void *vc, cudaStream_t s);
+                                 const uint32_t *at, void *q, void *kc, void *vc, uint32_t *err,
+                                 cudaStream_t s);
 cudaError_t launch_attention_split(const tg_params &p, const void *q, const void *kc,
                                    const void *vc, const uint32_t *at, float *po, float *pml,
                                    cudaStream_t s);
 cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, const float *po,
                                      const float *pml, void *out, cudaStream_t s);
 cudaError_t launch_gemv_residual(const tg_params &p, const void *x, const void *w,
-                                 const float *res, float *out, cudaStream_t s);
+                                 const float *res, float *out, uint32_t *err, cudaStream_t s);
 cudaError_t launch_gemv_gate_up(const tg_params &p, const float *x, const float *g,
-                                const void *w, void *out, cudaStream_t s);
+                                const void *w, void *out, uint32_t *err, cudaStream_t s);
+// Split and combine in one kernel: a thread-block cluster per (row, kv head).
+cudaError_t launch_attention_decode(const tg_params &p, const void *q, const void *kc, const void *vc,
+                                    const uint32_t *at, void *out, cudaStream_t s);
 cudaError_t launch_stream_read(const tg_params &p, const uint32_t *data, uint32_t *out,
                                cudaStream_t s, int sm_count);
 cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
@@ -118,6 +142,9 @@ cudaError_t launch_silu_mul_rows(const tg_params &p, const uint32_t *at, const f
 // f32 operands on a SIMT kernel. Returns cudaErrorInvalidValue for shapes it does not tile.
 cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c,
                         uint32_t *err, cudaStream_t s);
+// One cooperative launch for the whole step (batches of up to 2 rows); cudaErrorNotSupported when
+// the shape or batch is not one it takes.
+cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s);
 // The decode constants: positions per attention chunk.
 constexpr uint32_t ATTN_CHUNK = 64;
 // The rows of a prefill attention tile; each run starts on a multiple of it.
