@@ -110,8 +110,8 @@ typedef enum {
     TG_KERNEL_ATTENTION_COMBINE = 3,
     /* x f32 [rows][k], W T [n][k], residual f32 [rows][n] -> out f32 [rows][n] gemv_residual.comp */
     TG_KERNEL_GEMV_RESIDUAL = 4,
-    /* x f32 [rows][hidden], gain f32, W T [2 inner][hidden] -> out f32 [rows][inner]
-     *                                                                            gemv_gate_up.comp */
+    /* x f32 [rows][hidden], gain f32, W T [2 inner][hidden] (gate and up rows interleaved as for
+     * TG_KERNEL_GEMM_SILU) -> out f32 [rows][inner]                             gemv_gate_up.comp */
     TG_KERNEL_GEMV_GATE_UP = 5,
     /* data u32 -> out u32 (one word per block)                                  stream_read.comp */
     TG_KERNEL_STREAM_READ = 6,
@@ -125,7 +125,8 @@ typedef enum {
     TG_KERNEL_ROPE_ROWS = 9,
     /* at u32, q T [rows][heads][hd], k cache T, v cache T -> out T           attention_rows.comp */
     TG_KERNEL_ATTENTION_ROWS = 10,
-    /* at u32, c f32 [rows][2 inner] -> out T [rows][inner]                     silu_mul_rows.comp */
+    /* at u32, c f32 [rows][2 inner] (columns in gate_up's interleaved order) -> out T [rows][inner]
+     *                                                                           silu_mul_rows.comp */
     TG_KERNEL_SILU_MUL_ROWS = 11,
     /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32) */
     TG_KERNEL_GEMM = 12,
@@ -133,7 +134,11 @@ typedef enum {
      * ATTENTION_COMBINE in one dispatch, a thread-block cluster per (row, kv head) whose blocks
      * keep their chunks' partials in shared memory; the same results bit for bit */
     TG_KERNEL_ATTENTION_DECODE = 13,
-    TG_KERNEL_COUNT = 14
+    /* a bf16 [m][k], b bf16 [2 inner][k] with gate and up rows interleaved in blocks of 128
+     * (gate rows i..i+127, then up rows i..i+127, i = 0, 128, ...) -> out bf16 [m][inner] =
+     * SiLU(gate) up of a b^T, in the tcgen05 GEMM's epilogue     gemm.mlir + silu_mul_rows.comp */
+    TG_KERNEL_GEMM_SILU = 14,
+    TG_KERNEL_COUNT = 15
 } tg_kernel_id;
 
 /* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the

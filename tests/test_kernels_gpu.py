@@ -130,3 +130,41 @@ def test_fused_decode_attention_equals_split_and_combine(pkg, ctx, syn, dtype):
         e = np.exp(s - s.max())
         want = (e / e.sum()) @ vf[2, h // 8, :65].astype(np.float64)
         assert np.max(np.abs(got[2, h] - want)) < 1e-5
+
+
+@pytest.mark.parametrize("m,inner,k", [(200, 256, 256), (512, 4096, 1024)])
+def test_gemm_silu_epilogue_equals_gemm_then_silu_mul_rows(pkg, ctx, syn, m, inner, k):
+    """The fused epilogue takes SiLU(gate) up of the same f32 accumulators the plain GEMM stores, so
+    it matches gemm + silu_mul_rows bit for bit; gate and up rows are interleaved in blocks of 128."""
+    rng = np.random.default_rng(m + inner)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    gate = rng.standard_normal((inner, k), dtype=np.float32) * 0.05
+    up = rng.standard_normal((inner, k), dtype=np.float32) * 0.05
+    w = np.concatenate([np.concatenate([gate[i:i + 128], up[i:i + 128]]) for i in range(0, inner, 128)])
+    ab, wb = syn.bf16_bits(a), syn.bf16_bits(w)
+    ma, mw = _mem(pkg, ctx, ab), _mem(pkg, ctx, wb)
+    shape = pkg.Shape(hidden=256, inner=inner, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "bf16", rows=m, m=m, n=2 * inner, k=k)
+    fused = pkg.Memory(ctx, m * inner * 2)
+    pkg.dispatch_once(ctx, "gemm_silu", p, [(ma, 0, ab.nbytes), (mw, 0, wb.nbytes), (fused, 0, m * inner * 2)])
+    c = pkg.Memory(ctx, m * 2 * inner * 4)
+    pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, ab.nbytes), (mw, 0, wb.nbytes), (c, 0, m * 2 * inner * 4)])
+    words = _mem(pkg, ctx, np.zeros(m, np.uint32))
+    split = pkg.Memory(ctx, m * inner * 2)
+    pkg.dispatch_once(ctx, "silu_mul_rows", p, [(words, 0, m * 4), (c, 0, m * 2 * inner * 4),
+                                                (split, 0, m * inner * 2)])
+    got = fused.read(np.uint16, m * inner).reshape(m, inner)
+    np.testing.assert_array_equal(got, split.read(np.uint16, m * inner).reshape(m, inner))
+    af = syn.bf16_to_f32(ab).astype(np.float64)
+    g64 = af @ syn.bf16_to_f32(syn.bf16_bits(gate)).astype(np.float64).T
+    u64 = af @ syn.bf16_to_f32(syn.bf16_bits(up)).astype(np.float64).T
+    want = g64 / (1.0 + np.exp(-g64)) * u64
+    assert distance(syn.bf16_to_f32(got), want)[1] < 1e-2
+
+
+def test_gemm_silu_refuses_a_width_it_does_not_tile(pkg, ctx):
+    shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "bf16", rows=128, m=128, n=384, k=64)
+    a, b, out = pkg.Memory(ctx, 128 * 64 * 2), pkg.Memory(ctx, 384 * 64 * 2), pkg.Memory(ctx, 128 * 192 * 2)
+    with pytest.raises(pkg.ShapeError):
+        pkg.dispatch_once(ctx, "gemm_silu", p, [(a, 0, a.nbytes), (b, 0, b.nbytes), (out, 0, out.nbytes)])

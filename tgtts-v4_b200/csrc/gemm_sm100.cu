@@ -144,10 +144,14 @@ struct TcLayout {
     static constexpr int SMEM = BARRIERS + 256 + 1024;  // + barriers + alignment slack
 };
 
-template <int BN>
+// Epilogues: C in f32, or (BN = 256, B's rows in gate_up_row's order) SiLU(gate) up in bf16, the
+// tile's columns 0..127 the gate and 128..255 the up of the same 128 outputs.
+enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1 };
+
+template <int BN, int EPI = TC_EPI_F32>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   float *__restrict__ C, int M, int N, int K, uint32_t *err) {
+                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err) {
     using L = TcLayout<BN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -225,14 +229,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     const int row = m0 + warp * 32 + lane;
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    if constexpr (EPI == TC_EPI_SILU) {
+        static_assert(BN == 256, "the SiLU epilogue pairs columns c and c + 128 of a 256-wide tile");
+        bf16 *out = static_cast<bf16 *>(Cout);
+        const int inner = N / 2;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(lane_base + c0, v);
-        if (row < M && n0 + c0 < N) {
-            float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+        for (int c0 = 0; c0 < 128; c0 += 16) {
+            float g[16], u[16];
+            tmem_ld16(lane_base + c0, g);
+            tmem_ld16(lane_base + 128 + c0, u);
+            if (row < M) {
+                uint32_t packed[8];
 #pragma unroll
-            for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                for (int i = 0; i < 8; i++) {
+                    const __nv_bfloat162 v = __floats2bfloat162_rn(silu_mul(g[2 * i], u[2 * i]), silu_mul(g[2 * i + 1], u[2 * i + 1]));
+                    packed[i] = *reinterpret_cast<const uint32_t *>(&v);
+                }
+                uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)row * inner + n0 / 2 + c0);
+                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            }
+        }
+    } else {
+        float *C = static_cast<float *>(Cout);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(lane_base + c0, v);
+            if (row < M && n0 + c0 < N) {
+                float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+#pragma unroll
+                for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            }
         }
     }
     tc_fence_before();
@@ -277,13 +305,13 @@ static bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int BN>
-static cudaError_t launch_tc(const void *a, const void *b, float *c, int M, int N, int K, uint32_t *err,
+template <int BN, int EPI = TC_EPI_F32>
+static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
                              cudaStream_t s) {
     CUtensorMap ma, mb;
     if (!make_map(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map(&mb, b, (uint64_t)N, (uint64_t)K, BN))
         return cudaErrorInvalidValue;
-    auto kern = gemm_tc_kernel<BN>;
+    auto kern = gemm_tc_kernel<BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<BN>::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid(N / BN, (M + TC_BM - 1) / TC_BM);
@@ -305,6 +333,13 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
     if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s);
     if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s);
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,
+                             cudaStream_t s) {
+    const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
+    if (p.dtype != TG_BF16 || M <= 0 || N % 256 || K % TC_BK) return cudaErrorInvalidValue;
+    return launch_tc<256, TC_EPI_SILU>(a, b, out, M, N, K, err, s);
 }
 
 }  // namespace tg

@@ -155,7 +155,7 @@ TG_DEVICE int unit_row(const tg_params &p, int u, int r) {
         const int half = p.head_dim / 2;
         return (u / half) * p.head_dim + u % half + r * half;
     } else if constexpr (EPI == EPI_GATE_UP) {
-        return u + r * (int)p.inner;
+        return (int)gate_up_row((uint32_t)u, (uint32_t)r);
     } else {
         return u;
     }

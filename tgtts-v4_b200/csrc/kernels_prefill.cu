@@ -107,18 +107,22 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// silu_mul_rows.comp:16-27: out = SiLU(gate) up from the f32 gate/up projection, gate first.
+// silu_mul_rows.comp:16-27: out = SiLU(gate) up from the f32 gate/up projection, whose columns
+// follow gate_up's rows (gate_up_row). A block to a row, four columns a thread.
 template <typename T>
 __global__ void __launch_bounds__(256)
     silu_mul_rows_kernel(tg_params p, const uint32_t *__restrict__ at, const float *__restrict__ c,
                          T *__restrict__ out) {
-    const int inner = p.inner;
-    const size_t total = (size_t)p.rows * inner;
-    for (size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-         idx += (size_t)gridDim.x * blockDim.x) {
-        const size_t row = idx / inner, i = idx % inner;
-        const float *cr = c + row * 2 * inner;
-        out[idx] = from_f32<T>(silu_mul(cr[i], cr[inner + i]));
+    const int inner = p.inner, row = blockIdx.x;
+    const float *cr = c + (size_t)row * 2 * inner;
+    for (int i = 4 * threadIdx.x; i < inner; i += 4 * blockDim.x) {
+        const float4 g = *reinterpret_cast<const float4 *>(cr + gate_up_row(i, 0));
+        const float4 u = *reinterpret_cast<const float4 *>(cr + gate_up_row(i, 1));
+        T *o = out + (size_t)row * inner + i;
+        o[0] = from_f32<T>(silu_mul(g.x, u.x));
+        o[1] = from_f32<T>(silu_mul(g.y, u.y));
+        o[2] = from_f32<T>(silu_mul(g.z, u.z));
+        o[3] = from_f32<T>(silu_mul(g.w, u.w));
     }
 }
 
@@ -236,6 +240,227 @@ __global__ void __launch_bounds__(256)
     }
 }
 
+// attention_rows.comp on tensor cores, for bf16: flash attention with mma.sync m16n8k16 (bf16 in,
+// f32 accumulate). Block (t, h) takes the PREFILL_TILE rows from t PREFILL_TILE for query head h,
+// a warp to 16 rows; the keys and values of the rows' slot stream through shared memory in tiles
+// of 64 positions (cp.async, two buffers), up to the last of the rows' positions. Per tile: S =
+// Q K^T by 32 MMAs a warp, scaled and masked past each row's position, an online softmax in
+// registers, then O += P V by 32 MMAs, P taken from S's accumulators as bf16 A fragments. Keys
+// past the tile's last position are read as zero.
+namespace fa {
+
+constexpr int KT = 64;  // keys per tile
+constexpr int PAD = 8;  // bf16 elements of padding per shared row (ldmatrix without bank conflicts)
+
+TG_DEVICE void cp_async16(void *smem, const void *gmem, bool valid) {
+    const uint32_t dst = smem_u32(smem);
+    const int bytes = valid ? 16 : 0;  // zero-fill when invalid
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(gmem), "r"(bytes) : "memory");
+}
+TG_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+TG_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+TG_DEVICE void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+TG_DEVICE void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+TG_DEVICE void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+TG_DEVICE uint32_t pack_bf16(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+}  // namespace fa
+
+template <int HD>
+__global__ void __launch_bounds__(128)
+    attention_rows_mma_kernel(tg_params p, const uint32_t *__restrict__ at, const bf16 *__restrict__ q,
+                              const bf16 *__restrict__ kc, const bf16 *__restrict__ vc, bf16 *__restrict__ out) {
+    using namespace fa;
+    constexpr int ROW = HD + PAD;  // shared row stride in bf16
+    constexpr int KS = HD / 16;    // k-steps over the head dimension
+    constexpr int NT = HD / 8;     // n-tiles of the output
+    extern __shared__ __align__(128) unsigned char fa_smem[];
+    bf16 *qs = reinterpret_cast<bf16 *>(fa_smem);  // [PREFILL_TILE][ROW]
+    bf16 *ks[2] = {qs + PREFILL_TILE * ROW, qs + PREFILL_TILE * ROW + KT * ROW};  // [KT][ROW] each
+    bf16 *vs[2] = {qs + PREFILL_TILE * ROW + 2 * KT * ROW, qs + PREFILL_TILE * ROW + 3 * KT * ROW};
+    __shared__ uint32_t tile_last, tile_slot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, t4 = lane & 3;
+    const int r0 = blockIdx.x * PREFILL_TILE;
+    const int head = blockIdx.y, heads = p.heads, kvh = p.kv_heads, kv = head / (heads / kvh);
+    if (tid == 0) {
+        tile_last = 0;
+        tile_slot = 0xffffffffu;
+    }
+    __syncthreads();
+    if (tid < PREFILL_TILE && r0 + tid < (int)p.rows) {
+        uint32_t pos, slot;
+        if (placed(at, p.rows, r0 + tid, p.capacity, p.slots, pos, slot)) {
+            atomicMax(&tile_last, pos);
+            atomicMin(&tile_slot, slot);
+        }
+    }
+    __syncthreads();
+    if (tile_slot == 0xffffffffu) return;  // every row of the tile is padding
+    const uint32_t last = tile_last;
+    const size_t cache = ((size_t)tile_slot * kvh + kv) * p.capacity;
+    // This thread's two rows (g and g + 8 of its warp's 16) and their positions (-1: padding).
+    int qpos[2];
+    for (int i = 0; i < 2; i++) {
+        const int row = r0 + warp * 16 + g + 8 * i;
+        uint32_t pos, slot;
+        qpos[i] = (row < (int)p.rows && placed(at, p.rows, row, p.capacity, p.slots, pos, slot)) ? (int)pos : -1;
+    }
+    // Q tile into shared memory (rows past the run read as zero), then A fragments.
+    for (int i = tid; i < PREFILL_TILE * HD / 8; i += blockDim.x) {
+        const int r = i / (HD / 8), c = i % (HD / 8);
+        const bool ok = r0 + r < (int)p.rows;
+        cp_async16(qs + r * ROW + c * 8, q + ((size_t)(ok ? r0 + r : r0) * heads + head) * HD + c * 8, ok);
+    }
+    auto load_kv = [&](int kt, int buf) {
+        for (int i = tid; i < KT * HD / 8; i += blockDim.x) {
+            const int r = i / (HD / 8), c = i % (HD / 8);
+            const uint32_t key = kt * KT + r;
+            const bool ok = key <= last;
+            const size_t off = (cache + (ok ? key : 0)) * HD + c * 8;
+            cp_async16(ks[buf] + r * ROW + c * 8, kc + off, ok);
+            cp_async16(vs[buf] + r * ROW + c * 8, vc + off, ok);
+        }
+    };
+    load_kv(0, 0);
+    cp_async_commit();
+    const int ntiles = (int)(last / KT) + 1;
+    uint32_t qa[KS][4];
+    float o[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
+    const float scale = 1.0f / sqrtf((float)HD);
+    for (int kt = 0; kt < ntiles; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < ntiles) load_kv(kt + 1, buf ^ 1);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();
+        if (kt == 0) {
+#pragma unroll
+            for (int s = 0; s < KS; s++) {
+                const int mi = lane >> 3, rr = lane & 7;
+                ldmatrix_x4(qa[s], qs + (warp * 16 + (mi & 1) * 8 + rr) * ROW + s * 16 + (mi >> 1) * 8);
+            }
+        }
+        // S = Q K^T: 8 n-tiles of 8 keys.
+        float sc[KT / 8][4];
+#pragma unroll
+        for (int j = 0; j < KT / 8; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+        for (int s = 0; s < KS; s++) {
+#pragma unroll
+            for (int j = 0; j < KT / 8; j += 2) {
+                // Two n-tiles (keys 8j .. 8j + 15) by one ldmatrix.x4: matrices (keys 8j.., hd 16s),
+                // (keys 8j.., hd 16s + 8), (keys 8j + 8.., hd 16s), (keys 8j + 8.., hd 16s + 8).
+                uint32_t b[4];
+                const int mi = lane >> 3, rr = lane & 7;
+                ldmatrix_x4(b, ks[buf] + (8 * j + (mi >> 1) * 8 + rr) * ROW + s * 16 + (mi & 1) * 8);
+                mma_bf16(sc[j], qa[s], b[0], b[1]);
+                mma_bf16(sc[j + 1], qa[s], b[2], b[3]);
+            }
+        }
+        // Scale, mask past each row's position, online softmax.
+        float tmax[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < KT / 8; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int key = kt * KT + 8 * j + 2 * t4 + (e & 1);
+                const int i = e >> 1;
+                const float v = key <= qpos[i] ? sc[j][e] * scale : -INFINITY;
+                sc[j][e] = v;
+                tmax[i] = fmaxf(tmax[i], v);
+            }
+        float corr[2];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            tmax[i] = fmaxf(tmax[i], __shfl_xor_sync(0xffffffffu, tmax[i], 1));
+            tmax[i] = fmaxf(tmax[i], __shfl_xor_sync(0xffffffffu, tmax[i], 2));
+            const float next = fmaxf(m[i], tmax[i]);
+            corr[i] = next == -INFINITY ? 1.0f : expf(m[i] - next);
+            m[i] = next;
+            l[i] *= corr[i];
+        }
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            o[j][0] *= corr[0];
+            o[j][1] *= corr[0];
+            o[j][2] *= corr[1];
+            o[j][3] *= corr[1];
+        }
+        float tsum[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < KT / 8; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int i = e >> 1;
+                const float pe = sc[j][e] == -INFINITY ? 0.0f : expf(sc[j][e] - m[i]);
+                sc[j][e] = pe;
+                tsum[i] += pe;
+            }
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            tsum[i] += __shfl_xor_sync(0xffffffffu, tsum[i], 1);
+            tsum[i] += __shfl_xor_sync(0xffffffffu, tsum[i], 2);
+            l[i] += tsum[i];
+        }
+        // O += P V: P's accumulators as A fragments (k-step s = keys 16s .. 16s + 15).
+#pragma unroll
+        for (int s = 0; s < KT / 16; s++) {
+            uint32_t pa[4];
+            pa[0] = pack_bf16(sc[2 * s][0], sc[2 * s][1]);
+            pa[1] = pack_bf16(sc[2 * s][2], sc[2 * s][3]);
+            pa[2] = pack_bf16(sc[2 * s + 1][0], sc[2 * s + 1][1]);
+            pa[3] = pack_bf16(sc[2 * s + 1][2], sc[2 * s + 1][3]);
+#pragma unroll
+            for (int j = 0; j < NT; j += 2) {
+                // V^T fragments by ldmatrix.trans: matrices (keys 16s.., hd 8j), (keys 16s + 8.., hd 8j),
+                // (keys 16s.., hd 8j + 8), (keys 16s + 8.., hd 8j + 8).
+                uint32_t b[4];
+                const int mi = lane >> 3, rr = lane & 7;
+                ldmatrix_x4_trans(b, vs[buf] + (16 * s + (mi & 1) * 8 + rr) * ROW + 8 * j + (mi >> 1) * 8);
+                mma_bf16(o[j], pa, b[0], b[1]);
+                mma_bf16(o[j + 1], pa, b[2], b[3]);
+            }
+        }
+        __syncthreads();
+    }
+    // Normalise and store the live rows, bf16.
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        if (qpos[i] < 0) continue;
+        const int row = r0 + warp * 16 + g + 8 * i;
+        const float inv = 1.0f / l[i];
+        bf16 *dst = out + ((size_t)row * heads + head) * HD;
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            const __nv_bfloat162 v = __floats2bfloat162_rn(o[j][2 * i] * inv, o[j][2 * i + 1] * inv);
+            *reinterpret_cast<__nv_bfloat162 *>(dst + 8 * j + 2 * t4) = v;
+        }
+    }
+}
+
 // ---- launchers -------------------------------------------------------------------------------
 
 cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
@@ -273,12 +498,11 @@ cudaError_t launch_rope_rows(const tg_params &p, const uint32_t *at, const float
 
 cudaError_t launch_silu_mul_rows(const tg_params &p, const uint32_t *at, const float *c,
                                  void *out, cudaStream_t s) {
-    const size_t total = (size_t)p.rows * p.inner;
-    const int blocks = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+    if (p.inner % 4) return cudaErrorInvalidValue;
     if (p.dtype == TG_BF16)
-        silu_mul_rows_kernel<bf16><<<blocks, 256, 0, s>>>(p, at, c, (bf16 *)out);
+        silu_mul_rows_kernel<bf16><<<p.rows, 256, 0, s>>>(p, at, c, (bf16 *)out);
     else
-        silu_mul_rows_kernel<float><<<blocks, 256, 0, s>>>(p, at, c, (float *)out);
+        silu_mul_rows_kernel<float><<<p.rows, 256, 0, s>>>(p, at, c, (float *)out);
     return cudaGetLastError();
 }
 
@@ -286,6 +510,19 @@ cudaError_t launch_attention_rows(const tg_params &p, const uint32_t *at, const 
                                   const void *kc, const void *vc, void *out, cudaStream_t s) {
     const dim3 grid((p.rows + PREFILL_TILE - 1) / PREFILL_TILE, p.heads);
     const int threads = PREFILL_TILE * 4;
+    if (p.dtype == TG_BF16) {
+        // Tensor cores for bf16.
+        auto run = [&](auto kern, int hd) {
+            const size_t smem = (size_t)(PREFILL_TILE + 4 * fa::KT) * (hd + fa::PAD) * sizeof(bf16);
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (e != cudaSuccess) return e;
+            kern<<<grid, 128, smem, s>>>(p, at, (const bf16 *)q, (const bf16 *)kc, (const bf16 *)vc, (bf16 *)out);
+            return cudaGetLastError();
+        };
+        if (p.head_dim == 64) return run(attention_rows_mma_kernel<64>, 64);
+        if (p.head_dim == 128) return run(attention_rows_mma_kernel<128>, 128);
+        return cudaErrorInvalidValue;
+    }
     if (p.head_dim == 64) {
         if (p.dtype == TG_BF16)
             attention_rows_kernel<bf16, 64><<<grid, threads, 0, s>>>(p, at, (const bf16 *)q, (const bf16 *)kc, (const bf16 *)vc, (bf16 *)out);

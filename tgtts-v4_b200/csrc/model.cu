@@ -145,6 +145,7 @@ static int check_shape(const tg_shape &s, tg_dtype dtype) {
                     s.heads * s.head_dim, vec);
     if (s.heads % s.kv_heads || (s.head_dim != 64 && s.head_dim != 128))
         return fail(TG_ESHAPE, "%u heads over %u of %u", s.heads, s.kv_heads, s.head_dim);
+    if (s.inner % GU_BLOCK) return fail(TG_ESHAPE, "inner %u is not a multiple of %u", s.inner, GU_BLOCK);
     if (s.capacity == 0 || s.capacity % ATTN_CHUNK)
         return fail(TG_ESHAPE, "a cache of %u positions (a multiple of %u)", s.capacity, ATTN_CHUNK);
     if (!(s.eps >= 0.0f) || !std::isfinite(s.residual_scale)) return fail(TG_ESHAPE, "eps %g, residual scale %g", s.eps, s.residual_scale);
@@ -436,13 +437,17 @@ extern "C" int tg_decoder_load(tg_decoder *d, const char *name, const void *src,
         TG_TRY(want(H * s.heads * hd));
         return write_values(d, o.o, src, count, src_dtype, false);
     }
-    if (r == "mlp.gate_proj.weight") {
+    if (r == "mlp.gate_proj.weight" || r == "mlp.up_proj.weight") {
         TG_TRY(want(I * H));
-        return write_values(d, o.gate_up, src, count, src_dtype, false);
-    }
-    if (r == "mlp.up_proj.weight") {
-        TG_TRY(want(I * H));
-        return write_values(d, o.gate_up + I * H * T, src, count, src_dtype, false);
+        // Interleaved in blocks of GU_BLOCK rows (gate_up_row).
+        const uint32_t up = r == "mlp.up_proj.weight" ? 1 : 0;
+        const uint64_t src_es = src_dtype == TG_BF16 ? 2 : 4;
+        for (uint32_t i = 0; i < I; i += GU_BLOCK) {
+            const uint64_t rows = std::min<uint64_t>(GU_BLOCK, I - i);
+            TG_TRY(write_values(d, o.gate_up + (uint64_t)gate_up_row(i, up) * H * T,
+                                static_cast<const char *>(src) + (uint64_t)i * H * src_es, rows * H, src_dtype, false));
+        }
+        return TG_OK;
     }
     if (r == "mlp.down_proj.weight") {
         TG_TRY(want(H * I));
@@ -650,9 +655,19 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
         push(v, TG_KERNEL_ADD_NORM_ROWS, base, "add_norm_rows",
              {{p.words.ptr(), words}, {p.proj.ptr(), R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
               {p.mid.ptr(), R * H * F}, {p.normed.ptr(), R * H * T}});
-        gemm("gate_up_proj", p.normed.ptr(), d.w(o.gate_up), p.gu.ptr(), 2 * I, H);
-        push(v, TG_KERNEL_SILU_MUL_ROWS, base, "silu_mul_rows",
-             {{p.words.ptr(), words}, {p.gu.ptr(), R * 2 * I * F}, {p.mlp.ptr(), R * I * T}});
+        if (d.dtype == TG_BF16) {
+            // SiLU-mul in the GEMM's epilogue: the f32 gate/up rows never reach memory.
+            tg_params g = base;
+            g.m = rows;
+            g.n = (uint32_t)(2 * I);
+            g.k = (uint32_t)H;
+            push(v, TG_KERNEL_GEMM_SILU, g, "gate_up_proj",
+                 {{p.normed.ptr(), R * H * T}, {d.w(o.gate_up), 2 * I * H * T}, {p.mlp.ptr(), R * I * T}});
+        } else {
+            gemm("gate_up_proj", p.normed.ptr(), d.w(o.gate_up), p.gu.ptr(), 2 * I, H);
+            push(v, TG_KERNEL_SILU_MUL_ROWS, base, "silu_mul_rows",
+                 {{p.words.ptr(), words}, {p.gu.ptr(), R * 2 * I * F}, {p.mlp.ptr(), R * I * T}});
+        }
         gemm("down_proj", p.mlp.ptr(), d.w(o.down), p.proj.ptr(), H, I);
         const bool last = l + 1 == s.layers;
         tg_params an = base;
@@ -686,7 +701,7 @@ extern "C" int tg_prefill_create(tg_decoder *d, uint32_t max_rows, int timed, tg
     TG_TRY(p->q.alloc(ctx, R * d->attn() * T));
     TG_TRY(p->att.alloc(ctx, R * d->attn() * T));
     TG_TRY(p->proj.alloc(ctx, R * H * F));
-    TG_TRY(p->gu.alloc(ctx, R * 2 * I * F));
+    if (d->dtype != TG_BF16) TG_TRY(p->gu.alloc(ctx, R * 2 * I * F));  // bf16 fuses SiLU into the GEMM
     TG_TRY(p->mlp.alloc(ctx, R * I * T));
     TG_TRY(p->out.alloc(ctx, R * H * F));
     TG_TRY(p->stage_x.alloc(ctx, R * H * F, TG_RES_UPLOAD));

@@ -132,6 +132,10 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"q", rows * attn * F}, {"k_cache", cache}, {"v_cache", cache}, {"at", words},
                    {"out", rows * attn * F}};
             break;
+        case TG_KERNEL_GEMM_SILU:
+            out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
+                   {"out", (uint64_t)p.m * (p.n / 2) * T}};
+            break;
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
@@ -142,7 +146,7 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm", "attention_decode"};
+        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
 }
 
@@ -184,6 +188,10 @@ static int check_shape(const Launch &l) {
         case TG_KERNEL_STREAM_READ:
             if (p.k % 4 || p.n < 1) return fail(TG_ESHAPE, "stream_read: %u words", p.k);
             break;
+        case TG_KERNEL_GEMM_SILU:
+            if (p.dtype != TG_BF16 || p.m == 0 || p.k % 64 || p.n == 0 || p.n % 256)
+                return fail(TG_ESHAPE, "gemm_silu %ux%ux%u: bf16 with n a multiple of 256 and k of 64", p.m, p.n, p.k);
+            break;
         case TG_KERNEL_GEMM:
             if (p.m == 0 || p.n == 0 || p.k == 0) return fail(TG_ESHAPE, "gemm %ux%ux%u", p.m, p.n, p.k);
             if (p.dtype == TG_BF16 && (p.k % 64 || p.n % 64))
@@ -192,7 +200,8 @@ static int check_shape(const Launch &l) {
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
-    if (l.kernel != TG_KERNEL_STREAM_READ && l.kernel != TG_KERNEL_GEMM && l.kernel != TG_KERNEL_GEMV_RESIDUAL && p.rows == 0)
+    if (l.kernel != TG_KERNEL_STREAM_READ && l.kernel != TG_KERNEL_GEMM && l.kernel != TG_KERNEL_GEMM_SILU &&
+        l.kernel != TG_KERNEL_GEMV_RESIDUAL && p.rows == 0)
         return fail(TG_ESHAPE, "%s: 0 rows", kernel_name(l.kernel));
     if (p.rows > 0 && p.slots == 0) return fail(TG_ESHAPE, "%s: 0 slots", kernel_name(l.kernel));
     return TG_OK;
@@ -238,6 +247,7 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case TG_KERNEL_ATTENTION_ROWS: e = launch_attention_rows(p, U(0), b[1], b[2], b[3], b[4], s); break;
         case TG_KERNEL_SILU_MUL_ROWS: e = launch_silu_mul_rows(p, U(0), F(1), b[2], s); break;
         case TG_KERNEL_GEMM: e = launch_gemm(p, b[0], b[1], F(2), err, s); break;
+        case TG_KERNEL_GEMM_SILU: e = launch_gemm_silu(p, b[0], b[1], b[2], err, s); break;
         case TG_KERNEL_ATTENTION_DECODE: e = launch_attention_decode(p, b[0], b[1], b[2], U(3), b[4], s); break;
         case KERNEL_DECODE_STEP: e = launch_decode_step(l.step, sm_count, s); break;
         default: return fail(TG_EINVAL, "no kernel %u", l.kernel);

@@ -149,5 +149,15 @@ cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s
 constexpr uint32_t ATTN_CHUNK = 64;
 // The rows of a prefill attention tile; each run starts on a multiple of it.
 constexpr uint32_t PREFILL_TILE = 64;
+// gate_up's rows are gate and up interleaved in blocks of GU_BLOCK: gate rows i .. i + 127 then up
+// rows i .. i + 127, for i = 0, 128, ... (so that a 256-wide GEMM tile holds matching gate and up
+// columns, and its epilogue can take SiLU(gate) up).
+constexpr uint32_t GU_BLOCK = 128;
+__host__ __device__ inline uint32_t gate_up_row(uint32_t i, uint32_t up) {
+    return (i / GU_BLOCK) * (2 * GU_BLOCK) + up * GU_BLOCK + i % GU_BLOCK;
+}
+// out[m][n / 2] = SiLU(gate) up of C = A B^T, B's rows in gate_up_row's order (bf16, n % 256 == 0).
+cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,
+                             cudaStream_t s);
 
 }  // namespace tg
