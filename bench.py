@@ -320,6 +320,99 @@ def side_measurements(pkg, syn, ctx, torch, tc_peak, peak_kind, weights):
                          "share": {k: round(v / sum(per.values()), 4) for k, v in sorted(per.items(), key=lambda kv: -kv[1])}}
     pre.close()
     dec.close()
+    out["decode_c3"] = continuous_c3(pkg, syn, ctx, torch, weights)
+    return out
+
+
+def continuous_c3(pkg, syn, ctx, torch, weights, steps=300, check=8, slots=64):
+    """Config 3: 64 requests under continuous batching (contexts uniform 64-2048, seed 2; each
+    finishes after uniform 32-512 steps and is replaced by a request with a fresh 128-position
+    prompt), `steps` decode steps with the refills' prefills between them, timed with CUDA events
+    on the runtime's stream (device time from the first step to the last, host gaps included). The
+    same schedule again with every step's outputs read to the host (e2e); then `check` requests that
+    ran start to finish are re-run alone through the same server and compared bit for bit."""
+    from tgtts_v4_b200 import serving
+
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=2560)
+    dec = pkg.Decoder(ctx, shape, rows=slots, slots=slots, dtype="bf16")
+    dec.load(weights)
+    pre = pkg.Prefill(dec, max_rows=8192)
+    server = pkg.Server(dec, pre)
+    stream = stream_ctx(ctx)
+
+    def run(read):
+        st = serving.ContinuousStream(cfg.hidden, slots=slots)
+        drv = serving.Driver(server, st.pool, slots)
+        first = st.initial()
+        drv.admit(first)
+        server.sync()
+        d0, p0 = drv.decoded, drv.prefilled
+        started = {r.id for r in first}
+        finished = []
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        e0.record(stream)
+        for _ in range(steps):
+            done = drv.step(read=read, keep=set() if not read else None)
+            finished += done
+            if done:
+                new = [st.replacement() for _ in done]
+                drv.admit(new)
+                started |= {r.id for r in new}
+        e1.record(stream)
+        e1.synchronize()
+        server.sync()
+        wall = time.perf_counter() - t0
+        return drv, e0.elapsed_time(e1), wall, drv.decoded - d0, drv.prefilled - p0, finished, st
+
+    def clear(drv):
+        for s in list(drv.owner):
+            server.finish(s)
+        drv.owner.clear()
+        drv.left.clear()
+
+    drv, ms, _, decoded, prefilled, finished, _ = run(False)
+    clear(drv)
+    # e2e: every step's outputs to the host; outputs kept for the invariance check.
+    st = serving.ContinuousStream(cfg.hidden, slots=slots)
+    drv2 = serving.Driver(server, st.pool, slots)
+    first = st.initial()
+    drv2.admit(first)
+    server.sync()
+    ids_full = []
+    t0 = time.perf_counter()
+    d0 = drv2.decoded
+    for _ in range(steps):
+        done = drv2.step(read=True, keep=None)
+        if done:
+            ids_full += done  # admitted before or inside the run: every step of it was read
+            drv2.admit([st.replacement() for _ in done])
+    wall = time.perf_counter() - t0
+    e2e_tokens = drv2.decoded - d0
+    clear(drv2)
+    rng = np.random.default_rng(7)
+    sample = [ids_full[i] for i in sorted(rng.choice(len(ids_full), min(check, len(ids_full)), replace=False))]
+    same = 0
+    for r in sample:
+        alone = serving.Driver(server, st.pool, slots)
+        alone.admit([r])
+        keep = {r.id}
+        for _ in range(r.steps):
+            alone.step(read=True, keep=keep)
+        same += int(all(np.array_equal(a, b) for a, b in zip(alone.outputs[r.id], drv2.outputs[r.id]))
+                    and len(alone.outputs[r.id]) == r.steps == len(drv2.outputs[r.id]))
+        clear(alone)
+    out = {"slots": slots, "steps": steps, "decode_tokens": decoded, "prefill_rows": prefilled,
+           "ms": round(ms, 3), "tokens_per_s": round(decoded / (ms / 1e3), 1),
+           "mean_rows_per_step": round(decoded / steps, 2),
+           "e2e_tokens_per_s": round(e2e_tokens / wall, 1),
+           "invariance": f"{same}/{len(sample)} requests re-run alone bit-identical at every step",
+           "schedule": "contexts U[64,2048] seed 2, lifetimes U[32,512], refills of 128 positions, "
+                       "prefills of refills inside the timed region"}
+    server.close()
+    pre.close()
+    dec.close()
     return out
 
 

@@ -218,7 +218,9 @@ int tg_batch_placement(uint32_t n_rows, uint32_t slots, const tg_row *rows, uint
                        uint32_t *words, uint32_t *n_words);
 
 /* Decoder::with_batch (decode.rs:790-806): the decode step of `s` for a batch of `rows` rows
- * in a cache of `slots` slots, recorded once, with zero weights until loaded. */
+ * in a cache of `slots` slots, recorded once, with zero weights until loaded. The step is recorded
+ * for each of the generator's row buckets (each power of two below `rows`, then `rows`,
+ * crates/graph/src/generator.rs:115-123) over the same buffers. */
 int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, uint32_t slots,
                       tg_dtype dtype, int timed, tg_decoder **out);
 int tg_decoder_destroy(tg_decoder *d);
@@ -234,6 +236,12 @@ int tg_decoder_load(tg_decoder *d, const char *name, const void *src, uint64_t c
 int tg_decoder_step_rows(tg_decoder *d, const tg_row *rows, const float *x, float *out);
 /* Decoder::set_rows / start / output (decode.rs:857-872), for callers that overlap host work. */
 int tg_decoder_set_rows(tg_decoder *d, const tg_row *rows, const float *x);
+/* A step of the first n (1 <= n <= rows) rows, run by the smallest row bucket that holds them (the
+ * bucket's other rows spare), as the generator runs the rows under way (generator.rs:306-330).
+ * x and out hold n rows. A row's result is the same bits whatever n and bucket it runs in. */
+int tg_decoder_set_rows_n(tg_decoder *d, uint32_t n, const tg_row *rows, const float *x);
+int tg_decoder_step_rows_n(tg_decoder *d, uint32_t n, const tg_row *rows, const float *x,
+                           float *out);
 int tg_decoder_start(tg_decoder *d);
 int tg_decoder_wait(tg_decoder *d, uint64_t timeout_ns);
 int tg_decoder_output(tg_decoder *d, float *out);
@@ -288,6 +296,40 @@ int tg_prefill_elapsed_ns(tg_prefill *p, double *ns);
 int tg_prefill_timings(tg_prefill *p, double *ns, size_t n, size_t *n_dispatches);
 int tg_prefill_dispatch_label(tg_prefill *p, size_t i, char *label, size_t label_bytes);
 uint32_t tg_prefill_max_rows(const tg_prefill *p);
+
+/* ---- Continuous batching (crates/graph/src/generator.rs:99-352) ---------------------------------
+ * Requests hold the decoder's slots; each step packs the requests under way into rows (in slot
+ * order) and runs the smallest row bucket that holds them; requests are admitted between steps by
+ * a prefill into their slots. On the backbone alone a request's next input is its last output
+ * (the prompt's last, then each step's), fed back on the GPU. The decoder needs a row per slot. */
+typedef struct tg_server tg_server;
+typedef struct {
+    uint32_t slot;  /* the slot it holds (a request there before is ended) */
+    uint32_t len;   /* prompt positions, prefilled at 0..len-1 */
+    uint32_t steps; /* decode steps after it, at positions len..len+steps-1 */
+} tg_request;
+int tg_server_create(tg_decoder *d, tg_prefill *p, tg_server **out);
+int tg_server_destroy(tg_server *s);
+/* Generator::start (generator.rs:189-262): runs the requests' prompts, x [sum len][hidden] f32 in
+ * request order, into their slots (as few prefill launches as max_rows allows). Refuses a slot
+ * twice, an empty prompt or no steps, and len + steps past the capacity (TG_ESHAPE). */
+int tg_server_start(tg_server *s, const tg_request *reqs, uint32_t n, const float *x);
+/* Generator::step (generator.rs:295-352): one decode step of every request under way. x: NULL to
+ * feed each request's last output back (on the GPU), else [n][hidden] f32 inputs in slot order.
+ * Writes the number of rows run, their slots (if `slots`), and their outputs [n][hidden] (if
+ * `out`: the step is then waited for; else it is only enqueued and later steps queue behind it). A
+ * request whose steps have all run stays held, no longer under way, until finished. */
+int tg_server_step(tg_server *s, const float *x, uint32_t *n_rows, uint32_t *slots, float *out);
+/* The slots under way (ascending; `slots` may be NULL to count them). */
+int tg_server_under_way(const tg_server *s, uint32_t *slots, uint32_t *n);
+int tg_server_request(const tg_server *s, uint32_t slot, uint32_t *held, uint32_t *position,
+                      uint32_t *left);
+/* Generator::finish: frees the slot. */
+int tg_server_finish(tg_server *s, uint32_t slot);
+/* The slot's last output (its next input), [hidden] f32. */
+int tg_server_last_output(tg_server *s, uint32_t slot, float *out);
+/* Waits for every step enqueued (TG_ETIMEOUT after timeout_ns; 0: no limit). */
+int tg_server_sync(tg_server *s, uint64_t timeout_ns);
 
 /* ---- Decode attention without allocation -------------------------------------------------------
  * No counterpart in tgtts-v4. For callers that cannot allocate device memory themselves or let a

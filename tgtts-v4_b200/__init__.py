@@ -113,6 +113,10 @@ class TgRun(ctypes.Structure):
     _fields_ = [("start", ctypes.c_uint32), ("len", ctypes.c_uint32), ("slot", ctypes.c_uint32)]
 
 
+class TgRequest(ctypes.Structure):
+    _fields_ = [("slot", ctypes.c_uint32), ("len", ctypes.c_uint32), ("steps", ctypes.c_uint32)]
+
+
 class TgParams(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in
                 ("dtype", "hidden", "inner", "heads", "kv_heads", "head_dim", "capacity", "rows",
@@ -171,6 +175,8 @@ SIGNATURES = {
     "tg_decoder_load": (_I, [_P, ctypes.c_char_p, _P, _U64, _I]),
     "tg_decoder_step_rows": (_I, [_P, ctypes.POINTER(TgRow), _FP, _FP]),
     "tg_decoder_set_rows": (_I, [_P, ctypes.POINTER(TgRow), _FP]),
+    "tg_decoder_set_rows_n": (_I, [_P, _U32, ctypes.POINTER(TgRow), _FP]),
+    "tg_decoder_step_rows_n": (_I, [_P, _U32, ctypes.POINTER(TgRow), _FP, _FP]),
     "tg_decoder_start": (_I, [_P]),
     "tg_decoder_wait": (_I, [_P, _U64]),
     "tg_decoder_output": (_I, [_P, _FP]),
@@ -193,6 +199,15 @@ SIGNATURES = {
     "tg_prefill_dispatch_label": (_I, [_P, _SZ, ctypes.c_char_p, _SZ]),
     "tg_prefill_max_rows": (_U32, [_P]),
     "tg_attention_decode_noalloc": (_I, [ctypes.POINTER(TgParams), _P, _P, _P, _P, _P, _P]),
+    "tg_server_create": (_I, [_P, _P, ctypes.POINTER(_P)]),
+    "tg_server_destroy": (_I, [_P]),
+    "tg_server_start": (_I, [_P, ctypes.POINTER(TgRequest), _U32, _FP]),
+    "tg_server_step": (_I, [_P, _FP, ctypes.POINTER(_U32), ctypes.POINTER(_U32), _FP]),
+    "tg_server_under_way": (_I, [_P, ctypes.POINTER(_U32), ctypes.POINTER(_U32)]),
+    "tg_server_request": (_I, [_P, _U32, ctypes.POINTER(_U32), ctypes.POINTER(_U32), ctypes.POINTER(_U32)]),
+    "tg_server_finish": (_I, [_P, _U32]),
+    "tg_server_last_output": (_I, [_P, _U32, _FP]),
+    "tg_server_sync": (_I, [_P, _U64]),
 }
 
 _lib: Optional[ctypes.CDLL] = None
@@ -607,6 +622,19 @@ class Decoder:
         check(library().tg_decoder_step_rows(self.handle, self._c_rows(rows), _fptr(x), _fptr(out)))
         return out
 
+    def step_rows_n(self, rows: Sequence[Optional[Row]], x: np.ndarray) -> np.ndarray:
+        """A step of len(rows) <= batch rows, run by the smallest row bucket that holds them
+        (generator.rs:115-123, :306-330): x [n][hidden] -> [n][hidden]."""
+        n = len(rows)
+        if not 1 <= n <= self.batch.rows:
+            raise ShapeError(f"{n} rows in a decoder of {self.batch.rows}")
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        if x.size != n * self.shape.hidden:
+            raise ShapeError(f"{x.size} values for {n} rows of {self.shape.hidden}")
+        out = np.empty((n, self.shape.hidden), np.float32)
+        check(library().tg_decoder_step_rows_n(self.handle, n, _rows(rows), _fptr(x), _fptr(out)))
+        return out
+
     def set_rows(self, rows: Sequence[Optional[Row]], x: np.ndarray) -> None:
         x = self._x(x)
         check(library().tg_decoder_set_rows(self.handle, self._c_rows(rows), _fptr(x)))
@@ -760,6 +788,84 @@ class Prefill:
     def close(self) -> None:
         if getattr(self, "handle", None):
             library().tg_prefill_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Server:
+    """Continuous batching over a decoder (a row per slot) and its prefill (generator.rs:99-352):
+    requests hold slots, each step runs every request under way packed into rows by the smallest
+    row bucket that holds them, requests are admitted between steps by a prefill. A request's next
+    input is its last output, fed back on the GPU, unless the step is given inputs."""
+
+    def __init__(self, decoder: Decoder, prefill: "Prefill"):
+        self.decoder, self.prefill = decoder, prefill
+        h = ctypes.c_void_p()
+        check(library().tg_server_create(decoder.handle, prefill.handle, ctypes.byref(h)))
+        self.handle = h
+
+    def start(self, requests: Sequence[tuple[int, int, int]], x: np.ndarray) -> None:
+        """Generator::start for (slot, len, steps) requests, their prompts' rows of x in order."""
+        hdim = self.decoder.shape.hidden
+        x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        total = sum(r[1] for r in requests)
+        if x.size != total * hdim:
+            raise ShapeError(f"{x.size} values for {total} prompt rows of {hdim}")
+        c = (TgRequest * max(len(requests), 1))(*[TgRequest(*r) for r in requests])
+        check(library().tg_server_start(self.handle, c, len(requests), _fptr(x)))
+
+    def step(self, x: Optional[np.ndarray] = None, read: bool = True):
+        """One step of every request under way: (slots, outputs [n][hidden]) when `read`, else
+        (slots, None) with the step only enqueued."""
+        hdim = self.decoder.shape.hidden
+        under = self.under_way()
+        n = len(under)
+        xp = None
+        if x is not None:
+            x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+            if x.size != n * hdim:
+                raise ShapeError(f"{x.size} values for {n} rows under way")
+            xp = _fptr(x)
+        slots = (ctypes.c_uint32 * max(n, 1))()
+        out = np.empty((n, hdim), np.float32) if read else None
+        got = ctypes.c_uint32()
+        check(library().tg_server_step(self.handle, xp, ctypes.byref(got), slots,
+                                       _fptr(out) if read and n else None))
+        return list(slots)[:got.value], out
+
+    def under_way(self) -> list[int]:
+        n = ctypes.c_uint32()
+        check(library().tg_server_under_way(self.handle, None, ctypes.byref(n)))
+        slots = (ctypes.c_uint32 * max(n.value, 1))()
+        check(library().tg_server_under_way(self.handle, slots, ctypes.byref(n)))
+        return list(slots)[:n.value]
+
+    def request(self, slot: int) -> tuple[bool, int, int]:
+        """(held, position of the next step, steps left) of the slot's request."""
+        held, pos, left = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+        check(library().tg_server_request(self.handle, slot, ctypes.byref(held), ctypes.byref(pos),
+                                          ctypes.byref(left)))
+        return bool(held.value), pos.value, left.value
+
+    def finish(self, slot: int) -> None:
+        check(library().tg_server_finish(self.handle, slot))
+
+    def last_output(self, slot: int) -> np.ndarray:
+        out = np.empty(self.decoder.shape.hidden, np.float32)
+        check(library().tg_server_last_output(self.handle, slot, _fptr(out)))
+        return out
+
+    def sync(self, timeout_ns: int = 0) -> None:
+        check(library().tg_server_sync(self.handle, timeout_ns))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            library().tg_server_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -9,8 +9,8 @@
 #include <memory>
 #include <string>
 
+#include "model.h"
 #include "tg_common.cuh"
-#include "tg_internal.h"
 
 using namespace tg;
 
@@ -72,69 +72,6 @@ extern "C" int tg_batch_placement(uint32_t n_rows, uint32_t slots, const tg_row 
 
 // ---- decoder --------------------------------------------------------------------------------------
 
-namespace {
-
-struct Owned {
-    tg_mem *m = nullptr;
-    ~Owned() { tg_mem_free(m); }
-    int alloc(tg_ctx *ctx, uint64_t bytes, tg_residence r = TG_RES_DEVICE) { return tg_mem_alloc(ctx, bytes, r, &m); }
-    char *ptr() const { return static_cast<char *>(m->ptr); }
-    char *host() const { return static_cast<char *>(m->host); }
-};
-
-uint64_t align256(uint64_t v) { return (v + 255) & ~uint64_t(255); }
-
-struct LayerOffsets {
-    uint64_t qkv, o, gate_up, down, in_norm, post_norm;
-};
-
-}  // namespace
-
-struct tg_decoder {
-    tg_ctx *ctx = nullptr;
-    tg_shape shape{};
-    std::vector<double> factors;
-    uint32_t rows = 0, slots = 0;
-    tg_dtype dtype = TG_F32;
-    bool timed = false;
-    uint64_t esize = 4;
-    // Weights: every layer's projections (storage type) and gains (f32), then the final gain.
-    Owned weights;
-    std::vector<LayerOffsets> layer;
-    uint64_t final_norm = 0;
-    Owned cos, sin, kcache, vcache;  // caches: [layers][slots][kv][capacity][hd]
-    uint64_t cache_layer = 0;        // bytes of one layer's cache
-    // Activations of the step, [rows][...].
-    Owned x_in, h, mid, out, q, att, mlp, words;
-    Owned po, pml, psync, offs;  // the persistent step's attention partials, barrier words, weight offsets
-    bool persistent = false;     // the step is one persistent launch (rows <= 2), else six kernels a layer
-    Owned stage_x, stage_words, stage_out;  // pinned host staging
-    Program prog;
-    std::vector<Launch> launches;
-
-    uint64_t width() const { return (uint64_t)(shape.heads + 2 * shape.kv_heads) * shape.head_dim; }
-    uint64_t attn() const { return (uint64_t)shape.heads * shape.head_dim; }
-    tg_params params() const {
-        tg_params p{};
-        p.dtype = dtype;
-        p.hidden = shape.hidden;
-        p.inner = shape.inner;
-        p.heads = shape.heads;
-        p.kv_heads = shape.kv_heads;
-        p.head_dim = shape.head_dim;
-        p.capacity = shape.capacity;
-        p.rows = rows;
-        p.slots = slots;
-        p.eps = shape.eps;
-        p.residual_scale = shape.residual_scale;
-        p.rope = shape.rope;
-        return p;
-    }
-    char *w(uint64_t off) const { return weights.ptr() + off; }
-    char *kc(uint32_t l) const { return kcache.ptr() + l * cache_layer; }
-    char *vc(uint32_t l) const { return vcache.ptr() + l * cache_layer; }
-};
-
 static int check_shape(const tg_shape &s, tg_dtype dtype) {
     const uint32_t vec = dtype == TG_BF16 ? 256 : 128;
     if (dtype != TG_F32 && dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %d", (int)dtype);
@@ -152,12 +89,6 @@ static int check_shape(const tg_shape &s, tg_dtype dtype) {
     return TG_OK;
 }
 
-#define TG_TRY(x)                 \
-    do {                          \
-        const int st_ = (x);      \
-        if (st_) return st_;      \
-    } while (0)
-
 static void push(std::vector<Launch> &v, uint32_t kernel, const tg_params &p, const char *label,
                  std::initializer_list<std::pair<void *, uint64_t>> b) {
     Launch l;
@@ -173,8 +104,9 @@ static void push(std::vector<Launch> &v, uint32_t kernel, const tg_params &p, co
 
 // decode_batch_graph (decode.rs:457-736): per layer qkv_rope, attention_split, attention_combine,
 // o_proj (+ residual), gate_up (+ norm, SiLU), down_proj (+ residual); then the final norm.
-static void decode_launches(tg_decoder &d) {
-    const tg_params base = d.params();
+static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
+    const tg_params base = d.params(R);
+    std::vector<Launch> v;
     if (d.persistent) {
         Launch l;
         l.kernel = KERNEL_DECODE_STEP;
@@ -202,47 +134,79 @@ static void decode_launches(tg_decoder &d) {
         st.cache_layer = d.cache_layer;
         st.sync = reinterpret_cast<uint32_t *>(d.psync.ptr());
         st.err = d.ctx->err_dev;
-        d.launches.assign(1, l);
-        return;
+        v.push_back(l);
+        return v;
     }
-    const uint64_t T = d.esize, F = 4, R = d.rows;
+    const uint64_t T = d.esize, F = 4;
     const tg_shape &s = d.shape;
     const uint64_t H = s.hidden, I = s.inner, hd = s.head_dim, heads = s.heads;
     const uint64_t chunks = s.capacity / ATTN_CHUNK;
-    const uint64_t words = (d.slots > 1 ? 2 : 1) * R * 4;
+    const uint64_t words = (d.slots > 1 ? 2 : 1) * (uint64_t)R * 4;
     const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
-    d.launches.clear();
     for (uint32_t l = 0; l < s.layers; l++) {
         const LayerOffsets &o = d.layer[l];
         char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
-        push(d.launches, TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
+        push(v, TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
              {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
               {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * F},
               {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
-        push(d.launches, TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
+        push(v, TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
              {{d.q.ptr(), R * d.attn() * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}});
-        push(d.launches, TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
+        push(v, TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
              {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.att.ptr(), R * d.attn() * F}});
         tg_params po = base;
         po.n = (uint32_t)H;
         po.k = (uint32_t)d.attn();
-        push(d.launches, TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
+        push(v, TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
              {{d.att.ptr(), R * d.attn() * F}, {d.w(o.o), H * d.attn() * T}, {in, R * H * F}, {d.mid.ptr(), R * H * F}});
-        push(d.launches, TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
+        push(v, TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
              {{d.mid.ptr(), R * H * F}, {d.w(o.post_norm), H * F}, {d.w(o.gate_up), 2 * I * H * T},
               {d.mlp.ptr(), R * I * F}});
         tg_params pd = base;
         pd.n = (uint32_t)H;
         pd.k = (uint32_t)I;
-        push(d.launches, TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
+        push(v, TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
              {{d.mlp.ptr(), R * I * F}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
     }
-    push(d.launches, TG_KERNEL_RMSNORM, base, "final_norm",
+    push(v, TG_KERNEL_RMSNORM, base, "final_norm",
          {{d.h.ptr(), R * H * F}, {d.w(d.final_norm), H * F}, {d.out.ptr(), R * H * F}});
+    return v;
 }
+
+namespace tg {
+
+std::vector<uint32_t> program_rows(uint32_t rows) {
+    std::vector<uint32_t> out;
+    for (uint32_t r = 1; r < rows; r *= 2) out.push_back(r);
+    out.push_back(rows);
+    return out;
+}
+
+size_t bucket_for(const tg_decoder &d, uint32_t n) {
+    for (size_t i = 0; i < d.buckets.size(); i++)
+        if (d.buckets[i].rows >= n) return i;
+    return d.buckets.size() - 1;
+}
+
+int decoder_place(tg_decoder &d, size_t b, uint32_t n, const tg_row *rows) {
+    const uint32_t R = d.buckets[b].rows;
+    std::vector<tg_row> all(R, tg_row{TG_SPARE, 0});
+    std::copy(rows, rows + n, all.begin());
+    uint32_t nw = 0;
+    size_t i = 0;
+    TG_TRY(d.word_ring.acquire(i));
+    TG_TRY(tg_batch_placement(R, d.slots, all.data(), d.shape.capacity, static_cast<uint32_t *>(d.word_ring.host(i)),
+                              &nw));
+    TG_TRY(d.word_ring.upload(i, d.words.ptr(), (uint64_t)nw * 4, d.ctx->stream));
+    d.active = b;
+    d.n_active = n;
+    return TG_OK;
+}
+
+}  // namespace tg
 
 static int record_step(tg_decoder &d, bool persistent);
 
@@ -317,7 +281,7 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
         TG_TRY(tg_mem_write(d->offs.m, 0, offs.data(), offs.size() * 8));
     }
     TG_TRY(d->stage_x.alloc(ctx, R * H * F, TG_RES_UPLOAD));
-    TG_TRY(d->stage_words.alloc(ctx, 2 * R * 4, TG_RES_UPLOAD));
+    TG_TRY(d->word_ring.init(ctx, 8, 2 * R * 4));
     TG_TRY(d->stage_out.alloc(ctx, R * H * F, TG_RES_READBACK));
     TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
     // Six kernels a layer by default: at batch 1 on B200 they take ~690 us a step against the
@@ -327,21 +291,31 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     return TG_OK;
 }
 
-// Records the step as one persistent launch or as six kernels a layer. A persistent recording the
-// device or shape does not take falls back to the kernels (the same results bit for bit).
+// Records every bucket's step as one persistent launch or as six kernels a layer. A persistent
+// recording the device or shape does not take falls back to the kernels (the same results bit for
+// bit).
+static int record_buckets(tg_decoder &d) {
+    for (Bucket &b : d.buckets) {
+        program_release(b.prog);
+        b.prog = Program();
+        b.launches = decode_launches(d, b.rows);
+        TG_TRY(program_build(d.ctx, b.launches, d.timed, b.prog));
+    }
+    return TG_OK;
+}
+
 static int record_step(tg_decoder &d, bool persistent) {
-    if (d.prog.pending) TG_TRY(program_wait(d.prog, 0));
-    program_release(d.prog);
-    d.prog = Program();
+    TG_TRY(d.wait_pending());
+    if (d.buckets.empty())
+        for (uint32_t r : program_rows(d.rows)) {
+            d.buckets.emplace_back();
+            d.buckets.back().rows = r;
+        }
     d.persistent = persistent;
-    decode_launches(d);
-    int st = program_build(d.ctx, d.launches, d.timed, d.prog);
+    int st = record_buckets(d);
     if (st != TG_OK && persistent) {
-        program_release(d.prog);
-        d.prog = Program();
         d.persistent = false;
-        decode_launches(d);
-        st = program_build(d.ctx, d.launches, d.timed, d.prog);
+        st = record_buckets(d);
     }
     return st;
 }
@@ -360,8 +334,8 @@ extern "C" int tg_decoder_persistent(const tg_decoder *d) { return d && d->persi
 extern "C" int tg_decoder_destroy(tg_decoder *d) {
     if (!d) return TG_OK;
     cudaSetDevice(d->ctx->device);
-    if (d->prog.pending) program_wait(d->prog, 0);
-    program_release(d->prog);
+    d->wait_pending();
+    for (Bucket &b : d->buckets) program_release(b.prog);
     delete d;
     return TG_OK;
 }
@@ -464,89 +438,98 @@ extern "C" int tg_decoder_load(tg_decoder *d, const char *name, const void *src,
     return fail(TG_EINVAL, "no weight %s", name);
 }
 
-static int set_words(tg_decoder *d, const tg_row *rows) {
-    uint32_t n = 0;
-    TG_TRY(tg_batch_placement(d->rows, d->slots, rows, d->shape.capacity,
-                              reinterpret_cast<uint32_t *>(d->stage_words.host()), &n));
-    TG_CUDA(cudaMemcpyAsync(d->words.ptr(), d->stage_words.ptr(), (uint64_t)n * 4, cudaMemcpyDefault, d->ctx->stream));
+extern "C" int tg_decoder_set_rows_n(tg_decoder *d, uint32_t n, const tg_row *rows, const float *x) {
+    if (!d || !rows || !x) return fail(TG_EINVAL, "tg_decoder_set_rows: null argument");
+    if (n == 0 || n > d->rows) return fail(TG_ESHAPE, "%u rows in a decoder of %u", n, d->rows);
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    TG_TRY(d->wait_pending());
+    const uint64_t bytes = (uint64_t)n * d->shape.hidden * 4;
+    memcpy(d->stage_x.host(), x, bytes);
+    TG_TRY(decoder_place(*d, bucket_for(*d, n), n, rows));
+    TG_CUDA(cudaMemcpyAsync(d->x_in.ptr(), d->stage_x.ptr(), bytes, cudaMemcpyDefault, d->ctx->stream));
     return TG_OK;
 }
 
 extern "C" int tg_decoder_set_rows(tg_decoder *d, const tg_row *rows, const float *x) {
-    if (!d || !rows || !x) return fail(TG_EINVAL, "tg_decoder_set_rows: null argument");
-    TG_CUDA(cudaSetDevice(d->ctx->device));
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
-    const uint64_t bytes = (uint64_t)d->rows * d->shape.hidden * 4;
-    memcpy(d->stage_x.host(), x, bytes);
-    TG_TRY(set_words(d, rows));
-    TG_CUDA(cudaMemcpyAsync(d->x_in.ptr(), d->stage_x.ptr(), bytes, cudaMemcpyDefault, d->ctx->stream));
-    return TG_OK;
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    return tg_decoder_set_rows_n(d, d->rows, rows, x);
 }
 
 extern "C" int tg_decoder_start(tg_decoder *d) {
     if (!d) return fail(TG_EINVAL, "null decoder");
     TG_CUDA(cudaSetDevice(d->ctx->device));
     std::lock_guard<std::mutex> lock(d->ctx->mu);
-    return program_start(d->prog);
+    return program_start(d->prog());
 }
 
 extern "C" int tg_decoder_wait(tg_decoder *d, uint64_t timeout_ns) {
     if (!d) return fail(TG_EINVAL, "null decoder");
-    return program_wait(d->prog, timeout_ns);
+    return program_wait(d->prog(), timeout_ns);
 }
 
 extern "C" int tg_decoder_output(tg_decoder *d, float *out) {
     if (!d || !out) return fail(TG_EINVAL, "tg_decoder_output: null argument");
     TG_CUDA(cudaSetDevice(d->ctx->device));
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
-    const uint64_t bytes = (uint64_t)d->rows * d->shape.hidden * 4;
+    TG_TRY(d->wait_pending());
+    const uint64_t bytes = (uint64_t)(d->n_active ? d->n_active : d->rows) * d->shape.hidden * 4;
     TG_CUDA(cudaMemcpyAsync(d->stage_out.ptr(), d->out.ptr(), bytes, cudaMemcpyDefault, d->ctx->stream));
     TG_CUDA(cudaStreamSynchronize(d->ctx->stream));
     memcpy(out, d->stage_out.host(), bytes);
     return TG_OK;
 }
 
-extern "C" int tg_decoder_step_rows(tg_decoder *d, const tg_row *rows, const float *x, float *out) {
-    TG_TRY(tg_decoder_set_rows(d, rows, x));
+extern "C" int tg_decoder_step_rows_n(tg_decoder *d, uint32_t n, const tg_row *rows, const float *x, float *out) {
+    TG_TRY(tg_decoder_set_rows_n(d, n, rows, x));
     TG_TRY(tg_decoder_start(d));
     TG_TRY(tg_decoder_wait(d, 60ull * 1000000000ull));
     return tg_decoder_output(d, out);
 }
 
+extern "C" int tg_decoder_step_rows(tg_decoder *d, const tg_row *rows, const float *x, float *out) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    return tg_decoder_step_rows_n(d, d->rows, rows, x, out);
+}
+
 extern "C" int tg_decoder_step_device(tg_decoder *d, const uint32_t *words, const float *x_dev, float *out_dev) {
     if (!d || !words || !x_dev || !out_dev) return fail(TG_EINVAL, "tg_decoder_step_device: null argument");
     TG_CUDA(cudaSetDevice(d->ctx->device));
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
     const uint32_t nw = d->slots > 1 ? 2 * d->rows : d->rows;
-    memcpy(d->stage_words.host(), words, (uint64_t)nw * 4);
     const uint64_t bytes = (uint64_t)d->rows * d->shape.hidden * 4;
     std::lock_guard<std::mutex> lock(d->ctx->mu);
-    TG_CUDA(cudaMemcpyAsync(d->words.ptr(), d->stage_words.ptr(), (uint64_t)nw * 4, cudaMemcpyDefault, d->ctx->stream));
+    // Queued behind the step before without waiting for it: the placement goes through the word
+    // ring, x and out are stream-ordered device copies.
+    size_t i = 0;
+    TG_TRY(d->word_ring.acquire(i));
+    memcpy(d->word_ring.host(i), words, (uint64_t)nw * 4);
+    d->active = d->buckets.size() - 1;
+    d->n_active = d->rows;
+    TG_TRY(d->word_ring.upload(i, d->words.ptr(), (uint64_t)nw * 4, d->ctx->stream));
     TG_CUDA(cudaMemcpyAsync(d->x_in.ptr(), x_dev, bytes, cudaMemcpyDeviceToDevice, d->ctx->stream));
-    TG_TRY(program_start(d->prog));
+    TG_TRY(program_launch(d->prog()));
     TG_CUDA(cudaMemcpyAsync(out_dev, d->out.ptr(), bytes, cudaMemcpyDeviceToDevice, d->ctx->stream));
     return TG_OK;
 }
 
 extern "C" int tg_decoder_elapsed_ns(tg_decoder *d, double *ns) {
     if (!d || !ns) return fail(TG_EINVAL, "null argument");
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
-    *ns = program_elapsed_ns(d->prog);
+    TG_TRY(d->wait_pending());
+    *ns = program_elapsed_ns(d->prog());
     return TG_OK;
 }
 
 extern "C" int tg_decoder_timings(tg_decoder *d, double *ns, size_t n, size_t *n_dispatches) {
     if (!d) return fail(TG_EINVAL, "null decoder");
-    if (n_dispatches) *n_dispatches = d->launches.size();
+    if (n_dispatches) *n_dispatches = d->cur().launches.size();
     if (!ns) return TG_OK;
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
-    return program_timings(d->prog, ns, n);
+    TG_TRY(d->wait_pending());
+    return program_timings(d->prog(), ns, n);
 }
 
 extern "C" int tg_decoder_dispatch_label(tg_decoder *d, size_t i, char *label, size_t label_bytes) {
     if (!d || !label) return fail(TG_EINVAL, "null argument");
-    if (i >= d->launches.size()) return fail(TG_EINVAL, "dispatch %zu of %zu", i, d->launches.size());
-    snprintf(label, label_bytes, "%s", d->launches[i].label.c_str());
+    const std::vector<Launch> &l = d->cur().launches;
+    if (i >= l.size()) return fail(TG_EINVAL, "dispatch %zu of %zu", i, l.size());
+    snprintf(label, label_bytes, "%s", l[i].label.c_str());
     return TG_OK;
 }
 
@@ -557,7 +540,7 @@ extern "C" int tg_decoder_read_cache(tg_decoder *d, uint32_t layer, uint32_t slo
     if (layer >= s.layers || slot >= d->slots || kind > 1 || first > s.capacity || count > s.capacity - first)
         return fail(TG_ESHAPE, "cache layer %u slot %u kind %u positions %u+%u", layer, slot, kind, first, count);
     TG_CUDA(cudaSetDevice(d->ctx->device));
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    TG_TRY(d->wait_pending());
     const uint64_t hd = s.head_dim, T = d->esize;
     std::vector<uint8_t> raw((uint64_t)count * hd * T);
     tg_mem *m = kind == 0 ? d->kcache.m : d->vcache.m;
@@ -586,7 +569,7 @@ extern "C" int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, u
         return fail(TG_ESHAPE, "copy of %u positions from slot %u to %u of %u", count, from, to, d->slots);
     if (from == to || count == 0) return TG_OK;
     TG_CUDA(cudaSetDevice(d->ctx->device));
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    TG_TRY(d->wait_pending());
     const uint64_t hd = s.head_dim, T = d->esize;
     std::vector<tg_region> regions;
     for (uint32_t l = 0; l < s.layers; l++)
@@ -606,17 +589,6 @@ extern "C" uint64_t tg_decoder_weight_bytes(const tg_decoder *d) {
 extern "C" void *tg_ctx_stream(tg_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
 
 // ---- prefill ----------------------------------------------------------------------------------------
-
-struct tg_prefill {
-    tg_decoder *d = nullptr;
-    uint32_t max_rows = 0;  // a multiple of 128
-    bool timed = false;
-    Owned words, x_in, h, mid, normed, qkv, q, att, proj, gu, mlp, out;
-    Owned stage_x, stage_words, stage_out;
-    std::map<uint32_t, Program> programs;  // by rows, a multiple of 128
-    std::map<uint32_t, std::vector<std::string>> labels;
-    Program *last = nullptr;
-};
 
 // prefill_graph / append_prefill (prefill.rs:181-413): the first input norm, then per layer the
 // q/k/v GEMM, rope_rows, attention_rows, the o GEMM, add_norm_rows, the gate/up GEMM,
@@ -761,8 +733,8 @@ static int layout_runs(tg_prefill *p, const tg_run *runs, uint32_t n_runs, uint3
     return TG_OK;
 }
 
-static int run_rows(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x, bool x_on_device,
-                    float *out, bool out_on_device) {
+int tg::prefill_rows(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x, bool x_on_device,
+                     float *out, bool out_on_device) {
     tg_decoder *d = p->d;
     tg_ctx *ctx = d->ctx;
     const uint64_t H = d->shape.hidden, F = 4;
@@ -772,7 +744,8 @@ static int run_rows(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const fl
     const uint32_t rows = (used + 127) / 128 * 128;
     Program *prog = nullptr;
     TG_TRY(program_for(p, rows, &prog));
-    if (d->prog.pending) TG_TRY(program_wait(d->prog, 0));
+    // The staging buffers are free once this prefill's last launch has run; the decoder's steps
+    // need no wait (the stream orders them with this launch).
     for (auto &kv : p->programs)
         if (kv.second.pending) TG_TRY(program_wait(kv.second, 0));
     uint32_t *w = reinterpret_cast<uint32_t *>(p->stage_words.host());
@@ -830,7 +803,7 @@ extern "C" int tg_prefill_run(tg_prefill *p, uint32_t start, uint32_t slot, cons
     for (uint32_t done = 0; done < len;) {
         const uint32_t n = std::min(len - done, p->max_rows);
         const tg_run r = {start + done, n, slot};
-        TG_TRY(run_rows(p, &r, 1, x + (uint64_t)done * s.hidden, false, out + (uint64_t)done * s.hidden, false));
+        TG_TRY(prefill_rows(p, &r, 1, x + (uint64_t)done * s.hidden, false, out + (uint64_t)done * s.hidden, false));
         done += n;
     }
     return TG_OK;
@@ -839,14 +812,14 @@ extern "C" int tg_prefill_run(tg_prefill *p, uint32_t start, uint32_t slot, cons
 extern "C" int tg_prefill_run_batch(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x, float *out) {
     if (!p || !runs || !n_runs || !x || !out) return fail(TG_EINVAL, "tg_prefill_run_batch: null argument");
     TG_CUDA(cudaSetDevice(p->d->ctx->device));
-    return run_rows(p, runs, n_runs, x, false, out, false);
+    return prefill_rows(p, runs, n_runs, x, false, out, false);
 }
 
 extern "C" int tg_prefill_run_batch_device(tg_prefill *p, const tg_run *runs, uint32_t n_runs, const float *x_dev,
                                            float *out_dev) {
     if (!p || !runs || !n_runs || !x_dev || !out_dev) return fail(TG_EINVAL, "tg_prefill_run_batch_device: null argument");
     TG_CUDA(cudaSetDevice(p->d->ctx->device));
-    return run_rows(p, runs, n_runs, x_dev, true, out_dev, true);
+    return prefill_rows(p, runs, n_runs, x_dev, true, out_dev, true);
 }
 
 extern "C" int tg_prefill_elapsed_ns(tg_prefill *p, double *ns) {

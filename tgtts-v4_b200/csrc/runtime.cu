@@ -328,6 +328,12 @@ int program_start(Program &p) {
     return TG_OK;
 }
 
+int program_launch(Program &p) {
+    TG_CUDA(cudaGraphLaunch(p.exec, p.ctx->stream));
+    p.pending = true;
+    return TG_OK;
+}
+
 int program_wait(Program &p, uint64_t timeout_ns) {
     if (!p.pending) return TG_OK;
     const int st = wait_event(p.events.back(), timeout_ns);

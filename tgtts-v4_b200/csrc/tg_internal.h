@@ -95,6 +95,9 @@ struct Program {
 // context's stream. `pre` may be empty.
 int program_build(tg_ctx *ctx, const std::vector<Launch> &launches, bool timed, Program &out);
 int program_start(Program &p);
+// Launches the program behind whatever the stream holds, without waiting for an earlier run of it
+// (stream order keeps the runs apart); a later wait waits for the last.
+int program_launch(Program &p);
 int program_wait(Program &p, uint64_t timeout_ns);
 void program_release(Program &p);
 double program_elapsed_ns(Program &p);
