@@ -271,6 +271,14 @@ int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, uint32_t cou
 int tg_decoder_retune(tg_decoder *d, int persistent, int timed);
 /* 1 when the decoder's step is the persistent launch. */
 int tg_decoder_persistent(const tg_decoder *d);
+/* 1 when the decoder's projections run on tcgen05 (bf16 decoders of 16 rows or more, in every row
+ * bucket), 0 when they run as GEMVs on the CUDA cores. */
+int tg_decoder_tensor(const tg_decoder *d);
+/* Records the step again with its projections on tcgen05 (tensor != 0) or as GEMVs, over the same
+ * weights and cache. The two give results within their roundings of each other, not the same
+ * bits: a decoder that checks a request against its run beside others uses the family those ran
+ * in. TG_ESHAPE when tcgen05 does not take the decoder's dtype or shape. */
+int tg_decoder_set_tensor(tg_decoder *d, int tensor);
 /* The weight bytes one step reads at this dtype (Shape::weight_bytes at its element size). */
 uint64_t tg_decoder_weight_bytes(const tg_decoder *d);
 

@@ -80,8 +80,10 @@ def test_a_row_comes_out_bit_for_bit_as_it_does_alone(pkg, ctx, syn, dtype):
     # Each request's positions: request r starts at position 3r % 40.
     start = [(3 * r) % 40 for r in range(64)]
 
-    def run(rows, slots, requests):
+    def run(rows, slots, requests, tensor=False):
         dec = pkg.Decoder(ctx, shape, rows=rows, slots=slots, dtype=dtype)
+        if dec.tensor != tensor:
+            dec.with_tensor(tensor)
         dec.load(w)
         outs = []
         for t in range(steps):
@@ -108,6 +110,12 @@ def test_a_row_comes_out_bit_for_bit_as_it_does_alone(pkg, ctx, syn, dtype):
         for i, r in enumerate(requests):
             if r in alone:
                 assert np.array_equal(batched[:, i], alone[r]), (rows, r)
+    if dtype == "bf16":
+        # The tcgen05 projections (a 64-row decoder's own): alone and beside 63 others alike.
+        alone_tc = {r: run(1, 1, [r], tensor=True)[:, 0] for r in (0, 17, 63)}
+        batched = run(64, 64, list(range(64)), tensor=True)
+        for r, want in alone_tc.items():
+            assert np.array_equal(batched[:, r], want), ("tensor", r)
 
 
 def test_spare_rows_write_nothing_and_slots_are_kept_apart(pkg, ctx, syn):

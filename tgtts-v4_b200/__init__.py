@@ -189,6 +189,8 @@ SIGNATURES = {
     "tg_decoder_weight_bytes": (_U64, [_P]),
     "tg_decoder_retune": (_I, [_P, _I, _I]),
     "tg_decoder_persistent": (_I, [_P]),
+    "tg_decoder_tensor": (_I, [_P]),
+    "tg_decoder_set_tensor": (_I, [_P, _I]),
     "tg_prefill_create": (_I, [_P, _U32, _I, ctypes.POINTER(_P)]),
     "tg_prefill_destroy": (_I, [_P]),
     "tg_prefill_run": (_I, [_P, _U32, _U32, _FP, _U32, _FP]),
@@ -702,6 +704,16 @@ class Decoder:
     @property
     def persistent(self) -> bool:
         return bool(library().tg_decoder_persistent(self.handle))
+
+    @property
+    def tensor(self) -> bool:
+        """True when the projections run on tcgen05 (bf16 decoders of 16 rows or more)."""
+        return bool(library().tg_decoder_tensor(self.handle))
+
+    def with_tensor(self, on: bool = True) -> "Decoder":
+        """Records the step again with its projections on tcgen05 (or as GEMVs); returns self."""
+        check(library().tg_decoder_set_tensor(self.handle, int(on)))
+        return self
 
     def _x(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)

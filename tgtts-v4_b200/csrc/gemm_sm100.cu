@@ -10,10 +10,7 @@
 // its limit the kernel sets the context's error word and runs to its end.
 //
 // f32: a SIMT kernel, each sum sequential in k.
-#include <cuda.h>
-
-#include "tg_common.cuh"
-#include "tg_internal.h"
+#include "tc_common.cuh"
 
 namespace tg {
 
@@ -66,75 +63,6 @@ __global__ void __launch_bounds__(256)
 constexpr int TC_BM = 128, TC_BK = 64, TC_STAGES = 4, TC_THREADS = 128;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB per stage
 
-
-// Waits for the phase of parity `parity` of `bar` to complete, for at most 2 s (1 ms once the
-// block has given up on a wait). Past that it records ERR_WAIT_TIMEOUT and returns, so that the
-// kernel always ends.
-TG_DEVICE void mbar_wait(uint32_t bar, uint32_t parity, uint32_t *err, volatile int *gave_up) {
-    if (mbar_try_wait(bar, parity)) return;
-    const uint64_t limit = *gave_up ? 1000000ull : 2000000000ull;
-    const uint64_t t0 = globaltimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (globaltimer() - t0 > limit) {
-            *gave_up = 1;
-            atomicExch(err, ERR_WAIT_TIMEOUT);
-            return;
-        }
-    }
-}
-
-TG_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
-// The shared-memory matrix descriptor of a K-major tile with 128-byte rows in the 128-byte
-// swizzle TMA writes: start address, leading byte offset 16 (unused for this layout), stride
-// byte offset 1024 between groups of 8 rows, descriptor version 1, swizzle mode 2 (128 B).
-TG_DEVICE uint64_t sw128_desc(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3fff) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// The instruction descriptor of kind::f16 with bf16 A and B (both K-major), f32 D, M x N.
-__host__ __device__ constexpr uint32_t bf16_idesc(int m, int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
-TG_DEVICE void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-TG_DEVICE void tc_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
-                 : "memory");
-}
-
-TG_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-TG_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-// 16 consecutive f32 columns of this warp's 32 TMEM lanes: lane i of the warp gets row
-// (warp % 4) * 32 + i.
-TG_DEVICE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
-}
 
 template <int BN>
 struct TcLayout {
@@ -273,43 +201,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
 // ---- host -------------------------------------------------------------------------------------
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        cudaDriverEntryPointQueryResult q;
-        void *p = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    });
-    return fn;
-}
-
-// A 2-D map over a row-major [rows][k] bf16 matrix, boxes of 64 columns x `box_rows` rows in the
-// 128-byte swizzle.
-static bool make_map(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {k, rows};
-    cuuint64_t strides[1] = {k * 2};
-    cuuint32_t box[2] = {TC_BK, box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <int BN, int EPI = TC_EPI_F32>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
                              cudaStream_t s) {
     CUtensorMap ma, mb;
-    if (!make_map(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map(&mb, b, (uint64_t)N, (uint64_t)K, BN))
+    if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, BN))
         return cudaErrorInvalidValue;
     auto kern = gemm_tc_kernel<BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<BN>::SMEM);

@@ -171,36 +171,7 @@ TG_DEVICE void gemv_epilogue(const GemvArgs &a, int u, int b, float y0, float y1
     } else if constexpr (EPI == EPI_GATE_UP) {
         a.out[(size_t)b * p.inner + u] = silu_mul(y0, y1);
     } else {
-        const int hd = p.head_dim, half = hd / 2, heads = p.heads, kvh = p.kv_heads;
-        const int head = u / half, i = u % half;
-        uint32_t pos, slot;
-        if (!placed(a.at, p.rows, b, p.capacity, p.slots, pos, slot)) return;
-        T *kc = static_cast<T *>(a.kc);
-        T *vc = static_cast<T *>(a.vc);
-        float ra = y0, rc = y1;
-        if (head >= heads + kvh) {
-            const size_t to = (((size_t)slot * kvh + (head - heads - kvh)) * p.capacity + pos) * hd + i;
-            vc[to] = from_f32<T>(ra);
-            vc[to + half] = from_f32<T>(rc);
-            return;
-        }
-        if (p.rope) {
-            // As upstream: x cos + rotate_half(x) sin (gemv_qkv_rope.comp:85-90).
-            const float co = a.cosv[(size_t)pos * half + i], si = a.sinv[(size_t)pos * half + i];
-            const float na = __fmaf_rn(ra, co, -__fmul_rn(rc, si));
-            const float nc = __fmaf_rn(rc, co, __fmul_rn(ra, si));
-            ra = na;
-            rc = nc;
-        }
-        if (head < heads) {
-            const size_t to = ((size_t)b * heads + head) * hd + i;
-            a.q[to] = ra;
-            a.q[to + half] = rc;
-        } else {
-            const size_t to = (((size_t)slot * kvh + (head - heads)) * p.capacity + pos) * hd + i;
-            kc[to] = from_f32<T>(ra);
-            kc[to + half] = from_f32<T>(rc);
-        }
+        qkv_store<T>(p, a.at, a.cosv, a.sinv, a.q, a.kc, a.vc, u, b, y0, y1);
     }
 }
 

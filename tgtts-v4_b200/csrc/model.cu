@@ -146,7 +146,7 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
     for (uint32_t l = 0; l < s.layers; l++) {
         const LayerOffsets &o = d.layer[l];
         char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
-        push(v, TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
+        push(v, d.tensor ? KERNEL_DTC_QKV_ROPE : TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
              {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
               {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * F},
               {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
@@ -160,15 +160,15 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
         tg_params po = base;
         po.n = (uint32_t)H;
         po.k = (uint32_t)d.attn();
-        push(v, TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
+        push(v, d.tensor ? KERNEL_DTC_RESIDUAL : TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
              {{d.att.ptr(), R * d.attn() * F}, {d.w(o.o), H * d.attn() * T}, {in, R * H * F}, {d.mid.ptr(), R * H * F}});
-        push(v, TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
+        push(v, d.tensor ? KERNEL_DTC_GATE_UP : TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
              {{d.mid.ptr(), R * H * F}, {d.w(o.post_norm), H * F}, {d.w(o.gate_up), 2 * I * H * T},
               {d.mlp.ptr(), R * I * F}});
         tg_params pd = base;
         pd.n = (uint32_t)H;
         pd.k = (uint32_t)I;
-        push(v, TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
+        push(v, d.tensor ? KERNEL_DTC_RESIDUAL : TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
              {{d.mlp.ptr(), R * I * F}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
     }
     push(v, TG_KERNEL_RMSNORM, base, "final_norm",
@@ -284,6 +284,9 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(d->word_ring.init(ctx, 8, 2 * R * 4));
     TG_TRY(d->stage_out.alloc(ctx, R * H * F, TG_RES_READBACK));
     TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
+    // A decoder of DTC_MIN_ROWS rows or more runs its projections on tcgen05 in every bucket (so that
+    // a row's bits do not depend on the bucket); smaller ones run the GEMVs.
+    d->tensor = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && dtc_supported(d->params(rows));
     // Six kernels a layer by default: at batch 1 on B200 they take ~690 us a step against the
     // persistent launch's ~970 us (tg_decoder_retune selects either).
     TG_TRY(record_step(*d, false));
@@ -330,6 +333,17 @@ extern "C" int tg_decoder_retune(tg_decoder *d, int persistent, int timed) {
 }
 
 extern "C" int tg_decoder_persistent(const tg_decoder *d) { return d && d->persistent ? 1 : 0; }
+
+extern "C" int tg_decoder_tensor(const tg_decoder *d) { return d && d->tensor ? 1 : 0; }
+
+extern "C" int tg_decoder_set_tensor(tg_decoder *d, int tensor) {
+    if (!d) return fail(TG_EINVAL, "null decoder");
+    if (tensor && !(d->dtype == TG_BF16 && dtc_supported(d->params(d->rows))))
+        return fail(TG_ESHAPE, "no tcgen05 projections for this decoder's dtype or shape");
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    d->tensor = tensor != 0;
+    return record_step(*d, d->persistent && !d->tensor);
+}
 
 extern "C" int tg_decoder_destroy(tg_decoder *d) {
     if (!d) return TG_OK;

@@ -108,6 +108,7 @@ struct tg_decoder {
     tg::Owned x_in, h, mid, out, q, att, mlp, words;
     tg::Owned po, pml, psync, offs;  // the persistent step's attention partials, barrier words, weight offsets
     bool persistent = false;         // the step is one persistent launch (rows <= 2), else six kernels a layer
+    bool tensor = false;             // the projections run on tcgen05 (rows >= DTC_MIN_ROWS, bf16)
     tg::Owned stage_x, stage_out;  // pinned host staging
     tg::StageRing word_ring;                    // placements of device-resident steps
     std::vector<tg::Bucket> buckets;            // ascending rows; the last holds `rows`

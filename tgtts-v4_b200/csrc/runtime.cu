@@ -207,8 +207,22 @@ static int check_shape(const Launch &l) {
     return TG_OK;
 }
 
-int check_launch(const Launch &l) {
-    if (l.kernel == KERNEL_DECODE_STEP) return TG_OK;  // recorded by the decoder over its own buffers
+// The table kernel whose bindings and shape rules a library-recorded launch shares.
+static uint32_t table_kernel(uint32_t k) {
+    switch (k) {
+        case KERNEL_DTC_QKV_ROPE: return TG_KERNEL_GEMV_QKV_ROPE;
+        case KERNEL_DTC_GATE_UP: return TG_KERNEL_GEMV_GATE_UP;
+        case KERNEL_DTC_RESIDUAL: return TG_KERNEL_GEMV_RESIDUAL;
+        default: return k;
+    }
+}
+
+int check_launch(const Launch &l0) {
+    if (l0.kernel == KERNEL_DECODE_STEP) return TG_OK;  // recorded by the decoder over its own buffers
+    Launch l = l0;
+    l.kernel = table_kernel(l0.kernel);
+    if (l.kernel != l0.kernel && !dtc_supported(l.p))
+        return fail(TG_ESHAPE, "%s: no tcgen05 plan for %u rows of this shape", l0.label.c_str(), l.p.rows);
     int st = check_shape(l);
     if (st) return st;
     std::vector<Need> need;
@@ -250,11 +264,14 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case TG_KERNEL_GEMM_SILU: e = launch_gemm_silu(p, b[0], b[1], b[2], err, s); break;
         case TG_KERNEL_ATTENTION_DECODE: e = launch_attention_decode(p, b[0], b[1], b[2], U(3), b[4], s); break;
         case KERNEL_DECODE_STEP: e = launch_decode_step(l.step, sm_count, s); break;
+        case KERNEL_DTC_QKV_ROPE: e = launch_dtc_qkv_rope(p, F(0), F(1), b[2], F(3), F(4), U(5), F(6), b[7], b[8], err, s); break;
+        case KERNEL_DTC_GATE_UP: e = launch_dtc_gate_up(p, F(0), F(1), b[2], F(3), err, s); break;
+        case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
         default: return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
     if (e != cudaSuccess)
         return fail(e == cudaErrorNotSupported ? TG_ESHAPE : TG_ECUDA, "launching %s (%s): %s",
-                    l.kernel == KERNEL_DECODE_STEP ? "decode_step" : kernel_name(l.kernel), l.label.c_str(),
+                    l.kernel == KERNEL_DECODE_STEP ? "decode_step" : kernel_name(table_kernel(l.kernel)), l.label.c_str(),
                     cudaGetErrorString(e));
     return TG_OK;
 }
@@ -278,7 +295,7 @@ int program_build(tg_ctx *ctx, const std::vector<Launch> &launches, bool timed, 
     out.ctx = ctx;
     out.timed = timed;
     out.labels.clear();
-    for (const Launch &l : launches) out.labels.push_back(l.label.empty() ? kernel_name(l.kernel) : l.label);
+    for (const Launch &l : launches) out.labels.push_back(l.label.empty() ? kernel_name(table_kernel(l.kernel)) : l.label);
     const size_t nev = timed ? launches.size() + 1 : 2;
     for (size_t i = 0; i < nev; i++) {
         cudaEvent_t e;

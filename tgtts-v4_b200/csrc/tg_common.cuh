@@ -7,6 +7,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "tgcuda.h"
+
 #define TG_DEVICE __device__ __forceinline__
 
 namespace tg {
@@ -127,6 +129,44 @@ TG_DEVICE bool placed(const uint32_t *at, int rows, int b, uint32_t capacity, ui
     pos = at[b];
     slot = slots > 1 ? at[rows + b] : 0u;
     return pos < capacity && slot < slots;
+}
+
+// The q/k/v epilogue of decode unit u (a RoPE pair of rows (i, i + hd/2) of head u / (hd/2)) for
+// batch row b, given the pair's two sums (gemv_qkv_rope.comp:51-107): q heads are rotated and
+// stored f32 at q[b][head][hd], k heads rotated and v heads as they are into the row's slot of the
+// caches at its position. A spare row stores nothing.
+template <typename T>
+TG_DEVICE void qkv_store(const tg_params &p, const uint32_t *at, const float *cosv, const float *sinv, float *q,
+                         void *kcache, void *vcache, int u, int b, float ra, float rc) {
+    const int hd = p.head_dim, half = hd / 2, heads = p.heads, kvh = p.kv_heads;
+    const int head = u / half, i = u % half;
+    uint32_t pos, slot;
+    if (!placed(at, p.rows, b, p.capacity, p.slots, pos, slot)) return;
+    T *kc = static_cast<T *>(kcache);
+    T *vc = static_cast<T *>(vcache);
+    if (head >= heads + kvh) {
+        const size_t to = (((size_t)slot * kvh + (head - heads - kvh)) * p.capacity + pos) * hd + i;
+        vc[to] = from_f32<T>(ra);
+        vc[to + half] = from_f32<T>(rc);
+        return;
+    }
+    if (p.rope) {
+        // As upstream: x cos + rotate_half(x) sin (gemv_qkv_rope.comp:85-90).
+        const float co = cosv[(size_t)pos * half + i], si = sinv[(size_t)pos * half + i];
+        const float na = __fmaf_rn(ra, co, -__fmul_rn(rc, si));
+        const float nc = __fmaf_rn(rc, co, __fmul_rn(ra, si));
+        ra = na;
+        rc = nc;
+    }
+    if (head < heads) {
+        const size_t to = ((size_t)b * heads + head) * hd + i;
+        q[to] = ra;
+        q[to + half] = rc;
+    } else {
+        const size_t to = (((size_t)slot * kvh + (head - heads)) * p.capacity + pos) * hd + i;
+        kc[to] = from_f32<T>(ra);
+        kc[to + half] = from_f32<T>(rc);
+    }
 }
 
 // ---- mbarriers, bulk copies, programmatic dependent launch (sm_90+) ------------------------------

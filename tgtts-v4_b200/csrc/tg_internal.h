@@ -64,6 +64,13 @@ struct DecodeStep {
 };
 // Kernel ids past the table's, for launches the library records itself.
 constexpr uint32_t KERNEL_DECODE_STEP = 1000;  // the persistent decode step (DecodeStep)
+// The batched decoder's projections on tcgen05, with the bindings of GEMV_QKV_ROPE, GEMV_GATE_UP
+// and GEMV_RESIDUAL.
+constexpr uint32_t KERNEL_DTC_QKV_ROPE = 1001;
+constexpr uint32_t KERNEL_DTC_GATE_UP = 1002;
+constexpr uint32_t KERNEL_DTC_RESIDUAL = 1003;
+// Decoders of at least this many rows run their projections on tcgen05 (every bucket of them).
+constexpr uint32_t DTC_MIN_ROWS = 16;
 
 // One dispatch resolved to device pointers, as the kernel table launches it.
 struct Launch {
@@ -145,6 +152,16 @@ cudaError_t launch_silu_mul_rows(const tg_params &p, const uint32_t *at, const f
 // f32 operands on a SIMT kernel. Returns cudaErrorInvalidValue for shapes it does not tile.
 cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c,
                         uint32_t *err, cudaStream_t s);
+// The batched decode projections (kernels_decode_tc.cu): true when every projection of a step of
+// p.rows rows of this shape has a plan.
+bool dtc_supported(const tg_params &p);
+cudaError_t launch_dtc_qkv_rope(const tg_params &p, const float *x, const float *g, const void *w, const float *cosv,
+                                const float *sinv, const uint32_t *at, float *q, void *kc, void *vc, uint32_t *err,
+                                cudaStream_t s);
+cudaError_t launch_dtc_gate_up(const tg_params &p, const float *x, const float *g, const void *w, float *out,
+                               uint32_t *err, cudaStream_t s);
+cudaError_t launch_dtc_residual(const tg_params &p, const float *x, const void *w, const float *res, float *out,
+                                uint32_t *err, cudaStream_t s);
 // One cooperative launch for the whole step (batches of up to 2 rows); cudaErrorNotSupported when
 // the shape or batch is not one it takes.
 cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s);
