@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the prefill/GEMM side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--workload", default="decode", choices=["decode", "serve"],
+                    help="decode: config 2 (the headline line); serve: config 5, request-sharded serving")
+    ap.add_argument("--requests", type=int, default=2048, help="serve: requests over all GPUs")
     return ap.parse_args()
 
 
@@ -483,11 +486,117 @@ def run_reference(args, rank, world, local):
                     "the reference arm is the C restatement of its CPU f32 model (oracle/)"}
 
 
+SERVE_METRIC = "serving decode tokens/s, all GPUs (0.5B-shaped bf16 backbone, <= 128 requests per GPU)"
+
+
+def run_serve(args, rank, world, local):
+    """Config 5: `--requests` requests (prompts uniform 64-1024, decodes uniform 64-768, seed 3,
+    Poisson arrivals at 4096 a second, which keeps every GPU's 128 slots full), spread over the
+    GPUs by a least-loaded rule every rank computes alike; each rank serves its share with one
+    weight replica, continuous batching and no collective on the data path. Time: CUDA events on
+    the rank's stream from the first admission to the last step (prefills included), max over
+    ranks; per-step decode latency from events around each step, p50/p99 over all steps."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    pkg = entry.load_package()
+    from tgtts_v4_b200 import serving
+    from tgtts_v4_b200 import synthetic as syn
+
+    torch.cuda.set_device(local)
+    ctx = pkg.Context(local)
+    cfg = syn.S05B
+    slots = 128
+    shape = syn.shape_of(cfg, capacity=1024 + 768)
+    weights = syn.make_weights(cfg, seed=0, as_bits=True)
+    dec = pkg.Decoder(ctx, shape, rows=slots, slots=slots, dtype="bf16")
+    dec.load(weights)
+    pre = pkg.Prefill(dec, max_rows=8192)
+    server = pkg.Server(dec, pre)
+    stream = stream_ctx(ctx)
+    reqs, pool = serving.poisson_requests(args.requests, cfg.hidden, seed=3)
+    mine = serving.assign_least_loaded(reqs, world)[rank]
+    drv = serving.Driver(server, pool, slots)
+    clocks = Clocks(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    clocks.__enter__()
+    ev = lambda: torch.cuda.Event(enable_timing=True)
+    e0 = ev()
+    e0.record(stream)
+    t0 = time.perf_counter()
+    waiting = list(mine)
+    marks = []
+    while waiting or drv.owner:
+        now = time.perf_counter() - t0
+        free = len(drv.free_slots())
+        ready = []
+        while waiting and free and waiting[0].arrival <= now:
+            ready.append(waiting.pop(0))
+            free -= 1
+        drv.admit(ready)
+        if not drv.owner:
+            time.sleep(max(0.0, min(0.001, waiting[0].arrival - now)))
+            continue
+        a, b = ev(), ev()
+        a.record(stream)
+        drv.step(read=False)
+        b.record(stream)
+        marks.append((a, b))
+    e1 = ev()
+    e1.record(stream)
+    e1.synchronize()
+    clocks.__exit__(None, None, None)
+    ms = e0.elapsed_time(e1)
+    step_ms = sorted(x.elapsed_time(y) for x, y in marks)
+    ms_max = max_over_ranks(ms, world)
+    decoded = drv.decoded
+    prefilled = drv.prefilled
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([decoded, prefilled, len(marks)], dtype=torch.float64)
+        dist.all_reduce(t)
+        decoded, prefilled, n_steps = (int(v) for v in t.tolist())
+        lat = torch.tensor([step_ms[len(step_ms) // 2], step_ms[int(len(step_ms) * 0.99)]], dtype=torch.float64)
+        dist.all_reduce(lat, op=dist.ReduceOp.MAX)
+        p50, p99 = lat.tolist()
+    else:
+        n_steps = len(marks)
+        p50, p99 = step_ms[len(step_ms) // 2], step_ms[int(len(step_ms) * 0.99)]
+    result = None
+    if rank == 0:
+        c = clocks.summary()
+        result = {
+            "metric": SERVE_METRIC, "value": round(decoded / (ms_max / 1e3), 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": n_steps, "warmup": 0, "ms_per_step": round(ms_max / max(1, n_steps // world), 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights seed 0, N(0,1) bf16-valued prompt rows, request lengths seed 3",
+            "config": {"workload": "config 5: request-sharded serving, one weight replica per GPU, no collective",
+                       "requests": args.requests, "slots_per_gpu": slots, "prompt": "U[64,1024]",
+                       "decode": "U[64,768]", "arrivals": "Poisson 4096/s (saturating)",
+                       "parallelism": f"replicas x{world}, least-loaded assignment"},
+            "prefill_tokens": prefilled, "decode_tokens": decoded, "seconds": round(ms_max / 1e3, 3),
+            "step_latency_ms": {"p50": round(p50, 4), "p99": round(p99, 4), "max_over_ranks": world > 1},
+            # Decode steps only: the gather, the step's 6 per layer and the final norm, the scatter.
+            "gpu_launches": n_steps * (6 * shape.layers + 3),
+            "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
+        }
+    server.close()
+    pre.close()
+    dec.close()
+    ctx.close()
+    return result
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args.gpus)
     if args.impl == "reference":
         res = run_reference(args, rank, world, local)
+    elif args.workload == "serve":
+        res = run_serve(args, rank, world, local)
     else:
         res = run_ours(args, rank, world, local)
     if rank == 0 and res is not None:

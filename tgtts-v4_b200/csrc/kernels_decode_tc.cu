@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     __shared__ float sq[DTC_MAX_ROWS];     // this block's partial sums of squares, by row
     __shared__ float scale[DTC_MAX_ROWS];  // the rows' RMSNorm scales
     __shared__ __align__(16) float gs[DTC_MAX_KB * 64];
+    __shared__ uint32_t at_s[2 * DTC_MAX_ROWS];  // the placement words (written before the step)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int r = (int)cluster.block_rank(), S = a.S;
@@ -158,9 +159,11 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     if (norm)
         for (int i = tid; i < Kc / 4; i += DTC_THREADS)
             reinterpret_cast<float4 *>(gs)[i] = reinterpret_cast<const float4 *>(a.g + k0)[i];
+    if constexpr (EPI == DTC_QKV)
+        for (int i = tid; i < (a.p.slots > 1 ? 2 : 1) * R; i += DTC_THREADS) at_s[i] = a.at[i];
     pdl_launch_dependents();
     pdl_wait();
-    __syncthreads();  // the gain is in shared memory for every warp
+    __syncthreads();  // the gain and the placement are in shared memory for every warp
 
     // 2-4. B for each group of rows (four items' loads in flight per thread), then its MMAs. Where
     // the projection norms its input, B holds x g (the gain applied, the RMSNorm scale not yet):
@@ -233,15 +236,16 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     tc_fence_after();
 
     // 5. Rounds of `cc` accumulator columns. Block r owns units [r per, (r + 1) per) of the tile
-    // (rows for the residual, gate/up columns, RoPE pairs for q/k/v): every block pushes each
-    // accumulator row it holds into the owner's receive buffer, [from block][owned row][column],
-    // with stores into distributed shared memory; after a cluster barrier each block sums its rows
-    // over the S partials in rank order from its own shared memory and runs the epilogue. The
+    // (rows for the residual, gate/up columns, RoPE pairs for q/k/v): every block adds each hi/lo
+    // pair of the accumulator rows it holds and pushes the sums into the owner's receive buffer,
+    // [from block][owned row][batch row], with stores into distributed shared memory; after a
+    // cluster barrier each block sums its rows over the S partials in rank order from its own
+    // shared memory and runs the epilogue, whose global inputs it loaded before the barrier. The
     // receive buffer reuses W's and B's space, so a barrier first makes sure every block's MMAs are
     // done with them. The RMSNorm scales join the S blocks' sums of squares in rank order.
     const int per = UNITS / S;                   // units a block owns
     const int own = NT * 128 / S;                // accumulator rows a block owns
-    const int stride = a.cc + 4;                 // floats per received row (padded against conflicts)
+    const int stride = a.cc / 2 + 4;             // floats per received row (padded against conflicts)
     float *recv = reinterpret_cast<float *>(smem);
     const int q = warp & 3, half_w = warp >> 2;  // TMEM lane quarter, and which half of the columns
     const int m = q * 32 + lane;                 // the accumulator row this thread holds
@@ -259,8 +263,10 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
         }
     }
     const uint32_t lanes = tmem + ((uint32_t)(q * 32) << 16);
+    constexpr int PF = 8;  // epilogue items a thread takes per round (the plan keeps it so)
     for (int c0 = 0; c0 < Ntot; c0 += a.cc) {
         const int cw = min(a.cc, Ntot - c0);
+        const int nbr = cw / 2;  // batch rows of this round
         cluster.sync();  // every block's MMAs (first round) or reduction (later rounds) is done
         if (norm && c0 == 0) {
             for (int b = tid; b < R; b += DTC_THREADS) {
@@ -287,50 +293,96 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
                     if (cc + 32 * i >= cw) break;
-                    uint4 *d4 = reinterpret_cast<uint4 *>(dst + cc + 32 * i);
+                    float w[8];
 #pragma unroll
-                    for (int e = 0; e < 4; e++) d4[e] = make_uint4(v[i][4 * e], v[i][4 * e + 1], v[i][4 * e + 2], v[i][4 * e + 3]);
+                    for (int e = 0; e < 8; e++) w[e] = __fadd_rn(__uint_as_float(v[i][2 * e]), __uint_as_float(v[i][2 * e + 1]));
+                    float4 *d4 = reinterpret_cast<float4 *>(dst + (cc + 32 * i) / 2);
+                    d4[0] = make_float4(w[0], w[1], w[2], w[3]);
+                    d4[1] = make_float4(w[4], w[5], w[6], w[7]);
+                }
+            }
+        }
+        // This thread's epilogue items of the round: their global inputs, before the barrier.
+        const int items = per * nbr;
+        float pre_a[PF], pre_b[PF];
+#pragma unroll
+        for (int k = 0; k < PF; k++) {
+            pre_a[k] = pre_b[k] = 0.0f;
+            const int idx = tid + k * DTC_THREADS;
+            if (idx >= items) continue;
+            const int ul = idx % per, c = c0 + 2 * (idx / per);
+            const int gi = c / a.Npg, bl = (c % a.Npg) / 2, b = gi * a.G + bl;
+            if (bl >= a.G || b >= R) continue;
+            const int unit = r * per + ul;
+            if constexpr (EPI == DTC_RESIDUAL) {
+                pre_a[k] = __ldcg(a.res + (size_t)b * a.p.n + tile * 128 + unit);
+            } else if constexpr (EPI == DTC_QKV) {
+                const int hf = a.p.head_dim / 2, i = unit % hf;
+                const uint32_t pos = at_s[b];
+                if (a.p.rope && pos < a.p.capacity) {
+                    pre_a[k] = __ldg(a.cosv + (size_t)pos * hf + i);
+                    pre_b[k] = __ldg(a.sinv + (size_t)pos * hf + i);
                 }
             }
         }
         cluster.sync();  // every push has landed (and the scales are in)
-        auto reduce = [&](int row, int cl) {
-            float2 part[DTC_MAX_S];
+        auto reduce = [&](int row, int j) {
+            float part[DTC_MAX_S];
+#pragma unroll
+            for (int s = 0; s < DTC_MAX_S; s++) part[s] = s < S ? recv[((size_t)s * own + row) * stride + j] : 0.0f;
+            float y = 0.0f;
 #pragma unroll
             for (int s = 0; s < DTC_MAX_S; s++)
-                part[s] = s < S ? *reinterpret_cast<const float2 *>(recv + ((size_t)s * own + row) * stride + cl)
-                                : make_float2(0.f, 0.f);
-            float h = 0.0f, l = 0.0f;
-#pragma unroll
-            for (int s = 0; s < DTC_MAX_S; s++)
-                if (s < S) {
-                    h = __fadd_rn(h, part[s].x);
-                    l = __fadd_rn(l, part[s].y);
-                }
-            return __fadd_rn(h, l);
+                if (s < S) y = __fadd_rn(y, part[s]);
+            return y;
         };
-        const int npairs = cw / 2;
-        for (int idx = tid; idx < per * npairs; idx += DTC_THREADS) {
-            const int ul = idx % per, j = idx / per;
-            const int c = c0 + 2 * j;
-            const int gi = c / a.Npg, bl = (c % a.Npg) / 2;
-            const int b = gi * a.G + bl;
+#pragma unroll
+        for (int k = 0; k < PF; k++) {
+            const int idx = tid + k * DTC_THREADS;
+            if (idx >= items) break;
+            const int ul = idx % per, j = idx / per, c = c0 + 2 * j;
+            const int gi = c / a.Npg, bl = (c % a.Npg) / 2, b = gi * a.G + bl;
             if (bl >= a.G || b >= R) continue;
             const int unit = r * per + ul;
             if constexpr (EPI == DTC_RESIDUAL) {
-                const float y = reduce(ul, 2 * j);
-                const size_t o = (size_t)b * a.p.n + tile * 128 + unit;
-                a.out[o] = __fmaf_rn(a.p.residual_scale, y, __ldcg(a.res + o));
+                a.out[(size_t)b * a.p.n + tile * 128 + unit] = __fmaf_rn(a.p.residual_scale, reduce(ul, j), pre_a[k]);
             } else if constexpr (EPI == DTC_GATE_UP) {
                 const float sc = scale[b];
-                const float yg = __fmul_rn(reduce(ul, 2 * j), sc), yu = __fmul_rn(reduce(per + ul, 2 * j), sc);
+                const float yg = __fmul_rn(reduce(ul, j), sc), yu = __fmul_rn(reduce(per + ul, j), sc);
                 a.out[(size_t)b * a.p.inner + tile * 128 + unit] = silu_mul(yg, yu);
             } else {
                 const int hd = a.p.head_dim, hf = hd / 2;
                 const float sc = scale[b];
-                const float ya = __fmul_rn(reduce(2 * ul, 2 * j), sc), yc = __fmul_rn(reduce(2 * ul + 1, 2 * j), sc);
-                const int head = tile * (128 / hd) + unit / hf;
-                qkv_store<bf16>(a.p, a.at, a.cosv, a.sinv, a.q, a.kc, a.vc, head * hf + unit % hf, b, ya, yc);
+                float ra = __fmul_rn(reduce(2 * ul, j), sc), rc = __fmul_rn(reduce(2 * ul + 1, j), sc);
+                const int head = tile * (128 / hd) + unit / hf, i = unit % hf;
+                const uint32_t pos = at_s[b], slot = a.p.slots > 1 ? at_s[R + b] : 0u;
+                if (pos >= a.p.capacity || slot >= a.p.slots) continue;  // a spare row stores nothing
+                const int heads = a.p.heads, kvh = a.p.kv_heads;
+                bf16 *kc = static_cast<bf16 *>(a.kc);
+                bf16 *vc = static_cast<bf16 *>(a.vc);
+                if (head >= heads + kvh) {
+                    const size_t to = (((size_t)slot * kvh + (head - heads - kvh)) * a.p.capacity + pos) * hd + i;
+                    vc[to] = from_f32<bf16>(ra);
+                    vc[to + hf] = from_f32<bf16>(rc);
+                    continue;
+                }
+                if (a.p.rope) {
+                    // x cos + rotate_half(x) sin, as qkv_store (gemv_qkv_rope.comp:85-90).
+                    const float co = pre_a[k], si = pre_b[k];
+                    const float na = __fmaf_rn(ra, co, -__fmul_rn(rc, si));
+                    const float nc = __fmaf_rn(rc, co, __fmul_rn(ra, si));
+                    ra = na;
+                    rc = nc;
+                }
+                if (head < heads) {
+                    const size_t to = ((size_t)b * heads + head) * hd + i;
+                    a.q[to] = ra;
+                    a.q[to + hf] = rc;
+                } else {
+                    const size_t to = (((size_t)slot * kvh + (head - heads)) * a.p.capacity + pos) * hd + i;
+                    kc[to] = from_f32<bf16>(ra);
+                    kc[to + hf] = from_f32<bf16>(rc);
+                }
             }
         }
     }
@@ -377,12 +429,15 @@ bool plan(int K, int NT, int S, int rows, bool norm, DtcPlan &pl) {
     pl.tmem_cols = cols;
     const uint32_t b_bytes = (uint32_t)pl.Npg * pl.Kc * 2;
     uint32_t smem = pl.a_bytes + b_bytes;
-    // Staging: NT x 128 rows x (cc + 4) f32, as wide as the cap allows, up to every column.
+    // Receive buffer: NT x 128 rows x (cc / 2 + 4) f32, as wide as the cap allows, up to every
+    // column, and narrow enough that a thread takes at most 8 epilogue items a round.
+    const int per = (NT == 1 && !norm ? 128 : NT == 2 ? 128 : 64) / S;
     int cc = ntot;
-    while ((uint32_t)(NT * 128 * (cc + 4) * 4) > DTC_SMEM_CAP) cc -= 16;
-    if (cc < 16) return false;
+    while (cc > 16 && ((uint32_t)(NT * 128 * (cc / 2 + 4) * 4) > DTC_SMEM_CAP || per * (cc / 2) > 8 * DTC_THREADS))
+        cc -= 16;
+    if ((uint32_t)(NT * 128 * (cc / 2 + 4) * 4) > DTC_SMEM_CAP || per * (cc / 2) > 8 * DTC_THREADS) return false;
     pl.cc = cc;
-    smem = std::max<uint32_t>(smem, (uint32_t)(NT * 128 * (cc + 4) * 4));
+    smem = std::max<uint32_t>(smem, (uint32_t)(NT * 128 * (cc / 2 + 4) * 4));
     smem = std::max<uint32_t>(smem, DTC_SMEM_MIN);
     pl.smem = smem + 1024;  // alignment slack
     return true;
