@@ -47,8 +47,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the prefill/GEMM side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--workload", default="decode", choices=["decode", "serve"],
-                    help="decode: config 2 (the headline line); serve: config 5, request-sharded serving")
+    ap.add_argument("--workload", default="decode", choices=["decode", "serve", "sweep"],
+                    help="decode: config 2 (the headline line); serve: config 5, request-sharded "
+                         "serving; sweep: decode step time by batch rows")
     ap.add_argument("--requests", type=int, default=2048, help="serve: requests over all GPUs")
     return ap.parse_args()
 
@@ -590,6 +591,54 @@ def run_serve(args, rank, world, local):
     return result
 
 
+def run_sweep(args, rank, world, local):
+    """Decode step time by batch rows (1, 16, 64, 128): one decoder per size (rows = slots,
+    capacity 2560, positions uniform 64-2048), `--steps` device-resident steps timed with CUDA
+    events on the runtime's stream after `--warmup`; the projections' family as the decoder picks
+    it (GEMVs below 16 rows, tcgen05 from 16)."""
+    if rank != 0:
+        return None
+    import torch
+
+    import __graft_entry__ as entry
+
+    pkg = entry.load_package()
+    from tgtts_v4_b200 import synthetic as syn
+
+    torch.cuda.set_device(local)
+    ctx = pkg.Context(local)
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=2560)
+    weights = syn.make_weights(cfg, seed=0, as_bits=True)
+    stream = stream_ctx(ctx)
+    out = {}
+    for rows in (1, 16, 64, 128):
+        dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
+        dec.load(weights)
+        pos = np.random.default_rng(2).integers(64, 2049, rows)
+        words = [int(v) for v in pos] + (list(range(rows)) if rows > 1 else [])
+        x = torch.randn(rows, cfg.hidden, device=f"cuda:{local}")
+        y = torch.empty_like(x)
+        for _ in range(args.warmup):
+            dec.step_device(words, x.data_ptr(), y.data_ptr())
+        ctx.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            dec.step_device(words, x.data_ptr(), y.data_ptr())
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        kv = sum(shape.cache_bytes(int(p), 2) for p in pos)
+        out[str(rows)] = {"ms": round(ms, 4), "tokens_per_s": round(rows / ms * 1e3, 1),
+                          "projections": "tcgen05" if dec.tensor else "gemv",
+                          "hbm_gbs": round((shape.weight_bytes(2) + kv) / (ms * 1e6), 1)}
+        dec.close()
+    ctx.close()
+    return {"workload": "decode step time by batch rows (0.5B-shaped bf16, positions U[64,2048])",
+            "steps": args.steps, "warmup": args.warmup, "by_rows": out}
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args.gpus)
@@ -597,6 +646,8 @@ def main():
         res = run_reference(args, rank, world, local)
     elif args.workload == "serve":
         res = run_serve(args, rank, world, local)
+    elif args.workload == "sweep":
+        res = run_sweep(args, rank, world, local)
     else:
         res = run_ours(args, rank, world, local)
     if rank == 0 and res is not None:
