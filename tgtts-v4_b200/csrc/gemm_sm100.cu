@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(256)
 
 // ---- tcgen05 bf16 ------------------------------------------------------------------------------
 
-constexpr int TC_BM = 128, TC_BK = 64, TC_STAGES = 4, TC_THREADS = 128;
+constexpr int TC_BM = 128, TC_BK = 64;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB per stage
 
 
@@ -68,40 +68,54 @@ template <int BN>
 struct TcLayout {
     static constexpr int B_BYTES = BN * TC_BK * 2;
     static constexpr int STAGE = TC_A_BYTES + B_BYTES;
-    static constexpr int BARRIERS = TC_STAGES * STAGE;  // offset of the mbarriers
-    static constexpr int SMEM = BARRIERS + 256 + 1024;  // + barriers + alignment slack
+    static constexpr int STAGES = (4 * (TC_A_BYTES + 256 * TC_BK * 2)) / STAGE;  // 192 KiB of stages
+    static constexpr int BARRIERS = STAGES * STAGE;                           // offset of the mbarriers
+    static constexpr int SMEM = BARRIERS + 256 + 1024;                        // + barriers + alignment slack
 };
 
 // Epilogues: C in f32, or (BN = 256, B's rows in gate_up_row's order) SiLU(gate) up in bf16, the
 // tile's columns 0..127 the gate and 128..255 the up of the same 128 outputs.
 enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1 };
 
+// Persistent: one block per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m fastest, so the
+// blocks at work share B tiles in L2). Warp 0 streams A and B tiles into a ring of stages with
+// TMA; warp 1 owns TMEM (two accumulators of BN columns) and issues the MMAs; warps 2-5 drain an
+// accumulator (tcgen05.ld) and store it while the MMAs fill the other, so that a tile's epilogue
+// overlaps the next tile's main loop.
+constexpr int TC_EPI_WARPS = 4;
+constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
+
 template <int BN, int EPI = TC_EPI_F32>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_PTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    void *__restrict__ Cout, int M, int N, int K, uint32_t *err) {
     using L = TcLayout<BN>;
+    constexpr int S = L::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base = smem_u32(smem);
     const uint32_t bars = base + L::BARRIERS;
     auto full = [&](int s) { return bars + 8u * s; };
-    auto empty = [&](int s) { return bars + 8u * (TC_STAGES + s); };
-    const uint32_t done = bars + 8u * (2 * TC_STAGES);
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::BARRIERS + 8 * (2 * TC_STAGES + 1));
+    auto empty = [&](int s) { return bars + 8u * (S + s); };
+    auto acc_full = [&](int a) { return bars + 8u * (2 * S + a); };
+    auto acc_empty = [&](int a) { return bars + 8u * (2 * S + 2 + a); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::BARRIERS + 8 * (2 * S + 4));
     __shared__ int gave_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * BN;
+    const int mt = (M + TC_BM - 1) / TC_BM, tiles = mt * (N / BN);
     const int nk = K / TC_BK;
 
     if (threadIdx.x == 0) {
         gave_up = 0;
-        for (int s = 0; s < TC_STAGES; s++) {
+        for (int s = 0; s < S; s++) {
             mbar_init(full(s), 1);
             mbar_init(empty(s), 1);
         }
-        mbar_init(done, 1);
+        for (int a = 0; a < 2; a++) {
+            mbar_init(acc_full(a), 1);
+            mbar_init(acc_empty(a), TC_EPI_WARPS * 32);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_a)) : "memory");
@@ -109,7 +123,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"((uint32_t)BN)
+                     "r"((uint32_t)(2 * BN))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -118,83 +132,111 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // Producer: stage kb of A and B into slot kb % STAGES once the MMAs have released it.
-        int issued = 0;
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % TC_STAGES;
-            mbar_wait(empty(s), ((kb / TC_STAGES) & 1) ^ 1, err, &gave_up);
-            mbar_arrive_expect_tx(full(s), L::STAGE);
-            tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
-            tma_load_2d(base + s * L::STAGE + TC_A_BYTES, &map_b, kb * TC_BK, n0, full(s));
-            issued = kb + 1;
-        }
-        // Every copy this thread started has landed before the block can end.
-        for (int kb = issued > TC_STAGES ? issued - TC_STAGES : 0; kb < issued; kb++)
-            mbar_wait(full(kb % TC_STAGES), (kb / TC_STAGES) & 1, err, &gave_up);
-    } else if (warp == 1 && lane == 0) {
-        // MMA issuer: four K = 16 steps per stage, accumulating after the first.
-        constexpr uint32_t idesc = bf16_idesc(TC_BM, BN);
-        for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % TC_STAGES;
-            mbar_wait(full(s), (kb / TC_STAGES) & 1, err, &gave_up);
-            tc_fence_after();
-            const uint32_t a_addr = base + s * L::STAGE;
-            const uint32_t b_addr = a_addr + TC_A_BYTES;
-#pragma unroll
-            for (int k = 0; k < TC_BK / 16; k++) {
-                tc_mma(tmem, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
-                       (kb > 0 || k > 0) ? 1u : 0u);
-            }
-            tc_commit(empty(s));
-        }
-        tc_commit(done);
-    }
-    __syncwarp();
-
-    // Epilogue: row m0 + 32 warp + lane, BN columns from TMEM, 16 at a time.
-    mbar_wait(done, 0, err, &gave_up);
-    tc_fence_after();
-    const int row = m0 + warp * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-    if constexpr (EPI == TC_EPI_SILU) {
-        static_assert(BN == 256, "the SiLU epilogue pairs columns c and c + 128 of a 256-wide tile");
-        bf16 *out = static_cast<bf16 *>(Cout);
-        const int inner = N / 2;
-#pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 16) {
-            float g[16], u[16];
-            tmem_ld16(lane_base + c0, g);
-            tmem_ld16(lane_base + 128 + c0, u);
-            if (row < M) {
-                uint32_t packed[8];
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const __nv_bfloat162 v = __floats2bfloat162_rn(silu_mul(g[2 * i], u[2 * i]), silu_mul(g[2 * i + 1], u[2 * i + 1]));
-                    packed[i] = *reinterpret_cast<const uint32_t *>(&v);
+    if (warp == 0) {
+        if (lane == 0) {
+            // Producer: k-block g (over all this block's tiles) into stage g % S once its MMAs
+            // have released it.
+            int g = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+                const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+                for (int kb = 0; kb < nk; kb++, g++) {
+                    const int s = g % S;
+                    mbar_wait(empty(s), ((g / S) & 1) ^ 1, err, &gave_up);
+                    mbar_arrive_expect_tx(full(s), L::STAGE);
+                    tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
+                    tma_load_2d(base + s * L::STAGE + TC_A_BYTES, &map_b, kb * TC_BK, n0, full(s));
                 }
-                uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)row * inner + n0 / 2 + c0);
-                dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+            }
+            // Every copy this thread started has landed before the block can end.
+            for (int h = g > S ? g - S : 0; h < g; h++) mbar_wait(full(h % S), (h / S) & 1, err, &gave_up);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // MMA issuer: tile i into accumulator i % 2 once the epilogue has drained it.
+            constexpr uint32_t idesc = bf16_idesc(TC_BM, BN);
+            int g = 0, i = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
+                const int acc = i & 1;
+                mbar_wait(acc_empty(acc), ((i >> 1) & 1) ^ 1, err, &gave_up);
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(acc * BN);
+                for (int kb = 0; kb < nk; kb++, g++) {
+                    const int s = g % S;
+                    mbar_wait(full(s), (g / S) & 1, err, &gave_up);
+                    tc_fence_after();
+                    const uint32_t a_addr = base + s * L::STAGE;
+                    const uint32_t b_addr = a_addr + TC_A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < TC_BK / 16; k++)
+                        tc_mma(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
+                               (kb > 0 || k > 0) ? 1u : 0u);
+                    tc_commit(empty(s));
+                }
+                tc_commit(acc_full(acc));
             }
         }
     } else {
-        float *C = static_cast<float *>(Cout);
+        // Epilogue: warp w drains TMEM lanes (w % 4) * 32 .. + 31, i.e. rows m0 + that of the tile.
+        const int q = warp & 3;
+        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        int i = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
+            const int acc = i & 1;
+            const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+            mbar_wait(acc_full(acc), (i >> 1) & 1, err, &gave_up);
+            tc_fence_after();
+            const int row = m0 + q * 32 + lane;
+            const uint32_t lane_base = tmem + lane_off + (uint32_t)(acc * BN);
+            if constexpr (EPI == TC_EPI_SILU) {
+                static_assert(BN == 256, "the SiLU epilogue pairs columns c and c + 128 of a 256-wide tile");
+                bf16 *out = static_cast<bf16 *>(Cout);
+                const int inner = N / 2;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-            float v[16];
-            tmem_ld16(lane_base + c0, v);
-            if (row < M && n0 + c0 < N) {
-                float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+                for (int c0 = 0; c0 < 128; c0 += 16) {
+                    uint32_t g[16], u[16];
+                    tmem_ld16_nowait(lane_base + c0, g);
+                    tmem_ld16_nowait(lane_base + 128 + c0, u);
+                    tmem_wait_ld();
+                    if (row < M) {
+                        uint32_t packed[8];
 #pragma unroll
-                for (int i = 0; i < 4; i++) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                        for (int e = 0; e < 8; e++) {
+                            const __nv_bfloat162 v = __floats2bfloat162_rn(
+                                silu_mul(__uint_as_float(g[2 * e]), __uint_as_float(u[2 * e])),
+                                silu_mul(__uint_as_float(g[2 * e + 1]), __uint_as_float(u[2 * e + 1])));
+                            packed[e] = *reinterpret_cast<const uint32_t *>(&v);
+                        }
+                        uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)row * inner + n0 / 2 + c0);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    }
+                }
+            } else {
+                float *C = static_cast<float *>(Cout);
+#pragma unroll 1
+                for (int c0 = 0; c0 < BN; c0 += 32) {
+                    uint32_t v[2][16];
+                    tmem_ld16_nowait(lane_base + c0, v[0]);
+                    tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
+                    tmem_wait_ld();
+                    if (row < M) {
+                        float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+#pragma unroll
+                        for (int e = 0; e < 8; e++)
+                            dst[e] = make_float4(__uint_as_float(v[e / 4][4 * (e % 4)]), __uint_as_float(v[e / 4][4 * (e % 4) + 1]),
+                                                 __uint_as_float(v[e / 4][4 * (e % 4) + 2]), __uint_as_float(v[e / 4][4 * (e % 4) + 3]));
+                    }
+                }
             }
+            // The accumulator is drained: the MMAs may fill it again.
+            tc_fence_before();
+            mbar_arrive(acc_empty(acc));
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)BN)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
                      : "memory");
     }
 }
@@ -210,8 +252,11 @@ static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N
     auto kern = gemm_tc_kernel<BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<BN>::SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid(N / BN, (M + TC_BM - 1) / TC_BM);
-    kern<<<grid, TC_THREADS, TcLayout<BN>::SMEM, s>>>(ma, mb, c, M, N, K, err);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN);
+    kern<<<tiles < sms ? tiles : sms, TC_PTHREADS, TcLayout<BN>::SMEM, s>>>(ma, mb, c, M, N, K, err);
     return cudaGetLastError();
 }
 

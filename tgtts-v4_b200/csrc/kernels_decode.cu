@@ -59,7 +59,6 @@ template <typename T, int NB>
 __device__ void stage_rows(const float *__restrict__ x, const float *gs, bool norm, int rows, int b0, int k,
                            float eps, float *xs, float *raw, float *scales) {
     const int quads = k / 4;
-    float *dst = norm ? raw : xs;
     for (int i = threadIdx.x; i < NB * quads; i += blockDim.x) {
         const int b = i / quads, c = i % quads;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -465,7 +464,7 @@ __global__ void __launch_bounds__(128)
     attention_split_kernel(tg_params p, const float *__restrict__ q, const T *__restrict__ kc,
                            const T *__restrict__ vc, const uint32_t *__restrict__ at,
                            float *__restrict__ po, float *__restrict__ pml) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     pdl_launch_dependents();
     uint32_t pos, slot;
     const int c = blockIdx.x, kv = blockIdx.y, b = blockIdx.z;
@@ -526,7 +525,7 @@ __global__ void __launch_bounds__(128)
                             const T *__restrict__ vc, const uint32_t *__restrict__ at, float *__restrict__ out) {
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     pdl_launch_dependents();
     const int r = (int)cluster.block_rank(), kv = blockIdx.y, b = blockIdx.z;
     const int hd = p.head_dim, heads = p.heads, group = heads / p.kv_heads;
@@ -629,10 +628,6 @@ TG_DEVICE uint32_t ld_acquire(const uint32_t *p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-
-TG_DEVICE void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 // Waits on an mbarrier phase, giving up at the time limit or when another block aborted.

@@ -188,6 +188,10 @@ TG_DEVICE void mbar_fence_init() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+TG_DEVICE void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 TG_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
