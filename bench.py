@@ -47,9 +47,11 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the prefill/GEMM side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--workload", default="decode", choices=["decode", "serve", "sweep"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "serve", "sweep", "gemm"],
                     help="decode: config 2 (the headline line); serve: config 5, request-sharded "
-                         "serving; sweep: decode step time by batch rows")
+                         "serving; sweep: decode step time by batch rows; gemm: config 4's four "
+                         "projection GEMMs alone")
+    ap.add_argument("--rows", type=int, default=32768, help="gemm: rows (M)")
     ap.add_argument("--requests", type=int, default=2048, help="serve: requests over all GPUs")
     return ap.parse_args()
 
@@ -639,6 +641,50 @@ def run_sweep(args, rank, world, local):
             "steps": args.steps, "warmup": args.warmup, "by_rows": out}
 
 
+def run_gemm(args, rank, world, local):
+    """Config 4's projection GEMMs, each alone: C = A B^T with A [rows][K] bf16 activations and B
+    the layer's [N][K] bf16 weights (q/k/v 1280 x 1024, o 1024 x 1024, gate/up 8192 x 1024 with
+    the SiLU epilogue, down 1024 x 4096), `--steps` launches in one program after `--warmup`,
+    CUDA events at its ends; operands larger than L2 at the default 32768 rows."""
+    if rank != 0:
+        return None
+    import torch
+
+    import __graft_entry__ as entry
+
+    pkg = entry.load_package()
+    from tgtts_v4_b200 import synthetic as syn
+
+    torch.cuda.set_device(local)
+    ctx = pkg.Context(local)
+    _, tc, peak_kind = peaks()
+    shape = syn.shape_of(syn.S05B, capacity=64)
+    M = args.rows
+    out = {}
+    for name, kernel, N, K in (("qkv_proj", "gemm", 1280, 1024), ("o_proj", "gemm", 1024, 1024),
+                               ("gate_up_proj", "gemm_silu", 8192, 1024), ("down_proj", "gemm", 1024, 4096)):
+        a, b = pkg.Memory(ctx, M * K * 2), pkg.Memory(ctx, N * K * 2)
+        a.fill(0x3F803F80)  # bf16 1.0 pairs: finite operands, the values do not change the time
+        b.fill(0x3F803F80)
+        cb = M * N * 4 if kernel == "gemm" else M * (N // 2) * 2
+        c = pkg.Memory(ctx, cb)
+        p = pkg.params(shape, "bf16", rows=M, m=M, n=N, k=K)
+        warm = pkg.Program(ctx, [(kernel, p, [(a, 0, a.nbytes), (b, 0, b.nbytes), (c, 0, cb)], name)] * max(1, args.warmup))
+        warm.run()
+        prog = pkg.Program(ctx, [(kernel, p, [(a, 0, a.nbytes), (b, 0, b.nbytes), (c, 0, cb)], name)] * args.steps)
+        prog.run()
+        ns = prog.elapsed_ns() / args.steps
+        tflops = 2.0 * M * N * K / ns / 1e3
+        out[name] = {"m": M, "n": N, "k": K, "us": round(ns / 1e3, 2), "tflops": round(tflops, 1),
+                     "frac": round(tflops / tc, 4)}
+        warm.close()
+        prog.close()
+        del a, b, c
+    ctx.close()
+    return {"workload": "config 4 projection GEMMs alone (tcgen05, persistent)", "steps": args.steps,
+            "warmup": args.warmup, "peak_tflops": tc, "peak_source": peak_kind, "by_projection": out}
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args.gpus)
@@ -648,6 +694,8 @@ def main():
         res = run_serve(args, rank, world, local)
     elif args.workload == "sweep":
         res = run_sweep(args, rank, world, local)
+    elif args.workload == "gemm":
+        res = run_gemm(args, rank, world, local)
     else:
         res = run_ours(args, rank, world, local)
     if rank == 0 and res is not None:

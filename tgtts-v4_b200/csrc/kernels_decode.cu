@@ -1078,7 +1078,9 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 
 template <typename F>
 static cudaError_t with_smem(F kernel, size_t bytes) {
-    if (bytes <= 48 * 1024) return cudaSuccess;
+    // Past 48 KiB of shared memory a block needs the opt-in, static arrays included: opt in well
+    // before.
+    if (bytes <= 32 * 1024) return cudaSuccess;
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
@@ -1099,6 +1101,10 @@ static int device_sms() {
 
 // The shared memory a decode GEMV block may take, weights and staged vectors together.
 constexpr size_t GEMV_SMEM_LIMIT = 200 * 1024;
+#ifndef TG_GEMV_SMEM_SHARE
+#define TG_GEMV_SMEM_SHARE (96 * 1024)
+#endif
+constexpr size_t GEMV_SMEM_SHARE = TG_GEMV_SMEM_SHARE;
 
 // Launches gemv_stream_kernel over `units` units of R rows of k columns: one block per SM, each
 // taking an equal share, or more blocks when a share's weights would not fit in shared memory.
@@ -1114,7 +1120,9 @@ static cudaError_t launch_gemv(GemvArgs a, cudaStream_t s) {
     if (xs_bytes + R * row_bytes > GEMV_SMEM_LIMIT) return cudaErrorInvalidValue;
     int blocks = std::min(a.units, device_sms());
     a.per_block = (a.units + blocks - 1) / blocks;
-    while ((size_t)a.per_block * R * row_bytes + xs_bytes > GEMV_SMEM_LIMIT) {
+    // Slices small enough that two blocks fit an SM: the next kernel's blocks can then start (and
+    // stream their weights) beside this kernel's last ones.
+    while (a.per_block > 1 && (size_t)a.per_block * R * row_bytes + xs_bytes > GEMV_SMEM_SHARE) {
         a.per_block = (a.per_block + 1) / 2;
     }
     blocks = (a.units + a.per_block - 1) / a.per_block;
