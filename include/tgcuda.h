@@ -138,7 +138,11 @@ typedef enum {
      * (gate rows i..i+127, then up rows i..i+127, i = 0, 128, ...) -> out bf16 [m][inner] =
      * SiLU(gate) up of a b^T, in the tcgen05 GEMM's epilogue     gemm.mlir + silu_mul_rows.comp */
     TG_KERNEL_GEMM_SILU = 14,
-    TG_KERNEL_COUNT = 15
+    /* ATTENTION_ROWS on tcgen05, for bf16 and head_dim 64: the same bindings and results within
+     * rounding; rows a multiple of 128, each 128-row tile one run's rows (one slot; a tile that
+     * mixes slots is refused at run time with the kernel error word). attention_rows.comp */
+    TG_KERNEL_ATTENTION_ROWS_TC = 15,
+    TG_KERNEL_COUNT = 16
 } tg_kernel_id;
 
 /* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the
@@ -291,7 +295,7 @@ int tg_prefill_destroy(tg_prefill *p);
 int tg_prefill_run(tg_prefill *p, uint32_t start, uint32_t slot, const float *x, uint32_t len,
                    float *out);
 /* Several runs at once, each in its own slot, rows packed in order (each run's rows start on a
- * multiple of 64 inside the launch): the batched prefill of BASELINE config 4. */
+ * multiple of 128 inside the launch): the batched prefill of BASELINE config 4. */
 typedef struct {
     uint32_t start, len, slot;
 } tg_run;

@@ -23,15 +23,16 @@ def _filled(pkg, ctx, syn, rows, layers, capacity, seed):
     rng = np.random.default_rng(seed)
     lens = [int(v) for v in rng.integers(1, capacity // 2, rows)]
     prompts = [rng.standard_normal((n, cfg.hidden), dtype=np.float32) for n in lens]
-    # All prompts at once, as the server admits them (runs of up to 1024 rows a launch).
+    # All prompts at once, as the server admits them (runs of up to 1024 rows a launch, each
+    # starting on a multiple of 128 rows).
     runs, xs, used = [], [], 0
     for s, (n, x) in enumerate(zip(lens, prompts)):
-        if used + n + 64 > 1024:
+        if used + n + 128 > 1024:
             pre.run_batch(runs, np.concatenate(xs))
             runs, xs, used = [], [], 0
         runs.append((0, n, s))
         xs.append(x)
-        used += (n + 63) // 64 * 64
+        used += (n + 127) // 128 * 128
     pre.run_batch(runs, np.concatenate(xs))
     return cfg, shape, w, dec, pre, lens, prompts
 

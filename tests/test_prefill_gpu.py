@@ -99,3 +99,41 @@ def test_config2_full_stack_prefill_512_and_decode(pkg, ctx, syn):
         hr = ref.decode_step([(512 + t, 0)], hr[None])[0]
         m, _, cos = distance(h, hr)
         assert m <= 2e-2 and cos >= 0.9999, (t, m, cos)
+
+
+def test_tcgen05_attention_matches_the_mma_sync_kernel_within_rounding(pkg, ctx, syn):
+    """The prefill attention on tcgen05 (bf16, head_dim 64) against the mma.sync kernel of the
+    kernel table on the same q and cache: runs of 128-aligned rows, causal, spare rows between."""
+    import numpy as np
+
+    from conftest import distance
+
+    shape = pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=1, capacity=512)
+    rows, heads, hd, kvh, cap, slots = 512, 16, 64, 2, 512, 3
+    rng = np.random.default_rng(8)
+    q = syn.bf16_bits(rng.standard_normal((rows, heads, hd), dtype=np.float32))
+    k = syn.bf16_bits(rng.standard_normal((slots, kvh, cap, hd), dtype=np.float32))
+    v = syn.bf16_bits(rng.standard_normal((slots, kvh, cap, hd), dtype=np.float32))
+    # Runs: 200 rows of slot 1 from position 37, 128 rows of slot 0 from 0, 100 rows of slot 2 from 400.
+    words = np.full(2 * rows, 0xFFFFFFFF, np.uint32)
+    for first, n, start, slot in ((0, 200, 37, 1), (256, 128, 0, 0), (384, 100, 400, 2)):
+        words[first:first + n] = np.arange(start, start + n)
+        words[rows + first:rows + first + n] = slot
+    def mem(a):
+        m = pkg.Memory(ctx, a.nbytes)
+        m.write(np.ascontiguousarray(a))
+        return m
+
+    mw, mq, mk, mv = mem(words), mem(q), mem(k), mem(v)
+    p = pkg.params(shape, "bf16", rows=rows, slots=slots)
+    outs = []
+    for kernel in ("attention_rows", "attention_rows_tc"):
+        o = pkg.Memory(ctx, rows * heads * hd * 2)
+        o.fill(0)
+        pkg.dispatch_once(ctx, kernel, p, [(mw, 0, words.nbytes), (mq, 0, q.nbytes), (mk, 0, k.nbytes),
+                                           (mv, 0, v.nbytes), (o, 0, rows * heads * hd * 2)])
+        outs.append(syn.bf16_to_f32(o.read(np.uint16, rows * heads * hd)).reshape(rows, heads, hd))
+    live = words[:rows] != 0xFFFFFFFF
+    m, rel, cos = distance(outs[1][live], outs[0][live])
+    assert rel < 1e-2 and cos > 0.9999, (m, rel, cos)
+    assert np.all(outs[1][~live] == 0)  # spare rows are not written

@@ -634,7 +634,7 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
         push(v, TG_KERNEL_ROPE_ROWS, base, "rope_rows",
              {{p.words.ptr(), words}, {p.qkv.ptr(), R * W * F}, {d.cos.ptr(), table}, {d.sin.ptr(), table},
               {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
-        push(v, TG_KERNEL_ATTENTION_ROWS, base, "attention_rows",
+        push(v, attention_tc_supported(base) ? TG_KERNEL_ATTENTION_ROWS_TC : TG_KERNEL_ATTENTION_ROWS, base, "attention_rows",
              {{p.words.ptr(), words}, {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {p.att.ptr(), R * A * T}});
         gemm("o_proj", p.att.ptr(), d.w(o.o), p.proj.ptr(), H, A);
@@ -723,7 +723,7 @@ static int program_for(tg_prefill *p, uint32_t rows, Program **out) {
     return TG_OK;
 }
 
-// Lays `runs` out as rows of one launch: each run's rows start on a multiple of PREFILL_TILE
+// Lays `runs` out as rows of one launch: each run's rows start on a multiple of RUN_ALIGN
 // (padding rows between are spare). Fills the words (positions, then slots, at the bucket's
 // stride) and returns the rows used and each run's first row.
 static int layout_runs(tg_prefill *p, const tg_run *runs, uint32_t n_runs, uint32_t &used,
@@ -738,7 +738,7 @@ static int layout_runs(tg_prefill *p, const tg_run *runs, uint32_t n_runs, uint3
             return fail(TG_ESHAPE, "run %u: %u positions from %u in slot %u of %u in a cache of %u", i, r.len, r.start,
                         r.slot, p->d->slots, s.capacity);
         slot_taken[r.slot] = true;
-        row = (row + PREFILL_TILE - 1) / PREFILL_TILE * PREFILL_TILE;
+        row = (row + RUN_ALIGN - 1) / RUN_ALIGN * RUN_ALIGN;
         first.push_back(row);
         row += r.len;
         if (row > p->max_rows) return fail(TG_ESHAPE, "runs of %u rows in a prefill of at most %u", row, p->max_rows);

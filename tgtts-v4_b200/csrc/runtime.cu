@@ -118,6 +118,7 @@ static int needs(const Launch &l, std::vector<Need> &out) {
                    {"q", rows * attn * T}, {"k_cache", cache}, {"v_cache", cache}};
             break;
         case TG_KERNEL_ATTENTION_ROWS:
+        case TG_KERNEL_ATTENTION_ROWS_TC:
             out = {{"at", words}, {"q", rows * attn * T}, {"k_cache", cache}, {"v_cache", cache},
                    {"out", rows * attn * T}};
             break;
@@ -146,7 +147,7 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu"};
+        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
 }
 
@@ -184,6 +185,11 @@ static int check_shape(const Launch &l) {
             break;
         case TG_KERNEL_SILU_MUL_ROWS:
             if (p.inner == 0) return fail(TG_ESHAPE, "silu_mul_rows: inner 0");
+            break;
+        case TG_KERNEL_ATTENTION_ROWS_TC:
+            if (!heads_ok() || !attention_tc_supported(p))
+                return fail(TG_ESHAPE, "attention_rows_tc: bf16, head_dim 64 and rows a multiple of 128 (%u rows, hd %u)",
+                            p.rows, p.head_dim);
             break;
         case TG_KERNEL_STREAM_READ:
             if (p.k % 4 || p.n < 1) return fail(TG_ESHAPE, "stream_read: %u words", p.k);
@@ -267,6 +273,7 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case KERNEL_DTC_QKV_ROPE: e = launch_dtc_qkv_rope(p, F(0), F(1), b[2], F(3), F(4), U(5), F(6), b[7], b[8], err, s); break;
         case KERNEL_DTC_GATE_UP: e = launch_dtc_gate_up(p, F(0), F(1), b[2], F(3), err, s); break;
         case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
+        case TG_KERNEL_ATTENTION_ROWS_TC: e = launch_attention_rows_tc(p, U(0), b[1], b[2], b[3], b[4], err, s); break;
         default: return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
     if (e != cudaSuccess)

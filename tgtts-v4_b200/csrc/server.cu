@@ -123,7 +123,7 @@ extern "C" int tg_server_start(tg_server *s, const tg_request *reqs, uint32_t n,
             if (launched[i]) continue;
             const Piece &pc = pieces[i];
             if (slot_in[pc.run.slot]) break;  // a later piece of a slot in this launch waits
-            const uint32_t start = (rows + PREFILL_TILE - 1) / PREFILL_TILE * PREFILL_TILE;
+            const uint32_t start = (rows + RUN_ALIGN - 1) / RUN_ALIGN * RUN_ALIGN;
             if (start + pc.run.len > s->p->max_rows) break;
             slot_in[pc.run.slot] = true;
             rows = start + pc.run.len;

@@ -69,6 +69,7 @@ constexpr uint32_t KERNEL_DECODE_STEP = 1000;  // the persistent decode step (De
 constexpr uint32_t KERNEL_DTC_QKV_ROPE = 1001;
 constexpr uint32_t KERNEL_DTC_GATE_UP = 1002;
 constexpr uint32_t KERNEL_DTC_RESIDUAL = 1003;
+
 // Decoders of at least this many rows run their projections on tcgen05 (every bucket of them).
 constexpr uint32_t DTC_MIN_ROWS = 16;
 
@@ -167,8 +168,13 @@ cudaError_t launch_dtc_residual(const tg_params &p, const float *x, const void *
 cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s);
 // The decode constants: positions per attention chunk.
 constexpr uint32_t ATTN_CHUNK = 64;
-// The rows of a prefill attention tile; each run starts on a multiple of it.
+// The rows of a prefill attention tile (the CUDA-core and mma.sync kernels).
 constexpr uint32_t PREFILL_TILE = 64;
+// Each run of a prefill launch starts on a multiple of this many rows (the tcgen05 attention's tile).
+constexpr uint32_t RUN_ALIGN = 128;
+bool attention_tc_supported(const tg_params &p);
+cudaError_t launch_attention_rows_tc(const tg_params &p, const uint32_t *at, const void *q, const void *kc,
+                                     const void *vc, void *out, uint32_t *err, cudaStream_t s);
 // gate_up's rows are gate and up interleaved in blocks of GU_BLOCK: gate rows i .. i + 127 then up
 // rows i .. i + 127, for i = 0, 128, ... (so that a 256-wide GEMM tile holds matching gate and up
 // columns, and its epilogue can take SiLU(gate) up).
