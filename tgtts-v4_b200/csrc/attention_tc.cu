@@ -2,28 +2,31 @@
 // dimension of 64: flash attention with both products on the tensor cores and their accumulators
 // in TMEM.
 //
-// Block (t, h) takes query rows [128 t, 128 t + 128) of the launch (one run's rows: runs start on
-// multiples of 128) for query head h, and walks its slot's cache from position 0 to the tile's last
-// position in tiles of 128 keys. Six warps:
-//   warp 0   TMA: the Q tile once, then K and V tiles into two stages (128-byte swizzle, no
-//            multicast);
-//   warp 1   TMEM (two S buffers of 128 columns and O's 64) and the MMAs: S_j = Q K_j^T
-//            (M = 128, N = 128, K = 64) into S[j % 2], one tile ahead of the softmax, and
-//            PV_j = P_j V_j (M = 128, N = 64, K = 128; V read MN-major) into O;
-//   warps 2-5 a thread to a query row: S_j from TMEM, the causal mask, the online softmax
-//            (base 2, the scale folded in), P_j as bf16 into shared memory as PV's A operand,
-//            and PV_{j-1} from TMEM folded into the row's f32 output in registers.
-// Every wait on an mbarrier is bounded (the context's error word, then the block runs out).
+// Block (t, g) takes query rows [128 t, 128 t + 128) of the launch (one run's rows: runs start on
+// multiples of 128) for query heads 2g and 2g + 1 (one KV head's), and walks its slot's cache from
+// position 0 to the tile's last position in tiles of 128 keys, shared by the two heads. Ten warps:
+//   warp 0     TMA: the two Q tiles once, then K and V tiles into two stages (128-byte swizzle,
+//              no multicast);
+//   warp 1     TMEM (per head: S, 128 columns, and O, 64) and the MMAs: S_j = Q K_j^T
+//              (M = 128, N = 128, K = 64) and PV_j = P_j V_j (M = 128, N = 64, K = 128, V read
+//              MN-major), each head's S_{j+1} issued as soon as its PV_j is;
+//   warps 2-5  head 2g, warps 6-9 head 2g + 1: a thread to a query row: S_j from TMEM (the mask,
+//              the row maximum, then the base-2 exponentials with the scale folded in), P_j as
+//              bf16 into shared memory as PV's A operand, and PV_{j-1} from TMEM folded into the
+//              row's f32 output in registers.
+// The two heads' softmax warps run while the other head's MMAs do. Every wait on an mbarrier is
+// bounded (the context's error word, then the block runs out).
 #include "tc_common.cuh"
 
 namespace tg {
 
 namespace {
 
-constexpr int FA_THREADS = 192;
-constexpr uint32_t FA_TILE = 128 * 64 * 2;                    // a 128-row x 64-column bf16 box
-constexpr uint32_t FA_Q = 0, FA_K = FA_TILE, FA_V = 3 * FA_TILE, FA_P = 5 * FA_TILE;  // P: 2 boxes
-constexpr uint32_t FA_SMEM = 120 * 1024 + 1024;               // one block to an SM (TMEM: 512 columns)
+constexpr int FA_THREADS = 320;
+constexpr uint32_t FA_TILE = 128 * 64 * 2;  // a 128-row x 64-column bf16 box
+// Shared memory: Q of the two heads, K and V in two stages, P of the two heads (two boxes each).
+constexpr uint32_t FA_Q = 0, FA_K = 2 * FA_TILE, FA_V = 4 * FA_TILE, FA_P = 6 * FA_TILE;
+constexpr uint32_t FA_SMEM = 10 * FA_TILE + 1024;
 
 // 2^x by the hardware's approximate base-2 exponential (PTX ex2.approx.ftz.f32: relative error
 // about 2^-22, far below the bf16 rounding the probabilities take next); 2^-inf = 0.
@@ -37,9 +40,8 @@ TG_DEVICE uint32_t fa_sw128(int n, int c) {
     return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4));
 }
 
-// A K-major operand with 128-byte rows in the 128-byte swizzle (sw128_desc), or the same bytes read
-// MN-major: V's tile [keys][64] is B = V^T with N = 64 along a row and K = keys down the rows, in
-// atoms of 8 keys x 128 bytes, 1024 bytes apart along K.
+// The same bytes as a K-major SW128 tile read MN-major: V's tile [keys][64] is B = V^T with N = 64
+// along a row and K = keys down the rows, in atoms of 8 keys x 128 bytes, 1024 bytes apart along K.
 TG_DEVICE uint64_t fa_desc_mn(uint32_t addr) {
     return (uint64_t)((addr >> 4) & 0x3fff) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
@@ -54,14 +56,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base = smem_u32(smem);
-    __shared__ __align__(8) uint64_t bq, bkv_full[2], bkv_empty[2], bs_full[2], bs_empty[2], bp_full, bo_full, bo_empty;
+    __shared__ __align__(8) uint64_t bq, bkv_full[2], bkv_empty[2];
+    __shared__ __align__(8) uint64_t bs_full[2], bs_empty[2], bp_full[2], bo_full[2], bo_empty[2];  // by head
     __shared__ uint32_t tmem_slot, t_last, t_slot, t_slot_max;
     __shared__ int gave_up;
     __shared__ int pos_s[128];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int tile = gridDim.x - 1 - blockIdx.x;  // the latest rows, the longest walks, first
-    const int head = blockIdx.y, heads = p.heads, kvh = p.kv_heads, kv = head / (heads / kvh);
+    const int head0 = 2 * blockIdx.y, heads = p.heads, kvh = p.kv_heads, kv = head0 / (heads / kvh);
     const int r0 = tile * 128;
     auto B = [](uint64_t &b) { return smem_u32(&b); };
 
@@ -76,10 +79,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             mbar_init(B(bkv_empty[i]), 1);
             mbar_init(B(bs_full[i]), 1);
             mbar_init(B(bs_empty[i]), 128);
+            mbar_init(B(bp_full[i]), 128);
+            mbar_init(B(bo_full[i]), 1);
+            mbar_init(B(bo_empty[i]), 128);
         }
-        mbar_init(B(bp_full), 128);
-        mbar_init(B(bo_full), 1);
-        mbar_init(B(bo_empty), 128);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -109,11 +112,15 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const bool mixed = t_slot != 0xffffffffu && t_slot != t_slot_max;
     if (mixed && tid == 0) atomicExch(err, ERR_BAD_INDEX);
     const int n = (t_slot == 0xffffffffu || mixed) ? 0 : (int)(t_last / 128 + 1);  // key tiles
+    // TMEM columns: head h's S at 256 h, its O at 256 h + 128.
+    auto s_col = [](int h) { return (uint32_t)(256 * h); };
+    auto o_col = [](int h) { return (uint32_t)(256 * h + 128); };
 
     if (warp == 0) {
         if (lane == 0 && n > 0) {
-            mbar_arrive_expect_tx(B(bq), FA_TILE);
-            tma_load_2d(base + FA_Q, &qmap, head * 64, r0, B(bq));
+            mbar_arrive_expect_tx(B(bq), 2 * FA_TILE);
+            tma_load_2d(base + FA_Q, &qmap, head0 * 64, r0, B(bq));
+            tma_load_2d(base + FA_Q + FA_TILE, &qmap, (head0 + 1) * 64, r0, B(bq));
             const int row0 = (int)((t_slot * (uint32_t)kvh + kv) * p.capacity);
             for (int j = 0; j < n; j++) {
                 const int b = j & 1;
@@ -130,36 +137,41 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             constexpr uint32_t idesc_s = bf16_idesc(128, 128);
             constexpr uint32_t idesc_o = bf16_idesc(128, 64) | (1u << 16);  // B (V) MN-major
             mbar_wait(B(bq), 0, err, &gave_up);
-            auto issue_s = [&](int j) {
-                const int b = j & 1;
-                mbar_wait(B(bkv_full[b]), (j >> 1) & 1, err, &gave_up);
-                mbar_wait(B(bs_empty[b]), ((j >> 1) & 1) ^ 1, err, &gave_up);
+            auto issue_s = [&](int j, int h) {  // S_j of head h (K_j landed, S_{j-1} read)
+                if (j > 0) mbar_wait(B(bs_empty[h]), (j - 1) & 1, err, &gave_up);
                 tc_fence_after();
+                const uint32_t kt = base + FA_K + (j & 1) * FA_TILE;
 #pragma unroll
                 for (int k = 0; k < 4; k++)
-                    tc_mma(tmem + (uint32_t)(b * 128), sw128_desc(base + FA_Q + k * 32),
-                           sw128_desc(base + FA_K + b * FA_TILE + k * 32), idesc_s, k > 0 ? 1u : 0u);
-                tc_commit(B(bs_full[b]));
+                    tc_mma(tmem + s_col(h), sw128_desc(base + FA_Q + h * FA_TILE + k * 32), sw128_desc(kt + k * 32),
+                           idesc_s, k > 0 ? 1u : 0u);
+                tc_commit(B(bs_full[h]));
             };
-            issue_s(0);
+            mbar_wait(B(bkv_full[0]), 0, err, &gave_up);
+            issue_s(0, 0);
+            issue_s(0, 1);
             for (int j = 0; j < n; j++) {
-                if (j + 1 < n) issue_s(j + 1);
-                mbar_wait(B(bp_full), j & 1, err, &gave_up);
-                if (j > 0) mbar_wait(B(bo_empty), (j - 1) & 1, err, &gave_up);
-                tc_fence_after();
+                if (j + 1 < n) mbar_wait(B(bkv_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, err, &gave_up);
                 const uint32_t v = base + FA_V + (j & 1) * FA_TILE;
+                for (int h = 0; h < 2; h++) {
+                    mbar_wait(B(bp_full[h]), j & 1, err, &gave_up);
+                    if (j > 0) mbar_wait(B(bo_empty[h]), (j - 1) & 1, err, &gave_up);
+                    tc_fence_after();
 #pragma unroll
-                for (int kk = 0; kk < 8; kk++)
-                    tc_mma(tmem + 256u, sw128_desc(base + FA_P + (kk / 4) * FA_TILE + (kk % 4) * 32),
-                           fa_desc_mn(v + kk * 2048), idesc_o, kk > 0 ? 1u : 0u);
-                tc_commit(B(bo_full));
-                tc_commit(B(bkv_empty[j & 1]));
+                    for (int kk = 0; kk < 8; kk++)
+                        tc_mma(tmem + o_col(h), sw128_desc(base + FA_P + (2 * h + kk / 4) * FA_TILE + (kk % 4) * 32),
+                               fa_desc_mn(v + kk * 2048), idesc_o, kk > 0 ? 1u : 0u);
+                    tc_commit(B(bo_full[h]));
+                    if (j + 1 < n) issue_s(j + 1, h);
+                }
+                tc_commit(B(bkv_empty[j & 1]));  // K_j and V_j are read by every MMA issued so far
             }
         }
     } else if (n > 0) {
-        // Softmax: thread = query row m of the tile.
+        // Softmax: head h = head0 + (warps 6-9), thread = query row m of the tile.
+        const int h = warp >= 6 ? 1 : 0;
         const int q = warp & 3, m = q * 32 + lane;
-        const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+        const uint32_t lanes = tmem + ((uint32_t)(q * 32) << 16);
         const int pos = pos_s[m];
         const float scale2 = 1.4426950408889634f / sqrtf((float)p.head_dim);  // log2(e) / sqrt(hd)
         float o[64];
@@ -167,79 +179,87 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         for (int d = 0; d < 64; d++) o[d] = 0.0f;
         float mrow = -INFINITY, l = 0.0f, a_pend = 0.0f;
         auto fold_pv = [&](int j) {  // o = o a_pend + PV_j, PV_j from TMEM
-            mbar_wait(B(bo_full), j & 1, err, &gave_up);
+            mbar_wait(B(bo_full[h]), j & 1, err, &gave_up);
             tc_fence_after();
             uint32_t v[4][16];
 #pragma unroll
-            for (int c = 0; c < 4; c++) tmem_ld16_nowait(tmem + lane_off + 256u + c * 16, v[c]);
+            for (int c = 0; c < 4; c++) tmem_ld16_nowait(lanes + o_col(h) + c * 16, v[c]);
             tmem_wait_ld();
 #pragma unroll
             for (int d = 0; d < 64; d++) o[d] = __fmaf_rn(o[d], a_pend, __uint_as_float(v[d / 16][d % 16]));
         };
-        for (int j = 0; j < n; j++) {
-            const int b = j & 1;
-            mbar_wait(B(bs_full[b]), (j >> 1) & 1, err, &gave_up);
-            tc_fence_after();
-            uint32_t sv[8][16];
+        // Half c2 (64 keys) of S_j, scaled to base 2 and masked past the row's position.
+        auto load_half = [&](int j, int c2, float (&sv)[64]) {
+            uint32_t r[4][16];
 #pragma unroll
-            for (int c = 0; c < 8; c++) tmem_ld16_nowait(tmem + lane_off + (uint32_t)(b * 128 + c * 16), sv[c]);
+            for (int c = 0; c < 4; c++) tmem_ld16_nowait(lanes + s_col(h) + (uint32_t)(c2 * 64 + c * 16), r[c]);
             tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(B(bs_empty[b]));
-            // Scores in base 2, masked past the row's position; a spare row takes none.
-            const int k0 = j * 128;
-            // Eight running maxima and sums (column c to c % 8), joined in a fixed order, so the
-            // chains are short.
+            const int k0 = j * 128 + c2 * 64;
+#pragma unroll
+            for (int c = 0; c < 64; c++)
+                sv[c] = k0 + c <= pos ? __uint_as_float(r[c / 16][c % 16]) * scale2 : -INFINITY;
+        };
+        for (int j = 0; j < n; j++) {
+            mbar_wait(B(bs_full[h]), j & 1, err, &gave_up);
+            tc_fence_after();
+            // The row maximum: eight running maxima (column c to c % 8) over both halves.
             float mx8[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) mx8[e] = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < 128; c++) {
-                const bool ok = k0 + c <= pos;
-                const float s = ok ? __uint_as_float(sv[c / 16][c % 16]) * scale2 : -INFINITY;
-                sv[c / 16][c % 16] = __float_as_uint(s);
-                mx8[c % 8] = fmaxf(mx8[c % 8], s);
+            for (int c2 = 0; c2 < 2; c2++) {
+                float sv[64];
+                load_half(j, c2, sv);
+#pragma unroll
+                for (int c = 0; c < 64; c++) mx8[c % 8] = fmaxf(mx8[c % 8], sv[c]);
             }
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float m_new = fmaxf(mrow, mx);
             const bool live = m_new != -INFINITY;  // false only for a spare row
             const float a = live ? fa_exp2(mrow - m_new) : 1.0f;
+            if (j > 0) {
+                fold_pv(j - 1);  // PV_{j-1} is done: this head's P buffer is free, O holds PV_{j-1}
+                tc_fence_before();
+                mbar_arrive(B(bo_empty[h]));
+            }
             float sum8[8];
 #pragma unroll
             for (int e = 0; e < 8; e++) sum8[e] = 0.0f;
-            uint32_t pk[64];
 #pragma unroll
-            for (int c = 0; c < 128; c += 2) {
-                const float p0 = live ? fa_exp2(__uint_as_float(sv[c / 16][c % 16]) - m_new) : 0.0f;
-                const float p1 = live ? fa_exp2(__uint_as_float(sv[(c + 1) / 16][(c + 1) % 16]) - m_new) : 0.0f;
-                sum8[c % 8] += p0;
-                sum8[(c + 1) % 8] += p1;
-                const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                pk[c / 2] = *reinterpret_cast<const uint32_t *>(&pp);
+            for (int c2 = 0; c2 < 2; c2++) {
+                float sv[64];
+                load_half(j, c2, sv);
+                uint32_t pk[32];
+#pragma unroll
+                for (int c = 0; c < 64; c += 2) {
+                    const float p0 = live ? fa_exp2(sv[c] - m_new) : 0.0f;
+                    const float p1 = live ? fa_exp2(sv[c + 1] - m_new) : 0.0f;
+                    sum8[c % 8] += p0;
+                    sum8[(c + 1) % 8] += p1;
+                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                    pk[c / 2] = *reinterpret_cast<const uint32_t *>(&pp);
+                }
+                // Keys 64 c2 .. 64 c2 + 63 of row m: box c2 of this head's P, swizzled.
+#pragma unroll
+                for (int ch = 0; ch < 8; ch++) {
+                    uint8_t *dst = smem + FA_P + (2 * h + c2) * FA_TILE + fa_sw128(m, ch);
+                    *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
+                }
             }
+            tc_fence_before();
+            mbar_arrive(B(bs_empty[h]));  // S_j is read: the MMAs may write S_{j+1}
             const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
             l = __fmaf_rn(l, a, sum);
             mrow = m_new;
-            if (j > 0) {
-                fold_pv(j - 1);  // PV_{j-1} is done: P's buffer is free and O holds PV_{j-1}
-                tc_fence_before();
-                mbar_arrive(B(bo_empty));
-            }
-            // P_j, row m: keys 0..63 in the first box, 64..127 in the second, swizzled.
-#pragma unroll
-            for (int ch = 0; ch < 16; ch++) {
-                uint8_t *dst = smem + FA_P + (ch / 8) * FA_TILE + fa_sw128(m, ch % 8);
-                *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(B(bp_full));
+            mbar_arrive(B(bp_full[h]));
             a_pend = a;
         }
         fold_pv(n - 1);
         if (pos >= 0) {
             const float inv = 1.0f / l;
-            uint4 *dst = reinterpret_cast<uint4 *>(out + ((size_t)(r0 + m) * heads + head) * 64);
+            uint4 *dst = reinterpret_cast<uint4 *>(out + ((size_t)(r0 + m) * heads + head0 + h) * 64);
 #pragma unroll
             for (int c = 0; c < 8; c++) {
                 uint32_t w[4];
@@ -260,7 +280,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 }
 
 bool attention_tc_supported(const tg_params &p) {
-    return p.dtype == TG_BF16 && p.head_dim == 64 && p.rows % 128 == 0 && p.rows > 0;
+    return p.dtype == TG_BF16 && p.head_dim == 64 && p.rows % 128 == 0 && p.rows > 0 && p.kv_heads > 0 &&
+           p.heads % p.kv_heads == 0 && (p.heads / p.kv_heads) % 2 == 0;
 }
 
 cudaError_t launch_attention_rows_tc(const tg_params &p, const uint32_t *at, const void *q, const void *kc,
@@ -273,7 +294,7 @@ cudaError_t launch_attention_rows_tc(const tg_params &p, const uint32_t *at, con
         return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(attention_rows_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)FA_SMEM);
     if (e != cudaSuccess) return e;
-    attention_rows_tc_kernel<<<dim3(p.rows / 128, p.heads), FA_THREADS, FA_SMEM, s>>>(qm, km, vm, p, at, (bf16 *)out, err);
+    attention_rows_tc_kernel<<<dim3(p.rows / 128, p.heads / 2), FA_THREADS, FA_SMEM, s>>>(qm, km, vm, p, at, (bf16 *)out, err);
     return cudaGetLastError();
 }
 
