@@ -142,7 +142,12 @@ typedef enum {
      * rounding; rows a multiple of 128, each 128-row tile one run's rows (one slot; a tile that
      * mixes slots is refused at run time with the kernel error word). attention_rows.comp */
     TG_KERNEL_ATTENTION_ROWS_TC = 15,
-    TG_KERNEL_COUNT = 16
+    /* a bf16 [m][hidden] normed rows, b bf16 [(heads + 2 kv) hd][hidden] (the q/k/v projection),
+     * at u32 (rows = m), cos, sin -> q T [m][heads hd], k/v appended to the caches: the GEMM with
+     * ROPE_ROWS in its epilogue (the f32 projection never stored); bf16, (heads + 2 kv) hd a
+     * multiple of 256.                                                gemm.mlir + rope_rows.comp */
+    TG_KERNEL_GEMM_QKV_ROPE = 16,
+    TG_KERNEL_COUNT = 17
 } tg_kernel_id;
 
 /* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the

@@ -168,3 +168,42 @@ def test_gemm_silu_refuses_a_width_it_does_not_tile(pkg, ctx):
     a, b, out = pkg.Memory(ctx, 128 * 64 * 2), pkg.Memory(ctx, 384 * 64 * 2), pkg.Memory(ctx, 128 * 192 * 2)
     with pytest.raises(pkg.ShapeError):
         pkg.dispatch_once(ctx, "gemm_silu", p, [(a, 0, a.nbytes), (b, 0, b.nbytes), (out, 0, out.nbytes)])
+
+
+def test_gemm_qkv_rope_equals_gemm_then_rope_rows(pkg, ctx, syn):
+    """RoPE and the cache append in the q/k/v GEMM's epilogue give the same bits as the GEMM's f32
+    rows through rope_rows: q rows, and the caches at each row's position and slot."""
+    H, heads, kvh, hd, cap, slots, m = 1024, 16, 2, 64, 256, 3, 384
+    W = (heads + 2 * kvh) * hd
+    shape = pkg.Shape(hidden=H, inner=4096, heads=heads, kv_heads=kvh, head_dim=hd, layers=1, capacity=cap)
+    rng = np.random.default_rng(12)
+    a = syn.bf16_bits(rng.standard_normal((m, H), dtype=np.float32))
+    w = syn.bf16_bits(rng.standard_normal((W, H), dtype=np.float32) * 0.03)
+    words = np.full(2 * m, 0xFFFFFFFF, np.uint32)
+    for first, n, start, slot in ((0, 200, 17, 2), (256, 100, 0, 0)):
+        words[first:first + n] = np.arange(start, start + n)
+        words[m + first:m + first + n] = slot
+    cs, sn = shape.rope_tables()
+    ma, mw, mwd, mc, ms = (_mem(pkg, ctx, x) for x in (a, w, words, cs, sn))
+    p = pkg.params(shape, "bf16", rows=m, slots=slots, m=m, n=W, k=H)
+    cache = slots * kvh * cap * hd * 2
+    qb = m * heads * hd * 2
+    got, want = [], []
+    for fused in (True, False):
+        q, kc, vc = pkg.Memory(ctx, qb), pkg.Memory(ctx, cache), pkg.Memory(ctx, cache)
+        if fused:
+            pkg.dispatch_once(ctx, "gemm_qkv_rope", p, [(ma, 0, a.nbytes), (mw, 0, w.nbytes), (mwd, 0, words.nbytes),
+                                                        (mc, 0, cs.nbytes), (ms, 0, sn.nbytes), (q, 0, qb),
+                                                        (kc, 0, cache), (vc, 0, cache)])
+        else:
+            c = pkg.Memory(ctx, m * W * 4)
+            pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, a.nbytes), (mw, 0, w.nbytes), (c, 0, m * W * 4)])
+            pkg.dispatch_once(ctx, "rope_rows", p, [(mwd, 0, words.nbytes), (c, 0, m * W * 4), (mc, 0, cs.nbytes),
+                                                    (ms, 0, sn.nbytes), (q, 0, qb), (kc, 0, cache), (vc, 0, cache)])
+        out = (q.read(np.uint16, qb // 2), kc.read(np.uint16, cache // 2), vc.read(np.uint16, cache // 2))
+        (got if fused else want).append(out)
+    live = np.repeat(words[:m] != 0xFFFFFFFF, heads * hd)
+    np.testing.assert_array_equal(got[0][0][live], want[0][0][live])
+    np.testing.assert_array_equal(got[0][1], want[0][1])
+    np.testing.assert_array_equal(got[0][2], want[0][2])
+    assert np.any(got[0][1] != 0) and np.any(got[0][2] != 0)

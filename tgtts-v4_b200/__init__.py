@@ -94,7 +94,7 @@ KERNELS = {
     "rmsnorm": 0, "gemv_qkv_rope": 1, "attention_split": 2, "attention_combine": 3,
     "gemv_residual": 4, "gemv_gate_up": 5, "stream_read": 6, "norm_rows": 7, "add_norm_rows": 8,
     "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12, "attention_decode": 13,
-    "gemm_silu": 14, "attention_rows_tc": 15,
+    "gemm_silu": 14, "attention_rows_tc": 15, "gemm_qkv_rope": 16,
 }
 
 

@@ -74,8 +74,17 @@ struct TcLayout {
 };
 
 // Epilogues: C in f32, or (BN = 256, B's rows in gate_up_row's order) SiLU(gate) up in bf16, the
-// tile's columns 0..127 the gate and 128..255 the up of the same 128 outputs.
-enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1 };
+// tile's columns 0..127 the gate and 128..255 the up of the same 128 outputs, or (BN = 256, B the
+// q/k/v projection) rope_rows.comp's work: RoPE on each head's column pairs (i, i + hd/2), q rows
+// stored bf16, k and v rows appended to the cache at the row's position and slot.
+enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1, TC_EPI_ROPE = 2 };
+
+struct RopeEpi {
+    tg_params p;
+    const uint32_t *at;
+    const float *cosv, *sinv;
+    bf16 *q, *kc, *vc;
+};
 
 // Persistent: one block per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m fastest, so the
 // blocks at work share B tiles in L2). Warp 0 streams A and B tiles into a ring of stages with
@@ -88,7 +97,7 @@ constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
 template <int BN, int EPI = TC_EPI_F32>
 __global__ void __launch_bounds__(TC_PTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err) {
+                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ RopeEpi re) {
     using L = TcLayout<BN>;
     constexpr int S = L::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -187,7 +196,74 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             tc_fence_after();
             const int row = m0 + q * 32 + lane;
             const uint32_t lane_base = tmem + lane_off + (uint32_t)(acc * BN);
-            if constexpr (EPI == TC_EPI_SILU) {
+            if constexpr (EPI == TC_EPI_ROPE) {
+                static_assert(BN == 256, "whole heads a tile");
+                const tg_params &p = re.p;
+                const int hd = p.head_dim, half = hd / 2, heads = p.heads, kvh = p.kv_heads;
+                uint32_t pos = 0, slot = 0;
+                const bool ok = row < M && placed(re.at, p.rows, row, p.capacity, p.slots, pos, slot);
+                // 16 pair columns at a time: the row's cos and sin for them once (every head of the
+                // tile shares the position), then each head's pairs.
+#pragma unroll 1
+                for (int c0 = 0; c0 < half; c0 += 16) {
+                    float cs[16], sn[16];
+                    if (ok && p.rope) {
+                        const float4 *c4 = reinterpret_cast<const float4 *>(re.cosv + (size_t)pos * half + c0);
+                        const float4 *s4 = reinterpret_cast<const float4 *>(re.sinv + (size_t)pos * half + c0);
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const float4 cv = __ldg(c4 + e), sv = __ldg(s4 + e);
+                            cs[4 * e] = cv.x, cs[4 * e + 1] = cv.y, cs[4 * e + 2] = cv.z, cs[4 * e + 3] = cv.w;
+                            sn[4 * e] = sv.x, sn[4 * e + 1] = sv.y, sn[4 * e + 2] = sv.z, sn[4 * e + 3] = sv.w;
+                        }
+                    }
+#pragma unroll 1
+                    for (int hb = 0; hb < BN; hb += hd) {
+                        const int head = (n0 + hb) / hd;
+                        uint32_t va[16], vb[16];
+                        tmem_ld16_nowait(lane_base + hb + c0, va);
+                        tmem_ld16_nowait(lane_base + hb + half + c0, vb);
+                        tmem_wait_ld();
+                        if (!ok) continue;
+                        float a[16], b[16];
+#pragma unroll
+                        for (int e = 0; e < 16; e++) {
+                            a[e] = __uint_as_float(va[e]);
+                            b[e] = __uint_as_float(vb[e]);
+                        }
+                        if (head < heads + kvh && p.rope) {
+                            // As upstream: x cos + rotate_half(x) sin (rope_rows.comp:33-70).
+#pragma unroll
+                            for (int e = 0; e < 16; e++) {
+                                const float na = __fmaf_rn(a[e], cs[e], -__fmul_rn(b[e], sn[e]));
+                                const float nb = __fmaf_rn(b[e], cs[e], __fmul_rn(a[e], sn[e]));
+                                a[e] = na;
+                                b[e] = nb;
+                            }
+                        }
+                        bf16 *dst;
+                        if (head < heads)
+                            dst = re.q + ((size_t)row * heads + head) * hd;
+                        else if (head < heads + kvh)
+                            dst = re.kc + (((size_t)slot * kvh + (head - heads)) * p.capacity + pos) * hd;
+                        else
+                            dst = re.vc + (((size_t)slot * kvh + (head - heads - kvh)) * p.capacity + pos) * hd;
+                        uint32_t wa[8], wb[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e++) {
+                            const __nv_bfloat162 x = __floats2bfloat162_rn(a[2 * e], a[2 * e + 1]);
+                            const __nv_bfloat162 y = __floats2bfloat162_rn(b[2 * e], b[2 * e + 1]);
+                            wa[e] = *reinterpret_cast<const uint32_t *>(&x);
+                            wb[e] = *reinterpret_cast<const uint32_t *>(&y);
+                        }
+                        uint4 *da = reinterpret_cast<uint4 *>(dst + c0), *db = reinterpret_cast<uint4 *>(dst + half + c0);
+                        da[0] = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+                        da[1] = make_uint4(wa[4], wa[5], wa[6], wa[7]);
+                        db[0] = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+                        db[1] = make_uint4(wb[4], wb[5], wb[6], wb[7]);
+                    }
+                }
+            } else if constexpr (EPI == TC_EPI_SILU) {
                 static_assert(BN == 256, "the SiLU epilogue pairs columns c and c + 128 of a 256-wide tile");
                 bf16 *out = static_cast<bf16 *>(Cout);
                 const int inner = N / 2;
@@ -245,7 +321,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
 
 template <int BN, int EPI = TC_EPI_F32>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
-                             cudaStream_t s) {
+                             cudaStream_t s, const RopeEpi &re = RopeEpi{}) {
     CUtensorMap ma, mb;
     if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, BN))
         return cudaErrorInvalidValue;
@@ -256,7 +332,7 @@ static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN);
-    kern<<<tiles < sms ? tiles : sms, TC_PTHREADS, TcLayout<BN>::SMEM, s>>>(ma, mb, c, M, N, K, err);
+    kern<<<tiles < sms ? tiles : sms, TC_PTHREADS, TcLayout<BN>::SMEM, s>>>(ma, mb, c, M, N, K, err, re);
     return cudaGetLastError();
 }
 
@@ -274,6 +350,17 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
     if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s);
     if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s);
     return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *b, const uint32_t *at,
+                                 const float *cosv, const float *sinv, void *q, void *kc, void *vc, uint32_t *err,
+                                 cudaStream_t s) {
+    const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
+    if (p.dtype != TG_BF16 || M <= 0 || N % 256 || K % TC_BK || 256 % p.head_dim ||
+        N != (int)((p.heads + 2 * p.kv_heads) * p.head_dim) || p.rows != p.m)
+        return cudaErrorInvalidValue;
+    RopeEpi re{p, at, cosv, sinv, (bf16 *)q, (bf16 *)kc, (bf16 *)vc};
+    return launch_tc<256, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, re);
 }
 
 cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,

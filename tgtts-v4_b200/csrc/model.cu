@@ -630,10 +630,21 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
     for (uint32_t l = 0; l < s.layers; l++) {
         const LayerOffsets &o = d.layer[l];
         char *in = l == 0 ? p.x_in.ptr() : p.h.ptr();
-        gemm("qkv_proj", p.normed.ptr(), d.w(o.qkv), p.qkv.ptr(), W, H);
-        push(v, TG_KERNEL_ROPE_ROWS, base, "rope_rows",
-             {{p.words.ptr(), words}, {p.qkv.ptr(), R * W * F}, {d.cos.ptr(), table}, {d.sin.ptr(), table},
-              {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
+        if (d.dtype == TG_BF16 && W % 256 == 0) {
+            // RoPE and the cache append in the GEMM's epilogue: the f32 q/k/v rows never reach memory.
+            tg_params g = base;
+            g.m = rows;
+            g.n = (uint32_t)W;
+            g.k = (uint32_t)H;
+            push(v, TG_KERNEL_GEMM_QKV_ROPE, g, "qkv_proj",
+                 {{p.normed.ptr(), R * H * T}, {d.w(o.qkv), W * H * T}, {p.words.ptr(), words}, {d.cos.ptr(), table},
+                  {d.sin.ptr(), table}, {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
+        } else {
+            gemm("qkv_proj", p.normed.ptr(), d.w(o.qkv), p.qkv.ptr(), W, H);
+            push(v, TG_KERNEL_ROPE_ROWS, base, "rope_rows",
+                 {{p.words.ptr(), words}, {p.qkv.ptr(), R * W * F}, {d.cos.ptr(), table}, {d.sin.ptr(), table},
+                  {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
+        }
         push(v, attention_tc_supported(base) ? TG_KERNEL_ATTENTION_ROWS_TC : TG_KERNEL_ATTENTION_ROWS, base, "attention_rows",
              {{p.words.ptr(), words}, {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {p.att.ptr(), R * A * T}});
@@ -683,7 +694,8 @@ extern "C" int tg_prefill_create(tg_decoder *d, uint32_t max_rows, int timed, tg
     TG_TRY(p->h.alloc(ctx, R * H * F));
     TG_TRY(p->mid.alloc(ctx, R * H * F));
     TG_TRY(p->normed.alloc(ctx, R * H * T));
-    TG_TRY(p->qkv.alloc(ctx, R * d->width() * F));
+    if (d->dtype != TG_BF16 || d->width() % 256)  // else RoPE runs in the q/k/v GEMM's epilogue
+        TG_TRY(p->qkv.alloc(ctx, R * d->width() * F));
     TG_TRY(p->q.alloc(ctx, R * d->attn() * T));
     TG_TRY(p->att.alloc(ctx, R * d->attn() * T));
     TG_TRY(p->proj.alloc(ctx, R * H * F));

@@ -137,6 +137,10 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
                    {"out", (uint64_t)p.m * (p.n / 2) * T}};
             break;
+        case TG_KERNEL_GEMM_QKV_ROPE:
+            out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T}, {"at", words}, {"cos", table},
+                   {"sin", table}, {"q", rows * attn * T}, {"k_cache", cache}, {"v_cache", cache}};
+            break;
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
@@ -147,7 +151,7 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc"};
+        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
 }
 
@@ -185,6 +189,12 @@ static int check_shape(const Launch &l) {
             break;
         case TG_KERNEL_SILU_MUL_ROWS:
             if (p.inner == 0) return fail(TG_ESHAPE, "silu_mul_rows: inner 0");
+            break;
+        case TG_KERNEL_GEMM_QKV_ROPE:
+            if (p.dtype != TG_BF16 || !heads_ok() || p.m == 0 || p.m != p.rows || p.k % 64 || p.n % 256 ||
+                p.n != (p.heads + 2 * p.kv_heads) * p.head_dim)
+                return fail(TG_ESHAPE, "gemm_qkv_rope %ux%ux%u: bf16, rows = m, n = (heads + 2 kv) hd a multiple of 256",
+                            p.m, p.n, p.k);
             break;
         case TG_KERNEL_ATTENTION_ROWS_TC:
             if (!heads_ok() || !attention_tc_supported(p))
@@ -274,6 +284,9 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case KERNEL_DTC_GATE_UP: e = launch_dtc_gate_up(p, F(0), F(1), b[2], F(3), err, s); break;
         case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
         case TG_KERNEL_ATTENTION_ROWS_TC: e = launch_attention_rows_tc(p, U(0), b[1], b[2], b[3], b[4], err, s); break;
+        case TG_KERNEL_GEMM_QKV_ROPE:
+            e = launch_gemm_qkv_rope(p, b[0], b[1], U(2), F(3), F(4), b[5], b[6], b[7], err, s);
+            break;
         default: return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
     if (e != cudaSuccess)

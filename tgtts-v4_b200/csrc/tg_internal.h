@@ -182,6 +182,10 @@ constexpr uint32_t GU_BLOCK = 128;
 __host__ __device__ inline uint32_t gate_up_row(uint32_t i, uint32_t up) {
     return (i / GU_BLOCK) * (2 * GU_BLOCK) + up * GU_BLOCK + i % GU_BLOCK;
 }
+// The q/k/v projection with rope_rows in its epilogue (bf16, n = (heads + 2 kv) hd, a multiple of 256).
+cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *b, const uint32_t *at,
+                                 const float *cosv, const float *sinv, void *q, void *kc, void *vc, uint32_t *err,
+                                 cudaStream_t s);
 // out[m][n / 2] = SiLU(gate) up of C = A B^T, B's rows in gate_up_row's order (bf16, n % 256 == 0).
 cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,
                              cudaStream_t s);
