@@ -147,7 +147,13 @@ typedef enum {
      * ROPE_ROWS in its epilogue (the f32 projection never stored); bf16, (heads + 2 kv) hd a
      * multiple of 256.                                                gemm.mlir + rope_rows.comp */
     TG_KERNEL_GEMM_QKV_ROPE = 16,
-    TG_KERNEL_COUNT = 17
+    /* x0 f32 [rows][k], x1 f32 [rows][k1] (any 16 bytes when k1 = 0), W T [n][k + k1], bias f32 [n]
+     * -> out f32 [rows][stride]: out[b][offset + i] = act(W [x0; x1] + bias)[i] (the LM side's
+     * linear layers: enc_to_lm_proj, the scalar quantizer's in/out, fusion_concat_proj,
+     * stop_proj/stop_head). The reference stores f16 bias and output; here both are f32.
+     *                                                                       gemv_linear.comp */
+    TG_KERNEL_GEMV_LINEAR = 17,
+    TG_KERNEL_COUNT = 18
 } tg_kernel_id;
 
 /* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the
@@ -161,6 +167,11 @@ typedef struct {
     uint32_t rope;       /* 0: q and k are not rotated */
     uint32_t normed_f32; /* ADD_NORM_ROWS: normed is f32 (the final norm) rather than T */
     uint32_t m, n, k;    /* GEMM, GEMV_RESIDUAL (n outputs of k), STREAM_READ (k words) */
+    /* GEMV_LINEAR: n outputs of k + k1 inputs (x0's k then x1's k1), written at out[b][offset + i]
+     * of rows `stride` long, through activation `act` (0 none, 1 SiLU, 2 the scalar quantizer's
+     * tanh rounded to a multiple of 1 / levels). */
+    uint32_t k1, offset, stride, act;
+    float levels;
 } tg_params;
 
 typedef struct {

@@ -71,6 +71,8 @@ def library() -> ctypes.CDLL:
         lib.tgo_gemm_abt.argtypes = [_FP, _FP, _FP, ctypes.c_int32, ctypes.c_int32,
                                      ctypes.c_int32, ctypes.c_int32]
         lib.tgo_gemm_abt.restype = None
+        lib.tgo_gemv_linear.argtypes = [_FP, _FP, _FP, _FP, _FP] + [ctypes.c_int32] * 7 + [ctypes.c_float]
+        lib.tgo_gemv_linear.restype = None
         _lib = lib
     return _lib
 
@@ -103,6 +105,22 @@ def gemm_abt(a: np.ndarray, b: np.ndarray, threads: int = 0) -> np.ndarray:
     library().tgo_gemm_abt(_fp(a), _fp(b), _fp(c), a.shape[0], b.shape[0], a.shape[1],
                            threads or os.cpu_count() or 1)
     return c
+
+
+def gemv_linear(x0: np.ndarray, x1: Optional[np.ndarray], w: np.ndarray, bias: np.ndarray, act: int = 0,
+                levels: float = 9.0, offset: int = 0, stride: Optional[int] = None) -> np.ndarray:
+    """tgo_gemv_linear: out [rows][stride] with act(W [x0; x1] + bias) at columns offset.."""
+    x0 = np.ascontiguousarray(x0, np.float32)
+    rows, k0 = x0.shape
+    x1 = np.zeros((rows, 0), np.float32) if x1 is None else np.ascontiguousarray(x1, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    n = w.shape[0]
+    stride = offset + n if stride is None else stride
+    out = np.zeros((rows, stride), np.float32)
+    library().tgo_gemv_linear(_fp(x0), _fp(x1) if x1.size else None, _fp(w),
+                              _fp(np.ascontiguousarray(bias, np.float32)), _fp(out), rows, n, k0, x1.shape[1],
+                              offset, stride, act, ctypes.c_float(levels))
+    return out
 
 
 class OracleStack:

@@ -314,3 +314,25 @@ int32_t tgo_prefill(const tgo_shape *s, const tgo_layer *layers, const float *fi
     free(at);
     return 0;
 }
+
+void tgo_gemv_linear(const float *x0, const float *x1, const float *w, const float *bias, float *out,
+                     int32_t rows, int32_t n, int32_t k0, int32_t k1, int32_t offset, int32_t stride,
+                     int32_t act, float levels) {
+    const int64_t k = (int64_t)k0 + k1;
+    for (int32_t b = 0; b < rows; b++) {
+        for (int32_t i = 0; i < n; i++) {
+            const float *wr = w + (int64_t)i * k;
+            float acc = 0.0f;
+            for (int64_t c = 0; c < k0; c++) acc = fmaf(wr[c], x0[(int64_t)b * k0 + c], acc);
+            for (int64_t c = 0; c < k1; c++) acc = fmaf(wr[k0 + c], x1[(int64_t)b * k1 + c], acc);
+            float v = acc + bias[i];
+            if (act == 1) {
+                v = v / (1.0f + expf(-v));
+            } else if (act == 2) {
+                const float t = 1.0f - 2.0f / (expf(2.0f * fabsf(v)) + 1.0f);
+                v = rintf(copysignf(t, v) * levels) / levels;
+            }
+            out[(int64_t)b * stride + offset + i] = v;
+        }
+    }
+}

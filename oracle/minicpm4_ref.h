@@ -74,6 +74,14 @@ int32_t tgo_prefill(const tgo_shape *s, const tgo_layer *layers, const float *fi
 void tgo_gemm_abt(const float *a, const float *b, float *c, int32_t m, int32_t n, int32_t k,
                   int32_t threads);
 
+/* The LM side's linear layer (kernels/glsl/gemv_linear.comp:41-60): for each of `rows` rows,
+ * out[b][offset + i] = act(W[i] . [x0[b]; x1[b]] + bias[i]) over W [n][k0 + k1], each dot in f32
+ * and sequential over the columns; act 0 none, 1 SiLU v / (1 + e^-v), 2 the scalar quantizer:
+ * t = 1 - 2 / (e^(2|v|) + 1), round-half-even(sign(v) t levels) / levels. */
+void tgo_gemv_linear(const float *x0, const float *x1, const float *w, const float *bias, float *out,
+                     int32_t rows, int32_t n, int32_t k0, int32_t k1, int32_t offset, int32_t stride,
+                     int32_t act, float levels);
+
 #ifdef __cplusplus
 }
 #endif

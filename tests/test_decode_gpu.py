@@ -231,3 +231,28 @@ def test_the_persistent_step_takes_small_batches_only(pkg, ctx, syn):
     assert not dec.retuned(False).persistent and len(dec.labels()) == 7
     with pytest.raises(pkg.ShapeError):
         pkg.Decoder(ctx, shape, rows=3, slots=3, dtype="bf16").retuned(True)
+
+
+def test_a_checkpoint_file_loads_the_same_bits_as_the_arrays(pkg, ctx, syn, tmp_path):
+    """Decoder::load from a safetensors file (checkpoint.rs) under a prefix: the same step, bit for
+    bit, as loading the arrays themselves."""
+    from tgtts_v4_b200 import checkpoint
+
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=128, layers=2)
+    w = syn.make_weights(cfg, seed=0, layers=2, jitter_gains=True, as_bits=True)
+    path = tmp_path / "stack.safetensors"
+    checkpoint.save(path, {"base_lm." + k: v for k, v in w.items()})
+    x = syn.make_inputs(1, cfg.hidden, seed=4)
+    outs = []
+    for how in ("arrays", "file"):
+        dec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16")
+        if how == "arrays":
+            dec.load(w)
+        else:
+            dec.load_checkpoint(path, prefix="base_lm.")
+        outs.append(dec.step(5, x))
+        dec.close()
+    np.testing.assert_array_equal(outs[0], outs[1])
+    with pytest.raises(pkg.Error):
+        pkg.Decoder(ctx, shape, rows=1, dtype="bf16").load_checkpoint(path, prefix="residual_lm.")

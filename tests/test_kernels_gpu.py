@@ -207,3 +207,52 @@ def test_gemm_qkv_rope_equals_gemm_then_rope_rows(pkg, ctx, syn):
     np.testing.assert_array_equal(got[0][1], want[0][1])
     np.testing.assert_array_equal(got[0][2], want[0][2])
     assert np.any(got[0][1] != 0) and np.any(got[0][2] != 0)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_gemv_linear_against_the_oracle_and_alone(pkg, ctx, syn, dtype):
+    """gemv_linear.comp on the GPU: W [x0; x1] + bias through each activation, written at an
+    offset of longer rows, within f32 rounding of the CPU oracle; each batch row the same bits
+    computed alone."""
+    import oracle
+
+    rng = np.random.default_rng(21)
+    rows, k0, k1, n, offset, stride = 5, 1024, 256, 200, 24, 256
+    x0 = rng.standard_normal((rows, k0), dtype=np.float32)
+    x1 = rng.standard_normal((rows, k1), dtype=np.float32)
+    w = rng.standard_normal((n, k0 + k1), dtype=np.float32) * 0.03
+    if dtype == "bf16":
+        wb = syn.bf16_bits(w)
+        w = syn.bf16_to_f32(wb)
+    else:
+        wb = w
+    bias = rng.standard_normal(n).astype(np.float32)
+    shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    mx0, mx1, mw, mb = (_mem(pkg, ctx, a) for a in (x0, x1, wb, bias))
+
+    def run(act, r, xa, xb):
+        p = pkg.params(shape, dtype, rows=r, n=n, k=k0, k1=k1, offset=offset, stride=stride, act=act, levels=9.0)
+        out = pkg.Memory(ctx, r * stride * 4)
+        out.fill(0)
+        pkg.dispatch_once(ctx, "gemv_linear", p, [(xa, 0, r * k0 * 4), (xb, 0, r * k1 * 4), (mw, 0, wb.nbytes),
+                                                  (mb, 0, bias.nbytes), (out, 0, r * stride * 4)])
+        return out.read(np.float32, r * stride).reshape(r, stride)
+
+    for act in (0, 1, 2):
+        got = run(act, rows, mx0, mx1)
+        want = oracle.gemv_linear(x0, x1, w, bias, act=act, levels=9.0, offset=offset, stride=stride)
+        assert np.all(got[:, :offset] == 0) and np.all(got[:, offset + n:] == 0)
+        if act == 2:
+            lin = oracle.gemv_linear(x0, x1, w, bias, act=0)
+            t9 = np.abs(np.tanh(lin.astype(np.float64)) * 9)
+            safe = np.abs(t9 % 1 - 0.5) > 1e-3  # away from a rounding boundary
+            assert np.array_equal(got[:, offset:offset + n][safe], want[:, offset:offset + n][safe])
+        else:
+            np.testing.assert_allclose(got, want, rtol=2e-5, atol=2e-5)
+        for b in (0, 3):
+            alone = run(act, 1, _mem(pkg, ctx, x0[b:b + 1]), _mem(pkg, ctx, x1[b:b + 1]))
+            np.testing.assert_array_equal(alone[0], got[b])
+    bad = pkg.params(shape, dtype, rows=rows, n=n, k=k0, k1=k1, offset=100, stride=256, act=0, levels=9.0)
+    with pytest.raises(pkg.ShapeError):
+        pkg.dispatch_once(ctx, "gemv_linear", bad, [(mx0, 0, x0.nbytes), (mx1, 0, x1.nbytes), (mw, 0, wb.nbytes),
+                                                    (mb, 0, bias.nbytes), (pkg.Memory(ctx, rows * 256 * 4), 0, rows * 256 * 4)])

@@ -161,3 +161,31 @@ def test_oracle_reproduces_its_committed_outputs_for_config_1(pkg, syn):
     for t in range(16):
         h = stack.decode_step([(32 + t, 0)], h[None])[0]
         np.testing.assert_allclose(h, gold["decode"][t], atol=1e-5)
+
+
+def test_gemv_linear_oracle_against_f64_and_known_answers():
+    """The LM side's linear layer (gemv_linear.comp:41-60): W [x0; x1] + bias through none, SiLU
+    or the scalar quantizer, at an offset of a longer row."""
+    rng = np.random.default_rng(3)
+    x0 = rng.standard_normal((3, 48), dtype=np.float32)
+    x1 = rng.standard_normal((3, 16), dtype=np.float32)
+    w = rng.standard_normal((10, 64), dtype=np.float32) * 0.1
+    bias = rng.standard_normal(10).astype(np.float32)
+    lin = np.concatenate([x0, x1], 1).astype(np.float64) @ w.T.astype(np.float64) + bias
+    got = oracle.gemv_linear(x0, x1, w, bias, act=0, offset=5, stride=20)
+    assert np.all(got[:, :5] == 0) and np.all(got[:, 15:] == 0)
+    np.testing.assert_allclose(got[:, 5:15], lin, rtol=1e-5, atol=1e-5)
+    silu = oracle.gemv_linear(x0, x1, w, bias, act=1)
+    np.testing.assert_allclose(silu, lin / (1 + np.exp(-lin)), rtol=1e-5, atol=1e-6)
+    q = oracle.gemv_linear(x0, x1, w, bias, act=2, levels=9.0)
+    t = np.tanh(lin)
+    near_half = np.abs(np.abs(t * 9) % 1 - 0.5) < 1e-4
+    want = np.round(t * 9) / 9  # numpy rounds halves to even, as rintf
+    assert np.all((q == want.astype(np.float32)) | near_half)
+    # Known answers: a zero layer gives the bias through each activation; the quantizer's levels.
+    z = np.zeros((1, 8), np.float32)
+    wz = np.zeros((3, 8), np.float32)
+    b = np.array([0.0, 100.0, -0.06], np.float32)
+    np.testing.assert_array_equal(oracle.gemv_linear(z, None, wz, b, act=0)[0], b)
+    np.testing.assert_array_equal(oracle.gemv_linear(z, None, wz, b, act=2, levels=9.0)[0],
+                                  np.array([0.0, 1.0, -1.0 / 9], np.float32))

@@ -94,7 +94,7 @@ KERNELS = {
     "rmsnorm": 0, "gemv_qkv_rope": 1, "attention_split": 2, "attention_combine": 3,
     "gemv_residual": 4, "gemv_gate_up": 5, "stream_read": 6, "norm_rows": 7, "add_norm_rows": 8,
     "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12, "attention_decode": 13,
-    "gemm_silu": 14, "attention_rows_tc": 15, "gemm_qkv_rope": 16,
+    "gemm_silu": 14, "attention_rows_tc": 15, "gemm_qkv_rope": 16, "gemv_linear": 17,
 }
 
 
@@ -121,7 +121,8 @@ class TgParams(ctypes.Structure):
     _fields_ = [(n, ctypes.c_uint32) for n in
                 ("dtype", "hidden", "inner", "heads", "kv_heads", "head_dim", "capacity", "rows",
                  "slots")] + [("eps", ctypes.c_float), ("residual_scale", ctypes.c_float)] + [
-        (n, ctypes.c_uint32) for n in ("rope", "normed_f32", "m", "n", "k")]
+        (n, ctypes.c_uint32) for n in ("rope", "normed_f32", "m", "n", "k", "k1", "offset", "stride",
+                                       "act")] + [("levels", ctypes.c_float)]
 
 
 class TgBinding(ctypes.Structure):
@@ -602,6 +603,19 @@ class Decoder:
             if key not in weights:
                 raise Error(f"checkpoint: no tensor {key}")
             self.load_tensor(name, weights[key])
+
+    def load_checkpoint(self, path, prefix: str = "") -> None:
+        """Decoder::load from a safetensors file (crates/graph/src/checkpoint.rs): every weight of
+        the stack by its upstream name after `prefix`, read a tensor at a time."""
+        from .checkpoint import Checkpoint
+
+        with Checkpoint(path) as ck:
+            names = [f"layers.{l}.{w}" for l in range(self.shape.layers) for w in WEIGHT_NAMES]
+            names.append("norm.weight")
+            for name in names:
+                if ck.shape(prefix + name) is None:
+                    raise Error(f"checkpoint: no tensor {prefix + name}")
+                self.load_tensor(name, ck.tensor(prefix + name))
 
     def load_tensor(self, name: str, values: np.ndarray) -> None:
         a = np.ascontiguousarray(values)

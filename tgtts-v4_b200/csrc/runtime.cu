@@ -6,6 +6,7 @@
 
 #include <chrono>
 #include <cstdio>
+#include <algorithm>
 #include <cstring>
 #include <thread>
 
@@ -141,6 +142,11 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T}, {"at", words}, {"cos", table},
                    {"sin", table}, {"q", rows * attn * T}, {"k_cache", cache}, {"v_cache", cache}};
             break;
+        case TG_KERNEL_GEMV_LINEAR:
+            out = {{"x0", rows * p.k * F}, {"x1", std::max<uint64_t>(rows * p.k1 * F, 16)},
+                   {"W", (uint64_t)p.n * (p.k + p.k1) * T}, {"bias", (uint64_t)p.n * F},
+                   {"out", rows * p.stride * F}};
+            break;
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
@@ -151,7 +157,7 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope"};
+        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope", "gemv_linear"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
 }
 
@@ -190,6 +196,15 @@ static int check_shape(const Launch &l) {
         case TG_KERNEL_SILU_MUL_ROWS:
             if (p.inner == 0) return fail(TG_ESHAPE, "silu_mul_rows: inner 0");
             break;
+        case TG_KERNEL_GEMV_LINEAR: {
+            const uint32_t vec = p.dtype == TG_BF16 ? 8 : 4;  // a 16-byte load of each input's columns
+            if (p.n == 0 || p.k == 0 || p.k % vec || p.k1 % vec || p.act > 2 || p.offset + p.n > p.stride ||
+                (p.act == 2 && !(p.levels > 0.0f)) || p.rows > 64)
+                return fail(TG_ESHAPE, "gemv_linear: %u outputs of %u + %u (multiples of %u) at %u of rows %u long, "
+                            "act %u, levels %g, %u rows (at most 64)", p.n, p.k, p.k1, vec, p.offset, p.stride, p.act,
+                            p.levels, p.rows);
+            break;
+        }
         case TG_KERNEL_GEMM_QKV_ROPE:
             if (p.dtype != TG_BF16 || !heads_ok() || p.m == 0 || p.m != p.rows || p.k % 64 || p.n % 256 ||
                 p.n != (p.heads + 2 * p.kv_heads) * p.head_dim)
@@ -284,6 +299,7 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case KERNEL_DTC_GATE_UP: e = launch_dtc_gate_up(p, F(0), F(1), b[2], F(3), err, s); break;
         case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
         case TG_KERNEL_ATTENTION_ROWS_TC: e = launch_attention_rows_tc(p, U(0), b[1], b[2], b[3], b[4], err, s); break;
+        case TG_KERNEL_GEMV_LINEAR: e = launch_gemv_linear(p, F(0), F(1), b[2], F(3), F(4), s); break;
         case TG_KERNEL_GEMM_QKV_ROPE:
             e = launch_gemm_qkv_rope(p, b[0], b[1], U(2), F(3), F(4), b[5], b[6], b[7], err, s);
             break;

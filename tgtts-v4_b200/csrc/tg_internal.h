@@ -182,6 +182,9 @@ constexpr uint32_t GU_BLOCK = 128;
 __host__ __device__ inline uint32_t gate_up_row(uint32_t i, uint32_t up) {
     return (i / GU_BLOCK) * (2 * GU_BLOCK) + up * GU_BLOCK + i % GU_BLOCK;
 }
+// gemv_linear.comp: out[b][offset + i] = act(W [x0; x1] + bias)[i] (kernels_linear.cu).
+cudaError_t launch_gemv_linear(const tg_params &p, const float *x0, const float *x1, const void *w, const float *bias,
+                               float *out, cudaStream_t s);
 // The q/k/v projection with rope_rows in its epilogue (bf16, n = (heads + 2 kv) hd, a multiple of 256).
 cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *b, const uint32_t *at,
                                  const float *cosv, const float *sinv, void *q, void *kc, void *vc, uint32_t *err,
