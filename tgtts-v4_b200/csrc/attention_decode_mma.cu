@@ -1,0 +1,202 @@
+// The batched decoder's attention_split (attention_split.comp:52-112) on the tensor cores, for bf16
+// caches and a head dimension of 64: a warp takes one chunk of ATTN_CHUNK positions of one row's
+// KV head, its query heads (a GQA group of up to 16) the rows of mma.sync.m16n8k16:
+//   S = q K^T over the chunk (8 n-tiles of 8 positions x 4 k-steps of 16 dimensions), q split
+//       into bf16 hi + lo (two MMAs a step) so the scores carry 16 bits of each query value;
+//   the chunk's softmax, unnormalised: m = the largest scaled score (positions past the row's
+//       masked), e = exp(s - m), l = sum e — each row's values in its quad of lanes;
+//   O = e V, e split into bf16 hi + lo the same way, V^T fragments by ldmatrix.trans.
+// It writes the partials attention_combine reads, as attention_split_kernel does: the same
+// layout and meaning (natural exponent, scale 1/sqrt(hd)), not the same bits. A block holds four
+// warps (four consecutive chunks of one row and KV head); each warp streams its chunk's keys and
+// values into its own shared memory with cp.async: the positions before the row's (written by
+// earlier steps) before the wait on the kernel before, the row's own position after it.
+#include "mma_common.cuh"
+#include "tg_internal.h"
+
+namespace tg {
+
+namespace {
+
+constexpr int AM_WARPS = 4;
+constexpr int AM_ROW = 64 + fa::PAD;  // bf16 per shared row
+constexpr int AM_WARP_SMEM = 2 * (int)ATTN_CHUNK * AM_ROW * 2;  // K and V of one chunk
+
+TG_DEVICE void split_pack(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float h0 = __low2float(h), h1 = __high2float(h);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(AM_WARPS * 32)
+    attention_split_mma_kernel(tg_params p, const float *__restrict__ q, const bf16 *__restrict__ kc,
+                               const bf16 *__restrict__ vc, const uint32_t *__restrict__ at, float *__restrict__ po,
+                               float *__restrict__ pml) {
+    using namespace fa;
+    extern __shared__ __align__(128) unsigned char am_smem[];
+    constexpr int C = ATTN_CHUNK, HD = 64;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
+    const int c = blockIdx.x * AM_WARPS + warp, kv = blockIdx.y, b = blockIdx.z;
+    const int heads = p.heads, kvh = p.kv_heads, group = heads / kvh, chunks = p.capacity / C;
+    bf16 *ks = reinterpret_cast<bf16 *>(am_smem + (size_t)warp * AM_WARP_SMEM);
+    bf16 *vs = ks + C * AM_ROW;
+    pdl_launch_dependents();
+    uint32_t pos = 0, slot = 0;
+    const bool live = placed(at, p.rows, b, p.capacity, p.slots, pos, slot) && c < chunks && c * C <= (int)pos;
+    const int start = c * C, own = (int)pos - start;  // the row's own position in the chunk, if any
+    const size_t base = (((size_t)slot * kvh + kv) * p.capacity + start) * HD;
+    if (live) {
+        for (int i = lane; i < C * 8; i += 32) {
+            const int r = i / 8, ch = i % 8;
+            if (r == own) continue;  // this step's, after the wait
+            const bool ok = r < own;
+            cp_async16(ks + r * AM_ROW + ch * 8, kc + base + (size_t)(ok ? r : 0) * HD + ch * 8, ok);
+            cp_async16(vs + r * AM_ROW + ch * 8, vc + base + (size_t)(ok ? r : 0) * HD + ch * 8, ok);
+        }
+        cp_async_commit();
+    }
+    pdl_wait();
+    if (!live) return;
+    if (own < C && lane < 8) {
+        cp_async16(ks + own * AM_ROW + lane * 8, kc + base + (size_t)own * HD + lane * 8, true);
+        cp_async16(vs + own * AM_ROW + lane * 8, vc + base + (size_t)own * HD + lane * 8, true);
+    }
+    cp_async_commit();
+    // q of the group's heads (rows g < group; rows g + 8 and past the group are zero), hi and lo.
+    uint32_t qh[4][4], ql[4][4];
+    const float *qg = q + ((size_t)b * heads + kv * group) * HD;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+#pragma unroll
+        for (int r = 0; r < 4; r++) qh[s][r] = ql[s][r] = 0u;
+        const int row0 = g, row1 = g + 8;
+        if (row0 < group) {
+            const float2 x0 = __ldcg(reinterpret_cast<const float2 *>(qg + row0 * HD + 16 * s + 2 * t4));
+            const float2 x2 = __ldcg(reinterpret_cast<const float2 *>(qg + row0 * HD + 16 * s + 8 + 2 * t4));
+            split_pack(x0.x, x0.y, qh[s][0], ql[s][0]);
+            split_pack(x2.x, x2.y, qh[s][2], ql[s][2]);
+        }
+        if (row1 < group) {
+            const float2 x1 = __ldcg(reinterpret_cast<const float2 *>(qg + row1 * HD + 16 * s + 2 * t4));
+            const float2 x3 = __ldcg(reinterpret_cast<const float2 *>(qg + row1 * HD + 16 * s + 8 + 2 * t4));
+            split_pack(x1.x, x1.y, qh[s][1], ql[s][1]);
+            split_pack(x3.x, x3.y, qh[s][3], ql[s][3]);
+        }
+    }
+    cp_async_wait<0>();
+    __syncwarp();
+    // S = q K^T: 8 n-tiles of 8 positions.
+    float sc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            uint32_t kb[4];
+            const int mi = lane >> 3, rr = lane & 7;
+            ldmatrix_x4(kb, ks + (8 * j + (mi >> 1) * 8 + rr) * AM_ROW + s * 16 + (mi & 1) * 8);
+            mma_bf16(sc[j], qh[s], kb[0], kb[1]);
+            mma_bf16(sc[j], ql[s], kb[0], kb[1]);
+            mma_bf16(sc[j + 1], qh[s], kb[2], kb[3]);
+            mma_bf16(sc[j + 1], ql[s], kb[2], kb[3]);
+        }
+    }
+    // The chunk's softmax, unnormalised, per query row (rows g and g + 8 of this lane's quad).
+    const float scale = 1.0f / sqrtf((float)HD);
+    float m[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int at_pos = start + 8 * j + 2 * t4 + (e & 1);
+            const float v = at_pos <= (int)pos ? sc[j][e] * scale : -INFINITY;
+            sc[j][e] = v;
+            m[e >> 1] = fmaxf(m[e >> 1], v);
+        }
+    float l[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], 1));
+        m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], 2));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float v = sc[j][e] == -INFINITY ? 0.0f : expf(sc[j][e] - m[e >> 1]);
+            sc[j][e] = v;
+            l[e >> 1] += v;
+        }
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
+        l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
+    }
+    // O = e V: e's accumulators as A fragments (hi and lo), V^T fragments by ldmatrix.trans.
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < 4; s++) {
+        uint32_t ph[4], pl[4];
+        split_pack(sc[2 * s][0], sc[2 * s][1], ph[0], pl[0]);
+        split_pack(sc[2 * s][2], sc[2 * s][3], ph[1], pl[1]);
+        split_pack(sc[2 * s + 1][0], sc[2 * s + 1][1], ph[2], pl[2]);
+        split_pack(sc[2 * s + 1][2], sc[2 * s + 1][3], ph[3], pl[3]);
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            uint32_t vb[4];
+            const int mi = lane >> 3, rr = lane & 7;
+            ldmatrix_x4_trans(vb, vs + (16 * s + (mi & 1) * 8 + rr) * AM_ROW + 8 * j + (mi >> 1) * 8);
+            mma_bf16(o[j], ph, vb[0], vb[1]);
+            mma_bf16(o[j], pl, vb[0], vb[1]);
+            mma_bf16(o[j + 1], ph, vb[2], vb[3]);
+            mma_bf16(o[j + 1], pl, vb[2], vb[3]);
+        }
+    }
+    // The partials of the group's heads (rows < group).
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int h = g + 8 * i;
+        if (h >= group) continue;
+        const size_t head = (size_t)b * heads + kv * group + h;
+        float *dst = po + (head * chunks + c) * HD;
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+            *reinterpret_cast<float2 *>(dst + 8 * j + 2 * t4) = make_float2(o[j][2 * i], o[j][2 * i + 1]);
+        if (t4 == 0) *reinterpret_cast<float2 *>(pml + (head * chunks + c) * 2) = make_float2(m[i], l[i]);
+    }
+}
+
+bool attention_split_mma_supported(const tg_params &p) {
+    return p.dtype == TG_BF16 && p.head_dim == 64 && p.kv_heads > 0 && p.heads % p.kv_heads == 0 &&
+           p.heads / p.kv_heads <= 16 && p.capacity % ATTN_CHUNK == 0;
+}
+
+cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
+                                       const uint32_t *at, float *po, float *pml, cudaStream_t s) {
+    if (!attention_split_mma_supported(p)) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)AM_WARPS * AM_WARP_SMEM;
+    cudaError_t e = cudaFuncSetAttribute(attention_split_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const int chunks = (int)(p.capacity / ATTN_CHUNK);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((chunks + AM_WARPS - 1) / AM_WARPS, p.kv_heads, p.rows);
+    cfg.blockDim = dim3(AM_WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, attention_split_mma_kernel, p, (const float *)q, (const bf16 *)kc, (const bf16 *)vc,
+                              at, po, pml);
+}
+
+}  // namespace tg

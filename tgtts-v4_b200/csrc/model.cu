@@ -150,7 +150,8 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
              {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
               {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * F},
               {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
-        push(v, TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
+        push(v, d.tensor && attention_split_mma_supported(base) ? KERNEL_ATTN_SPLIT_MMA : TG_KERNEL_ATTENTION_SPLIT,
+             base, "attention_split",
              {{d.q.ptr(), R * d.attn() * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}});

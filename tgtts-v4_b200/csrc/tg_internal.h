@@ -70,6 +70,11 @@ constexpr uint32_t KERNEL_DTC_QKV_ROPE = 1001;
 constexpr uint32_t KERNEL_DTC_GATE_UP = 1002;
 constexpr uint32_t KERNEL_DTC_RESIDUAL = 1003;
 
+// The batched decoder's attention_split on mma.sync (bf16, head_dim 64), ATTENTION_SPLIT's bindings.
+constexpr uint32_t KERNEL_ATTN_SPLIT_MMA = 1004;
+bool attention_split_mma_supported(const tg_params &p);
+cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
+                                       const uint32_t *at, float *po, float *pml, cudaStream_t s);
 // Decoders of at least this many rows run their projections on tcgen05 (every bucket of them).
 constexpr uint32_t DTC_MIN_ROWS = 16;
 
