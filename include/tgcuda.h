@@ -283,6 +283,14 @@ int tg_decoder_read_cache(tg_decoder *d, uint32_t layer, uint32_t slot, uint32_t
  * crates/graph/src/prompt.rs:587-633): moves positions [0, count) of slot `from` to slot `to`
  * in every layer, on the GPU. */
 int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, uint32_t count);
+/* Recording::copy_out / copy_in of a prefix's keys and values (crates/graph/src/prompt.rs:587-633,
+ * the prompt cache's kept prefix): positions [0, count) of `slot` in every layer, to or from
+ * `m` at `offset`, laid out [layers][k, v][kv_heads][count][head_dim] in the decoder's storage
+ * type; tg_decoder_prefix_bytes gives the size. Ordered on the context's stream with the steps
+ * and prefills around it. */
+uint64_t tg_decoder_prefix_bytes(const tg_decoder *d, uint32_t count);
+int tg_decoder_copy_out(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m, uint64_t offset);
+int tg_decoder_copy_in(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m, uint64_t offset);
 /* Decoder::retuned (decode.rs:874-890): records the step again over the same weights and cache, as
  * one persistent launch (persistent != 0; batches of up to 2 rows) or as six kernels a layer, timed
  * per dispatch when `timed`. Both give the same results bit for bit. A new decoder starts recorded
@@ -333,14 +341,16 @@ uint32_t tg_prefill_max_rows(const tg_prefill *p);
 typedef struct tg_server tg_server;
 typedef struct {
     uint32_t slot;  /* the slot it holds (a request there before is ended) */
-    uint32_t len;   /* prompt positions, prefilled at 0..len-1 */
+    uint32_t len;   /* prompt positions, prefilled at start..len-1 */
     uint32_t steps; /* decode steps after it, at positions len..len+steps-1 */
+    uint32_t start; /* positions already in the slot (a kept prefix copied in); 0 for none */
 } tg_request;
 int tg_server_create(tg_decoder *d, tg_prefill *p, tg_server **out);
 int tg_server_destroy(tg_server *s);
-/* Generator::start (generator.rs:189-262): runs the requests' prompts, x [sum len][hidden] f32 in
- * request order, into their slots (as few prefill launches as max_rows allows). Refuses a slot
- * twice, an empty prompt or no steps, and len + steps past the capacity (TG_ESHAPE). */
+/* Generator::start (generator.rs:189-262): runs the requests' prompts, x [sum (len - start)]
+ * [hidden] f32 in request order (each request's rows from its `start`), into their slots (as few
+ * prefill launches as max_rows allows). Refuses a slot twice, no positions to run or no steps,
+ * and len + steps past the capacity (TG_ESHAPE). */
 int tg_server_start(tg_server *s, const tg_request *reqs, uint32_t n, const float *x);
 /* Generator::step (generator.rs:295-352): one decode step of every request under way. x: NULL to
  * feed each request's last output back (on the GPU), else [n][hidden] f32 inputs in slot order.

@@ -123,3 +123,54 @@ def test_server_refusals(pkg, ctx, syn):
     wide = pkg.Decoder(ctx, shape, rows=2, slots=4, dtype="f32")
     with pytest.raises(pkg.ShapeError):
         pkg.Server(wide, pkg.Prefill(wide, max_rows=128))
+
+
+@pytest.mark.parametrize("dtype,layers", [("f32", None), ("bf16", 2)])
+def test_a_kept_prefix_gives_the_same_bits_as_the_whole_prompt(pkg, ctx, syn, dtype, layers):
+    """prompt.rs's prompt cache on the backbone: a request whose prompt begins with a kept prefix
+    copies its keys and values in and prefills only the rest, and comes out bit for bit as the
+    same request prefilled whole; the cache keeps to its budget."""
+    from tgtts_v4_b200.prompt_cache import PromptCache
+
+    cfg, shape, w, dec = _stack(pkg, ctx, syn, dtype, rows=4, capacity=512, layers=layers)
+    pre = pkg.Prefill(dec, max_rows=512)
+    server = pkg.Server(dec, pre)
+    cache = PromptCache(dec, budget=dec.prefix_bytes(300))
+    rng = np.random.default_rng(9)
+    voice = rng.standard_normal((260, cfg.hidden), dtype=np.float32)
+    tail = rng.standard_normal((40, cfg.hidden), dtype=np.float32)
+    prompt = np.concatenate([voice, tail])
+    steps = 6
+
+    def run(slot, start):
+        server.start([(slot, len(prompt), steps, start)], prompt[start:])
+        outs = []
+        for _ in range(steps):
+            slots, out = server.step()
+            outs.append(out[slots.index(slot)].copy())
+        server.finish(slot)
+        return outs
+
+    whole = run(0, 0)
+    # The voice alone, kept from its slot after its prefill.
+    server.start([(1, len(voice), 1)], voice)
+    server.step()
+    server.finish(1)
+    assert cache.keep(1, voice)
+    assert not cache.keep(1, voice[:100])  # already covered
+    start = cache.restore(2, prompt)
+    assert start == 260
+    cached = run(2, start)
+    for t in range(steps):
+        np.testing.assert_array_equal(cached[t], whole[t], err_msg=f"step {t}")
+    # The caches themselves match over the prompt's positions.
+    for layer in (0, shape.layers - 1):
+        np.testing.assert_array_equal(dec.read_cache(layer, 2, "k", 0, 300), dec.read_cache(layer, 0, "k", 0, 300))
+    # A second prefix past the budget drops the first.
+    other = rng.standard_normal((200, cfg.hidden), dtype=np.float32)
+    server.start([(3, 200, 1)], other)
+    server.step()
+    server.finish(3)
+    assert cache.keep(3, other)
+    assert cache.restore(0, prompt) == 0 and cache.bytes <= cache.budget
+    server.close()

@@ -114,7 +114,8 @@ class TgRun(ctypes.Structure):
 
 
 class TgRequest(ctypes.Structure):
-    _fields_ = [("slot", ctypes.c_uint32), ("len", ctypes.c_uint32), ("steps", ctypes.c_uint32)]
+    _fields_ = [("slot", ctypes.c_uint32), ("len", ctypes.c_uint32), ("steps", ctypes.c_uint32),
+                ("start", ctypes.c_uint32)]
 
 
 class TgParams(ctypes.Structure):
@@ -187,6 +188,9 @@ SIGNATURES = {
     "tg_decoder_dispatch_label": (_I, [_P, _SZ, ctypes.c_char_p, _SZ]),
     "tg_decoder_read_cache": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _FP]),
     "tg_decoder_copy_slot": (_I, [_P, _U32, _U32, _U32]),
+    "tg_decoder_prefix_bytes": (_U64, [_P, _U32]),
+    "tg_decoder_copy_out": (_I, [_P, _U32, _U32, _P, _U64]),
+    "tg_decoder_copy_in": (_I, [_P, _U32, _U32, _P, _U64]),
     "tg_decoder_weight_bytes": (_U64, [_P]),
     "tg_decoder_retune": (_I, [_P, _I, _I]),
     "tg_decoder_persistent": (_I, [_P]),
@@ -694,6 +698,17 @@ class Decoder:
         check(library().tg_decoder_timings(self.handle, ns, len(labels), None))
         return list(zip(labels, list(ns)))
 
+    def prefix_bytes(self, count: int) -> int:
+        return int(library().tg_decoder_prefix_bytes(self.handle, count))
+
+    def copy_out(self, slot: int, count: int, mem: "Memory", offset: int = 0) -> None:
+        """Positions [0, count) of the slot's keys and values into `mem` (a kept prefix)."""
+        check(library().tg_decoder_copy_out(self.handle, slot, count, mem.handle, offset))
+
+    def copy_in(self, slot: int, count: int, mem: "Memory", offset: int = 0) -> None:
+        """A kept prefix from `mem` into positions [0, count) of the slot."""
+        check(library().tg_decoder_copy_in(self.handle, slot, count, mem.handle, offset))
+
     def read_cache(self, layer: int, slot: int, kind: str, first: int, count: int) -> np.ndarray:
         """Keys ("k") or values ("v") of positions [first, first + count) of a slot, as f32
         [kv_heads][count][head_dim]."""
@@ -835,14 +850,16 @@ class Server:
         check(library().tg_server_create(decoder.handle, prefill.handle, ctypes.byref(h)))
         self.handle = h
 
-    def start(self, requests: Sequence[tuple[int, int, int]], x: np.ndarray) -> None:
-        """Generator::start for (slot, len, steps) requests, their prompts' rows of x in order."""
+    def start(self, requests: Sequence[tuple], x: np.ndarray) -> None:
+        """Generator::start for (slot, len, steps[, start]) requests, the rows of each prompt
+        from its start (positions already in the slot, a kept prefix copied in) in x, in order."""
         hdim = self.decoder.shape.hidden
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
-        total = sum(r[1] for r in requests)
+        reqs = [tuple(r) + (0,) * (4 - len(r)) for r in requests]
+        total = sum(r[1] - r[3] for r in reqs)
         if x.size != total * hdim:
             raise ShapeError(f"{x.size} values for {total} prompt rows of {hdim}")
-        c = (TgRequest * max(len(requests), 1))(*[TgRequest(*r) for r in requests])
+        c = (TgRequest * max(len(reqs), 1))(*[TgRequest(*r) for r in reqs])
         check(library().tg_server_start(self.handle, c, len(requests), _fptr(x)))
 
     def step(self, x: Optional[np.ndarray] = None, read: bool = True):

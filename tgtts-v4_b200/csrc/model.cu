@@ -597,6 +597,44 @@ extern "C" int tg_decoder_copy_slot(tg_decoder *d, uint32_t from, uint32_t to, u
     return tg_copy_regions(d->ctx, d->vcache.m, d->vcache.m, regions.data(), regions.size());
 }
 
+extern "C" uint64_t tg_decoder_prefix_bytes(const tg_decoder *d, uint32_t count) {
+    if (!d) return 0;
+    return (uint64_t)d->shape.layers * 2 * d->shape.kv_heads * count * d->shape.head_dim * d->esize;
+}
+
+// Positions [0, count) of `slot`, every layer and KV head, to (out) or from (in) `m` at `offset`.
+static int copy_prefix(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m, uint64_t offset, bool out) {
+    if (!d || !m) return fail(TG_EINVAL, "null argument");
+    const tg_shape &s = d->shape;
+    if (slot >= d->slots || count > s.capacity)
+        return fail(TG_ESHAPE, "%u positions of slot %u of %u", count, slot, d->slots);
+    const uint64_t bytes = tg_decoder_prefix_bytes(d, count);
+    if (offset + bytes > tg_mem_size(m)) return fail(TG_ESHAPE, "a prefix of %llu bytes past its buffer", (unsigned long long)bytes);
+    if (count == 0) return TG_OK;
+    TG_CUDA(cudaSetDevice(d->ctx->device));
+    const uint64_t hd = s.head_dim, T = d->esize, run = (uint64_t)count * hd * T;
+    uint64_t at = offset;
+    for (uint32_t l = 0; l < s.layers; l++)
+        for (int kind = 0; kind < 2; kind++)
+            for (uint32_t kv = 0; kv < s.kv_heads; kv++) {
+                char *cache = (kind == 0 ? d->kcache.ptr() : d->vcache.ptr()) + l * d->cache_layer +
+                              (((uint64_t)slot * s.kv_heads + kv) * s.capacity) * hd * T;
+                char *buf = static_cast<char *>(m->ptr) + at;
+                TG_CUDA(cudaMemcpyAsync(out ? buf : cache, out ? cache : buf, run, cudaMemcpyDeviceToDevice,
+                                        d->ctx->stream));
+                at += run;
+            }
+    return TG_OK;
+}
+
+extern "C" int tg_decoder_copy_out(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m, uint64_t offset) {
+    return copy_prefix(d, slot, count, m, offset, true);
+}
+
+extern "C" int tg_decoder_copy_in(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m, uint64_t offset) {
+    return copy_prefix(d, slot, count, m, offset, false);
+}
+
 extern "C" uint64_t tg_decoder_weight_bytes(const tg_decoder *d) {
     return d ? tg_shape_weight_bytes(&d->shape, (uint32_t)d->esize) : 0;
 }

@@ -89,9 +89,10 @@ extern "C" int tg_server_start(tg_server *s, const tg_request *reqs, uint32_t n,
     std::vector<bool> seen(d->slots, false);
     for (uint32_t i = 0; i < n; i++) {
         const tg_request &r = reqs[i];
-        if (r.slot >= d->slots || seen[r.slot] || r.len == 0 || r.steps == 0 || (uint64_t)r.len + r.steps > sh.capacity)
-            return fail(TG_ESHAPE, "request %u: slot %u of %u, %u positions and %u steps in a cache of %u", i, r.slot,
-                        d->slots, r.len, r.steps, sh.capacity);
+        if (r.slot >= d->slots || seen[r.slot] || r.start >= r.len || r.steps == 0 ||
+            (uint64_t)r.len + r.steps > sh.capacity)
+            return fail(TG_ESHAPE, "request %u: slot %u of %u, positions %u..%u and %u steps in a cache of %u", i,
+                        r.slot, d->slots, r.start, r.len, r.steps, sh.capacity);
         seen[r.slot] = true;
     }
     TG_CUDA(cudaSetDevice(d->ctx->device));
@@ -105,12 +106,13 @@ extern "C" int tg_server_start(tg_server *s, const tg_request *reqs, uint32_t n,
     std::vector<Piece> pieces;
     uint64_t src = 0;
     for (uint32_t i = 0; i < n; i++) {
-        for (uint32_t done = 0; done < reqs[i].len;) {
+        const uint32_t first = reqs[i].start;
+        for (uint32_t done = first; done < reqs[i].len;) {
             const uint32_t len = std::min(reqs[i].len - done, s->p->max_rows);
-            pieces.push_back({{done, len, reqs[i].slot}, src + done, done + len == reqs[i].len});
+            pieces.push_back({{done, len, reqs[i].slot}, src + (done - first), done + len == reqs[i].len});
             done += len;
         }
-        src += reqs[i].len;
+        src += reqs[i].len - first;
     }
     // Pieces of one slot run in order; each launch takes pieces of distinct slots while they fit.
     size_t at = 0;
