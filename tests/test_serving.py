@@ -122,3 +122,42 @@ def test_two_gloo_ranks_split_the_requests_and_take_the_max_time():
     for rank, ids, tmax in got:
         assert ids == [1] * 512  # every request on exactly one rank
         assert tmax == 2.0
+
+
+class FakeDecoder:
+    """A decoder's prefix copies recorded on the host: bytes per position, and what went where."""
+
+    def __init__(self, per_position=100):
+        self.per = per_position
+        self.ops = []
+
+    def prefix_bytes(self, n):
+        return n * self.per
+
+    def copy_out(self, slot, n, mem):
+        self.ops.append(("out", slot, n, mem))
+
+    def copy_in(self, slot, n, mem):
+        self.ops.append(("in", slot, n, mem))
+
+
+def test_prompt_cache_matches_the_longest_prefix_and_keeps_to_its_budget():
+    from tgtts_v4_b200.prompt_cache import PromptCache
+
+    dec = FakeDecoder()
+    cache = PromptCache(dec, budget=100 * 50, alloc=lambda n: ("mem", n))
+    rng = np.random.default_rng(1)
+    a = rng.standard_normal((30, 4), dtype=np.float32)
+    assert cache.keep(0, a[:20]) and cache.bytes == 2000
+    assert not cache.keep(0, a[:10])  # a prefix of a kept one
+    assert cache.keep(1, a)  # a longer one
+    k, n = cache.shared(np.concatenate([a[:25], rng.standard_normal((5, 4), dtype=np.float32)]))
+    assert n == 25 and len(k.bits) == 30
+    assert cache.shared(a[:12])[1] == 11  # the last position always runs
+    assert cache.restore(3, a[:12]) == 11 and dec.ops[-1][:3] == ("in", 3, 11)
+    assert cache.shared(rng.standard_normal((8, 4), dtype=np.float32))[1] == 0
+    # Past the budget the least recently used goes: a[:20] (not used since kept) before a.
+    b = rng.standard_normal((10, 4), dtype=np.float32)
+    assert cache.keep(2, b) and cache.bytes <= cache.budget
+    assert [len(k.bits) for k in cache.kept] == [30, 10]
+    assert not cache.keep(0, rng.standard_normal((60, 4), dtype=np.float32))  # larger than the budget

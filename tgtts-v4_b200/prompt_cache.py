@@ -16,7 +16,7 @@ from typing import Optional
 import numpy as np
 
 
-@dataclasses.dataclass
+@dataclasses.dataclass(eq=False)  # kept prefixes compare by identity
 class Kept:
     bits: np.ndarray  # [count][hidden] uint32: the rows' bits
     mem: object       # device memory holding the prefix's keys and values
@@ -25,9 +25,12 @@ class Kept:
 
 
 class PromptCache:
-    def __init__(self, decoder, budget: int):
+    def __init__(self, decoder, budget: int, alloc=None):
+        """`alloc(bytes)` gives device memory for a prefix (the package's Memory on the decoder's
+        context by default)."""
         self.decoder = decoder
         self.budget = budget
+        self.alloc = alloc
         self.bytes = 0
         self.clock = 0
         self.kept: list[Kept] = []
@@ -63,8 +66,6 @@ class PromptCache:
         """Keeps positions [0, len(rows)) of `slot` (written by the prompt `rows`) as a prefix,
         dropping the least recently used ones to make room; False when it cannot fit or is
         already kept."""
-        from . import Memory  # the package's device memory
-
         bits = self._bits(rows)
         for k in self.kept:
             if len(k.bits) >= len(bits) and np.array_equal(k.bits[:len(bits)], bits):
@@ -76,7 +77,12 @@ class PromptCache:
             old = min(self.kept, key=lambda k: k.used)
             self.kept.remove(old)
             self.bytes -= old.bytes
-        mem = Memory(self.decoder.ctx, need)
+        if self.alloc is None:
+            from . import Memory  # the package's device memory
+
+            mem = Memory(self.decoder.ctx, need)
+        else:
+            mem = self.alloc(need)
         self.decoder.copy_out(slot, len(rows), mem)
         self.clock += 1
         self.kept.append(Kept(bits.copy(), mem, need, self.clock))
