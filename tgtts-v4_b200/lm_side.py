@@ -124,9 +124,9 @@ class LmSide:
             [None if r is None else self.pkg.Row(*r) for r in rows], self.shape.base.capacity)
         self.enc.write(np.ascontiguousarray(enc, np.float32))
         self.programs[0].start()
-        self.base.step_device(words, self.embed.device_ptr(), self.base_out.device_ptr())
+        self.base.step_device(words, self.embed.device_ptr, self.base_out.device_ptr)
         self.programs[1].start()
-        self.residual.step_device(words, self.residual_in.device_ptr(), self.res_out.device_ptr())
+        self.residual.step_device(words, self.residual_in.device_ptr, self.res_out.device_ptr)
         self.programs[2].start()
         self.programs[2].wait()
         s = self.shape
