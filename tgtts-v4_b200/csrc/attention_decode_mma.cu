@@ -6,8 +6,10 @@
 //   the chunk's softmax, unnormalised: m = the largest scaled score (positions past the row's
 //       masked), e = exp(s - m), l = sum e — each row's values in its quad of lanes;
 //   O = e V, e split into bf16 hi + lo the same way, V^T fragments by ldmatrix.trans.
-// It writes the partials attention_combine reads, as attention_split_kernel does: the same
-// layout and meaning (natural exponent, scale 1/sqrt(hd)), not the same bits. A block holds four
+// It writes partials in attention_split_kernel's layout and meaning (natural exponent, scale
+// 1/sqrt(hd)), not the same bits, each over DECODE_WIDE_CHUNK positions rather than ATTN_CHUNK (a
+// warp walks its sub-chunks of ATTN_CHUNK with an online softmax), which attention_combine joins
+// told that width. A block holds four
 // warps (four consecutive chunks of one row and KV head); each warp streams its chunk's keys and
 // values into its own shared memory with cp.async: the positions before the row's (written by
 // earlier steps) before the wait on the kernel before, the row's own position after it.
@@ -32,40 +34,53 @@ TG_DEVICE void split_pack(float x0, float x1, uint32_t &hi, uint32_t &lo) {
 
 }  // namespace
 
+// SUB sub-chunks of ATTN_CHUNK positions a warp (a partial covers ATTN_CHUNK SUB positions): the
+// warp walks them in order with an online softmax (the running maximum, the sum and the output
+// rescaled as the maximum grows), so the partial is the same as one chunk's would be.
+template <int SUB>
 __global__ void __launch_bounds__(AM_WARPS * 32)
     attention_split_mma_kernel(tg_params p, const float *__restrict__ q, const bf16 *__restrict__ kc,
                                const bf16 *__restrict__ vc, const uint32_t *__restrict__ at, float *__restrict__ po,
                                float *__restrict__ pml) {
     using namespace fa;
     extern __shared__ __align__(128) unsigned char am_smem[];
-    constexpr int C = ATTN_CHUNK, HD = 64;
+    constexpr int C = ATTN_CHUNK, HD = 64, W = C * SUB;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const int c = blockIdx.x * AM_WARPS + warp, kv = blockIdx.y, b = blockIdx.z;
-    const int heads = p.heads, kvh = p.kv_heads, group = heads / kvh, chunks = p.capacity / C;
+    const int heads = p.heads, kvh = p.kv_heads, group = heads / kvh;
+    const int chunks = ((int)p.capacity + W - 1) / W, stride = (int)(p.capacity / ATTN_CHUNK);
     bf16 *ks = reinterpret_cast<bf16 *>(am_smem + (size_t)warp * AM_WARP_SMEM);
     bf16 *vs = ks + C * AM_ROW;
     pdl_launch_dependents();
     uint32_t pos = 0, slot = 0;
-    const bool live = placed(at, p.rows, b, p.capacity, p.slots, pos, slot) && c < chunks && c * C <= (int)pos;
-    const int start = c * C, own = (int)pos - start;  // the row's own position in the chunk, if any
-    const size_t base = (((size_t)slot * kvh + kv) * p.capacity + start) * HD;
-    if (live) {
-        for (int i = lane; i < C * 8; i += 32) {
-            const int r = i / 8, ch = i % 8;
-            if (r == own) continue;  // this step's, after the wait
-            const bool ok = r < own;
-            cp_async16(ks + r * AM_ROW + ch * 8, kc + base + (size_t)(ok ? r : 0) * HD + ch * 8, ok);
-            cp_async16(vs + r * AM_ROW + ch * 8, vc + base + (size_t)(ok ? r : 0) * HD + ch * 8, ok);
+    const bool live = placed(at, p.rows, b, p.capacity, p.slots, pos, slot) && c < chunks && c * W <= (int)pos;
+    const size_t slot_base = ((size_t)slot * kvh + kv) * p.capacity * HD;
+    // Sub-chunk i's keys and values into shared memory: positions before the row's as they are,
+    // past it zero; the row's own position only when `own_too` (after the wait).
+    auto load = [&](int i, bool own_too) {
+        const int start = c * W + i * C, own = (int)pos - start;
+        for (int e = lane; e < C * 8; e += 32) {
+            const int r = e / 8, ch = e % 8;
+            if (r == own && !own_too) continue;
+            const bool ok = r <= own && start + r < (int)p.capacity;
+            const size_t src = slot_base + (size_t)(ok ? start + r : 0) * HD + ch * 8;
+            cp_async16(ks + r * AM_ROW + ch * 8, kc + src, ok);
+            cp_async16(vs + r * AM_ROW + ch * 8, vc + src, ok);
+        }
+        cp_async_commit();
+    };
+    if (live) load(0, false);  // the first sub-chunk's earlier positions, before the wait
+    pdl_wait();
+    if (!live) return;
+    {
+        const int own = (int)pos - c * W;
+        if (own < C && lane < 8) {  // the row's own position, if in the first sub-chunk
+            const size_t src = slot_base + (size_t)pos * HD + lane * 8;
+            cp_async16(ks + own * AM_ROW + lane * 8, kc + src, true);
+            cp_async16(vs + own * AM_ROW + lane * 8, vc + src, true);
         }
         cp_async_commit();
     }
-    pdl_wait();
-    if (!live) return;
-    if (own < C && lane < 8) {
-        cp_async16(ks + own * AM_ROW + lane * 8, kc + base + (size_t)own * HD + lane * 8, true);
-        cp_async16(vs + own * AM_ROW + lane * 8, vc + base + (size_t)own * HD + lane * 8, true);
-    }
-    cp_async_commit();
     // q of the group's heads (rows g < group; rows g + 8 and past the group are zero), hi and lo.
     uint32_t qh[4][4], ql[4][4];
     const float *qg = q + ((size_t)b * heads + kv * group) * HD;
@@ -87,89 +102,111 @@ __global__ void __launch_bounds__(AM_WARPS * 32)
             split_pack(x3.x, x3.y, qh[s][3], ql[s][3]);
         }
     }
-    cp_async_wait<0>();
-    __syncwarp();
-    // S = q K^T: 8 n-tiles of 8 positions.
-    float sc[8][4];
-#pragma unroll
-    for (int j = 0; j < 8; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
-#pragma unroll
-    for (int s = 0; s < 4; s++) {
-#pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-            uint32_t kb[4];
-            const int mi = lane >> 3, rr = lane & 7;
-            ldmatrix_x4(kb, ks + (8 * j + (mi >> 1) * 8 + rr) * AM_ROW + s * 16 + (mi & 1) * 8);
-            mma_bf16(sc[j], qh[s], kb[0], kb[1]);
-            mma_bf16(sc[j], ql[s], kb[0], kb[1]);
-            mma_bf16(sc[j + 1], qh[s], kb[2], kb[3]);
-            mma_bf16(sc[j + 1], ql[s], kb[2], kb[3]);
-        }
-    }
-    // The chunk's softmax, unnormalised, per query row (rows g and g + 8 of this lane's quad).
     const float scale = 1.0f / sqrtf((float)HD);
-    float m[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int j = 0; j < 8; j++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int at_pos = start + 8 * j + 2 * t4 + (e & 1);
-            const float v = at_pos <= (int)pos ? sc[j][e] * scale : -INFINITY;
-            sc[j][e] = v;
-            m[e >> 1] = fmaxf(m[e >> 1], v);
-        }
-    float l[2] = {0.0f, 0.0f};
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-        m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], 1));
-        m[i] = fmaxf(m[i], __shfl_xor_sync(0xffffffffu, m[i], 2));
-    }
-#pragma unroll
-    for (int j = 0; j < 8; j++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const float v = sc[j][e] == -INFINITY ? 0.0f : expf(sc[j][e] - m[e >> 1]);
-            sc[j][e] = v;
-            l[e >> 1] += v;
-        }
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-        l[i] += __shfl_xor_sync(0xffffffffu, l[i], 1);
-        l[i] += __shfl_xor_sync(0xffffffffu, l[i], 2);
-    }
-    // O = e V: e's accumulators as A fragments (hi and lo), V^T fragments by ldmatrix.trans.
+    float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.0f, 0.0f};
     float o[8][4];
 #pragma unroll
     for (int j = 0; j < 8; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.0f;
+    for (int i = 0; i < SUB; i++) {
+        const int start = c * W + i * C;
+        if (start > (int)pos) break;
+        if (i > 0) {
+            __syncwarp();  // every lane is done with the last sub-chunk's shared memory
+            load(i, true);
+        }
+        cp_async_wait<0>();
+        __syncwarp();
+        // S = q K^T: 8 n-tiles of 8 positions.
+        float sc[8][4];
 #pragma unroll
-    for (int s = 0; s < 4; s++) {
-        uint32_t ph[4], pl[4];
-        split_pack(sc[2 * s][0], sc[2 * s][1], ph[0], pl[0]);
-        split_pack(sc[2 * s][2], sc[2 * s][3], ph[1], pl[1]);
-        split_pack(sc[2 * s + 1][0], sc[2 * s + 1][1], ph[2], pl[2]);
-        split_pack(sc[2 * s + 1][2], sc[2 * s + 1][3], ph[3], pl[3]);
+        for (int j = 0; j < 8; j++) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.0f;
 #pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-            uint32_t vb[4];
-            const int mi = lane >> 3, rr = lane & 7;
-            ldmatrix_x4_trans(vb, vs + (16 * s + (mi & 1) * 8 + rr) * AM_ROW + 8 * j + (mi >> 1) * 8);
-            mma_bf16(o[j], ph, vb[0], vb[1]);
-            mma_bf16(o[j], pl, vb[0], vb[1]);
-            mma_bf16(o[j + 1], ph, vb[2], vb[3]);
-            mma_bf16(o[j + 1], pl, vb[2], vb[3]);
+        for (int s = 0; s < 4; s++) {
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                uint32_t kb[4];
+                const int mi = lane >> 3, rr = lane & 7;
+                ldmatrix_x4(kb, ks + (8 * j + (mi >> 1) * 8 + rr) * AM_ROW + s * 16 + (mi & 1) * 8);
+                mma_bf16(sc[j], qh[s], kb[0], kb[1]);
+                mma_bf16(sc[j], ql[s], kb[0], kb[1]);
+                mma_bf16(sc[j + 1], qh[s], kb[2], kb[3]);
+                mma_bf16(sc[j + 1], ql[s], kb[2], kb[3]);
+            }
+        }
+        // The sub-chunk's maxima joined with the running ones; the running sums and outputs
+        // rescaled to the new maxima (the first sub-chunk's scale is 0 against an empty run).
+        float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int at_pos = start + 8 * j + 2 * t4 + (e & 1);
+                const float v = at_pos <= (int)pos ? sc[j][e] * scale : -INFINITY;
+                sc[j][e] = v;
+                mx[e >> 1] = fmaxf(mx[e >> 1], v);
+            }
+        float alpha[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+            mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+            const float next = fmaxf(m[r], mx[r]);
+            alpha[r] = m[r] == -INFINITY ? 0.0f : expf(m[r] - next);
+            m[r] = next;
+        }
+        float ls[2] = {0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float v = sc[j][e] == -INFINITY ? 0.0f : expf(sc[j][e] - m[e >> 1]);
+                sc[j][e] = v;
+                ls[e >> 1] += v;
+            }
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+            ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+            l[r] = __fmaf_rn(l[r], alpha[r], ls[r]);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            o[j][0] *= alpha[0];
+            o[j][1] *= alpha[0];
+            o[j][2] *= alpha[1];
+            o[j][3] *= alpha[1];
+        }
+        // O += e V: e's accumulators as A fragments (hi and lo), V^T fragments by ldmatrix.trans.
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+            uint32_t ph[4], pl[4];
+            split_pack(sc[2 * s][0], sc[2 * s][1], ph[0], pl[0]);
+            split_pack(sc[2 * s][2], sc[2 * s][3], ph[1], pl[1]);
+            split_pack(sc[2 * s + 1][0], sc[2 * s + 1][1], ph[2], pl[2]);
+            split_pack(sc[2 * s + 1][2], sc[2 * s + 1][3], ph[3], pl[3]);
+#pragma unroll
+            for (int j = 0; j < 8; j += 2) {
+                uint32_t vb[4];
+                const int mi = lane >> 3, rr = lane & 7;
+                ldmatrix_x4_trans(vb, vs + (16 * s + (mi & 1) * 8 + rr) * AM_ROW + 8 * j + (mi >> 1) * 8);
+                mma_bf16(o[j], ph, vb[0], vb[1]);
+                mma_bf16(o[j], pl, vb[0], vb[1]);
+                mma_bf16(o[j + 1], ph, vb[2], vb[3]);
+                mma_bf16(o[j + 1], pl, vb[2], vb[3]);
+            }
         }
     }
-    // The partials of the group's heads (rows < group).
+    // The partials of the group's heads (rows < group), at partial index c of `stride`.
 #pragma unroll
     for (int i = 0; i < 2; i++) {
         const int h = g + 8 * i;
         if (h >= group) continue;
         const size_t head = (size_t)b * heads + kv * group + h;
-        float *dst = po + (head * chunks + c) * HD;
+        float *dst = po + (head * stride + c) * HD;
 #pragma unroll
         for (int j = 0; j < 8; j++)
             *reinterpret_cast<float2 *>(dst + 8 * j + 2 * t4) = make_float2(o[j][2 * i], o[j][2 * i + 1]);
-        if (t4 == 0) *reinterpret_cast<float2 *>(pml + (head * chunks + c) * 2) = make_float2(m[i], l[i]);
+        if (t4 == 0) *reinterpret_cast<float2 *>(pml + (head * stride + c) * 2) = make_float2(m[i], l[i]);
     }
 }
 
@@ -181,10 +218,12 @@ bool attention_split_mma_supported(const tg_params &p) {
 cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
                                        const uint32_t *at, float *po, float *pml, cudaStream_t s) {
     if (!attention_split_mma_supported(p)) return cudaErrorInvalidValue;
+    constexpr int SUB = DECODE_WIDE_CHUNK / ATTN_CHUNK;
+    auto kern = attention_split_mma_kernel<SUB>;
     const size_t smem = (size_t)AM_WARPS * AM_WARP_SMEM;
-    cudaError_t e = cudaFuncSetAttribute(attention_split_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const int chunks = (int)(p.capacity / ATTN_CHUNK);
+    const int chunks = (int)((p.capacity + DECODE_WIDE_CHUNK - 1) / DECODE_WIDE_CHUNK);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((chunks + AM_WARPS - 1) / AM_WARPS, p.kv_heads, p.rows);
     cfg.blockDim = dim3(AM_WARPS * 32);
@@ -195,8 +234,7 @@ cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, attention_split_mma_kernel, p, (const float *)q, (const bf16 *)kc, (const bf16 *)vc,
-                              at, po, pml);
+    return cudaLaunchKernelEx(&cfg, kern, p, (const float *)q, (const bf16 *)kc, (const bf16 *)vc, at, po, pml);
 }
 
 }  // namespace tg

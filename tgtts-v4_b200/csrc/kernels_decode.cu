@@ -484,14 +484,15 @@ __global__ void __launch_bounds__(128)
 __global__ void __launch_bounds__(128)
     attention_combine_kernel(tg_params p, const uint32_t *__restrict__ at,
                              const float *__restrict__ po, const float *__restrict__ pml,
-                             float *__restrict__ out) {
+                             float *__restrict__ out, uint32_t width) {
     extern __shared__ __align__(128) unsigned char smem[];
     pdl_launch_dependents();
     pdl_wait();
     const int h = blockIdx.x, b = blockIdx.y, hd = p.head_dim;
     uint32_t pos, slot;
     if (!placed(at, p.rows, b, p.capacity, p.slots, pos, slot)) return;
-    const int chunks = p.capacity / ATTN_CHUNK, n = pos / ATTN_CHUNK + 1;
+    // Partials of `width` positions each, laid out as ATTN_CHUNK's (capacity / ATTN_CHUNK a head).
+    const int chunks = p.capacity / ATTN_CHUNK, n = pos / width + 1;
     float *ml = reinterpret_cast<float *>(smem);  // [n][2]
     float *w = ml + 2 * chunks;                    // [n]
     __shared__ float m_s, total_s;
@@ -1212,12 +1213,17 @@ cudaError_t launch_attention_split(const tg_params &p, const void *q, const void
                               : split_t<float>(p, q, kc, vc, at, po, pml, s);
 }
 
-cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, const float *po,
-                                     const float *pml, void *out, cudaStream_t s) {
+cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, const uint32_t *at, const float *po,
+                                           const float *pml, void *out, cudaStream_t s) {
     dim3 grid(p.heads, p.rows);
     const int threads = p.head_dim < 128 ? p.head_dim : 128;
     const size_t smem = (size_t)3 * (p.capacity / ATTN_CHUNK) * sizeof(float);
-    return launch_pdl(attention_combine_kernel, grid, dim3(threads), smem, s, p, at, po, pml, (float *)out);
+    return launch_pdl(attention_combine_kernel, grid, dim3(threads), smem, s, p, at, po, pml, (float *)out, chunk);
+}
+
+cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, const float *po,
+                                     const float *pml, void *out, cudaStream_t s) {
+    return launch_attention_combine_chunk(p, ATTN_CHUNK, at, po, pml, out, s);
 }
 
 static size_t cluster_attention_smem(const tg_params &p) {

@@ -150,12 +150,12 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
              {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
               {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * F},
               {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
-        push(v, d.tensor && attention_split_mma_supported(base) ? KERNEL_ATTN_SPLIT_MMA : TG_KERNEL_ATTENTION_SPLIT,
-             base, "attention_split",
+        const bool wide = d.tensor && attention_split_mma_supported(base);
+        push(v, wide ? KERNEL_ATTN_SPLIT_MMA : TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
              {{d.q.ptr(), R * d.attn() * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}});
-        push(v, TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
+        push(v, wide ? KERNEL_ATTN_COMBINE_WIDE : TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
              {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.att.ptr(), R * d.attn() * F}});
         tg_params po = base;

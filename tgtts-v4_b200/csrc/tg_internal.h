@@ -70,8 +70,15 @@ constexpr uint32_t KERNEL_DTC_QKV_ROPE = 1001;
 constexpr uint32_t KERNEL_DTC_GATE_UP = 1002;
 constexpr uint32_t KERNEL_DTC_RESIDUAL = 1003;
 
-// The batched decoder's attention_split on mma.sync (bf16, head_dim 64), ATTENTION_SPLIT's bindings.
+// The batched decoder's attention_split on mma.sync (bf16, head_dim 64), ATTENTION_SPLIT's bindings,
+// each partial over DECODE_WIDE_CHUNK positions; and attention_combine over such partials.
 constexpr uint32_t KERNEL_ATTN_SPLIT_MMA = 1004;
+constexpr uint32_t KERNEL_ATTN_COMBINE_WIDE = 1005;
+// 64: wider partials (a warp walking sub-chunks) measured slower on B200 at 16-128 rows: 2.15 ms
+// a step at 64 rows with 256 against 2.00 ms with 64.
+constexpr uint32_t DECODE_WIDE_CHUNK = 64;
+cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, const uint32_t *at, const float *po,
+                                           const float *pml, void *out, cudaStream_t s);
 bool attention_split_mma_supported(const tg_params &p);
 cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
                                        const uint32_t *at, float *po, float *pml, cudaStream_t s);
