@@ -258,6 +258,10 @@ def run_ours(args, rank, world, local):
     return result
 
 
+# DRAM bytes of one gemv_gate_up launch at config 2 from an ncu capture (read 16,824,832, written 0).
+GATE_UP_TRAFFIC = 16824832
+
+
 def gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind, layers=24, reps=20):
     """The dominant decode kernel, gemv_gate_up (56% of a step's weight bytes), timed alone: a
     program of one launch per layer over `layers` distinct weight buffers (403 MB, beyond L2), as
@@ -286,7 +290,7 @@ def gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind, layers=24, 
     return {"kernel": "gemv_gate_up (fused RMSNorm + gate/up GEMV + SiLU-mul), batch 1", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "bytes_per_launch": algo,
-            "launch_us": round(ns / 1e3, 3), "traffic": None,
+            "launch_us": round(ns / 1e3, 3), "traffic": GATE_UP_TRAFFIC, "traffic_source": "ncu --set full capture of one launch at config 2: dram__bytes_read.sum + dram__bytes_write.sum",
             "how": f"one program of {n} back-to-back launches cycling over {layers} distinct weight buffers, "
                    "CUDA events at its ends"}
 
