@@ -179,6 +179,8 @@ def run_ours(args, rank, world, local):
     stream = stream_ctx(ctx)
     H = cfg.hidden
 
+    launches_per_step = len(dec.labels())  # the recorded step's kernels (6 a layer + the final norm)
+
     # ---- value: device-resident decode steps, CUDA events on the runtime's stream ----
     x_dev = torch.from_numpy(pre_out[-1:].copy()).to(f"cuda:{local}")
     out_dev = torch.empty_like(x_dev)
@@ -248,7 +250,7 @@ def run_ours(args, rank, world, local):
                     "d2h_bytes_per_step": H * 4},
             "roofline": roof,
             "cpu_baseline": cpu,
-            "gpu_launches": (6 * shape.layers + 1) * args.steps,
+            "gpu_launches": launches_per_step * args.steps,
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
             "extras": extras,
         }
@@ -586,8 +588,8 @@ def run_serve(args, rank, world, local):
                        "parallelism": f"replicas x{world}, least-loaded assignment"},
             "prefill_tokens": prefilled, "decode_tokens": decoded, "seconds": round(ms_max / 1e3, 3),
             "step_latency_ms": {"p50": round(p50, 4), "p99": round(p99, 4), "max_over_ranks": world > 1},
-            # Decode steps only: the gather, the step's 6 per layer and the final norm, the scatter.
-            "gpu_launches": n_steps * (6 * shape.layers + 3),
+            # Decode steps only: the gather, the step's kernels, the scatter.
+            "gpu_launches": n_steps * (len(dec.labels()) + 2),
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
         }
     server.close()
