@@ -48,7 +48,8 @@ typedef enum {
     TG_RES_READBACK = 2  /* pinned host memory the GPU writes and the host reads */
 } tg_residence;
 
-typedef enum { TG_F32 = 0, TG_BF16 = 1 } tg_dtype;
+/* TG_F16 is the local stacks' storage type (and a source type for loads). */
+typedef enum { TG_F32 = 0, TG_BF16 = 1, TG_F16 = 2 } tg_dtype;
 
 typedef struct tg_ctx tg_ctx;
 typedef struct tg_mem tg_mem;
@@ -153,7 +154,47 @@ typedef enum {
      * stop_proj/stop_head). The reference stores f16 bias and output; here both are f32.
      *                                                                       gemv_linear.comp */
     TG_KERNEL_GEMV_LINEAR = 17,
-    TG_KERNEL_COUNT = 18
+    /* ---- VoxCPM2's local stacks (crates/graph/src/local/mod.rs:29-109), dtype TG_F16: f16
+     * weights and activations, f32 sums. `m` tokens in sequences of `capacity` tokens. The tokens
+     * a projection reads are stored k-block-major, [k / 64][m][64] ("kb"); the residual stream
+     * row-major [m][hidden].
+     * x f16 [m][hidden], gain f16 [hidden] -> out f16 kb                         local_norm.comp */
+    TG_KERNEL_LOCAL_NORM = 18,
+    /* x f16 kb [k / 64][m][64], W f16 [n][k] tiled -> partial f32 [parts][m][n]: part j the sums over columns
+     * [j k / parts, (j + 1) k / parts) (tcgen05; n a multiple of 128, k / parts of 64). W tiled: each
+     * 128 rows x 64 columns one contiguous 16 KiB block, block (t, b) at (t k / 64 + b) 16 KiB, row
+     * r's 16-byte chunk c of it at (r / 8) 1024 + (r % 8) 128 + (c ^ (r % 8)) 16 (the 128-byte
+     * swizzle; local::tiled's purpose, local/mod.rs:737-755). The q/k/v, output and down
+     * projections.                        local_partial.comp, local_qkv_rope.comp's products */
+    TG_KERNEL_LOCAL_PARTIAL = 19,
+    /* x f16 kb, W f16 [n][k] tiled as LOCAL_PARTIAL's, gate and up rows alternating (row 2i
+     * gate_proj row i, row 2i + 1 up_proj row i) -> out f16 kb [n / 128][m][64] = SiLU(gate) up (tcgen05)
+     *                                                                          local_gate_up.comp */
+    TG_KERNEL_LOCAL_GATE_UP = 20,
+    /* partial f32 [parts][m][(heads + 2 kv) hd] (the q/k/v projection's), cos f32, sin f32
+     * [capacity][hd / 2] -> out f16 kb [heads hd / 64][m][64]: the parts joined in order, q and k rotated, all
+     * rounded to f16, each token attending to every token of its sequence
+     *                                     local_qkv_rope.comp:57-91 + local_attention.comp */
+    TG_KERNEL_LOCAL_ATTENTION = 21,
+    /* partial f32 [parts][m][n], residual f16 [m][n], gain f16 [n] -> sum f16 [m][n], normed f16 kb
+     *                                                                       local_add_norm.comp */
+    TG_KERNEL_LOCAL_ADD_NORM = 22,
+    /* x f16 kb (m = rows capacity tokens) -> out f16 [rows][n], each sequence's first token
+     *                                                                            local_rows.comp */
+    TG_KERNEL_LOCAL_ROWS = 23,
+    /* src f32 [rows][feat][frames], W f16 [n][feat], bias f16 [n], tokens f16 ([copied][n] when
+     * flags & 2, else [rows][copied][n]) -> h f16 [rows][seqs][capacity][n]: tokens first ..
+     * first + frames - 1 projected from the frames, `copied` tokens at `at` copied (zero past the
+     * first sequence when flags & 1); the others left                           local_embed.comp */
+    TG_KERNEL_LOCAL_EMBED = 24,
+    /* noise f32 [rows][feat frames], sampling f32 [rows][2] -> x f32 = temperature noise
+     *                                                                            cfm_noise.comp */
+    TG_KERNEL_CFM_NOISE = 25,
+    /* h f16 kb (m = rows 2 capacity tokens), W f16 [feat][k], bias f16 [feat], sampling f32 [rows][2],
+     * x f32 [rows][feat][frames] (read and written): x -= dt times the guided velocity of tokens
+     * first .. first + frames - 1                                                dit_euler.comp */
+    TG_KERNEL_DIT_EULER = 26,
+    TG_KERNEL_COUNT = 27
 } tg_kernel_id;
 
 /* The stack's shape, as one struct all kernels' params share (decode.rs:66-83 `Shape`, plus the
@@ -172,6 +213,12 @@ typedef struct {
      * tanh rounded to a multiple of 1 / levels). */
     uint32_t k1, offset, stride, act;
     float levels;
+    /* The local stacks' kernels: the column parts of a projection's partial sums; LOCAL_EMBED's
+     * sequences a row, first projected token, first copied token, tokens copied and flags (1: the
+     * copies are zero past the first sequence, 2: one set of copied tokens for every row); a
+     * patch's frames and channels; DIT_EULER's step length. */
+    uint32_t parts, seqs, first, at, copied, flags, frames, feat;
+    float dt;
 } tg_params;
 
 typedef struct {
@@ -368,6 +415,74 @@ int tg_server_finish(tg_server *s, uint32_t slot);
 int tg_server_last_output(tg_server *s, uint32_t slot, float *out);
 /* Waits for every step enqueued (TG_ETIMEOUT after timeout_ns; 0: no limit). */
 int tg_server_sync(tg_server *s, uint64_t timeout_ns);
+
+/* ---- The local stacks: VoxCPM2's patch sampler and local encoder (crates/graph/src/local) ------
+ * Each is a bidirectional MiniCPM-4 stack over the few tokens of one patch per sequence (f16
+ * weights and activations, f32 sums), recorded once as one program (a CUDA graph) and run whole.
+ * A row's results are the same bits whatever rows run beside it. */
+typedef struct tg_sampler tg_sampler;
+typedef struct tg_encoder tg_encoder;
+
+/* local::Tuning's cuts that decide the order of the sums (local/mod.rs:187-214): the column parts
+ * of the q/k/v, output and down projections' sums, each part a multiple of 64 columns (0: the
+ * default, 4, 8 and 8, or the most the width allows). */
+typedef struct {
+    uint32_t qkv_parts, o_parts, down_parts;
+} tg_local_tuning;
+
+/* sampler_graph / Sampler::new (local/dit.rs:112-281): the DiT's stack `stack` (its capacity is
+ * set here: 2 + 1 + 2 patch_size tokens a sequence; `rope_factors` as the base LM's), patches of
+ * `patch_size` frames of `feat_dim` channels, `timesteps` Euler steps, `rows` rows (two
+ * sequences each). Every weight zero until loaded. Refuses shapes the kernels do not take
+ * (TG_ESHAPE), as the reference's checks (local/mod.rs:366-385, dit.rs:196-212). */
+int tg_sampler_create(tg_ctx *ctx, const tg_shape *stack, uint32_t feat_dim, uint32_t patch_size,
+                      uint32_t timesteps, uint32_t rows, const tg_local_tuning *tuning, int timed,
+                      tg_sampler **out);
+int tg_sampler_destroy(tg_sampler *s);
+/* load_sampler (local/dit.rs:325-370): one tensor by its upstream name, from f32, bf16 or f16
+ * values, rounded to f16: "feat_decoder.estimator.decoder.layers.{l}.self_attn.{q,k,v,o}_proj.weight",
+ * "...layers.{l}.mlp.{gate,up,down}_proj.weight", "...layers.{l}.{input,post_attention}_layernorm.weight",
+ * "feat_decoder.estimator.decoder.norm.weight", "feat_decoder.estimator.{in,cond,out}_proj.{weight,bias}",
+ * "feat_decoder.estimator.{time,delta_time}_mlp.linear_{1,2}.{weight,bias}". The steps' time tokens
+ * are computed from the two MLPs on the host in f64 (dit.rs:386-422) before the next sample. */
+int tg_sampler_load(tg_sampler *s, const char *name, const void *src, uint64_t count, tg_dtype src_dtype);
+/* Sampler::sample (local/dit.rs:298-313): mu f16 bits [rows][2][hidden], cond and noise f32
+ * [rows][feat_dim][patch_size], sampling f32 [rows][2] (temperature, guidance scale) -> patch f32
+ * [rows][feat_dim][patch_size]. */
+int tg_sampler_sample(tg_sampler *s, const uint16_t *mu, const float *cond, const float *noise,
+                      const float *sampling, float *patch);
+/* The same from device pointers, enqueued on the context's stream without waiting. */
+int tg_sampler_sample_device(tg_sampler *s, const void *mu, const float *cond, const float *noise,
+                             const float *sampling, float *patch);
+int tg_sampler_wait(tg_sampler *s, uint64_t timeout_ns);
+/* The time and step length of each step the DiT runs at (euler_steps). */
+int tg_sampler_steps(const tg_sampler *s, float *t, float *dt, size_t n, size_t *count);
+int tg_sampler_elapsed_ns(tg_sampler *s, double *ns);
+int tg_sampler_timings(tg_sampler *s, double *ns, size_t n, size_t *n_dispatches);
+int tg_sampler_dispatch_label(tg_sampler *s, size_t i, char *label, size_t label_bytes);
+/* Bytes of weights one run of the DiT reads (f16). */
+uint64_t tg_sampler_weight_bytes(const tg_sampler *s);
+
+/* dit.rs:39-81 as functions: the timesteps + 1 times the sampler steps through, and the steps
+ * (time, length) the DiT runs at (count written to *count; n the room in t and dt). */
+int tg_cfm_schedule(uint32_t timesteps, float *out);
+int tg_cfm_euler_steps(uint32_t timesteps, float *t, float *dt, size_t n, size_t *count);
+
+/* encoder_graph / Encoder (local/encoder.rs:41-124, :160-215): sequences of 1 + patch_size tokens,
+ * `rows` rows. Names: "feat_encoder.encoder.layers.{l}...", "feat_encoder.encoder.norm.weight",
+ * "feat_encoder.special_token", "feat_encoder.in_proj.{weight,bias}". */
+int tg_encoder_create(tg_ctx *ctx, const tg_shape *stack, uint32_t feat_dim, uint32_t patch_size,
+                      uint32_t rows, const tg_local_tuning *tuning, int timed, tg_encoder **out);
+int tg_encoder_destroy(tg_encoder *e);
+int tg_encoder_load(tg_encoder *e, const char *name, const void *src, uint64_t count, tg_dtype src_dtype);
+/* Encoder::encode: patches f32 [rows][feat_dim][patch_size] -> out f16 bits [rows][hidden]. */
+int tg_encoder_encode(tg_encoder *e, const float *patches, uint16_t *out);
+int tg_encoder_encode_device(tg_encoder *e, const float *patches, void *out);
+int tg_encoder_wait(tg_encoder *e, uint64_t timeout_ns);
+int tg_encoder_elapsed_ns(tg_encoder *e, double *ns);
+int tg_encoder_timings(tg_encoder *e, double *ns, size_t n, size_t *n_dispatches);
+int tg_encoder_dispatch_label(tg_encoder *e, size_t i, char *label, size_t label_bytes);
+uint64_t tg_encoder_weight_bytes(const tg_encoder *e);
 
 /* ---- Decode attention without allocation -------------------------------------------------------
  * No counterpart in tgtts-v4. For callers that cannot allocate device memory themselves or let a

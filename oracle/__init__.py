@@ -176,3 +176,135 @@ class OracleStack:
         if st:
             raise ValueError("oracle: shape refused")
         return out
+
+
+# ---- VoxCPM2's local stacks (local_ref.c) ---------------------------------------------------------
+
+class _LocalShape(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("hidden", "inner", "heads", "kv_heads", "head_dim", "layers", "tokens")] + [
+        ("eps", ctypes.c_float), ("cos", _FP), ("sin", _FP)]
+
+
+class _LocalLayer(ctypes.Structure):
+    _fields_ = [(n, _FP) for n in ("input_norm", "qkv", "o", "post_norm", "gate", "up", "down")]
+
+
+def _local_library() -> ctypes.CDLL:
+    lib = library()
+    if not getattr(lib, "_local_typed", False):
+        I32 = ctypes.c_int32
+        SP, LP, DP = ctypes.POINTER(_LocalShape), ctypes.POINTER(_LocalLayer), ctypes.POINTER(ctypes.c_double)
+        lib.tgo_local_set_threads.argtypes = [I32]
+        lib.tgo_round_f16.argtypes = [_FP, ctypes.c_int64]
+        lib.tgo_local_stack.argtypes = [SP, LP, _FP, I32, _FP, _FP]
+        lib.tgo_schedule.argtypes = [I32, _FP]
+        lib.tgo_euler_steps.argtypes = [I32, _FP, _FP]
+        lib.tgo_euler_steps.restype = I32
+        lib.tgo_time_tokens.argtypes = [I32] + [_FP] * 8 + [I32, _FP, DP]
+        lib.tgo_sampler.argtypes = [SP, LP, _FP] + [_FP] * 8 + [I32, I32, I32, I32, _FP, _FP, _FP, _FP, _FP]
+        lib.tgo_encoder.argtypes = [SP, LP, _FP, _FP, _FP, _FP, I32, I32, I32, _FP, _FP]
+        for f in ("tgo_local_set_threads", "tgo_round_f16", "tgo_local_stack", "tgo_schedule",
+                  "tgo_time_tokens", "tgo_sampler", "tgo_encoder"):
+            getattr(lib, f).restype = None
+        lib._local_typed = True
+    return lib
+
+
+def round_f16(x: np.ndarray) -> np.ndarray:
+    """The f32 values of x rounded to f16 (RNE), by the oracle's own conversion."""
+    a = np.array(x, np.float32, copy=True, order="C")
+    _local_library().tgo_round_f16(_fp(a), a.size)
+    return a
+
+
+def cfm_schedule(timesteps: int) -> np.ndarray:
+    out = np.zeros(timesteps + 1, np.float32)
+    _local_library().tgo_schedule(timesteps, _fp(out))
+    return out
+
+
+def cfm_euler_steps(timesteps: int) -> list[tuple[float, float]]:
+    t = np.zeros(timesteps + 1, np.float32)
+    dt = np.zeros_like(t)
+    n = _local_library().tgo_euler_steps(timesteps, _fp(t), _fp(dt))
+    return [(float(a), float(b)) for a, b in zip(t[:n], dt[:n])]
+
+
+class OracleLocal:
+    """A local stack (the sampler's DiT or the local encoder) on the CPU: f32 copies of its weights
+    rounded to f16, as the GPU holds them, run by local_ref.c. `prefix` is the stack's name prefix
+    ("feat_decoder.estimator." or "feat_encoder.")."""
+
+    def __init__(self, shape, weights: Mapping[str, np.ndarray], prefix: str, tokens: int,
+                 threads: Optional[int] = None):
+        lib = _local_library()
+        lib.tgo_local_set_threads(threads or os.cpu_count() or 1)
+        s = shape
+        self.shape, self.prefix, self.tokens = s, prefix, tokens
+        self.cos, self.sin = rope_tables(s.head_dim, tokens, s.rope_theta, s.rope_factors)
+        self._c = _LocalShape(s.hidden, s.inner, s.heads, s.kv_heads, s.head_dim, s.layers, tokens,
+                              s.eps, _fp(self.cos), _fp(self.sin))
+        self.w = {k: round_f16(np.asarray(v, np.float32)) for k, v in weights.items()
+                  if k.startswith(prefix)}
+        stack = prefix + ("decoder." if prefix.startswith("feat_decoder") else "encoder.")
+        self.layers = (_LocalLayer * s.layers)()
+        self._keep = []
+        for l in range(s.layers):
+            g = lambda n: self.w[f"{stack}layers.{l}.{n}.weight"]  # noqa: E731
+            qkv = np.ascontiguousarray(np.concatenate(
+                [g("self_attn.q_proj"), g("self_attn.k_proj"), g("self_attn.v_proj")]))
+            arrs = [g("input_layernorm"), qkv, g("self_attn.o_proj"), g("post_attention_layernorm"),
+                    g("mlp.gate_proj"), g("mlp.up_proj"), g("mlp.down_proj")]
+            arrs = [np.ascontiguousarray(a, np.float32) for a in arrs]
+            self._keep += arrs
+            self.layers[l] = _LocalLayer(*[_fp(a) for a in arrs])
+        self.final = np.ascontiguousarray(self.w[f"{stack}norm.weight"])
+
+    def stack(self, x: np.ndarray, seqs: int) -> np.ndarray:
+        """tgo_local_stack: x [seqs tokens][hidden] (f16 values) -> the tokens after the final norm."""
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.empty_like(x)
+        _local_library().tgo_local_stack(ctypes.byref(self._c), self.layers, _fp(self.final), seqs,
+                                         _fp(x), _fp(out))
+        return out
+
+    def time_tokens(self, times: Sequence[float]) -> np.ndarray:
+        """dit.rs:372-422 in f64, then rounded to f16 (as f32 values)."""
+        p, H = self.prefix, self.shape.hidden
+        ws = [np.ascontiguousarray(self.w[f"{p}{m}.linear_{i}.{kind}"], np.float32)
+              for m in ("time_mlp", "delta_time_mlp") for i in (1, 2) for kind in ("weight", "bias")]
+        t = np.ascontiguousarray(times, np.float32)
+        out = np.zeros((len(t), H), np.float64)
+        _local_library().tgo_time_tokens(H, *[_fp(a) for a in ws], len(t), _fp(t),
+                                         out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+        return out.astype(np.float16).astype(np.float32)
+
+    def sample(self, mu: np.ndarray, cond: np.ndarray, noise: np.ndarray, sampling: np.ndarray,
+               timesteps: int, feat: int, patch: int) -> np.ndarray:
+        """tgo_sampler: each row's patch, [rows][feat][patch]."""
+        p = self.prefix
+        steps = cfm_euler_steps(timesteps)
+        times = self.time_tokens([t for t, _ in steps]) if steps else np.zeros((1, self.shape.hidden), np.float32)
+        dts = np.ascontiguousarray([dt for _, dt in steps] or [0.0], np.float32)
+        rows = mu.shape[0]
+        f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+        mu, cond, noise, sampling = f(round_f16(mu)), f(cond), f(noise), f(sampling)
+        out = np.zeros((rows, feat, patch), np.float32)
+        lin = [f(self.w[f"{p}{n}.{k}"]) for n in ("in_proj", "cond_proj", "out_proj") for k in ("weight", "bias")]
+        _local_library().tgo_sampler(ctypes.byref(self._c), self.layers, _fp(self.final), *[_fp(a) for a in lin],
+                                     _fp(f(times)), _fp(dts), len(steps), rows, feat, patch, _fp(mu),
+                                     _fp(cond), _fp(noise), _fp(sampling), _fp(out))
+        return out
+
+    def encode(self, patches: np.ndarray, feat: int, patch: int) -> np.ndarray:
+        """tgo_encoder: each row's embedding, [rows][hidden] (f16 values)."""
+        p = self.prefix
+        f = lambda a: np.ascontiguousarray(a, np.float32)  # noqa: E731
+        patches = f(patches)
+        rows = patches.shape[0]
+        out = np.zeros((rows, self.shape.hidden), np.float32)
+        _local_library().tgo_encoder(ctypes.byref(self._c), self.layers, _fp(self.final), _fp(f(self.w[p + "in_proj.weight"])),
+                                     _fp(f(self.w[p + "in_proj.bias"])), _fp(f(self.w[p + "special_token"])), rows,
+                                     feat, patch, _fp(patches), _fp(out))
+        return out

@@ -99,3 +99,54 @@ class NumpyStack:
     def prefill(self, start, x, slot=0):
         x = np.asarray(x).reshape(-1, self.s.hidden)
         return self.run([(start + i, slot) for i in range(x.shape[0])], x)
+
+
+# ---- VoxCPM2's local stacks (crates/graph/src/local), cross-checking local_ref.c -----------------
+
+def f16(x):
+    return np.asarray(x, np.float64).astype(np.float16).astype(np.float64)
+
+
+def local_stack(shape, w, stack_prefix, tokens, x):
+    """local/mod.rs:573-680 in f64 with the f16 roundings of the kernels (local_*.comp): x
+    [seqs tokens][hidden] -> the tokens after the final norm. `w` holds f16-valued weights."""
+    s = shape
+    hd, half, H = s.head_dim, s.head_dim // 2, s.hidden
+    cos, sin = rope_tables(hd, tokens, s.rope_theta, s.rope_factors)
+    cos, sin = cos.astype(np.float64), sin.astype(np.float64)
+    g = lambda n: np.asarray(w[stack_prefix + n], np.float64)  # noqa: E731
+    M = x.shape[0]
+    pos = np.arange(M) % tokens
+
+    def norm(v, gain):
+        return f16(rmsnorm(v, gain, s.eps))
+
+    cur = np.asarray(x, np.float64)
+    normed = norm(cur, g("layers.0.input_layernorm.weight"))
+    group = s.heads // s.kv_heads
+    for l in range(s.layers):
+        L = lambda n: g(f"layers.{l}.{n}.weight")  # noqa: E731
+        def rot(v):  # [M][heads][hd]
+            a, b = v[..., :half], v[..., half:]
+            c, sn = cos[pos][:, None, :], sin[pos][:, None, :]
+            return np.concatenate([a * c - b * sn, b * c + a * sn], axis=-1)
+        q = f16(rot((normed @ L("self_attn.q_proj").T).reshape(M, s.heads, hd)))
+        k = f16(rot((normed @ L("self_attn.k_proj").T).reshape(M, s.kv_heads, hd)))
+        v = f16((normed @ L("self_attn.v_proj").T).reshape(M, s.kv_heads, hd))
+        att = np.zeros((M, s.heads, hd))
+        for m0 in range(0, M, tokens):
+            sl = slice(m0, m0 + tokens)
+            for h in range(s.heads):
+                kv = h // group
+                sc = q[sl, h] @ k[sl, kv].T / np.sqrt(hd)
+                e = np.exp(sc - sc.max(axis=1, keepdims=True))
+                att[sl, h] = (e @ v[sl, kv]) / e.sum(axis=1, keepdims=True)
+        att = f16(att.reshape(M, -1))
+        mid = f16(cur + att @ L("self_attn.o_proj").T)
+        normed = norm(mid, L("post_attention_layernorm"))
+        gate, up = normed @ L("mlp.gate_proj").T, normed @ L("mlp.up_proj").T
+        mlp = f16(gate / (1.0 + np.exp(-gate)) * up)
+        cur = f16(mid + mlp @ L("mlp.down_proj").T)
+        gain = g(f"layers.{l + 1}.input_layernorm.weight") if l + 1 < s.layers else g("norm.weight")
+        normed = norm(cur, gain)
+    return normed

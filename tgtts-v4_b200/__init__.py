@@ -86,8 +86,9 @@ _ERRORS = {c.status: c for c in (InvalidError, ShapeError, CudaError, OutOfMemor
 
 # ---- the library ---------------------------------------------------------------------------------
 
-F32, BF16 = 0, 1
-DTYPES = {"f32": F32, "fp32": F32, "float32": F32, "bf16": BF16, "bfloat16": BF16}
+F32, BF16, F16 = 0, 1, 2
+DTYPES = {"f32": F32, "fp32": F32, "float32": F32, "bf16": BF16, "bfloat16": BF16, "f16": F16,
+          "float16": F16}
 RES_DEVICE, RES_UPLOAD, RES_READBACK = 0, 1, 2
 
 KERNELS = {
@@ -95,6 +96,8 @@ KERNELS = {
     "gemv_residual": 4, "gemv_gate_up": 5, "stream_read": 6, "norm_rows": 7, "add_norm_rows": 8,
     "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12, "attention_decode": 13,
     "gemm_silu": 14, "attention_rows_tc": 15, "gemm_qkv_rope": 16, "gemv_linear": 17,
+    "local_norm": 18, "local_partial": 19, "local_gate_up": 20, "local_attention": 21,
+    "local_add_norm": 22, "local_rows": 23, "local_embed": 24, "cfm_noise": 25, "dit_euler": 26,
 }
 
 
@@ -123,7 +126,13 @@ class TgParams(ctypes.Structure):
                 ("dtype", "hidden", "inner", "heads", "kv_heads", "head_dim", "capacity", "rows",
                  "slots")] + [("eps", ctypes.c_float), ("residual_scale", ctypes.c_float)] + [
         (n, ctypes.c_uint32) for n in ("rope", "normed_f32", "m", "n", "k", "k1", "offset", "stride",
-                                       "act")] + [("levels", ctypes.c_float)]
+                                       "act")] + [("levels", ctypes.c_float)] + [
+        (n, ctypes.c_uint32) for n in ("parts", "seqs", "first", "at", "copied", "flags", "frames",
+                                       "feat")] + [("dt", ctypes.c_float)]
+
+
+class TgLocalTuning(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in ("qkv_parts", "o_parts", "down_parts")]
 
 
 class TgBinding(ctypes.Structure):
@@ -215,6 +224,31 @@ SIGNATURES = {
     "tg_server_finish": (_I, [_P, _U32]),
     "tg_server_last_output": (_I, [_P, _U32, _FP]),
     "tg_server_sync": (_I, [_P, _U64]),
+    "tg_sampler_create": (_I, [_P, ctypes.POINTER(TgShape), _U32, _U32, _U32, _U32,
+                               ctypes.POINTER(TgLocalTuning), _I, ctypes.POINTER(_P)]),
+    "tg_sampler_destroy": (_I, [_P]),
+    "tg_sampler_load": (_I, [_P, ctypes.c_char_p, _P, _U64, _I]),
+    "tg_sampler_sample": (_I, [_P, _P, _FP, _FP, _FP, _FP]),
+    "tg_sampler_sample_device": (_I, [_P, _P, _P, _P, _P, _P]),
+    "tg_sampler_wait": (_I, [_P, _U64]),
+    "tg_sampler_steps": (_I, [_P, _FP, _FP, _SZ, ctypes.POINTER(_SZ)]),
+    "tg_sampler_elapsed_ns": (_I, [_P, _DP]),
+    "tg_sampler_timings": (_I, [_P, _DP, _SZ, ctypes.POINTER(_SZ)]),
+    "tg_sampler_dispatch_label": (_I, [_P, _SZ, ctypes.c_char_p, _SZ]),
+    "tg_sampler_weight_bytes": (_U64, [_P]),
+    "tg_cfm_schedule": (_I, [_U32, _FP]),
+    "tg_cfm_euler_steps": (_I, [_U32, _FP, _FP, _SZ, ctypes.POINTER(_SZ)]),
+    "tg_encoder_create": (_I, [_P, ctypes.POINTER(TgShape), _U32, _U32, _U32,
+                               ctypes.POINTER(TgLocalTuning), _I, ctypes.POINTER(_P)]),
+    "tg_encoder_destroy": (_I, [_P]),
+    "tg_encoder_load": (_I, [_P, ctypes.c_char_p, _P, _U64, _I]),
+    "tg_encoder_encode": (_I, [_P, _FP, _P]),
+    "tg_encoder_encode_device": (_I, [_P, _P, _P]),
+    "tg_encoder_wait": (_I, [_P, _U64]),
+    "tg_encoder_elapsed_ns": (_I, [_P, _DP]),
+    "tg_encoder_timings": (_I, [_P, _DP, _SZ, ctypes.POINTER(_SZ)]),
+    "tg_encoder_dispatch_label": (_I, [_P, _SZ, ctypes.c_char_p, _SZ]),
+    "tg_encoder_weight_bytes": (_U64, [_P]),
 }
 
 _lib: Optional[ctypes.CDLL] = None

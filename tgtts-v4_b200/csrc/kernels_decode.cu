@@ -212,10 +212,23 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(const __grid_
             mbar_arrive_expect_tx(smem_u32(&bar[lane]), (uint32_t)(hi - lo) * R * row_bytes);
         }
         __syncwarp();
-        for (int j = lane; j < nu * R; j += 32) {
-            const int row = unit_row<EPI>(a.p, u0 + j / R, j % R);
-            bulk_load(smem_u32(ws + (size_t)j * k), static_cast<const T *>(a.w) + (size_t)row * k, row_bytes,
-                      smem_u32(&bar[(j / R) / max(per_stage, 1)]));
+        // Rows that follow each other in W go in one bulk copy: a copy costs the SM's copy engine
+        // about the same time whatever its size up to tens of KiB, so that row-sized copies cap a
+        // block's stream well below its share of HBM. Lane r copies the block's r-th rows (unit
+        // j's at ws row r nu + j), a run of consecutive rows at a time, split at stage edges.
+        if (lane < R) {
+            const int r = lane;
+            const T *w = static_cast<const T *>(a.w);
+            for (int j0 = 0; j0 < nu;) {
+                const int stage = j0 / max(per_stage, 1);
+                const int end = min(nu, (stage + 1) * max(per_stage, 1));
+                const int row0 = unit_row<EPI>(a.p, u0 + j0, r);
+                int j1 = j0 + 1;
+                while (j1 < end && unit_row<EPI>(a.p, u0 + j1, r) == row0 + (j1 - j0)) j1++;
+                bulk_load(smem_u32(ws + ((size_t)r * nu + j0) * k), w + (size_t)row0 * k, (uint32_t)(j1 - j0) * row_bytes,
+                          smem_u32(&bar[stage]));
+                j0 = j1;
+            }
         }
     }
     if (norm)  // the gain is a constant: read before waiting on the kernel before
@@ -231,7 +244,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_stream_kernel(const __grid_
             if (b0 == 0) mbar_wait_bounded(smem_u32(&bar[j / per_stage]), 0, a.err);
             const T *w[R];
 #pragma unroll
-            for (int r = 0; r < R; r++) w[r] = ws + (size_t)(j * R + r) * k;
+            for (int r = 0; r < R; r++) w[r] = ws + ((size_t)r * nu + j) * k;
             float acc[NB][R];
             dot_smem<T, NB, R>(w, k, xs, acc);
             float y[NB][R];
@@ -1058,32 +1071,6 @@ __global__ void __launch_bounds__(256) stream_read_kernel(const uint4 *__restric
 }
 
 // ---- launchers -------------------------------------------------------------------------------
-
-// Launches `kern` with the programmatic-stream-serialization attribute, so that in a stream (or a
-// graph captured from one) it may start while the kernel before it finishes (see pdl_wait).
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                              Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
-template <typename F>
-static cudaError_t with_smem(F kernel, size_t bytes) {
-    // Past 48 KiB of shared memory a block needs the opt-in, static arrays included: opt in well
-    // before.
-    if (bytes <= 32 * 1024) return cudaSuccess;
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-}
 
 #define TG_DISPATCH_NB(NB_VAR, ...)                           \
     switch (NB_VAR) {                                         \

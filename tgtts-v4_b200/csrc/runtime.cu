@@ -60,7 +60,9 @@ int take_kernel_error(tg_ctx *ctx) {
 
 // ---- the kernel table's checks -----------------------------------------------------------------
 
-static uint64_t esize(uint32_t dtype) { return dtype == TG_BF16 ? 2 : 4; }
+static uint64_t esize(uint32_t dtype) { return dtype == TG_F32 ? 4 : 2; }
+
+static bool is_local(uint32_t k) { return k >= TG_KERNEL_LOCAL_NORM && k <= TG_KERNEL_DIT_EULER; }
 
 struct Need {
     const char *name;
@@ -147,6 +149,40 @@ static int needs(const Launch &l, std::vector<Need> &out) {
                    {"W", (uint64_t)p.n * (p.k + p.k1) * T}, {"bias", (uint64_t)p.n * F},
                    {"out", rows * p.stride * F}};
             break;
+        // The local stacks: f16 (2 bytes) throughout but for the partial sums, tables and patches.
+        case TG_KERNEL_LOCAL_NORM:
+            out = {{"x", (uint64_t)p.m * H * 2}, {"gain", H * 2}, {"out", (uint64_t)p.m * H * 2}};
+            break;
+        case TG_KERNEL_LOCAL_PARTIAL:
+            out = {{"x", (uint64_t)p.m * p.k * 2}, {"W", (uint64_t)p.n * p.k * 2},
+                   {"partial", (uint64_t)p.parts * p.m * p.n * F}};
+            break;
+        case TG_KERNEL_LOCAL_GATE_UP:
+            out = {{"x", (uint64_t)p.m * p.k * 2}, {"W", (uint64_t)p.n * p.k * 2}, {"out", (uint64_t)p.m * (p.n / 2) * 2}};
+            break;
+        case TG_KERNEL_LOCAL_ATTENTION:
+            out = {{"partial", (uint64_t)p.parts * p.m * width * F}, {"cos", table}, {"sin", table},
+                   {"out", (uint64_t)p.m * attn * 2}};
+            break;
+        case TG_KERNEL_LOCAL_ADD_NORM:
+            out = {{"partial", (uint64_t)p.parts * p.m * p.n * F}, {"residual", (uint64_t)p.m * p.n * 2},
+                   {"gain", (uint64_t)p.n * 2}, {"sum", (uint64_t)p.m * p.n * 2}, {"normed", (uint64_t)p.m * p.n * 2}};
+            break;
+        case TG_KERNEL_LOCAL_ROWS:
+            out = {{"x", rows * cap * p.n * 2}, {"out", rows * p.n * 2}};
+            break;
+        case TG_KERNEL_LOCAL_EMBED:
+            out = {{"src", rows * p.feat * p.frames * F}, {"W", (uint64_t)p.n * p.feat * 2}, {"bias", (uint64_t)p.n * 2},
+                   {"tokens", std::max<uint64_t>((p.flags & 2 ? 1 : rows) * p.copied * p.n * 2, 16)},
+                   {"h", rows * p.seqs * cap * p.n * 2}};
+            break;
+        case TG_KERNEL_CFM_NOISE:
+            out = {{"noise", rows * p.feat * p.frames * F}, {"sampling", rows * 2 * F}, {"x", rows * p.feat * p.frames * F}};
+            break;
+        case TG_KERNEL_DIT_EULER:
+            out = {{"h", rows * 2 * cap * p.k * 2}, {"W", (uint64_t)p.feat * p.k * 2}, {"bias", (uint64_t)p.feat * 2},
+                   {"sampling", rows * 2 * F}, {"x", rows * p.feat * p.frames * F}};
+            break;
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
@@ -157,13 +193,62 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope", "gemv_linear"};
+        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope", "gemv_linear",
+        "local_norm", "local_partial", "local_gate_up", "local_attention", "local_add_norm", "local_rows",
+        "local_embed", "cfm_noise", "dit_euler"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
+}
+
+// The local stacks' kernels' shape rules (local/mod.rs:366-385, dit.rs:196-212, encoder.rs:70-72).
+static int check_local_shape(const Launch &l) {
+    const tg_params &p = l.p;
+    const char *name = kernel_name(l.kernel);
+    if (p.dtype != TG_F16) return fail(TG_ESHAPE, "%s: dtype %u (the local stacks are f16)", name, p.dtype);
+    bool ok = true;
+    switch (l.kernel) {
+        case TG_KERNEL_LOCAL_NORM:
+            ok = p.m > 0 && p.hidden > 0 && p.hidden % 2 == 0 && p.hidden <= 2048;
+            break;
+        case TG_KERNEL_LOCAL_PARTIAL:
+            ok = p.parts > 0 && p.k % p.parts == 0 && local_proj_supported((int)p.m, (int)p.n, (int)p.k, (int)p.parts);
+            break;
+        case TG_KERNEL_LOCAL_GATE_UP:
+            ok = local_proj_supported((int)p.m, (int)p.n, (int)p.k, 1);
+            break;
+        case TG_KERNEL_LOCAL_ATTENTION:
+            ok = p.parts > 0 && p.capacity > 0 && p.capacity <= 32 && p.m > 0 && p.m % p.capacity == 0 &&
+                 p.kv_heads > 0 && p.heads % p.kv_heads == 0 && p.head_dim > 0 && p.head_dim % 8 == 0 &&
+                 p.head_dim <= 256;
+            break;
+        case TG_KERNEL_LOCAL_ADD_NORM:
+            ok = p.parts > 0 && p.m > 0 && p.n > 0 && p.n % 2 == 0 && p.n <= 2048;
+            break;
+        case TG_KERNEL_LOCAL_ROWS:
+            ok = p.rows > 0 && p.capacity > 0 && p.n > 0 && p.n % 8 == 0;
+            break;
+        case TG_KERNEL_LOCAL_EMBED:
+            ok = p.rows > 0 && p.seqs > 0 && p.n > 0 && p.feat > 0 && p.feat % 8 == 0 && p.frames > 0 && p.frames <= 8 &&
+                 p.first + p.frames <= p.capacity &&
+                 p.at + p.copied <= p.capacity && (uint64_t)p.feat * p.frames * 4 <= 200 * 1024;
+            break;
+        case TG_KERNEL_CFM_NOISE:
+            ok = p.rows > 0 && p.feat > 0 && p.frames > 0;
+            break;
+        case TG_KERNEL_DIT_EULER:
+            ok = p.rows > 0 && p.k > 0 && p.k % 8 == 0 && p.feat > 0 && p.frames > 0 && 2 * p.frames <= 16 &&
+                 p.first + p.frames <= p.capacity && 4 * (2ull * p.frames * p.k + 2ull * p.feat * p.frames) <= 200 * 1024;
+            break;
+    }
+    if (!ok)
+        return fail(TG_ESHAPE, "%s: shape not taken (m %u, n %u, k %u, parts %u, capacity %u, heads %u/%u of %u, rows %u)",
+                    name, p.m, p.n, p.k, p.parts, p.capacity, p.heads, p.kv_heads, p.head_dim, p.rows);
+    return TG_OK;
 }
 
 // Shapes the kernels cannot cover exactly are refused (decode.rs:468-491, prefill.rs:233-262).
 static int check_shape(const Launch &l) {
     const tg_params &p = l.p;
+    if (is_local(l.kernel)) return check_local_shape(l);
     if (p.dtype != TG_F32 && p.dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %u", p.dtype);
     const uint32_t vec = p.dtype == TG_BF16 ? 256 : 128;  // a warp's 16-byte step over K
     auto heads_ok = [&] {
@@ -310,6 +395,15 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case TG_KERNEL_GEMM_QKV_ROPE:
             e = launch_gemm_qkv_rope(p, b[0], b[1], U(2), F(3), F(4), b[5], b[6], b[7], err, s);
             break;
+        case TG_KERNEL_LOCAL_NORM: e = launch_local_norm(p, b[0], b[1], b[2], s); break;
+        case TG_KERNEL_LOCAL_PARTIAL: e = launch_local_partial(p, b[0], b[1], F(2), err, s); break;
+        case TG_KERNEL_LOCAL_GATE_UP: e = launch_local_gate_up(p, b[0], b[1], b[2], err, s); break;
+        case TG_KERNEL_LOCAL_ATTENTION: e = launch_local_attention(p, F(0), F(1), F(2), b[3], s); break;
+        case TG_KERNEL_LOCAL_ADD_NORM: e = launch_local_add_norm(p, F(0), b[1], b[2], b[3], b[4], s); break;
+        case TG_KERNEL_LOCAL_ROWS: e = launch_local_rows(p, b[0], b[1], s); break;
+        case TG_KERNEL_LOCAL_EMBED: e = launch_local_embed(p, F(0), b[1], b[2], b[3], b[4], s); break;
+        case TG_KERNEL_CFM_NOISE: e = launch_cfm_noise(p, F(0), F(1), F(2), s); break;
+        case TG_KERNEL_DIT_EULER: e = launch_dit_euler(p, b[0], b[1], b[2], F(3), F(4), s); break;
         default: return fail(TG_EINVAL, "no kernel %u", l.kernel);
     }
     if (e != cudaSuccess)

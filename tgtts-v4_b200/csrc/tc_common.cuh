@@ -1,6 +1,7 @@
-// tcgen05 building blocks shared by the prefill GEMM and the batched decode projections: bounded
-// mbarrier waits, 2-D TMA loads (no multicast), shared-memory and instruction descriptors for
-// kind::f16 with bf16 operands, the MMA, its commit, TMEM loads, and the host's tensor maps.
+// tcgen05 building blocks shared by the prefill GEMM, the batched decode projections and the local
+// stacks' projections: bounded mbarrier waits, 2-D TMA loads (no multicast), shared-memory and
+// instruction descriptors for kind::f16 with bf16 or f16 operands, the MMA, its commit, TMEM loads,
+// and the host's tensor maps.
 #pragma once
 
 #include <cuda.h>
@@ -36,6 +37,14 @@ TG_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, u
         : "memory");
 }
 
+TG_DEVICE void tma_load_3d(uint32_t dst, const CUtensorMap *map, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
 // The shared-memory matrix descriptor of a K-major tile with 128-byte rows in the 128-byte
 // swizzle TMA writes: start address, leading byte offset 16 (unused for this layout), stride
 // byte offset 1024 between groups of 8 rows, descriptor version 1, swizzle mode 2 (128 B).
@@ -47,6 +56,11 @@ TG_DEVICE uint64_t sw128_desc(uint32_t addr) {
 // The instruction descriptor of kind::f16 with bf16 A and B (both K-major), f32 D, M x N.
 __host__ __device__ constexpr uint32_t bf16_idesc(int m, int n) {
     return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// The instruction descriptor of kind::f16 with f16 A and B (both K-major), f32 D, M x N.
+__host__ __device__ constexpr uint32_t f16_idesc(int m, int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 TG_DEVICE void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
@@ -113,16 +127,42 @@ inline EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// A 2-D map over a row-major [rows][k] bf16 matrix, boxes of 64 columns x `box_rows` rows in the
-// 128-byte swizzle.
-inline bool make_map_bf16(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows) {
+// A 2-D map over a row-major [rows][k] matrix of 2-byte elements (bf16 or f16), boxes of 64 columns
+// x `box_rows` rows in the 128-byte swizzle; rows past `rows` read as zero.
+inline bool make_map_2byte(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows,
+                           CUtensorMapDataType type) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {k, rows};
     cuuint64_t strides[1] = {k * 2};
     cuuint32_t box[2] = {64, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box, estr,
+    return fn(map, type, 2, const_cast<void *>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+inline bool make_map_bf16(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows) {
+    return make_map_2byte(map, ptr, rows, k, box_rows, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+}
+
+inline bool make_map_f16(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows) {
+    return make_map_2byte(map, ptr, rows, k, box_rows, CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
+}
+
+// A 3-D map over an f16 matrix of `rows` rows and k columns stored k-block-major, [k / 64][rows]
+// [64]: boxes of 64 columns x `box_rows` rows x `box_kb` k-blocks, in the 128-byte swizzle (each
+// k-block's rows one after another, as a 2-D box of the same rows lays them out); rows past `rows`
+// read as zero.
+inline bool make_map_f16_blocked(CUtensorMap *map, const void *ptr, uint64_t rows, uint64_t k, uint32_t box_rows,
+                                 uint32_t box_kb) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || k % 64) return false;
+    cuuint64_t dims[3] = {64, rows, k / 64};
+    cuuint64_t strides[2] = {128, rows * 128};
+    cuuint32_t box[3] = {64, box_rows, box_kb};
+    cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }

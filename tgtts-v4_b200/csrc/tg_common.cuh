@@ -239,4 +239,33 @@ TG_DEVICE void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t
 TG_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 TG_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// ---- host ---------------------------------------------------------------------------------------
+
+// Launches `kern` with the programmatic-stream-serialization attribute, so that in a stream (or a
+// graph captured from one) it may start while the kernel before it finishes (see pdl_wait).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <typename F>
+inline cudaError_t with_smem(F kernel, size_t bytes) {
+    // Past 48 KiB of shared memory a block needs the opt-in, static arrays included: opt in well
+    // before.
+    if (bytes <= 32 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+}
+
+
 }  // namespace tg

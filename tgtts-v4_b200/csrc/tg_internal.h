@@ -205,4 +205,32 @@ cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *
 cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,
                              cudaStream_t s);
 
+// The local stacks (local.cu): f16 kernels over m tokens in sequences of p.capacity.
+bool local_proj_supported(int M, int N, int K, int parts);
+// A local projection's weight W [N][K] (f16) is stored tiled: the 128 x 64 block of rows
+// [128 t, +128) and columns [64 b, +64) is 16 KiB at ((t K / 64 + b) 16 KiB), its row r's 16-byte
+// chunk c (columns 64 b + 8 c ..) at (r / 8) 1024 + (r % 8) 128 + ((c ^ (r % 8)) 16): the 128-byte
+// swizzle of a K-major tcgen05 operand. The byte offset of element (row, col):
+__host__ __device__ inline uint64_t local_tiled_offset(uint32_t row, uint32_t col, uint32_t K) {
+    const uint32_t t = row / 128, r = row % 128, b = col / 64, c = (col % 64) / 8;
+    return ((uint64_t)t * (K / 64) + b) * 16384 + (r / 8) * 1024 + (r % 8) * 128 + ((c ^ (r % 8)) << 4) + (col % 8) * 2;
+}
+// Writes rows [row0 + i step] (i < rows) of a tiled weight of K columns from src [rows][K] f16.
+cudaError_t launch_local_tile_rows(const void *src, int rows, int K, void *dst, int row0, int step, cudaStream_t s);
+cudaError_t launch_local_norm(const tg_params &p, const void *x, const void *g, void *out, cudaStream_t s);
+cudaError_t launch_local_partial(const tg_params &p, const void *x, const void *w, float *part, uint32_t *err,
+                                 cudaStream_t s);
+cudaError_t launch_local_gate_up(const tg_params &p, const void *x, const void *w, void *out, uint32_t *err,
+                                 cudaStream_t s);
+cudaError_t launch_local_attention(const tg_params &p, const float *part, const float *cosv, const float *sinv,
+                                   void *out, cudaStream_t s);
+cudaError_t launch_local_add_norm(const tg_params &p, const float *part, const void *res, const void *g, void *sum,
+                                  void *normed, cudaStream_t s);
+cudaError_t launch_local_rows(const tg_params &p, const void *x, void *out, cudaStream_t s);
+cudaError_t launch_local_embed(const tg_params &p, const float *src, const void *w, const void *bias,
+                               const void *tokens, void *h, cudaStream_t s);
+cudaError_t launch_cfm_noise(const tg_params &p, const float *noise, const float *sampling, float *x, cudaStream_t s);
+cudaError_t launch_dit_euler(const tg_params &p, const void *h, const void *w, const void *bias,
+                             const float *sampling, float *x, cudaStream_t s);
+
 }  // namespace tg
