@@ -47,10 +47,10 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extras", action="store_true", help="skip the prefill/GEMM side measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
-    ap.add_argument("--workload", default="decode", choices=["decode", "serve", "sweep", "gemm"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "serve", "sweep", "gemm", "local"],
                     help="decode: config 2 (the headline line); serve: config 5, request-sharded "
                          "serving; sweep: decode step time by batch rows; gemm: config 4's four "
-                         "projection GEMMs alone")
+                         "projection GEMMs alone; local: VoxCPM2's patch sampler and local encoder")
     ap.add_argument("--rows", type=int, default=32768, help="gemm: rows (M)")
     ap.add_argument("--requests", type=int, default=2048, help="serve: requests over all GPUs")
     return ap.parse_args()
@@ -691,6 +691,105 @@ def run_gemm(args, rank, world, local):
             "warmup": args.warmup, "peak_tflops": tc, "peak_source": peak_kind, "by_projection": out}
 
 
+def run_local(args, rank, world, local):
+    """VoxCPM2's local stacks (crates/graph/src/local): the patch sampler (10 Euler steps: 9 runs of
+    the local DiT over each row's two sequences of 11 tokens) at 1 and 16 rows, and the local
+    encoder at 16 rows, on VoxCPM2's widths (1024 wide, 4096 inner, 16 heads of 128 over 2 KV heads,
+    patches of 4 frames of 64 channels) with 8 layers a stack (the checkpoint's layer count is not
+    here), synthetic weights. One step is one sample of every row; `value` is patches/s at 16 rows
+    with the inputs resident in HBM, `e2e` the same through tg_sampler_sample with host buffers."""
+    if rank != 0:
+        return None
+    import torch
+
+    import __graft_entry__ as entry
+    import oracle
+
+    pkg = entry.load_package()
+    from tgtts_v4_b200 import local as loc
+    from tgtts_v4_b200 import synthetic as syn
+
+    torch.cuda.set_device(local)
+    ctx = pkg.Context(local)
+    stream = stream_ctx(ctx)
+    hbm, _, peak_kind = peaks()
+    cfg, timesteps = syn.LOCAL_VOXCPM2, 10
+    shape = syn.local_shape(cfg)
+    w = syn.make_sampler_weights(cfg, seed=0)
+    steps, warm = max(1, args.steps // 10), max(3, args.warmup // 5)
+    lines = {}
+    for rows in (1, 16):
+        s = loc.Sampler(ctx, shape, cfg.feat_dim, cfg.patch_size, timesteps, rows)
+        s.load(w)
+        mu, cond, noise, sampling = syn.make_sampler_inputs(cfg, rows, seed=1)
+        dev = [torch.from_numpy(np.ascontiguousarray(a)).to(f"cuda:{local}") for a in (mu.view(np.int16), cond, noise, sampling)]
+        out = torch.empty_like(dev[1])
+        ptrs = [t.data_ptr() for t in dev] + [out.data_ptr()]
+        for _ in range(warm):
+            s.sample_device(*ptrs)
+        s.wait()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            e0.record(stream)
+            for _ in range(steps):
+                s.sample_device(*ptrs)
+            e1.record(stream)
+            e1.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        for _ in range(warm):
+            s.sample(mu, cond, noise, sampling)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            s.sample(mu, cond, noise, sampling)
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / steps
+        runs = len(s.steps())
+        wb = s.weight_bytes
+        lines[rows] = {"ms_per_sample": round(ms, 4), "patches_per_s": round(rows / ms * 1e3, 1),
+                       "e2e_ms": round(e2e_ms, 4), "e2e_patches_per_s": round(rows / e2e_ms * 1e3, 1),
+                       "dit_runs": runs, "weight_bytes_per_run": wb,
+                       "weight_gbs": round(runs * wb / (ms / 1e3) / 1e9, 1),
+                       "hbm_frac": round(runs * wb / (ms / 1e3) / 1e9 / hbm, 4),
+                       "launches": len(s.labels()), "clocks": clk.summary()}
+        s.close()
+    e = loc.Encoder(ctx, shape, cfg.feat_dim, cfg.patch_size, 16)
+    e.load(syn.make_encoder_weights(cfg, seed=0))
+    patches = np.random.default_rng(3).standard_normal((16, cfg.feat_dim, cfg.patch_size)).astype(np.float32)
+    for _ in range(warm):
+        e.encode(patches)
+    t = []
+    for _ in range(steps):
+        e.encode(patches)
+        t.append(e.elapsed_ns() / 1e6)
+    enc = {"rows": 16, "ms": round(statistics.median(t), 4), "weight_bytes": e.weight_bytes}
+    e.close()
+    # The CPU baseline: the oracle's sampler for one row on all host cores, one sample.
+    cores = os.cpu_count() or 1
+    ref = oracle.OracleLocal(shape, w, "feat_decoder.estimator.", 3 + 2 * cfg.patch_size, threads=cores)
+    mu, cond, noise, sampling = syn.make_sampler_inputs(cfg, 1, seed=1)
+    t0 = time.perf_counter()
+    ref.sample(mu, cond, noise, sampling, timesteps, cfg.feat_dim, cfg.patch_size)
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    ctx.close()
+    head = lines[16]
+    return {"metric": "local sampler patches/s (VoxCPM2-wide local DiT, 10 Euler steps, 16 rows)",
+            "value": head["patches_per_s"], "unit": "patches/s", "n_gpus": 1, "steps": steps, "warmup": warm,
+            "ms_per_step": head["ms_per_sample"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (seeded N(0, 0.02) weights; inputs as the reference's local tests)",
+            "config": {"workload": "local sampler + encoder", "hidden": cfg.hidden, "inner": cfg.inner,
+                       "heads": cfg.heads, "kv_heads": cfg.kv_heads, "head_dim": cfg.head_dim,
+                       "layers": cfg.layers, "feat_dim": cfg.feat_dim, "patch_size": cfg.patch_size,
+                       "timesteps": timesteps, "l2": "weights 277 MB a run > L2, no flush"},
+            "e2e": {"value": head["e2e_patches_per_s"], "unit": "patches/s",
+                    "h2d_bytes_per_step": 16 * (2 * cfg.hidden * 2 + 2 * cfg.feat_dim * cfg.patch_size * 4 + 8),
+                    "d2h_bytes_per_step": 16 * cfg.feat_dim * cfg.patch_size * 4},
+            "roofline": {"bound": "hbm", "achieved": head["weight_gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": head["hbm_frac"], "traffic": None, "peak_source": peak_kind},
+            "cpu_baseline": {"value": round(1e3 / cpu_ms, 3), "unit": "patches/s", "cores": cores, "kind": "port",
+                             "sample": "the oracle's sampler, 1 row, one sample of 10 steps"},
+            "gpu_launches": head["launches"] * steps, "by_rows": lines, "encoder": enc}
+
+
 def main():
     args = parse()
     rank, world, local = dist_init(args.gpus)
@@ -702,6 +801,8 @@ def main():
         res = run_sweep(args, rank, world, local)
     elif args.workload == "gemm":
         res = run_gemm(args, rank, world, local)
+    elif args.workload == "local":
+        res = run_local(args, rank, world, local)
     else:
         res = run_ours(args, rank, world, local)
     if rank == 0 and res is not None:

@@ -518,9 +518,28 @@ __global__ void __launch_bounds__(DE_THREADS)
     const int len = feat * frames, ntok = 2 * frames;
     float *hs = de_smem;             // [2 frames][K]
     float *vel = hs + ntok * K;      // [2][feat][frames]
-    for (int i = threadIdx.x; i < ntok * K; i += DE_THREADS) {
-        const int m = i / K, k = i % K, q = m / frames, f = m % frames;
-        hs[i] = __half2float(h[blocked((2 * row + q) * T + (int)p.first + f, k, (int)p.m)]);
+    // The tokens' rows, 8 values a 16-byte load, a batch of loads issued before the stores.
+    const int vecs = ntok * K / 8;
+    for (int i0 = threadIdx.x; i0 < vecs; i0 += DE_THREADS * DE_BATCH) {
+        uint4 v[DE_BATCH];
+#pragma unroll
+        for (int j = 0; j < DE_BATCH; j++) {
+            const int i = i0 + j * DE_THREADS;
+            if (i >= vecs) continue;
+            const int m = i / (K / 8), k = 8 * (i % (K / 8)), q = m / frames, f = m % frames;
+            v[j] = __ldg(reinterpret_cast<const uint4 *>(h) + blocked((2 * row + q) * T + (int)p.first + f, k, (int)p.m) / 8);
+        }
+#pragma unroll
+        for (int j = 0; j < DE_BATCH; j++) {
+            const int i = i0 + j * DE_THREADS;
+            if (i >= vecs) continue;
+            const half2 *h2 = reinterpret_cast<const half2 *>(&v[j]);
+            float4 *dst = reinterpret_cast<float4 *>(hs + (size_t)i * 8);
+            const float2 a = __half22float2(h2[0]), b = __half22float2(h2[1]), c = __half22float2(h2[2]),
+                         d = __half22float2(h2[3]);
+            dst[0] = make_float4(a.x, a.y, b.x, b.y);
+            dst[1] = make_float4(c.x, c.y, d.x, d.y);
+        }
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
