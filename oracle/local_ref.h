@@ -5,7 +5,13 @@
  *
  * Every tensor the reference keeps in f16 is rounded to f16 (RNE) at the same point here and held
  * as the f32 value of that f16; products are summed exactly enough (f64) that only the reference's
- * roundings remain. */
+ * roundings remain.
+ *
+ * Parity against the reference itself is unpinned for the stacks' values: the reference's local
+ * goldens (crates/graph/tests/local.rs) need the VoxCPM2 checkpoint, which is not here. What is
+ * pinned: the sampler's schedule and Euler steps against the reference's rules (dit.rs:39-81,
+ * "two steps, the first of which stays where it starts: one run of the DiT", local.rs:372-374),
+ * and the whole restatement against an independent numpy one (oracle/ref_numpy.py). */
 #ifndef TG_LOCAL_REF_H
 #define TG_LOCAL_REF_H
 

@@ -112,6 +112,23 @@ def test_a_voxcpm2_wide_sampler_samples_as_the_oracle_and_alone(pkg, local, ctx,
     np.testing.assert_array_equal(got, alone)
 
 
+def test_a_sampler_loads_a_checkpoint_file_as_the_arrays(pkg, local, ctx, syn, tmp_path):
+    # load_sampler from safetensors (f32 and bf16 tensors): the same patches as the arrays.
+    from tgtts_v4_b200 import checkpoint
+
+    cfg = syn.LOCAL_SMALL
+    w = syn.make_sampler_weights(cfg, seed=9)
+    bf16 = [n for n in w if n.endswith("mlp.down_proj.weight")]
+    path = tmp_path / "sampler.safetensors"
+    checkpoint.save(path, w, bf16=bf16)
+    w_bf16 = {n: (syn.bf16_round(v) if n in bf16 else v) for n, v in w.items()}
+    mu, cond, noise, sampling = syn.make_sampler_inputs(cfg, 2, seed=10)
+    a = make_sampler(pkg, local, ctx, syn, cfg, 2, 2, w_bf16)
+    b = local.Sampler(ctx, syn.local_shape(cfg), cfg.feat_dim, cfg.patch_size, 2, 2)
+    b.load_checkpoint(path)
+    np.testing.assert_array_equal(b.sample(mu, cond, noise, sampling), a.sample(mu, cond, noise, sampling))
+
+
 def make_encoder(pkg, local, ctx, syn, cfg, rows, weights, tuning=None, layers=None):
     e = local.Encoder(ctx, syn.local_shape(cfg, layers), cfg.feat_dim, cfg.patch_size, rows, tuning)
     e.load(weights)

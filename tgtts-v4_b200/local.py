@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass, replace
-from typing import Mapping, Optional, Sequence
+from typing import Mapping, Optional
 
 import numpy as np
 
@@ -182,6 +182,17 @@ class _Program:
     def load_tensor(self, name: str, values: np.ndarray) -> None:
         a, src = _src(values)
         check(self._fn("load")(self.handle, name.encode(), a.ctypes.data, a.size, src))
+
+    def load_checkpoint(self, path) -> None:
+        """load_sampler / load_encoder from a safetensors file (crates/graph/src/checkpoint.rs):
+        every tensor by its upstream name, read a tensor at a time, rounded to f16."""
+        from .checkpoint import Checkpoint
+
+        with Checkpoint(path) as ck:
+            for name in self.weight_names():
+                if ck.shape(name) is None:
+                    raise Error(f"checkpoint: no tensor {name}")
+                self.load_tensor(name, ck.tensor(name))
 
     def wait(self, timeout_ns: int = 0) -> None:
         check(self._fn("wait")(self.handle, timeout_ns))
