@@ -120,7 +120,7 @@ def test_a_sampler_loads_a_checkpoint_file_as_the_arrays(pkg, local, ctx, syn, t
     w = syn.make_sampler_weights(cfg, seed=9)
     bf16 = [n for n in w if n.endswith("mlp.down_proj.weight")]
     path = tmp_path / "sampler.safetensors"
-    checkpoint.save(path, w, bf16=bf16)
+    checkpoint.save(path, {n: (syn.bf16_bits(v) if n in bf16 else v) for n, v in w.items()})
     w_bf16 = {n: (syn.bf16_round(v) if n in bf16 else v) for n, v in w.items()}
     mu, cond, noise, sampling = syn.make_sampler_inputs(cfg, 2, seed=10)
     a = make_sampler(pkg, local, ctx, syn, cfg, 2, 2, w_bf16)

@@ -149,9 +149,12 @@ __global__ void __launch_bounds__(LA_THREADS)
     const int seq = blockIdx.x, h = blockIdx.y, kv = h / (heads / kvh), parts = (int)p.parts;
     const int width = (heads + 2 * kvh) * hd, m0 = seq * T;
     const size_t part_stride = (size_t)p.m * width;
-    float *qs = la_smem, *ks = qs + T * hd, *vs = ks + T * hd, *sc = vs + T * hd;  // sc: [T][T + 1]
+    // q and k rows padded by 4 floats, so that the score loop's rows fall on different banks.
+    const int hp = hd + 4;
+    float *qs = la_smem, *ks = qs + T * hp, *vs = ks + T * hp, *sc = vs + T * hd;  // sc: [T][T + 1]
     const int cols[3] = {h * hd, (heads + kv) * hd, (heads + kvh + kv) * hd};
     float *dsts[3] = {qs, ks, vs};
+    const int strides[3] = {hp, hp, hd};
     // Four columns a thread, every part's loads issued before the first sum.
     const int quads = half_d / 4;
     for (int i = threadIdx.x; i < 3 * T * quads; i += LA_THREADS) {
@@ -186,18 +189,25 @@ __global__ void __launch_bounds__(LA_THREADS)
                 x0 = ra;
                 x1 = rb;
             }
-            dsts[which][t * hd + c + e] = hround(x0);
-            dsts[which][t * hd + c + e + half_d] = hround(x1);
+            dsts[which][t * strides[which] + c + e] = hround(x0);
+            dsts[which][t * strides[which] + c + e + half_d] = hround(x1);
         }
     }
     __syncthreads();
     const float scale = 1.0f / sqrtf((float)hd);
     for (int i = threadIdx.x; i < T * T; i += LA_THREADS) {
         const int qi = i / T, j = i % T;
-        const float *qq = qs + qi * hd, *kk = ks + j * hd;
-        float acc = 0.0f;
-        for (int d = 0; d < hd; d++) acc = __fmaf_rn(qq[d], kk[d], acc);
-        sc[qi * (T + 1) + j] = acc * scale;
+        const float4 *qq = reinterpret_cast<const float4 *>(qs + qi * hp), *kk = reinterpret_cast<const float4 *>(ks + j * hp);
+        // Four running sums (dimension d to d % 4), joined (0 + 1) + (2 + 3).
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int d4 = 0; d4 < hd / 4; d4++) {
+            const float4 a = qq[d4], b = kk[d4];
+            acc.x = __fmaf_rn(a.x, b.x, acc.x);
+            acc.y = __fmaf_rn(a.y, b.y, acc.y);
+            acc.z = __fmaf_rn(a.z, b.z, acc.z);
+            acc.w = __fmaf_rn(a.w, b.w, acc.w);
+        }
+        sc[qi * (T + 1) + j] = ((acc.x + acc.y) + (acc.z + acc.w)) * scale;
     }
     __syncthreads();
     if (threadIdx.x < T) {
@@ -662,7 +672,8 @@ cudaError_t launch_local_add_norm(const tg_params &p, const float *part, const v
 }
 
 size_t local_attention_smem(const tg_params &p) {
-    return sizeof(float) * (3 * (size_t)p.capacity * p.head_dim + (size_t)p.capacity * (p.capacity + 1));
+    return sizeof(float) * (2 * (size_t)p.capacity * (p.head_dim + 4) + (size_t)p.capacity * p.head_dim +
+                            (size_t)p.capacity * (p.capacity + 1));
 }
 
 cudaError_t launch_local_attention(const tg_params &p, const float *part, const float *cosv, const float *sinv,
