@@ -1103,8 +1103,12 @@ static cudaError_t launch_gemv(GemvArgs a, cudaStream_t s) {
     int nb = 8;
     while (nb > 1 && (uint32_t)nb / 2 >= rows) nb /= 2;
     const size_t row_bytes = (size_t)a.k * sizeof(T);
-    // xs, and for a normed input its raw copy and the gain.
-    const size_t xs_bytes = (size_t)nb * a.k * 4 * (a.g ? 2 : 1) + (a.g ? (size_t)a.k * 4 : 0);
+    // xs, and for a normed input its raw copy and the gain: fewer batch rows staged at once when a
+    // wide input (a 6144-column down projection) would not fit beside a unit's weights. A row's sums
+    // do not depend on how many rows are staged with it.
+    auto staged = [&](int n) { return (size_t)n * a.k * 4 * (a.g ? 2 : 1) + (a.g ? (size_t)a.k * 4 : 0); };
+    while (nb > 1 && staged(nb) + R * row_bytes > GEMV_SMEM_LIMIT) nb /= 2;
+    const size_t xs_bytes = staged(nb);
     if (xs_bytes + R * row_bytes > GEMV_SMEM_LIMIT) return cudaErrorInvalidValue;
     int blocks = std::min(a.units, device_sms());
     a.per_block = (a.units + blocks - 1) / blocks;

@@ -444,8 +444,9 @@ bool plan(int K, int NT, int S, int rows, bool norm, DtcPlan &pl) {
 }
 
 int split_for(int K, int NT) {
-    // Eight blocks a cluster (the portable maximum); gate/up's two tiles a block take four.
-    return NT == 2 ? 4 : 8;
+    // Eight blocks a cluster (the portable maximum); gate/up's two tiles a block take four while
+    // a block's slice stays within the norm's 256 columns (hidden 1024), else eight (hidden 2048).
+    return NT == 2 && K / 4 <= 256 ? 4 : 8;
 }
 
 template <int EPI>
@@ -501,8 +502,12 @@ bool dtc_supported(const tg_params &p) {
     DtcPlan pl;
     return plan((int)p.hidden, 1, split_for((int)p.hidden, 1), (int)p.rows, true, pl) &&
            plan((int)p.hidden, 2, split_for((int)p.hidden, 2), (int)p.rows, true, pl) &&
-           plan((int)(p.heads * p.head_dim), 1, split_for((int)(p.heads * p.head_dim), 1), (int)p.rows, false, pl) &&
-           plan((int)p.inner, 1, split_for((int)p.inner, 1), (int)p.rows, false, pl);
+           plan((int)(p.heads * p.head_dim), 1, split_for((int)(p.heads * p.head_dim), 1), (int)p.rows, false, pl);
+}
+
+bool dtc_residual_supported(const tg_params &p, int K) {
+    DtcPlan pl;
+    return p.dtype == TG_BF16 && plan(K, 1, split_for(K, 1), (int)p.rows, false, pl);
 }
 
 cudaError_t launch_dtc_qkv_rope(const tg_params &p, const float *x, const float *g, const void *w, const float *cosv,

@@ -169,7 +169,8 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
         tg_params pd = base;
         pd.n = (uint32_t)H;
         pd.k = (uint32_t)I;
-        push(v, d.tensor ? KERNEL_DTC_RESIDUAL : TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
+        const bool tc_down = d.tensor && dtc_residual_supported(d.params(d.rows), (int)I);
+        push(v, tc_down ? KERNEL_DTC_RESIDUAL : TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
              {{d.mlp.ptr(), R * I * F}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
     }
     push(v, TG_KERNEL_RMSNORM, base, "final_norm",

@@ -165,9 +165,12 @@ cudaError_t launch_silu_mul_rows(const tg_params &p, const uint32_t *at, const f
 // f32 operands on a SIMT kernel. Returns cudaErrorInvalidValue for shapes it does not tile.
 cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c,
                         uint32_t *err, cudaStream_t s);
-// The batched decode projections (kernels_decode_tc.cu): true when every projection of a step of
-// p.rows rows of this shape has a plan.
+// The batched decode projections (kernels_decode_tc.cu): true when the q/k/v, gate/up and output
+// projections of a step of p.rows rows of this shape have a plan; the down projection runs on
+// tcgen05 when dtc_residual_supported(p, inner) too, else as the GEMV (a 6144-column slice of W
+// does not fit a cluster's shared memory).
 bool dtc_supported(const tg_params &p);
+bool dtc_residual_supported(const tg_params &p, int K);
 cudaError_t launch_dtc_qkv_rope(const tg_params &p, const float *x, const float *g, const void *w, const float *cosv,
                                 const float *sinv, const uint32_t *at, float *q, void *kc, void *vc, uint32_t *err,
                                 cudaStream_t s);

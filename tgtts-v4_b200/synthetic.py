@@ -44,7 +44,11 @@ class Config:
 # BASELINE.json configs[0] and configs[1..4]'s backbone.
 TINY = Config("tiny", hidden=256, inner=1024, heads=4, kv_heads=1, head_dim=64, layers=4, dtype="f32")
 S05B = Config("0p5b", hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=24, dtype="bf16")
-CONFIGS = {"tiny": TINY, "0p5b": S05B}
+# VoxCPM2's base LM (crates/graph/src/decode.rs:946-947's known answer: 2048 wide, 6144 inner,
+# 16 heads of 128 over 2 key-value heads, 28 layers): the shape a tgtts-v4 deployment runs.
+VOXCPM2_LM = Config("voxcpm2_lm", hidden=2048, inner=6144, heads=16, kv_heads=2, head_dim=128, layers=28,
+                    dtype="bf16")
+CONFIGS = {"tiny": TINY, "0p5b": S05B, "voxcpm2_lm": VOXCPM2_LM}
 
 
 def shape_of(cfg: Config, capacity: int, layers: int | None = None):
