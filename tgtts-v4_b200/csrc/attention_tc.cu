@@ -188,16 +188,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
             for (int d = 0; d < 64; d++) o[d] = __fmaf_rn(o[d], a_pend, __uint_as_float(v[d / 16][d % 16]));
         };
-        // Half c2 (64 keys) of S_j, scaled to base 2 and masked past the row's position.
+        // Half c2 (64 keys) of S_j as the raw scores, masked past the row's position (-inf) only in
+        // a half that reaches past it: the scale to base 2 is folded into the exponential's FMA, so
+        // that a score costs a max, an FMA, an exponential and an add.
         auto load_half = [&](int j, int c2, float (&sv)[64]) {
             uint32_t r[4][16];
 #pragma unroll
             for (int c = 0; c < 4; c++) tmem_ld16_nowait(lanes + s_col(h) + (uint32_t)(c2 * 64 + c * 16), r[c]);
             tmem_wait_ld();
             const int k0 = j * 128 + c2 * 64;
+            if (k0 + 63 <= pos) {
 #pragma unroll
-            for (int c = 0; c < 64; c++)
-                sv[c] = k0 + c <= pos ? __uint_as_float(r[c / 16][c % 16]) * scale2 : -INFINITY;
+                for (int c = 0; c < 64; c++) sv[c] = __uint_as_float(r[c / 16][c % 16]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; c++) sv[c] = k0 + c <= pos ? __uint_as_float(r[c / 16][c % 16]) : -INFINITY;
+            }
         };
         for (int j = 0; j < n; j++) {
             mbar_wait(B(bs_full[h]), j & 1, err, &gave_up);
@@ -215,7 +221,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            const float m_new = fmaxf(mrow, mx);
+            const float m_new = fmaxf(mrow, mx * scale2);  // the scale is positive: max, then scale
             const bool live = m_new != -INFINITY;  // false only for a spare row
             const float a = live ? fa_exp2(mrow - m_new) : 1.0f;
             if (j > 0) {
@@ -233,8 +239,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 uint32_t pk[32];
 #pragma unroll
                 for (int c = 0; c < 64; c += 2) {
-                    const float p0 = live ? fa_exp2(sv[c] - m_new) : 0.0f;
-                    const float p1 = live ? fa_exp2(sv[c + 1] - m_new) : 0.0f;
+                    const float p0 = live ? fa_exp2(__fmaf_rn(sv[c], scale2, -m_new)) : 0.0f;
+                    const float p1 = live ? fa_exp2(__fmaf_rn(sv[c + 1], scale2, -m_new)) : 0.0f;
                     sum8[c % 8] += p0;
                     sum8[(c + 1) % 8] += p1;
                     const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
