@@ -333,7 +333,32 @@ def side_measurements(pkg, syn, ctx, torch, tc_peak, peak_kind, weights):
     pre.close()
     dec.close()
     out["decode_c3"] = continuous_c3(pkg, syn, ctx, torch, weights)
+    out["logits_head"] = logits_head(pkg, syn, ctx)
     return out
+
+
+def logits_head(pkg, syn, ctx, vocab=32000, reps=99):
+    """The optional vocabulary head at batch 1 (gemv_linear, bf16 W [32000][1024], 65.5 MB): three
+    heads' weights (197 MB, past L2) taken in turn, `reps` launches in one program, CUDA events at
+    its ends."""
+    from tgtts_v4_b200.lm_side import LogitsHead
+
+    hbm, _, _ = peaks()
+    H = syn.S05B.hidden
+    heads = []
+    for i in range(3):
+        head = LogitsHead(pkg, ctx, H, vocab, rows=1)
+        head.load(np.random.default_rng(i).standard_normal((vocab, H), dtype=np.float32) * np.float32(0.02))
+        head(np.ones((1, H), np.float32))
+        heads.append(head)
+    prog = pkg.Program(ctx, [heads[i % 3].dispatch for i in range(reps)])
+    prog.run()
+    prog.run()
+    us = prog.elapsed_ns() / reps / 1e3
+    gbs = vocab * H * 2 / (us * 1e3)
+    prog.close()
+    return {"vocab": vocab, "hidden": H, "rows": 1, "us": round(us, 2), "weight_gbs": round(gbs, 1),
+            "frac_of_hbm": round(gbs / hbm, 4)}
 
 
 def continuous_c3(pkg, syn, ctx, torch, weights, steps=300, check=8, slots=64):

@@ -69,3 +69,26 @@ def test_a_row_of_the_lm_side_is_the_same_bits_alone(pkg, ctx, syn):
         np.testing.assert_array_equal(stop1[0], stop[1])
     both.close()
     alone.close()
+
+
+@pytest.mark.parametrize("rows", [1, 4])
+def test_a_32000_word_logits_head_matches_the_oracle(pkg, ctx, syn, rows):
+    """The optional vocabulary head (gemv_linear over the final hidden states) at V = 32000, the
+    synthetic size SURVEY gives for timing it, bf16 weights: within f32 rounding of the oracle, and
+    a row alone the same bits as among others."""
+    import oracle
+    from tgtts_v4_b200.lm_side import LogitsHead
+
+    H, V = 1024, 32000
+    rng = np.random.default_rng(31)
+    w = syn.bf16_round(rng.standard_normal((V, H), dtype=np.float32) * 0.02)
+    h = rng.standard_normal((rows, H), dtype=np.float32)
+    head = LogitsHead(pkg, ctx, H, V, rows=rows)
+    head.load(w)
+    got = head(h)
+    want = oracle.gemv_linear(h, None, w, np.zeros(V, np.float32))
+    np.testing.assert_allclose(got, want, rtol=2e-5, atol=2e-5)
+    if rows > 1:
+        one = LogitsHead(pkg, ctx, H, V, rows=1)
+        one.load(w)
+        np.testing.assert_array_equal(one(h[2:3])[0], got[2])

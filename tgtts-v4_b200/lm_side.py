@@ -157,3 +157,44 @@ def oracle_step(oracle, shape: LmSideShape, stacks, weights, rows, enc):
     res_out = residual.decode_step(rows, residual_in)
     mu = np.concatenate([lin("lm_to_dit_proj", lm_hidden), lin("res_to_dit_proj", res_out)], 1)
     return mu, stop, levels
+
+
+class LogitsHead:
+    """An output projection over a stack's final hidden states: logits [rows][vocab] = W h + bias,
+    one gemv_linear dispatch (TG_KERNEL_GEMV_LINEAR) recorded once. The decode stack itself ends at
+    the final norm (crates/graph/src/decode.rs:716-723) and VoxCPM2's only logits are the LM side's
+    stop head; this is the optional vocabulary head a plain LM adds, on the same kernel."""
+
+    def __init__(self, pkg, ctx, hidden: int, vocab: int, rows: int = 1, dtype: str = "bf16"):
+        self.pkg, self.ctx, self.hidden, self.vocab, self.rows, self.dtype = pkg, ctx, hidden, vocab, rows, dtype
+        es = 2 if dtype == "bf16" else 4
+        self.x = pkg.Memory(ctx, rows * hidden * 4)
+        self.out = pkg.Memory(ctx, rows * vocab * 4)
+        self.w = pkg.Memory(ctx, vocab * hidden * es)
+        self.b = pkg.Memory(ctx, max(16, vocab * 4))
+        self.b.fill(0)
+        shape = pkg.Shape(hidden=hidden, inner=hidden, heads=1, kv_heads=1, head_dim=64, layers=1, capacity=64)
+        self.params = pkg.params(shape, dtype, rows=rows, n=vocab, k=hidden, k1=0, offset=0, stride=vocab, act=0)
+        self.dispatch = ("gemv_linear", self.params,
+                         [(self.x, 0, rows * hidden * 4), (self.x, 0, 16), (self.w, 0, vocab * hidden * es),
+                          (self.b, 0, vocab * 4), (self.out, 0, rows * vocab * 4)], "logits")
+        self.program = pkg.Program(ctx, [self.dispatch])
+
+    def load(self, weight: np.ndarray, bias: Optional[np.ndarray] = None) -> None:
+        w = np.ascontiguousarray(weight)
+        if w.shape != (self.vocab, self.hidden):
+            raise self.pkg.ShapeError(f"logits weight: shape {w.shape}, not {(self.vocab, self.hidden)}")
+        if self.dtype == "bf16" and w.dtype != np.uint16:
+            from . import synthetic
+
+            w = synthetic.bf16_bits(w)
+        elif self.dtype == "f32":
+            w = np.ascontiguousarray(w, np.float32)
+        self.w.write(w)
+        self.b.write(np.zeros(self.vocab, np.float32) if bias is None else np.ascontiguousarray(bias, np.float32))
+
+    def __call__(self, h: np.ndarray) -> np.ndarray:
+        """h [rows][hidden] f32 -> logits [rows][vocab] f32."""
+        self.x.write(np.ascontiguousarray(h, np.float32).reshape(self.rows, self.hidden))
+        self.program.run()
+        return self.out.read(np.float32, self.rows * self.vocab).reshape(self.rows, self.vocab)
