@@ -121,3 +121,37 @@ def test_synthetic_weights_are_seeded_and_bf16_valued(syn):
     assert q.shape == (1024, 1024) and np.array_equal(q, syn.bf16_round(q))
     assert abs(float(q.std()) - 0.02) < 1e-3
     assert np.all(w["norm.weight"] == 1)
+
+
+def test_the_ctypes_structs_match_the_c_header(pkg, tmp_path):
+    """Every struct the Python binding mirrors has the C header's size and field offsets (gcc on
+    include/tgcuda.h), so that a params field added on one side cannot go unnoticed."""
+    import shutil
+    import subprocess
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    structs = {"tg_params": pkg.TgParams, "tg_shape": pkg.TgShape, "tg_row": pkg.TgRow, "tg_run": pkg.TgRun,
+               "tg_request": pkg.TgRequest, "tg_binding": pkg.TgBinding, "tg_dispatch": pkg.TgDispatch,
+               "tg_region": pkg.TgRegion, "tg_local_tuning": pkg.TgLocalTuning}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "tgcuda.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'printf("{cname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    root = Path(__file__).resolve().parent.parent
+    subprocess.run(["gcc", "-std=c11", "-I", str(root / "include"), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    got = {}
+    for line in out:
+        if line:
+            cname, field, value = line.split()
+            got[(cname, field)] = int(value)
+    for cname, py in structs.items():
+        assert got[(cname, "size")] == ctypes.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert got[(cname, field)] == getattr(py, field).offset, (cname, field)

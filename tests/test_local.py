@@ -138,6 +138,10 @@ def test_the_patch_config_derives_the_stack_as_upstream(pkg):
     mean = local.PatchConfig.from_dict({"lm_config": lm, "patch_size": 4, "feat_dim": 64, "encoder_config": stack,
                                         "dit_config": dict(stack, mean_mode=True)})
     assert mean.dit_config.mean_mode
+    # Sampler::new refuses the DiT's mean mode (dit.rs:189-192), before it reaches the GPU.
+    with pytest.raises(pkg.ShapeError):
+        local.Sampler.from_config(None, mean, timesteps=10, rows=1)
+    assert cfg.stack(cfg.encoder_config, 5).capacity == 5
 
 
 def test_the_tiled_layout_puts_each_value_where_the_kernels_read_it(pkg):
