@@ -36,8 +36,9 @@ void clear_error() { g_error.clear(); }
 
 int wait_event(cudaEvent_t ev, uint64_t timeout_ns) {
     const auto t0 = std::chrono::steady_clock::now();
-    // Spin briefly (a decode step is ~100 us), then poll with short sleeps
-    // (crates/vulkan/src/context.rs:119-136 spins, then blocks up to its limit).
+    // Spin through a step's whole time (a batch-1 decode step takes ~0.7 ms: a sleep, which the
+    // OS rounds up to tens of microseconds, would land after the step ends), then poll with short
+    // sleeps (crates/vulkan/src/context.rs:119-136 spins, then blocks up to its limit).
     for (uint64_t i = 0;; i++) {
         const cudaError_t e = cudaEventQuery(ev);
         if (e == cudaSuccess) return TG_OK;
@@ -47,7 +48,7 @@ int wait_event(cudaEvent_t ev, uint64_t timeout_ns) {
                                     .count();
         if (timeout_ns && waited > timeout_ns)
             return fail(TG_ETIMEOUT, "the GPU did not finish within %.3f ms", timeout_ns / 1e6);
-        if (waited > 200000) std::this_thread::sleep_for(std::chrono::microseconds(20));
+        if (waited > 2000000) std::this_thread::sleep_for(std::chrono::microseconds(20));
     }
 }
 
