@@ -285,6 +285,7 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(d->stage_x.alloc(ctx, R * H * F, TG_RES_UPLOAD));
     TG_TRY(d->word_ring.init(ctx, 8, 2 * R * 4));
     TG_TRY(d->stage_out.alloc(ctx, R * H * F, TG_RES_READBACK));
+    TG_CUDA(cudaEventCreateWithFlags(&d->out_done, cudaEventDisableTiming));
     TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
     // A decoder of DTC_MIN_ROWS rows or more runs its projections on tcgen05 in every bucket (so that
     // a row's bits do not depend on the bucket); smaller ones run the GEMVs.
@@ -352,6 +353,7 @@ extern "C" int tg_decoder_destroy(tg_decoder *d) {
     cudaSetDevice(d->ctx->device);
     d->wait_pending();
     for (Bucket &b : d->buckets) program_release(b.prog);
+    if (d->out_done) cudaEventDestroy(d->out_done);
     delete d;
     return TG_OK;
 }
@@ -495,10 +497,17 @@ extern "C" int tg_decoder_output(tg_decoder *d, float *out) {
 }
 
 extern "C" int tg_decoder_step_rows_n(tg_decoder *d, uint32_t n, const tg_row *rows, const float *x, float *out) {
+    if (!out) return fail(TG_EINVAL, "tg_decoder_step_rows: null output");
     TG_TRY(tg_decoder_set_rows_n(d, n, rows, x));
     TG_TRY(tg_decoder_start(d));
-    TG_TRY(tg_decoder_wait(d, 60ull * 1000000000ull));
-    return tg_decoder_output(d, out);
+    // The output's copy goes behind the step on the stream, so that one wait covers both.
+    const uint64_t bytes = (uint64_t)n * d->shape.hidden * 4;
+    TG_CUDA(cudaMemcpyAsync(d->stage_out.ptr(), d->out.ptr(), bytes, cudaMemcpyDefault, d->ctx->stream));
+    TG_CUDA(cudaEventRecord(d->out_done, d->ctx->stream));
+    TG_TRY(wait_event(d->out_done, 60ull * 1000000000ull));
+    TG_TRY(tg_decoder_wait(d, 0));  // done by now: clears the pending run and reads the error word
+    memcpy(out, d->stage_out.host(), bytes);
+    return TG_OK;
 }
 
 extern "C" int tg_decoder_step_rows(tg_decoder *d, const tg_row *rows, const float *x, float *out) {

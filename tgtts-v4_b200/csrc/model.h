@@ -110,6 +110,7 @@ struct tg_decoder {
     bool persistent = false;         // the step is one persistent launch (rows <= 2), else six kernels a layer
     bool tensor = false;             // the projections run on tcgen05 (rows >= DTC_MIN_ROWS, bf16)
     tg::Owned stage_x, stage_out;  // pinned host staging
+    cudaEvent_t out_done = nullptr;  // recorded after a step's output copy (tg_decoder_step_rows_n)
     tg::StageRing word_ring;                    // placements of device-resident steps
     std::vector<tg::Bucket> buckets;            // ascending rows; the last holds `rows`
     size_t active = 0;                          // the bucket the next start runs
