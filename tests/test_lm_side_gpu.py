@@ -74,7 +74,7 @@ def test_a_row_of_the_lm_side_is_the_same_bits_alone(pkg, ctx, syn):
 @pytest.mark.parametrize("rows", [1, 4])
 def test_a_32000_word_logits_head_matches_the_oracle(pkg, ctx, syn, rows):
     """The optional vocabulary head (gemv_linear over the final hidden states) at V = 32000, the
-    synthetic size SURVEY gives for timing it, bf16 weights: within f32 rounding of the oracle, and
+    synthetic size it is timed at, bf16 weights: within f32 rounding of the oracle, and
     a row alone the same bits as among others."""
     import oracle
     from tgtts_v4_b200.lm_side import LogitsHead
