@@ -232,9 +232,11 @@ def run_ours(args, rank, world, local):
         extras["step_hbm"] = {"bytes": step_bytes, "ms": round(ms_per_step, 4),
                               "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
                               "frac": round(step_bytes / (ms_per_step * 1e6) / hbm, 4)}
-        if not args.no_extras:
+        # The side measurements and the CPU baseline are single-GPU numbers: at N > 1 they would
+        # only hold the other GPUs.
+        if not args.no_extras and world == 1:
             extras.update(side_measurements(pkg, syn, ctx, torch, tc, peak_kind, weights))
-        cpu = None if args.no_cpu else cpu_baseline(syn, shape, weights)
+        cpu = None if args.no_cpu or world > 1 else cpu_baseline(syn, shape, weights)
         c = clocks.summary()
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
