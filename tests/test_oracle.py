@@ -36,6 +36,15 @@ def test_bf16_rounding_matches_the_bytes_torch_stored(syn):
     # Ties go to even: 1 + 2^-8 sits halfway between 1 and 1 + 2^-7.
     assert syn.bf16_bits(np.array([1 + 2**-8], np.float32))[0] == 0x3F80
     assert syn.bf16_bits(np.array([1 + 3 * 2**-8], np.float32))[0] == 0x3F82
+    # Every 65,521st bit pattern and the edges (the largest finite value, infinity, the negative
+    # NaNs where the rounding sum passes 2^32) against the rule in exact integers.
+    u = np.concatenate([np.arange(0, 2**32, 65521, dtype=np.uint64),
+                        np.array([0x7F7FFFFF, 0x7F800000, 0x00008000, 0x00018000, 0xFFFF7FFF, 0xFFFF8000,
+                                  0xFFFFFFFF], np.uint64)])
+    want = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF
+    got = syn.bf16_bits(u.astype(np.uint32).view(np.float32))
+    assert np.array_equal(got.astype(np.uint64), want)
+    assert np.array_equal(syn.bf16_to_f32(got).view(np.uint32), got.astype(np.uint32) << 16)
 
 
 @pytest.mark.parametrize("tables", ["oracle", "numpy"])

@@ -63,14 +63,20 @@ def shape_of(cfg: Config, capacity: int, layers: int | None = None):
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:
     """The bf16 bits of f32 values, rounded to nearest even (finite values: the low 16 bits are
-    rounded into the high 16, ties to the even result)."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
-    return rounded.astype(np.uint16)
+    rounded into the high 16, ties to the even result). The sum is taken in u32: where it wraps
+    (only negative NaNs), its high 16 bits are those of the exact sum modulo 2^16, the same bits."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = (u >> 16) & np.uint32(1)
+    r += u
+    r += np.uint32(0x7FFF)
+    r >>= 16
+    return r.astype(np.uint16)
 
 
 def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
-    return (bits.astype(np.uint32) << 16).view(np.float32)
+    u = bits.astype(np.uint32)
+    u <<= 16
+    return u.view(np.float32)
 
 
 def bf16_round(x: np.ndarray) -> np.ndarray:
