@@ -549,6 +549,7 @@ extern "C" int tg_ctx_create(int device, tg_ctx **out) {
     if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->err_dev), ctx->err_host, 0);
     if (e != cudaSuccess) {
         if (ctx->stream) cudaStreamDestroy(ctx->stream);
+        if (ctx->err_host) cudaFreeHost(ctx->err_host);
         delete ctx;
         return cuda_fail(e, "tg_ctx_create");
     }
@@ -611,6 +612,9 @@ extern "C" int tg_mem_alloc(tg_ctx *ctx, uint64_t bytes, tg_residence residence,
         return fail(TG_EINVAL, "residence %d", (int)residence);
     }
     if (e != cudaSuccess) {
+        // What the failing step left allocated goes back before the error is reported.
+        if (residence == TG_RES_DEVICE && m->ptr) cudaFree(m->ptr);
+        if (residence != TG_RES_DEVICE && m->host) cudaFreeHost(m->host);
         delete m;
         return cuda_fail(e, "tg_mem_alloc");
     }
