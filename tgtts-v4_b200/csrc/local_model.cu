@@ -328,6 +328,7 @@ struct tg_sampler {
     bool timed = false;
     uint64_t mu_bytes() const { return (uint64_t)rows * 2 * dit.shape.hidden * 2; }
     uint64_t patch_bytes() const { return (uint64_t)rows * feat * patch * 4; }
+    ~tg_sampler() { program_release(prog); }
 };
 
 extern "C" int tg_cfm_schedule(uint32_t timesteps, float *out) {
@@ -507,7 +508,6 @@ extern "C" int tg_sampler_destroy(tg_sampler *s) {
     if (!s) return TG_OK;
     cudaSetDevice(s->ctx->device);
     if (s->prog.pending) wait_program(s->prog, 0);
-    program_release(s->prog);
     delete s;
     return TG_OK;
 }
@@ -647,6 +647,7 @@ struct tg_encoder {
     bool timed = false;
     uint64_t patch_bytes() const { return (uint64_t)rows * feat * patch * 4; }
     uint64_t out_bytes() const { return (uint64_t)rows * enc.shape.hidden * 2; }
+    ~tg_encoder() { program_release(prog); }
 };
 
 // encoder_graph (encoder.rs:41-124): the learned token and the frames projected, the stack, and
@@ -710,7 +711,6 @@ extern "C" int tg_encoder_destroy(tg_encoder *e) {
     if (!e) return TG_OK;
     cudaSetDevice(e->ctx->device);
     if (e->prog.pending) wait_program(e->prog, 0);
-    program_release(e->prog);
     delete e;
     return TG_OK;
 }

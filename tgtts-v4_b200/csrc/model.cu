@@ -352,8 +352,6 @@ extern "C" int tg_decoder_destroy(tg_decoder *d) {
     if (!d) return TG_OK;
     cudaSetDevice(d->ctx->device);
     d->wait_pending();
-    for (Bucket &b : d->buckets) program_release(b.prog);
-    if (d->out_done) cudaEventDestroy(d->out_done);
     delete d;
     return TG_OK;
 }
@@ -761,10 +759,8 @@ extern "C" int tg_prefill_create(tg_decoder *d, uint32_t max_rows, int timed, tg
 extern "C" int tg_prefill_destroy(tg_prefill *p) {
     if (!p) return TG_OK;
     cudaSetDevice(p->d->ctx->device);
-    for (auto &kv : p->programs) {
+    for (auto &kv : p->programs)
         if (kv.second.pending) program_wait(kv.second, 0);
-        program_release(kv.second);
-    }
     delete p;
     return TG_OK;
 }

@@ -116,6 +116,13 @@ struct tg_decoder {
     size_t active = 0;                          // the bucket the next start runs
     uint32_t n_active = 0;                      // the rows given to the last set_rows
 
+    // Releases the recorded programs and the event, also when creation fails part way (the
+    // caller has waited for any run in flight and made the decoder's device current).
+    ~tg_decoder() {
+        for (tg::Bucket &b : buckets) tg::program_release(b.prog);
+        if (out_done) cudaEventDestroy(out_done);
+    }
+
     uint64_t width() const { return (uint64_t)(shape.heads + 2 * shape.kv_heads) * shape.head_dim; }
     uint64_t attn() const { return (uint64_t)shape.heads * shape.head_dim; }
     tg_params params(uint32_t R) const {
@@ -156,6 +163,10 @@ struct tg_prefill {
     tg::Owned stage_x, stage_words, stage_out;
     std::map<uint32_t, tg::Program> programs;  // by rows, a multiple of 128
     tg::Program *last = nullptr;
+
+    ~tg_prefill() {
+        for (auto &kv : programs) tg::program_release(kv.second);
+    }
 };
 
 namespace tg {
