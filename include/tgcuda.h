@@ -36,7 +36,7 @@ typedef enum {
     TG_ECUDA = 3,      /* vulkan::Error::Vk: a CUDA call failed */
     TG_ENOMEM = 4,     /* vulkan::Error::NoMemoryType: an allocation failed */
     TG_ETIMEOUT = 5,   /* a wait ran past its deadline (crates/vulkan/src/context.rs:119-136) */
-    TG_ENOTFINITE = 6, /* graph::Error::NotFinite */
+    TG_ENOTFINITE = 6, /* graph::Error::NotFinite: a sampled patch came out NaN or infinite */
     TG_EKERNEL = 7,    /* a kernel reported an error word (a bounded wait that gave up) */
     TG_ENODEVICE = 8   /* vulkan::Error::NoDevice */
 } tg_status;
@@ -448,7 +448,9 @@ int tg_sampler_destroy(tg_sampler *s);
 int tg_sampler_load(tg_sampler *s, const char *name, const void *src, uint64_t count, tg_dtype src_dtype);
 /* Sampler::sample (local/dit.rs:298-313): mu f16 bits [rows][2][hidden], cond and noise f32
  * [rows][feat_dim][patch_size], sampling f32 [rows][2] (temperature, guidance scale) -> patch f32
- * [rows][feat_dim][patch_size]. */
+ * [rows][feat_dim][patch_size]. TG_ENOTFINITE, with every patch written, when a row's patch came
+ * out NaN or infinite (the check crates/graph/src/generator.rs:418-421 makes on each sampled
+ * patch, Error::NotFinite); the device form leaves that check to its caller. */
 int tg_sampler_sample(tg_sampler *s, const uint16_t *mu, const float *cond, const float *noise,
                       const float *sampling, float *patch);
 /* The same from device pointers, enqueued on the context's stream without waiting. */

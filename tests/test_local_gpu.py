@@ -167,6 +167,22 @@ def test_the_encoder_embeds_as_the_oracle_and_alone_among_others(pkg, local, ctx
     assert not within(got, want)
 
 
+def test_a_patch_that_comes_out_nan_is_not_finite(pkg, local, ctx, syn):
+    """generator.rs:418-421: a sampled patch that is NaN or infinite is Error::NotFinite; the rows
+    beside it are sampled as before, and so is the next sample."""
+    cfg = syn.LOCAL_SMALL
+    w = syn.make_sampler_weights(cfg, seed=0)
+    mu, cond, noise, sampling = syn.make_sampler_inputs(cfg, 3, seed=1)
+    s = make_sampler(pkg, local, ctx, syn, cfg, 3, 2, w)
+    want = s.sample(mu, cond, noise, sampling)
+    assert np.all(np.isfinite(want))
+    bad = np.array(mu, np.float32)
+    bad[1].flat[5] = np.nan
+    with pytest.raises(pkg.NotFiniteError, match="row 1"):
+        s.sample(bad, cond, noise, sampling)
+    np.testing.assert_array_equal(s.sample(mu, cond, noise, sampling), want)
+
+
 def test_the_local_kernels_refuse_what_they_do_not_take(pkg, local, ctx, syn):
     cfg = syn.LOCAL_SMALL
     bad = syn.local_shape(cfg)

@@ -584,6 +584,13 @@ extern "C" int tg_sampler_sample(tg_sampler *s, const uint16_t *mu, const float 
     TG_TRY(wait_program(s->prog, 60ull * 1000000000ull));
     TG_CUDA(cudaStreamSynchronize(s->ctx->stream));
     memcpy(patch, s->stage_out.host(), s->patch_bytes());
+    // generator.rs:418-421: a patch that is not finite ends its request (the stop head might
+    // never say to stop after it).
+    const uint64_t per_row = (uint64_t)s->feat * s->patch;
+    for (uint32_t r = 0; r < s->rows; r++)
+        for (uint64_t i = 0; i < per_row; i++)
+            if (!std::isfinite(patch[r * per_row + i]))
+                return fail(TG_ENOTFINITE, "the patch of row %u came out NaN or infinite", r);
     return TG_OK;
 }
 
