@@ -137,3 +137,32 @@ def test_tcgen05_attention_matches_the_mma_sync_kernel_within_rounding(pkg, ctx,
     m, rel, cos = distance(outs[1][live], outs[0][live])
     assert rel < 1e-2 and cos > 0.9999, (m, rel, cos)
     assert np.all(outs[1][~live] == 0)  # spare rows are not written
+
+
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_nan_in_the_cache_past_a_run_changes_no_bit(pkg, ctx, syn, dtype):
+    """attention_rows.comp reads the keys past a tile's last position as zero (:77-83), so what a
+    slot held past the run (a request that came out NaN there before, or any stale value) cannot
+    reach the run's outputs: a prompt prefilled into a slot that is NaN everywhere gives the same
+    bits as into a clean one. 300 positions leave the last 128-key tile 84 positions past the run;
+    bf16 runs the tcgen05 kernel, f32 the CUDA-core one."""
+    cfg = syn.TINY if dtype == "f32" else syn.S05B
+    cap = 512
+    shape = syn.shape_of(cfg, capacity=cap, layers=2)
+    w = syn.make_weights(cfg, seed=0, layers=2, jitter_gains=True, as_bits=dtype == "bf16")
+    dec = pkg.Decoder(ctx, shape, rows=1, slots=2, dtype=dtype)
+    dec.load(w)
+    pre = pkg.Prefill(dec, max_rows=384)
+    x = syn.make_inputs(300, cfg.hidden, seed=2, bf16=dtype == "bf16")
+    want = pre.run(0, x, slot=0)
+    assert np.all(np.isfinite(want))
+    nan = pkg.Memory(ctx, dec.prefix_bytes(cap))
+    nan.fill(0x7FC07FC0 if dtype == "bf16" else 0x7FC00000)
+    dec.copy_in(1, cap, nan)
+    got = pre.run(0, x, slot=1)
+    np.testing.assert_array_equal(got, want)
+    # The next decode step reads the same cache from either slot.
+    step = x[-1:]
+    a = dec.step_rows([pkg.Row(300, 0)], step)
+    b = dec.step_rows([pkg.Row(300, 1)], step)
+    np.testing.assert_array_equal(a, b)

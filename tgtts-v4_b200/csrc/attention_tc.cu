@@ -58,6 +58,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const uint32_t base = smem_u32(smem);
     __shared__ __align__(8) uint64_t bq, bkv_full[2], bkv_empty[2];
     __shared__ __align__(8) uint64_t bs_full[2], bs_empty[2], bp_full[2], bo_full[2], bo_empty[2];  // by head
+    __shared__ __align__(8) uint64_t bv_clear;  // V_{n-1}'s rows past the tile's last position are zero
     __shared__ uint32_t tmem_slot, t_last, t_slot, t_slot_max;
     __shared__ int gave_up;
     __shared__ int pos_s[128];
@@ -83,6 +84,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             mbar_init(B(bo_full[i]), 1);
             mbar_init(B(bo_empty[i]), 128);
         }
+        mbar_init(B(bv_clear), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -112,6 +114,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     const bool mixed = t_slot != 0xffffffffu && t_slot != t_slot_max;
     if (mixed && tid == 0) atomicExch(err, ERR_BAD_INDEX);
     const int n = (t_slot == 0xffffffffu || mixed) ? 0 : (int)(t_last / 128 + 1);  // key tiles
+    // Keys past the tile's last position are read as zero (attention_rows.comp:77-83): their
+    // probabilities are 0, but a value there that is not finite (another request's, left in the
+    // slot, or the next cache range's) would still make 0 x v NaN in PV. When the last key tile
+    // reaches past it, warp 0 clears those rows of V_{n-1} before PV_{n-1} is issued.
+    const bool clear_v = n > 0 && t_last % 128 != 127;
     // TMEM columns: head h's S at 256 h, its O at 256 h + 128.
     auto s_col = [](int h) { return (uint32_t)(256 * h); };
     auto o_col = [](int h) { return (uint32_t)(256 * h + 128); };
@@ -131,6 +138,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
             // Every copy this thread started has landed before the block can end.
             for (int j = n > 2 ? n - 2 : 0; j < n; j++) mbar_wait(B(bkv_full[j & 1]), (j >> 1) & 1, err, &gave_up);
+        }
+        if (clear_v) {
+            __syncwarp();
+            mbar_wait(B(bkv_full[(n - 1) & 1]), ((n - 1) >> 1) & 1, err, &gave_up);
+            uint8_t *vt = smem + FA_V + ((n - 1) & 1) * FA_TILE;
+            const int keep = (int)(t_last % 128) + 1;
+            for (int i = lane; i < (128 - keep) * 8; i += 32) {
+                const int r = keep + i / 8;  // a row of the swizzled tile is 128 whole bytes
+                *reinterpret_cast<uint4 *>(vt + (r >> 3) * 1024 + (r & 7) * 128 + (i % 8) * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // for the tensor cores' reads
+            __syncwarp();
+            if (lane == 0) mbar_arrive(B(bv_clear));
         }
     } else if (warp == 1) {
         if (lane == 0 && n > 0) {
@@ -153,6 +173,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             for (int j = 0; j < n; j++) {
                 if (j + 1 < n) mbar_wait(B(bkv_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, err, &gave_up);
                 const uint32_t v = base + FA_V + (j & 1) * FA_TILE;
+                if (clear_v && j == n - 1) mbar_wait(B(bv_clear), 0, err, &gave_up);
                 for (int h = 0; h < 2; h++) {
                     mbar_wait(B(bp_full[h]), j & 1, err, &gave_up);
                     if (j > 0) mbar_wait(B(bo_empty[h]), (j - 1) & 1, err, &gave_up);
