@@ -39,7 +39,13 @@ def test_config1_prefill_then_feedback_decode_matches_the_oracle(pkg, ctx, syn):
     _within(got, want, "f32")
     h, hr = got[-1], want[-1]
     for t in range(16):
-        h = dec.step(32 + t, h)[0]
+        if t % 2:
+            h = dec.step(32 + t, h)[0]
+        else:  # Decoder::step's parts (decode.rs:833-837)
+            dec.set_input(32 + t, h)
+            dec.start()
+            dec.wait()
+            h = dec.output()[0]
         hr = ref.decode_step([(32 + t, 0)], hr[None])[0]
         _within(h, hr, "f32")
     # The cache holds what the oracle's does.

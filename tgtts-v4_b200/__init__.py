@@ -689,6 +689,11 @@ class Decoder:
         check(library().tg_decoder_step_rows_n(self.handle, n, _rows(rows), _fptr(x), _fptr(out)))
         return out
 
+    def set_input(self, position: int, x: np.ndarray) -> None:
+        """Decoder::set_input (decode.rs:841-845): the next run's input at batch 1, `x` the hidden
+        state of `position` in slot 0."""
+        self.set_rows([Row(position, 0)], x)
+
     def set_rows(self, rows: Sequence[Optional[Row]], x: np.ndarray) -> None:
         x = self._x(x)
         check(library().tg_decoder_set_rows(self.handle, self._c_rows(rows), _fptr(x)))
