@@ -257,8 +257,8 @@ int tg_program_timings(tg_program *p, double *ns, size_t n);
 /* ---- The stack: shape, placement, decoder, prefill (crates/graph/src/decode.rs,
  * crates/graph/src/prefill.rs) --------------------------------------------------------------- */
 
-/* decode.rs:66-83 `Shape`, plus `residual_scale`. rope_factors: head_dim/2 LongRoPE divisors, or
- * NULL for all 1 (plain RoPE). */
+/* decode.rs:66-83 `Shape`, plus `residual_scale`. capacity: a multiple of 32 (decode.rs:28 CHUNK).
+ * rope_factors: head_dim/2 LongRoPE divisors, or NULL for all 1 (plain RoPE). */
 typedef struct {
     uint32_t hidden, inner, heads, kv_heads, head_dim, layers, capacity;
     float eps, rope_theta, residual_scale;
@@ -496,7 +496,7 @@ uint64_t tg_encoder_weight_bytes(const tg_encoder *e);
  * [rows][heads][hd]), the caches (storage type), the placement words and out (f32
  * [rows][heads hd]), all device pointers, and a cudaStream_t (NULL: the legacy stream); the work
  * is enqueued there and not waited for. Refuses (TG_ESHAPE) a shape whose partials,
- * rows x heads x capacity/64 x (head_dim + 2) f32, do not fit. The first call on a device looks the
+ * rows x heads x ceil(capacity/64) x (head_dim + 2) f32, do not fit. The first call on a device looks the
  * array up for that device (and may load the library's module there): make it before any stream
  * capture. All calls on a device share the array, so calls that overlap on the GPU race. */
 #define TG_NOALLOC_SCRATCH_BYTES (4u << 20)

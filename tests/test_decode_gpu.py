@@ -166,9 +166,39 @@ def test_copy_slot_moves_a_prefix_between_slots(pkg, ctx, syn):
     assert np.array_equal(out[0], out[1])
 
 
+@pytest.mark.parametrize("family", ["f32", "bf16", "bf16 persistent", "bf16 tensor"])
+def test_a_cache_of_a_multiple_of_32_positions(pkg, ctx, syn, family):
+    """A capacity is a multiple of CHUNK = 32 (decode.rs:28, :480), so the last 64-position
+    attention chunk of a 160-position cache is half full: a prefill to position 140, then decode
+    steps to the last position (159), against the oracle, in every kernel family."""
+    dtype = family.split()[0]
+    cfg = syn.TINY if dtype == "f32" else syn.S05B
+    rows = 16 if family.endswith("tensor") else 1
+    cap, layers = 160, 2
+    shape = syn.shape_of(cfg, capacity=cap, layers=layers)
+    w = syn.make_weights(cfg, seed=0, layers=layers, jitter_gains=True)
+    dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype=dtype)
+    if family.endswith("persistent"):
+        dec.retuned(True)
+    assert dec.tensor == family.endswith("tensor")
+    dec.load(w)
+    ref = oracle.OracleStack(shape, w)
+    x = syn.make_inputs(140, cfg.hidden, seed=3, bf16=dtype == "bf16")
+    got, want = pkg.Prefill(dec, max_rows=256).run(0, x), ref.prefill(0, x)
+    _within(got, want, dtype)
+    h, hr = got[-1], want[-1]
+    for t in range(140, cap):
+        xs = np.zeros((rows, cfg.hidden), np.float32)
+        xs[0] = h
+        h = dec.step_rows([pkg.Row(t, 0)] + [None] * (rows - 1), xs)[0]
+        hr = ref.decode_step([(t, 0)], hr[None])[0]
+        _within(h, hr, dtype)
+    dec.close()
+
+
 def test_refusals(pkg, ctx, syn):
     cfg = syn.TINY
-    bad = syn.shape_of(cfg, capacity=100)  # not a multiple of the attention chunk
+    bad = syn.shape_of(cfg, capacity=100)  # not a multiple of 32 (decode.rs:28 CHUNK, :480)
     with pytest.raises(pkg.ShapeError):
         pkg.Decoder(ctx, bad, rows=1, dtype="f32")
     shape = syn.shape_of(cfg, capacity=64, layers=1)

@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(AM_WARPS * 32)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
     const int c = blockIdx.x * AM_WARPS + warp, kv = blockIdx.y, b = blockIdx.z;
     const int heads = p.heads, kvh = p.kv_heads, group = heads / kvh;
-    const int chunks = ((int)p.capacity + W - 1) / W, stride = (int)(p.capacity / ATTN_CHUNK);
+    const int chunks = ((int)p.capacity + W - 1) / W, stride = (int)attn_chunks(p.capacity);
     bf16 *ks = reinterpret_cast<bf16 *>(am_smem + (size_t)warp * AM_WARP_SMEM);
     bf16 *vs = ks + C * AM_ROW;
     pdl_launch_dependents();
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(AM_WARPS * 32)
 
 bool attention_split_mma_supported(const tg_params &p) {
     return p.dtype == TG_BF16 && p.head_dim == 64 && p.kv_heads > 0 && p.heads % p.kv_heads == 0 &&
-           p.heads / p.kv_heads <= 16 && p.capacity % ATTN_CHUNK == 0;
+           p.heads / p.kv_heads <= 16 && p.capacity % CAPACITY_STEP == 0;
 }
 
 cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,

@@ -445,7 +445,7 @@ TG_DEVICE float join_chunks(const float *o, size_t stride, const float *w, int n
 TG_DEVICE void attention_join(const tg_params &p, const float *__restrict__ po, const float *__restrict__ pml,
                               int b, int first_head, int n_heads, int n, float *__restrict__ out) {
     constexpr int MAXC = 64;  // chunks joined per pass of the weights below
-    const int hd = p.head_dim, chunks = p.capacity / ATTN_CHUNK;
+    const int hd = p.head_dim, chunks = attn_chunks(p.capacity);
     for (int i = threadIdx.x; i < n_heads * hd; i += blockDim.x) {
         const int h = first_head + i / hd, d = i % hd;
         const float *ml = pml + ((size_t)b * p.heads + h) * chunks * 2;
@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(128)
         pdl_wait();
         return;
     }
-    const int group = p.heads / p.kv_heads, chunks = p.capacity / ATTN_CHUNK;
+    const int group = p.heads / p.kv_heads, chunks = attn_chunks(p.capacity);
     const size_t head0 = (size_t)b * p.heads + kv * group;
     attention_chunk<T>(p, q, kc, vc, b, kv, c, pos, slot, po + (head0 * chunks + c) * p.head_dim,
                        (size_t)chunks * p.head_dim, pml + (head0 * chunks + c) * 2, (size_t)chunks * 2,
@@ -504,8 +504,8 @@ __global__ void __launch_bounds__(128)
     const int h = blockIdx.x, b = blockIdx.y, hd = p.head_dim;
     uint32_t pos, slot;
     if (!placed(at, p.rows, b, p.capacity, p.slots, pos, slot)) return;
-    // Partials of `width` positions each, laid out as ATTN_CHUNK's (capacity / ATTN_CHUNK a head).
-    const int chunks = p.capacity / ATTN_CHUNK, n = pos / width + 1;
+    // Partials of `width` positions each, laid out as ATTN_CHUNK's (attn_chunks(capacity) a head).
+    const int chunks = attn_chunks(p.capacity), n = pos / width + 1;
     float *ml = reinterpret_cast<float *>(smem);  // [n][2]
     float *w = ml + 2 * chunks;                    // [n]
     __shared__ float m_s, total_s;
@@ -543,7 +543,7 @@ __global__ void __launch_bounds__(128)
     pdl_launch_dependents();
     const int r = (int)cluster.block_rank(), kv = blockIdx.y, b = blockIdx.z;
     const int hd = p.head_dim, heads = p.heads, group = heads / p.kv_heads;
-    const int chunks = p.capacity / ATTN_CHUNK, mine = (chunks + ATTN_CLUSTER - 1) / ATTN_CLUSTER;
+    const int chunks = attn_chunks(p.capacity), mine = (chunks + ATTN_CLUSTER - 1) / ATTN_CLUSTER;
     // This block's partials: [mine][group][hd] outputs, then [mine][group][2] maxima and sums, then
     // (16-byte aligned) the chunk's working space.
     float *my_o = reinterpret_cast<float *>(smem);
@@ -850,7 +850,7 @@ __global__ void __launch_bounds__(PS_THREADS, 1) decode_step_kernel(const __grid
     bool ok = true;
     int g = 0;
     const int hd = p.head_dim, heads = p.heads, kvh = p.kv_heads, group = heads / kvh;
-    const int chunks = p.capacity / ATTN_CHUNK, H = p.hidden;
+    const int chunks = attn_chunks(p.capacity), H = p.hidden;
     uint32_t pos[PS_ROWS], slotw[PS_ROWS];
     int nchunks[PS_ROWS];
     bool live[PS_ROWS];
@@ -1193,7 +1193,7 @@ static cudaError_t split_t(const tg_params &p, const void *q, const void *kc, co
     auto kern = attention_split_kernel<T>;
     cudaError_t e = with_smem(kern, smem);
     if (e != cudaSuccess) return e;
-    dim3 grid(p.capacity / ATTN_CHUNK, p.kv_heads, p.rows);
+    dim3 grid(attn_chunks(p.capacity), p.kv_heads, p.rows);
     return launch_pdl(kern, grid, dim3(128), smem, s, p, (const float *)q, (const T *)kc, (const T *)vc, at, po, pml);
 }
 
@@ -1208,7 +1208,7 @@ cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, c
                                            const float *pml, void *out, cudaStream_t s) {
     dim3 grid(p.heads, p.rows);
     const int threads = p.head_dim < 128 ? p.head_dim : 128;
-    const size_t smem = (size_t)3 * (p.capacity / ATTN_CHUNK) * sizeof(float);
+    const size_t smem = (size_t)3 * (attn_chunks(p.capacity)) * sizeof(float);
     return launch_pdl(attention_combine_kernel, grid, dim3(threads), smem, s, p, at, po, pml, (float *)out, chunk);
 }
 
@@ -1219,7 +1219,7 @@ cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, con
 
 static size_t cluster_attention_smem(const tg_params &p) {
     const size_t group = p.heads / p.kv_heads, hd = p.head_dim;
-    const size_t chunks = p.capacity / ATTN_CHUNK, mine = (chunks + ATTN_CLUSTER - 1) / ATTN_CLUSTER;
+    const size_t chunks = attn_chunks(p.capacity), mine = (chunks + ATTN_CLUSTER - 1) / ATTN_CLUSTER;
     const size_t gather = chunks * (hd + 2) * sizeof(float);  // the join's copy of one head's partials
     return sizeof(float) * ((mine * group * (hd + 2) + 3) / 4 * 4) + std::max(attention_smem(p), gather);
 }
@@ -1302,7 +1302,7 @@ cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s
     const uint32_t kmax = std::max({p.hidden, p.inner, p.heads * p.head_dim});
     a.xs_floats = PS_ROWS * kmax;
     a.raw_floats = PS_ROWS * p.hidden;
-    const uint32_t chunks = p.capacity / ATTN_CHUNK;
+    const uint32_t chunks = attn_chunks(p.capacity);
     const size_t comb_floats = (size_t)PS_ROWS * p.heads * chunks * 3 + PS_ROWS * p.heads;
     const size_t scratch = std::max((size_t)(a.xs_floats + a.raw_floats) * 4 + comb_floats * 4, attention_smem(p));
     const size_t smem = (size_t)PS_SLOTS * PS_SLOT_BYTES + scratch;

@@ -83,8 +83,8 @@ static int check_shape(const tg_shape &s, tg_dtype dtype) {
     if (s.heads % s.kv_heads || (s.head_dim != 64 && s.head_dim != 128))
         return fail(TG_ESHAPE, "%u heads over %u of %u", s.heads, s.kv_heads, s.head_dim);
     if (s.inner % GU_BLOCK) return fail(TG_ESHAPE, "inner %u is not a multiple of %u", s.inner, GU_BLOCK);
-    if (s.capacity == 0 || s.capacity % ATTN_CHUNK)
-        return fail(TG_ESHAPE, "a cache of %u positions (a multiple of %u)", s.capacity, ATTN_CHUNK);
+    if (s.capacity == 0 || s.capacity % CAPACITY_STEP)
+        return fail(TG_ESHAPE, "a cache of %u positions (a multiple of %u)", s.capacity, CAPACITY_STEP);
     if (!(s.eps >= 0.0f) || !std::isfinite(s.residual_scale)) return fail(TG_ESHAPE, "eps %g, residual scale %g", s.eps, s.residual_scale);
     return TG_OK;
 }
@@ -140,7 +140,7 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
     const uint64_t T = d.esize, F = 4;
     const tg_shape &s = d.shape;
     const uint64_t H = s.hidden, I = s.inner, hd = s.head_dim, heads = s.heads;
-    const uint64_t chunks = s.capacity / ATTN_CHUNK;
+    const uint64_t chunks = attn_chunks(s.capacity);
     const uint64_t words = (d.slots > 1 ? 2 : 1) * (uint64_t)R * 4;
     const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
     for (uint32_t l = 0; l < s.layers; l++) {
@@ -262,7 +262,7 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     d->cache_layer = align256((uint64_t)slots * s->kv_heads * s->capacity * s->head_dim * T);
     TG_TRY(d->kcache.alloc(ctx, d->cache_layer * s->layers));
     TG_TRY(d->vcache.alloc(ctx, d->cache_layer * s->layers));
-    const uint64_t R = rows, chunks = s->capacity / ATTN_CHUNK;
+    const uint64_t R = rows, chunks = attn_chunks(s->capacity);
     TG_TRY(d->x_in.alloc(ctx, R * H * F));
     TG_TRY(d->h.alloc(ctx, R * H * F));
     TG_TRY(d->mid.alloc(ctx, R * H * F));

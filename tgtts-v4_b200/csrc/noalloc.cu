@@ -44,17 +44,17 @@ extern "C" int tg_attention_decode_noalloc(const tg_params *p, const float *q, c
             return fail(TG_EINVAL, "tg_attention_decode_noalloc: a pointer is not 16-byte aligned");
     if (p->dtype != TG_F32 && p->dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %u", p->dtype);
     if (p->rows == 0 || p->slots == 0 || p->kv_heads == 0 || p->heads % p->kv_heads ||
-        (p->head_dim != 64 && p->head_dim != 128) || p->capacity == 0 || p->capacity % ATTN_CHUNK)
+        (p->head_dim != 64 && p->head_dim != 128) || p->capacity == 0 || p->capacity % CAPACITY_STEP)
         return fail(TG_ESHAPE, "tg_attention_decode_noalloc: %u rows, %u heads over %u of %u, a cache of %u",
                     p->rows, p->heads, p->kv_heads, p->head_dim, p->capacity);
-    const uint64_t partials = (uint64_t)p->rows * p->heads * (p->capacity / ATTN_CHUNK);
+    const uint64_t partials = (uint64_t)p->rows * p->heads * attn_chunks(p->capacity);
     const uint64_t o_bytes = round256(partials * p->head_dim * 4);
     const uint64_t need = o_bytes + partials * 2 * 4;
     if (need > TG_NOALLOC_SCRATCH_BYTES)
         return fail(TG_ESHAPE,
                     "tg_attention_decode_noalloc: %u rows x %u heads x %u chunks need %llu bytes of scratch; "
                     "the fixed array holds %u",
-                    p->rows, p->heads, p->capacity / ATTN_CHUNK, (unsigned long long)need,
+                    p->rows, p->heads, attn_chunks(p->capacity), (unsigned long long)need,
                     (unsigned)TG_NOALLOC_SCRATCH_BYTES);
     int dev = 0;
     TG_CUDA(cudaGetDevice(&dev));

@@ -80,7 +80,7 @@ static int needs(const Launch &l, std::vector<Need> &out) {
     const uint64_t width = (heads + 2 * kvh) * hd, attn = heads * hd;
     const uint64_t words = (slots > 1 ? 2 : 1) * rows * 4;
     const uint64_t cache = slots * kvh * cap * hd * T;
-    const uint64_t chunks = cap / ATTN_CHUNK;
+    const uint64_t chunks = attn_chunks((uint32_t)cap);
     const uint64_t table = cap * (hd / 2) * F;
     switch (l.kernel) {
         case TG_KERNEL_RMSNORM:
@@ -254,7 +254,7 @@ static int check_shape(const Launch &l) {
     const uint32_t vec = p.dtype == TG_BF16 ? 256 : 128;  // a warp's 16-byte step over K
     auto heads_ok = [&] {
         return p.kv_heads > 0 && p.heads % p.kv_heads == 0 && (p.head_dim == 64 || p.head_dim == 128) &&
-               p.capacity > 0 && p.capacity % ATTN_CHUNK == 0;
+               p.capacity > 0 && p.capacity % CAPACITY_STEP == 0;
     };
     switch (l.kernel) {
         case TG_KERNEL_RMSNORM:
@@ -277,7 +277,7 @@ static int check_shape(const Launch &l) {
         case TG_KERNEL_ATTENTION_DECODE:
         case TG_KERNEL_ROPE_ROWS:
         case TG_KERNEL_ATTENTION_ROWS:
-            if (!heads_ok()) return fail(TG_ESHAPE, "%s: %u heads over %u of %u, capacity %u (multiple of %u)", kernel_name(l.kernel), p.heads, p.kv_heads, p.head_dim, p.capacity, ATTN_CHUNK);
+            if (!heads_ok()) return fail(TG_ESHAPE, "%s: %u heads over %u of %u, capacity %u (multiple of %u)", kernel_name(l.kernel), p.heads, p.kv_heads, p.head_dim, p.capacity, CAPACITY_STEP);
             break;
         case TG_KERNEL_SILU_MUL_ROWS:
             if (p.inner == 0) return fail(TG_ESHAPE, "silu_mul_rows: inner 0");

@@ -183,6 +183,11 @@ cudaError_t launch_dtc_residual(const tg_params &p, const float *x, const void *
 cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s);
 // The decode constants: positions per attention chunk.
 constexpr uint32_t ATTN_CHUNK = 64;
+// A cache's capacity is a multiple of this, as the reference's (decode.rs:28 CHUNK, :480); the
+// last attention chunk of a cache may then be half full.
+constexpr uint32_t CAPACITY_STEP = 32;
+// The attention chunks of a cache of `capacity` positions, the last perhaps partial.
+__host__ __device__ inline uint32_t attn_chunks(uint32_t capacity) { return (capacity + ATTN_CHUNK - 1) / ATTN_CHUNK; }
 // The rows of a prefill attention tile (the CUDA-core and mma.sync kernels).
 constexpr uint32_t PREFILL_TILE = 64;
 // Each run of a prefill launch starts on a multiple of this many rows (the tcgen05 attention's tile).
