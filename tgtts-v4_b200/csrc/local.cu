@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(LP_THREADS, 1)
                 // Rows 2j and 2j + 1 of W are gate j and up j: lanes 2i and 2i + 1 trade their
                 // tokens' sums, the even lane storing tokens c0 .. c0 + 7, the odd c0 + 8 .. + 15.
                 const bool odd = lane & 1;
-                const int j = (row0 + r) >> 1, inner = a.N >> 1;
+                const int j = (row0 + r) >> 1;
 #pragma unroll
                 for (int e = 0; e < 16; e++) {
                     const float mine = __uint_as_float(v[e]);

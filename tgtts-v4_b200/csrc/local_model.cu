@@ -159,9 +159,9 @@ static int to_f16(const void *src, uint64_t count, tg_dtype src_dtype, std::vect
 }
 
 static double f16_value(uint16_t bits) {
-    __half h;
-    memcpy(&h, &bits, 2);
-    return (double)__half2float(h);
+    __half_raw raw;
+    raw.x = bits;
+    return (double)__half2float(__half(raw));
 }
 
 static bool parse_layer(const std::string &name, uint32_t &l, std::string &rest) {

@@ -146,31 +146,31 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
     for (uint32_t l = 0; l < s.layers; l++) {
         const LayerOffsets &o = d.layer[l];
         char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
-        push(v, d.tensor ? KERNEL_DTC_QKV_ROPE : TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
+        push(v, d.tensor ? KERNEL_DTC_QKV_ROPE : (uint32_t)TG_KERNEL_GEMV_QKV_ROPE, base, "qkv_rope",
              {{in, R * H * F}, {d.w(o.in_norm), H * F}, {d.w(o.qkv), d.width() * H * T}, {d.cos.ptr(), table},
               {d.sin.ptr(), table}, {d.words.ptr(), words}, {d.q.ptr(), R * d.attn() * F},
               {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
         const bool wide = d.tensor && attention_split_mma_supported(base);
-        push(v, wide ? KERNEL_ATTN_SPLIT_MMA : TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
+        push(v, wide ? KERNEL_ATTN_SPLIT_MMA : (uint32_t)TG_KERNEL_ATTENTION_SPLIT, base, "attention_split",
              {{d.q.ptr(), R * d.attn() * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}});
-        push(v, wide ? KERNEL_ATTN_COMBINE_WIDE : TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
+        push(v, wide ? KERNEL_ATTN_COMBINE_WIDE : (uint32_t)TG_KERNEL_ATTENTION_COMBINE, base, "attention_combine",
              {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
               {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.att.ptr(), R * d.attn() * F}});
         tg_params po = base;
         po.n = (uint32_t)H;
         po.k = (uint32_t)d.attn();
-        push(v, d.tensor ? KERNEL_DTC_RESIDUAL : TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
+        push(v, d.tensor ? KERNEL_DTC_RESIDUAL : (uint32_t)TG_KERNEL_GEMV_RESIDUAL, po, "o_proj",
              {{d.att.ptr(), R * d.attn() * F}, {d.w(o.o), H * d.attn() * T}, {in, R * H * F}, {d.mid.ptr(), R * H * F}});
-        push(v, d.tensor ? KERNEL_DTC_GATE_UP : TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
+        push(v, d.tensor ? KERNEL_DTC_GATE_UP : (uint32_t)TG_KERNEL_GEMV_GATE_UP, base, "gate_up",
              {{d.mid.ptr(), R * H * F}, {d.w(o.post_norm), H * F}, {d.w(o.gate_up), 2 * I * H * T},
               {d.mlp.ptr(), R * I * F}});
         tg_params pd = base;
         pd.n = (uint32_t)H;
         pd.k = (uint32_t)I;
         const bool tc_down = d.tensor && dtc_residual_supported(d.params(d.rows), (int)I);
-        push(v, tc_down ? KERNEL_DTC_RESIDUAL : TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
+        push(v, tc_down ? KERNEL_DTC_RESIDUAL : (uint32_t)TG_KERNEL_GEMV_RESIDUAL, pd, "down_proj",
              {{d.mlp.ptr(), R * I * F}, {d.w(o.down), H * I * T}, {d.mid.ptr(), R * H * F}, {d.h.ptr(), R * H * F}});
     }
     push(v, TG_KERNEL_RMSNORM, base, "final_norm",
