@@ -20,7 +20,7 @@ OBJ = PKG / "build"
 LIB = PKG / "lib" / "libtgcuda.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3", "--expt-relaxed-constexpr",
+FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-O3,-Wall,-Wextra", "--expt-relaxed-constexpr",
          "-I", str(ROOT / "include"), "-I", str(CSRC)]
 
 
@@ -46,7 +46,7 @@ def _compile(src: Path, newest_header: float, verbose: bool) -> Path:
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"nvcc failed on {src.name}:\n{res.stdout}\n{res.stderr}")
-    if verbose and res.stderr:
+    if res.stderr and (verbose or "warning" in res.stderr):
         print(res.stderr)
     return obj
 
