@@ -5,6 +5,7 @@ machine without a GPU instead of timing anything on the CPU."""
 
 import json
 import os
+import socket
 import subprocess
 import sys
 from pathlib import Path
@@ -22,6 +23,12 @@ def _env():
     env.pop("WORLD_SIZE", None)
     env["MASTER_ADDR"] = "127.0.0.1"
     return env
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
 
 
 def _json_lines(text):
@@ -54,7 +61,7 @@ def test_the_reference_arm_prints_one_line():
 
 def test_the_reference_arm_under_torchrun_prints_from_rank_0_only():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
-           "--master-addr", "127.0.0.1", "--master-port", "29613", "bench.py", "--impl", "reference",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), "bench.py", "--impl", "reference",
            "--gpus", "2", "--steps", "3", "--warmup", "3"]
     res = subprocess.run(cmd, cwd=ROOT, env=_env(), capture_output=True, text=True, timeout=900)
     assert res.returncode == 0, res.stderr[-2000:]
