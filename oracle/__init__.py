@@ -5,7 +5,10 @@ tgtts-v4_b200 package) never imports, links or calls anything here.
 `OracleStack` holds one stack's f32 weights and KV caches and runs the C restatement
 (minicpm4_ref.c) of tgtts-v4's decode step (crates/graph/src/decode.rs:618-735) and prefill
 (crates/graph/src/prefill.rs:318-411). `ref_numpy` is an independent numpy restatement used to
-cross-check it.
+cross-check it. Pinned against the reference's known answers (the testkit rms_layernorm golden,
+the RoPE table answers, zero weights giving zero, the sequential-K GEMM); whole-stack parity
+against the reference itself is unpinned (its backbone goldens need the external VoxCPM2
+checkpoint, and it cannot run here).
 """
 
 from __future__ import annotations

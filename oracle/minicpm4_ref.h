@@ -22,6 +22,14 @@
  *
  * Every sum is taken in a fixed order that does not depend on the thread count, so results are
  * bit-identical for any `threads`.
+ *
+ * Pinned against the reference's own known answers (tests/test_oracle.py): the rms_layernorm
+ * golden of crates/testkit/tests/fixtures/testkit.safetensors, the RoPE table answers of
+ * decode.rs:1232-1242, zero weights giving zero (tests/prefill.rs:303-319) and the sequential-K
+ * GEMM definition (kernels/gpu/cpu_oracle.py:276-286). Parity of whole stacks against the
+ * reference is unpinned: tgtts-v4 keeps no backbone goldens in its tree (they need the external
+ * VoxCPM2 checkpoint) and cannot run here (Rust, Vulkan); an independent numpy restatement
+ * (ref_numpy.py) cross-checks this one instead.
  */
 #ifndef TGTTS_ORACLE_MINICPM4_REF_H
 #define TGTTS_ORACLE_MINICPM4_REF_H
