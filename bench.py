@@ -144,6 +144,12 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def kv_bytes(shape, position, bytes_per_value=2):
+    """The keys and values a decode step at `position` reads over every layer: positions
+    0 .. position exactly (the algorithmic bytes; past a row's position the kernels read nothing)."""
+    return shape.layers * 2 * shape.kv_heads * (position + 1) * shape.head_dim * bytes_per_value
+
+
 def peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -228,7 +234,7 @@ def run_ours(args, rank, world, local):
     if rank == 0:
         hbm, tc, peak_kind = peaks()
         roof = gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind)
-        step_bytes = shape.weight_bytes(2) + shape.cache_bytes(PREFILL + 15, 2)
+        step_bytes = shape.weight_bytes(2) + kv_bytes(shape, PREFILL + 15)
         extras["step_hbm"] = {"bytes": step_bytes, "ms": round(ms_per_step, 4),
                               "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
                               "frac": round(step_bytes / (ms_per_step * 1e6) / hbm, 4)}
@@ -664,7 +670,7 @@ def run_sweep(args, rank, world, local):
         e1.record(stream)
         e1.synchronize()
         ms = e0.elapsed_time(e1) / args.steps
-        kv = sum(shape.cache_bytes(int(p), 2) for p in pos)
+        kv = sum(kv_bytes(shape, int(p)) for p in pos)
         out[str(rows)] = {"ms": round(ms, 4), "tokens_per_s": round(rows / ms * 1e3, 1),
                           "projections": "tcgen05" if dec.tensor else "gemv",
                           "hbm_gbs": round((shape.weight_bytes(2) + kv) / (ms * 1e6), 1)}

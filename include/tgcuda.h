@@ -266,7 +266,9 @@ typedef struct {
     const double *rope_factors;
 } tg_shape;
 
-/* Shape::weight_bytes / cache_bytes (decode.rs:127-141) at `bytes_per_weight` (2 for f16/bf16). */
+/* Shape::weight_bytes / cache_bytes (decode.rs:127-141) at `bytes_per_weight` (2 for f16/bf16).
+ * cache_bytes counts positions 0 .. position in whole chunks of 32, at most the capacity, as the
+ * reference does; the kernels here read position + 1 of them. */
 uint64_t tg_shape_weight_bytes(const tg_shape *s, uint32_t bytes_per_weight);
 uint64_t tg_shape_cache_bytes(const tg_shape *s, uint32_t position, uint32_t bytes_per_value);
 /* Shape::rope_tables (decode.rs:143-168): [capacity][head_dim/2] each, computed in f32. */

@@ -47,8 +47,14 @@ def test_weight_bytes_of_the_base_lm(pkg):
     # The 0.5B-shaped backbone: 24 x 14,942,208 projection weights plus gains, in bf16.
     s5 = pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=24, capacity=2048)
     assert s5.weight_bytes(2) == 2 * (24 * (14_942_208 + 2 * 1024) + 1024)
-    # Keys and values read at position p: 2 x kv x hd x 2 bytes x (p + 1) per layer.
-    assert s5.cache_bytes(639, 2) == 24 * 2 * 2 * 64 * 2 * 640
+    # Keys and values read at position p (decode.rs:137-141): 2 x kv x hd x 2 bytes per position
+    # and layer, over positions 0 .. p in whole chunks of 32, at most the capacity.
+    per = 24 * 2 * 2 * 64 * 2
+    assert s5.cache_bytes(639, 2) == per * 640
+    assert s5.cache_bytes(512, 2) == per * 544
+    assert s5.cache_bytes(2047, 2) == per * 2048
+    assert pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=24,
+                     capacity=160).cache_bytes(150, 2) == per * 160
 
 
 def test_placement_words_and_refusals(pkg):

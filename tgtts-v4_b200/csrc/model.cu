@@ -26,7 +26,10 @@ extern "C" uint64_t tg_shape_weight_bytes(const tg_shape *s, uint32_t bytes_per_
 
 extern "C" uint64_t tg_shape_cache_bytes(const tg_shape *s, uint32_t position, uint32_t bytes_per_value) {
     if (!s) return 0;
-    const uint64_t read = std::min<uint64_t>((uint64_t)position + 1, s->capacity);
+    // decode.rs:137-141: positions 0 .. position in whole CHUNKs of 32, as the reference's kernels
+    // read them, at most the capacity.
+    const uint64_t chunked = ((uint64_t)position + CAPACITY_STEP) / CAPACITY_STEP * CAPACITY_STEP;
+    const uint64_t read = std::min<uint64_t>(chunked, s->capacity);
     return (uint64_t)s->layers * 2 * s->kv_heads * read * s->head_dim * bytes_per_value;
 }
 
