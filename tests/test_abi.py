@@ -175,3 +175,19 @@ def test_the_docs_name_only_entry_points_the_header_declares():
                          and not (ROOT / "tgtts-v4_b200" / "csrc" / f"{n}.cuh").exists()
                          and not (ROOT / "tgtts-v4_b200" / "csrc" / f"{n}.h").exists())
         assert not unknown, (doc, unknown)
+
+
+def test_the_per_step_calls_marshal_their_arrays_without_a_gpu(pkg, syn):
+    """Decoder.step_rows, step_rows_n, set_rows and output pass their arrays as addresses: with no
+    decoder behind them the library refuses the call (InvalidError) before it reads any of them,
+    which shows the arguments reach it as the header declares them."""
+    dec = object.__new__(pkg.Decoder)
+    dec.handle = None
+    dec.batch = pkg.Batch(2, 2)
+    dec.shape = syn.shape_of(syn.TINY, capacity=64)
+    x = np.zeros((2, dec.shape.hidden), np.float32)
+    rows = [pkg.Row(3, 0), None]
+    for call in (lambda: dec.step_rows(rows, x), lambda: dec.step_rows_n(rows[:1], x[:1]),
+                 lambda: dec.set_rows(rows, x), lambda: dec.output()):
+        with pytest.raises(pkg.InvalidError, match="null"):
+            call()
