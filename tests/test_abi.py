@@ -164,19 +164,6 @@ def test_the_ctypes_structs_match_the_c_header(pkg, tmp_path):
             assert got[(cname, field)] == getattr(py, field).offset, (cname, field)
 
 
-def test_the_docs_name_only_entry_points_the_header_declares():
-    """INTEGRATION.md and DESIGN.md name C entry points a binding would call: each must be one the
-    header declares (prefixes such as `tg_decoder_*` and source file stems aside)."""
-    header = HEADER.read_text()
-    declared = set(re.findall(r"\b(tg_[a-z0-9_]+)\b", header))
-    for doc in ("INTEGRATION.md", "DESIGN.md"):
-        named = set(re.findall(r"\b(tg_[a-z0-9_]+)\b", (ROOT / doc).read_text()))
-        unknown = sorted(n for n in named if not n.endswith("_") and n not in declared
-                         and not (ROOT / "tgtts-v4_b200" / "csrc" / f"{n}.cuh").exists()
-                         and not (ROOT / "tgtts-v4_b200" / "csrc" / f"{n}.h").exists())
-        assert not unknown, (doc, unknown)
-
-
 def test_the_per_step_calls_marshal_their_arrays_without_a_gpu(pkg, syn):
     """Decoder.step_rows, step_rows_n, set_rows and output pass their arrays as addresses: with no
     decoder behind them the library refuses the call (InvalidError) before it reads any of them,

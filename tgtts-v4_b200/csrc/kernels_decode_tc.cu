@@ -48,7 +48,7 @@ struct DtcArgs {
     int K, Kc, S;         // input width, one block's slice of it, blocks in a cluster
     int G, Npg, groups;   // batch rows per MMA group, the MMA's N per group, groups
     uint32_t tmem_cols;   // a power of two >= 32
-    int cc;               // accumulator columns staged per reduction round (a multiple of 16)
+    int cc;               // accumulator columns staged per reduction pass (a multiple of 16)
     uint32_t a_bytes;     // W's slice: k-blocks x tiles x 16 KiB
     const float *res;     // residual: out[b][n] = res[b][n] + s y
     float *out;           // residual [rows][n]; gate/up [rows][inner]
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
     mbar_wait(smem_u32(&bar_mma), (a.groups - 1) & 1, a.err, &gave_up);
     tc_fence_after();
 
-    // 5. Rounds of `cc` accumulator columns. Block r owns units [r per, (r + 1) per) of the tile
+    // 5. Passes of `cc` accumulator columns. Block r owns units [r per, (r + 1) per) of the tile
     // (rows for the residual, gate/up columns, RoPE pairs for q/k/v): every block adds each hi/lo
     // pair of the accumulator rows it holds and pushes the sums into the owner's receive buffer,
     // [from block][owned row][batch row], with stores into distributed shared memory; after a
@@ -263,11 +263,11 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
         }
     }
     const uint32_t lanes = tmem + ((uint32_t)(q * 32) << 16);
-    constexpr int PF = 8;  // epilogue items a thread takes per round (the plan keeps it so)
+    constexpr int PF = 8;  // epilogue items a thread takes per pass (the plan keeps it so)
     for (int c0 = 0; c0 < Ntot; c0 += a.cc) {
         const int cw = min(a.cc, Ntot - c0);
-        const int nbr = cw / 2;  // batch rows of this round
-        cluster.sync();  // every block's MMAs (first round) or reduction (later rounds) is done
+        const int nbr = cw / 2;  // batch rows of this pass
+        cluster.sync();  // every block's MMAs (first pass) or reduction (later passes) is done
         if (norm && c0 == 0) {
             for (int b = tid; b < R; b += DTC_THREADS) {
                 float part[DTC_MAX_S];
@@ -302,7 +302,7 @@ __global__ void __launch_bounds__(DTC_THREADS, 1)
                 }
             }
         }
-        // This thread's epilogue items of the round: their global inputs, before the barrier.
+        // This thread's epilogue items of the pass: their global inputs, before the barrier.
         const int items = per * nbr;
         float pre_a[PF], pre_b[PF];
 #pragma unroll
@@ -430,7 +430,7 @@ bool plan(int K, int NT, int S, int rows, bool norm, DtcPlan &pl) {
     const uint32_t b_bytes = (uint32_t)pl.Npg * pl.Kc * 2;
     uint32_t smem = pl.a_bytes + b_bytes;
     // Receive buffer: NT x 128 rows x (cc / 2 + 4) f32, as wide as the cap allows, up to every
-    // column, and narrow enough that a thread takes at most 8 epilogue items a round.
+    // column, and narrow enough that a thread takes at most 8 epilogue items a pass.
     const int per = (NT == 1 && !norm ? 128 : NT == 2 ? 128 : 64) / S;
     int cc = ntot;
     while (cc > 16 && ((uint32_t)(NT * 128 * (cc / 2 + 4) * 4) > DTC_SMEM_CAP || per * (cc / 2) > 8 * DTC_THREADS))
