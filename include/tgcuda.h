@@ -74,6 +74,13 @@ int tg_ctx_info(tg_ctx *ctx, char *name, size_t name_bytes, int *sm_count);
 /* The context's CUDA stream (a cudaStream_t), on which every program of the context runs: callers
  * time them with events recorded on it. */
 void *tg_ctx_stream(tg_ctx *ctx);
+/* Checks the kernels' failure detection (Submission::wait's bound, crates/vulkan/src/context.rs:
+ * 119-136, carried into the device): runs a kernel whose two waits - on an mbarrier no thread
+ * arrives on, and on a global word nothing writes - can never be met, each bounded by
+ * `limit_ns` (1 us to 2 s) as every wait in the library's kernels is. Both give up, the kernel
+ * returns, and this call returns what the context's next wait reports: TG_EKERNEL ("a bounded
+ * wait gave up"). The context stays usable afterwards. */
+int tg_ctx_selftest_wait(tg_ctx *ctx, uint64_t limit_ns);
 
 /* ---- Memory (Context::memory_in / buffer_in, crates/vulkan/src/context.rs:487-495) -------- */
 
@@ -496,8 +503,9 @@ uint64_t tg_encoder_weight_bytes(const tg_encoder *e);
  * partial sums kept in a fixed array inside the library, TG_NOALLOC_SCRATCH_BYTES per device,
  * instead of a buffer the caller passes. It allocates nothing. The caller passes q (f32
  * [rows][heads][hd]), the caches (storage type), the placement words and out (f32
- * [rows][heads hd]), all device pointers, and a cudaStream_t (NULL: the legacy stream); the work
- * is enqueued there and not waited for. Refuses (TG_ESHAPE) a shape whose partials,
+ * [rows][heads hd]), all device pointers, and a cudaStream_t of the current device (NULL: the
+ * legacy stream; a stream of another device is refused with TG_EINVAL); the work is enqueued
+ * there and not waited for. Refuses (TG_ESHAPE) a shape with no heads or whose partials,
  * rows x heads x ceil(capacity/64) x (head_dim + 2) f32, do not fit. The first call on a device looks the
  * array up for that device (and may load the library's module there): make it before any stream
  * capture. All calls on a device share the array, so calls that overlap on the GPU race. */

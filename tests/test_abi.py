@@ -178,3 +178,17 @@ def test_the_per_step_calls_marshal_their_arrays_without_a_gpu(pkg, syn):
                  lambda: dec.set_rows(rows, x), lambda: dec.output()):
         with pytest.raises(pkg.InvalidError, match="null"):
             call()
+
+
+def test_the_no_alloc_attention_refuses_bad_shapes_before_touching_a_device(pkg):
+    """tg_attention_decode_noalloc checks its shape before any CUDA call, so on a machine without a
+    GPU a shape it cannot run comes back as TG_ESHAPE (no heads, heads not a multiple of the KV
+    heads, an unsupported head width) and never reaches a device. The pointers are 16-byte
+    aligned stand-ins that nothing dereferences."""
+    shape = pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=1, capacity=256)
+    fake = 0x10000
+    for field, value in (("heads", 0), ("heads", 15), ("head_dim", 96), ("rows", 0), ("kv_heads", 0)):
+        p = pkg.params(shape, "bf16", rows=4, slots=4)
+        setattr(p, field, value)
+        with pytest.raises(pkg.ShapeError):
+            pkg.attention_decode_noalloc(p, fake, fake, fake, fake, fake, 0)

@@ -1,0 +1,132 @@
+"""BASELINE's configs 2, 3 and 4 against the CPU oracle at their own shapes and lengths, within
+BASELINE's bf16 tolerance (max-abs <= 2e-2 and cosine >= 0.9999 on the final hidden states; the
+same on the KV cache where a prefill fills it):
+
+- config 4: the prefill's tcgen05 attention and projections over 2048 positions (16 key tiles of
+  128, the online softmax rescaled across all of them), one run from position 0 and one that goes
+  on from a 300-position prefix and ends mid-tile (attention_rows.comp:46-126: causal to
+  start + row, keys past the run read as zero);
+- config 2: the 24-layer stack's 512-position prefill, then all 256 decode steps, each fed its own
+  previous output (crates/graph/tests/decode.rs:336-351 holds its stack to a golden over a run);
+- config 3: the tensor-family decoder (tcgen05 projections, mma.sync attention) at 64 rows over
+  contexts drawn uniform 64-2048 (seed 2, the bench's stream), where a row's attention runs over
+  up to 33 chunks of 64 positions that attention_combine joins.
+"""
+
+import numpy as np
+import pytest
+
+import oracle
+from conftest import distance
+
+pytestmark = pytest.mark.gpu
+
+BF16_MAX_ABS, BF16_COS = 2e-2, 0.9999
+
+
+def _within(got, want, what):
+    m, rel, cos = distance(got, want)
+    assert m <= BF16_MAX_ABS and cos >= BF16_COS, f"{what}: max |d| {m:.3e}, rel {rel:.3e}, cosine {cos:.7f}"
+    return m, cos
+
+
+def test_config4_prefill_over_2048_positions_matches_the_oracle(pkg, ctx, syn):
+    cfg = syn.S05B
+    layers, cap = 2, 2560
+    shape = syn.shape_of(cfg, capacity=cap, layers=layers)
+    w = syn.make_weights(cfg, seed=0, layers=layers, jitter_gains=True, as_bits=True)
+    dec = pkg.Decoder(ctx, shape, rows=2, slots=2, dtype="bf16")
+    dec.load(w)
+    pre = pkg.Prefill(dec, max_rows=4096)
+    ref = oracle.OracleStack(shape, syn.as_f32(w), slots=2)
+    # Slot 1 first holds a 300-position prefix; its run then covers positions 300 .. 1999, so its
+    # last row sits 80 rows into a 128-row tile and its last key tile reaches past the run.
+    prefix = syn.make_inputs(300, cfg.hidden, seed=11, bf16=True)
+    _within(pre.run(0, prefix, slot=1), ref.prefill(0, prefix, slot=1), "prefix")
+    a = syn.make_inputs(2048, cfg.hidden, seed=12, bf16=True)
+    b = syn.make_inputs(1700, cfg.hidden, seed=13, bf16=True)
+    got = pre.run_batch([(0, 2048, 0), (300, 1700, 1)], np.concatenate([a, b]))
+    want_a = ref.prefill(0, a, slot=0)
+    want_b = ref.prefill(300, b, slot=1)
+    _within(got[:2048], want_a, "run from 0, 2048 positions")
+    _within(got[2048:], want_b, "run from 300 to 1999")
+    # Rows at the ends of the run, where the causal mask and the last tiles are, on their own.
+    for r in (0, 127, 128, 1023, 2047):
+        _within(got[r], want_a[r], f"row {r}")
+    for r in (0, 1699):
+        _within(got[2048 + r], want_b[r], f"row {300 + r} of slot 1")
+    for layer in range(layers):
+        for slot, n in ((0, 2048), (1, 2000)):
+            for kind, cache in (("k", ref.k_cache), ("v", ref.v_cache)):
+                g = dec.read_cache(layer, slot, kind, 0, n)
+                _within(g, cache[layer][slot, :, :n], f"layer {layer} slot {slot} {kind} cache")
+    pre.close()
+    dec.close()
+
+
+def test_config2_prefill_512_then_256_fed_back_decode_steps(pkg, ctx, syn):
+    cfg = syn.S05B
+    shape = syn.shape_of(cfg, capacity=1024)
+    w = syn.make_weights(cfg, seed=0, as_bits=True)
+    dec = pkg.Decoder(ctx, shape, rows=1, dtype="bf16")
+    dec.load(w)
+    pre = pkg.Prefill(dec, max_rows=512)
+    ref = oracle.OracleStack(shape, syn.as_f32(w))
+    x = syn.make_inputs(512, cfg.hidden, seed=1, bf16=True)
+    got, want = pre.run(0, x), ref.prefill(0, x)
+    _within(got, want, "prefill")
+    h, hr = got[-1], want[-1]
+    worst = (0.0, 1.0, -1)
+    for t in range(256):
+        h = dec.step(512 + t, h)[0]
+        hr = ref.decode_step([(512 + t, 0)], hr[None])[0]
+        m, cos = _within(h, hr, f"decode step {t} (position {512 + t})")
+        if m > worst[0]:
+            worst = (m, cos, t)
+    print(f"config 2, 256 fed-back steps: worst max |d| {worst[0]:.3e} (cosine {worst[1]:.7f}) at step {worst[2]}")
+    pre.close()
+    dec.close()
+
+
+def test_config3_tensor_decoder_at_64_rows_over_contexts_to_2048(pkg, ctx, syn):
+    from tgtts_v4_b200 import serving
+
+    cfg = syn.S05B
+    layers, rows, steps = 4, 64, 3
+    shape = syn.shape_of(cfg, capacity=2080, layers=layers)
+    w = syn.make_weights(cfg, seed=0, layers=layers, jitter_gains=True, as_bits=True)
+    dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
+    assert dec.tensor
+    dec.load(w)
+    pre = pkg.Prefill(dec, max_rows=8192)
+    stream = serving.ContinuousStream(cfg.hidden, slots=rows, seed=2)
+    reqs = stream.initial()
+    lens = [r.len for r in reqs]
+    assert min(lens) >= 64 and max(lens) <= 2048
+    # The prompts in batches of runs, each run starting on a 128-row boundary of the batch.
+    runs, xs, used = [], [], 0
+    for s, r in enumerate(reqs):
+        n = r.len
+        if used + (n + 127) // 128 * 128 > 8192:
+            pre.run_batch(runs, np.concatenate(xs))
+            runs, xs, used = [], [], 0
+        runs.append((0, n, s))
+        xs.append(stream.pool.prompt(r))
+        used += (n + 127) // 128 * 128
+    pre.run_batch(runs, np.concatenate(xs))
+    order = np.argsort(lens)
+    check = [int(order[-1]), int(order[len(order) // 2]), int(order[0])]  # longest, middle, shortest
+    ref = oracle.OracleStack(shape, syn.as_f32(w), slots=len(check))
+    for j, s in enumerate(check):
+        ref.prefill(0, stream.pool.prompt(reqs[s]), slot=j)
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((rows, cfg.hidden), dtype=np.float32)
+    xr = x[check]
+    for t in range(steps):
+        got = dec.step_rows([pkg.Row(lens[s] + t, s) for s in range(rows)], x)
+        want = ref.decode_step([(lens[s] + t, j) for j, s in enumerate(check)], xr)
+        for j, s in enumerate(check):
+            _within(got[s], want[j], f"step {t}, slot {s} at position {lens[s] + t}")
+        x, xr = got, want
+    pre.close()
+    dec.close()

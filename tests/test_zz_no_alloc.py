@@ -85,3 +85,9 @@ def test_no_alloc_attention_refuses_what_its_array_cannot_hold(pkg, ctx):
     with pytest.raises(pkg.ShapeError, match="scratch"):
         pkg.attention_decode_noalloc(p, q.device_ptr, k.device_ptr, v.device_ptr, at.device_ptr,
                                      out.device_ptr, ctx.stream)
+    # No heads at all is a shape it cannot run either, refused before anything is enqueued.
+    p0 = pkg.params(shape, "bf16", rows=rows, slots=rows)
+    p0.heads = 0
+    with pytest.raises(pkg.ShapeError):
+        pkg.attention_decode_noalloc(p0, q.device_ptr, k.device_ptr, v.device_ptr, at.device_ptr,
+                                     out.device_ptr, ctx.stream)

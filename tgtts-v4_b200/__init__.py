@@ -161,6 +161,7 @@ SIGNATURES = {
     "tg_ctx_synchronize": (_I, [_P, _U64]),
     "tg_ctx_info": (_I, [_P, ctypes.c_char_p, _SZ, ctypes.POINTER(_I)]),
     "tg_ctx_stream": (_P, [_P]),
+    "tg_ctx_selftest_wait": (_I, [_P, _U64]),
     "tg_mem_alloc": (_I, [_P, _U64, _I, ctypes.POINTER(_P)]),
     "tg_mem_free": (_I, [_P]),
     "tg_mem_size": (_U64, [_P]),
@@ -463,6 +464,11 @@ class Context:
 
     def synchronize(self, timeout_ns: int = 0) -> None:
         check(self._lib.tg_ctx_synchronize(self.handle, timeout_ns))
+
+    def selftest_wait(self, limit_ns: int) -> None:
+        """Runs the kernels' bounded waits on things that never come (tg_ctx_selftest_wait):
+        raises KernelError once both have given up after `limit_ns`."""
+        check(self._lib.tg_ctx_selftest_wait(self.handle, limit_ns))
 
     def close(self) -> None:
         if self.handle:

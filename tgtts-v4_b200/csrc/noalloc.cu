@@ -16,6 +16,8 @@
 // it before any stream capture. Every call on a device shares the one array and it keeps the last
 // call's contents: calls that overlap on the GPU (on different streams without ordering between
 // them) race on it. Nothing in it needs to start at zero: each call writes every partial it reads.
+// The array used is the current device's, so the stream passed must belong to the current device;
+// a stream of another device is refused.
 #include <mutex>
 
 #include "tg_common.cuh"
@@ -43,7 +45,7 @@ extern "C" int tg_attention_decode_noalloc(const tg_params *p, const float *q, c
         if (reinterpret_cast<uintptr_t>(ptr) % 16)
             return fail(TG_EINVAL, "tg_attention_decode_noalloc: a pointer is not 16-byte aligned");
     if (p->dtype != TG_F32 && p->dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %u", p->dtype);
-    if (p->rows == 0 || p->slots == 0 || p->kv_heads == 0 || p->heads % p->kv_heads ||
+    if (p->rows == 0 || p->slots == 0 || p->heads == 0 || p->kv_heads == 0 || p->heads % p->kv_heads ||
         (p->head_dim != 64 && p->head_dim != 128) || p->capacity == 0 || p->capacity % CAPACITY_STEP)
         return fail(TG_ESHAPE, "tg_attention_decode_noalloc: %u rows, %u heads over %u of %u, a cache of %u",
                     p->rows, p->heads, p->kv_heads, p->head_dim, p->capacity);
@@ -72,6 +74,13 @@ extern "C" int tg_attention_decode_noalloc(const tg_params *p, const float *q, c
     float *po = static_cast<float *>(base);
     float *pml = reinterpret_cast<float *>(static_cast<char *>(base) + o_bytes);
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (s) {
+        int stream_dev = dev;
+        TG_CUDA(cudaStreamGetDevice(s, &stream_dev));
+        if (stream_dev != dev)
+            return fail(TG_EINVAL, "tg_attention_decode_noalloc: the stream belongs to device %d, the current device is %d",
+                        stream_dev, dev);
+    }
     cudaError_t e = launch_attention_split(*p, q, k_cache, v_cache, at, po, pml, s);
     if (e == cudaSuccess) e = launch_attention_combine(*p, at, po, pml, out, s);
     if (e != cudaSuccess) return cuda_fail(e, "tg_attention_decode_noalloc");

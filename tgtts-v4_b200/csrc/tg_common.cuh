@@ -222,6 +222,33 @@ TG_DEVICE bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint32_t *err, u
     return true;
 }
 
+// An acquiring load of a word other blocks (of this grid or another) update.
+TG_DEVICE uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Waits until the word at `flag` is at least `target`, for at most `limit_ns`; gives up early when
+// `abort` (if given) is nonzero. Past the limit it records ERR_WAIT_TIMEOUT in `err`, sets `abort`
+// so that the grid's other waits end too, and returns false. Called by one thread.
+TG_DEVICE bool flag_wait_bounded(const uint32_t *flag, uint32_t target, uint32_t *err, uint64_t limit_ns,
+                                 uint32_t *abort = nullptr) {
+    if (ld_acquire_gpu(flag) >= target) return true;
+    const uint64_t t0 = globaltimer();
+    for (uint32_t i = 0;; i++) {
+        if (ld_acquire_gpu(flag) >= target) return true;
+        if ((i & 7) == 0) {
+            if (abort && *(volatile uint32_t *)abort) return false;
+            if (globaltimer() - t0 > limit_ns) {
+                if (err) atomicExch(err, ERR_WAIT_TIMEOUT);
+                if (abort) atomicExch(abort, 1u);
+                return false;
+            }
+        }
+    }
+}
+
 // A 1-D bulk copy of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global to
 // this block's shared memory, completing on mbarrier `bar` (no multicast).
 TG_DEVICE void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
