@@ -6,8 +6,8 @@ same on the KV cache where a prefill fills it):
   128, the online softmax rescaled across all of them), one run from position 0 and one that goes
   on from a 300-position prefix and ends mid-tile (attention_rows.comp:46-126: causal to
   start + row, keys past the run read as zero);
-- config 2: the 24-layer stack's 512-position prefill, then all 256 decode steps, each fed its own
-  previous output (crates/graph/tests/decode.rs:336-351 holds its stack to a golden over a run);
+- config 2: the 24-layer stack's 512-position prefill, then all 256 decode steps over the cache
+  they build (crates/graph/tests/decode.rs:336-351 holds its stack to a golden over a run);
 - config 3: the tensor-family decoder (tcgen05 projections, mma.sync attention) at 64 rows over
   contexts drawn uniform 64-2048 (seed 2, the bench's stream), where a row's attention runs over
   up to 33 chunks of 64 positions that attention_combine joins.
@@ -64,7 +64,14 @@ def test_config4_prefill_over_2048_positions_matches_the_oracle(pkg, ctx, syn):
     dec.close()
 
 
-def test_config2_prefill_512_then_256_fed_back_decode_steps(pkg, ctx, syn):
+def test_config2_prefill_512_then_256_decode_steps(pkg, ctx, syn):
+    """All 256 steps after the 512-position prefill, each input the next row of the seed-1 N(0,1)
+    stream (the prompt's continuation), so that each step's KV append and attention over a cache
+    that keeps growing - every earlier step's keys and values as each side computed them - is held
+    to the tolerance on its own. Feeding each step its own output instead is chaotic in this
+    random-init stack: a perturbation of the KV cache as small as f16 rounding in the oracle itself
+    grows past the tolerance within about 40 steps (tests/test_oracle.py), so a fed-back run is held
+    to it only over its first steps (tests/test_prefill_gpu.py)."""
     cfg = syn.S05B
     shape = syn.shape_of(cfg, capacity=1024)
     w = syn.make_weights(cfg, seed=0, as_bits=True)
@@ -72,18 +79,22 @@ def test_config2_prefill_512_then_256_fed_back_decode_steps(pkg, ctx, syn):
     dec.load(w)
     pre = pkg.Prefill(dec, max_rows=512)
     ref = oracle.OracleStack(shape, syn.as_f32(w))
-    x = syn.make_inputs(512, cfg.hidden, seed=1, bf16=True)
+    stream = syn.make_inputs(512 + 256, cfg.hidden, seed=1, bf16=True)
+    x, steps = stream[:512], stream[512:]
     got, want = pre.run(0, x), ref.prefill(0, x)
     _within(got, want, "prefill")
-    h, hr = got[-1], want[-1]
     worst = (0.0, 1.0, -1)
     for t in range(256):
-        h = dec.step(512 + t, h)[0]
-        hr = ref.decode_step([(512 + t, 0)], hr[None])[0]
+        h = dec.step(512 + t, steps[t])[0]
+        hr = ref.decode_step([(512 + t, 0)], steps[t][None])[0]
         m, cos = _within(h, hr, f"decode step {t} (position {512 + t})")
         if m > worst[0]:
             worst = (m, cos, t)
-    print(f"config 2, 256 fed-back steps: worst max |d| {worst[0]:.3e} (cosine {worst[1]:.7f}) at step {worst[2]}")
+    # The cache the 256 steps appended, against the oracle's.
+    for layer in (0, 23):
+        for kind, cache in (("k", ref.k_cache), ("v", ref.v_cache)):
+            _within(dec.read_cache(layer, 0, kind, 512, 256), cache[layer][0, :, 512:768], f"layer {layer} {kind}")
+    print(f"config 2, 256 steps: worst max |d| {worst[0]:.3e} (cosine {worst[1]:.7f}) at step {worst[2]}")
     pre.close()
     dec.close()
 

@@ -93,8 +93,10 @@ def test_config2_full_stack_prefill_512_and_decode(pkg, ctx, syn):
     got, want = pre.run(0, x), ref.prefill(0, x)
     m, _, cos = distance(got, want)
     assert m <= 2e-2 and cos >= 0.9999, (m, cos)
+    # Each step fed its own output, as config 1 runs: the stack amplifies any difference over the
+    # steps (tests/test_oracle.py), so this holds over the first eight.
     h, hr = got[-1], want[-1]
-    for t in range(4):
+    for t in range(8):
         h = dec.step(512 + t, h)[0]
         hr = ref.decode_step([(512 + t, 0)], hr[None])[0]
         m, _, cos = distance(h, hr)

@@ -300,19 +300,82 @@ __global__ void __launch_bounds__(128)
 // of the group.
 //
 // `tid` and `nthreads` are the calling threads' index and count (a block, or the consumer warps
-// of one), and Sync::sync() their barrier. Loads of q and the cache bypass L1 (a persistent kernel
-// reads what other blocks wrote earlier in the same launch).
+// of one), and Sync::sync() their barrier. `wait()` is what the calling threads wait on before
+// reading what the step wrote (q and the position's own key and value): the kernel before, or in
+// the persistent step the phase counter of q/k/v. Loads of q and the cache bypass L1 (a persistent
+// kernel reads what other blocks wrote earlier in the same launch).
 struct BlockSync {
     static TG_DEVICE void sync() { __syncthreads(); }
 };
+struct PdlWait {
+    TG_DEVICE void operator()() const { pdl_wait(); }
+};
 
-//
-// With ONE_PASS (no kernel before it to wait on) q and every key and value are loaded in one batch.
-template <typename T, typename Sync = BlockSync, bool ONE_PASS = false>
+// A chunk's scores (attention_split.comp:73-86): thread t takes position t % C for the HPT heads
+// t / C, t / C + nh, ... (nh = threads / C, HPT = group / nh rounded up); each score is one chain
+// of fused multiply-adds in order over the head dimension, scaled, or -inf past the position. The
+// heads' chains run side by side and the head dimension is unrolled, so that shared-memory loads
+// run ahead of the arithmetic.
+template <int HPT, int C>
+TG_DEVICE void chunk_scores(const float *qs, const float4 *ks4, int row4, float *ps, int hd, int group, int start,
+                            int pos, float scale, int tid, int nthreads) {
+    const int nh = nthreads / C, pp = tid % C, h0 = tid / C;
+    const float4 *qr[HPT];
+#pragma unroll
+    for (int u = 0; u < HPT; u++) qr[u] = reinterpret_cast<const float4 *>(qs + min(h0 + u * nh, group - 1) * hd);
+    const float4 *kr = ks4 + pp * row4;
+    float acc[HPT];
+#pragma unroll
+    for (int u = 0; u < HPT; u++) acc[u] = 0.0f;
+#pragma unroll 8
+    for (int d4 = 0; d4 < hd / 4; d4++) {
+        const float4 kk = kr[d4];
+#pragma unroll
+        for (int u = 0; u < HPT; u++) {
+            const float4 qq = qr[u][d4];
+            acc[u] = __fmaf_rn(qq.x, kk.x, acc[u]);
+            acc[u] = __fmaf_rn(qq.y, kk.y, acc[u]);
+            acc[u] = __fmaf_rn(qq.z, kk.z, acc[u]);
+            acc[u] = __fmaf_rn(qq.w, kk.w, acc[u]);
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < HPT; u++) {
+        const int h = h0 + u * nh;
+        if (h < group) ps[h * C + pp] = (start + pp <= pos) ? acc[u] * scale : -INFINITY;
+    }
+}
+
+// A chunk's unnormalised outputs (attention_split.comp:95-108): thread t takes dimension t % hd for
+// the HPT heads t / hd, t / hd + nh, ...; each output one chain in order over the positions.
+template <int HPT, int C>
+TG_DEVICE void chunk_outputs(const float *vs, const float *ps, int hd, int group, float *o_out, size_t o_stride,
+                             int tid, int nthreads) {
+    const int nh = nthreads / hd, d = tid % hd, h0 = tid / hd;
+    const float *pr[HPT];
+#pragma unroll
+    for (int u = 0; u < HPT; u++) pr[u] = ps + min(h0 + u * nh, group - 1) * C;
+    float acc[HPT];
+#pragma unroll
+    for (int u = 0; u < HPT; u++) acc[u] = 0.0f;
+#pragma unroll 16
+    for (int pp = 0; pp < C; pp++) {
+        const float v = vs[pp * hd + d];
+#pragma unroll
+        for (int u = 0; u < HPT; u++) acc[u] = __fmaf_rn(pr[u][pp], v, acc[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < HPT; u++) {
+        const int h = h0 + u * nh;
+        if (h < group) o_out[h * o_stride + d] = acc[u];
+    }
+}
+
+template <typename T, typename Sync = BlockSync, typename Wait = PdlWait>
 __device__ void attention_chunk(const tg_params &p, const float *__restrict__ q, const T *__restrict__ kc,
                                 const T *__restrict__ vc, int b, int kv, int c, uint32_t pos, uint32_t slot,
                                 float *__restrict__ o_out, size_t o_stride, float *__restrict__ ml_out,
-                                size_t ml_stride, float *smem, int tid, int nthreads) {
+                                size_t ml_stride, float *smem, int tid, int nthreads, const Wait &wait = Wait()) {
     constexpr int C = ATTN_CHUNK;
     using VT = Vec<T>;
     using Raw = typename VT::Raw;
@@ -329,16 +392,12 @@ __device__ void attention_chunk(const tg_params &p, const float *__restrict__ q,
     const Raw *ksrc = reinterpret_cast<const Raw *>(kc + base);
     const Raw *vsrc = reinterpret_cast<const Raw *>(vc + base);
     const int per_row = hd / V;
-    if (ONE_PASS) {
-        const float4 *src = reinterpret_cast<const float4 *>(q + ((size_t)b * heads + first_head) * hd);
-        for (int i = tid; i < group * hd / 4; i += nthreads) reinterpret_cast<float4 *>(qs)[i] = __ldcg(src + i);
-    }
-    for (int pass = ONE_PASS ? 1 : 0; pass < 2; pass++) {
-        if (pass == 1 && !ONE_PASS) pdl_wait();  // a no-op after the first wait of the block
+    for (int pass = 0; pass < 2; pass++) {
+        if (pass == 1) wait();  // a no-op after the first wait of the block
         for (int i = tid; i < C * per_row; i += nthreads) {
             const int pp = i / per_row, j = i % per_row;
             const int at_pos = start + pp;
-            if (!ONE_PASS && (pass == 0) != (at_pos < (int)pos)) continue;
+            if ((pass == 0) != (at_pos < (int)pos)) continue;
             float kf[V], vf[V];
             if (at_pos <= (int)pos) {
                 VT::unpack(__ldcg(ksrc + i), kf);
@@ -355,34 +414,17 @@ __device__ void attention_chunk(const tg_params &p, const float *__restrict__ q,
             }
         }
     }
-    if (!ONE_PASS) {
+    {
         const float4 *src = reinterpret_cast<const float4 *>(q + ((size_t)b * heads + first_head) * hd);
         for (int i = tid; i < group * hd / 4; i += nthreads) reinterpret_cast<float4 *>(qs)[i] = __ldcg(src + i);
     }
     Sync::sync();
     const float scale = 1.0f / sqrtf((float)hd);
-    // Scores: thread t takes position t % C for heads t / C, t / C + nh, ... (nh = threads / C).
-    {
-        const int nh = nthreads / C, pp = tid % C;
-        for (int h0 = tid / C; h0 < group; h0 += 4 * nh) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            const int hs[4] = {h0, h0 + nh, h0 + 2 * nh, h0 + 3 * nh};
-            for (int d4 = 0; d4 < hd / 4; d4++) {
-                const float4 kk = ks4[pp * row4 + d4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    if (hs[u] >= group) continue;
-                    const float4 qq = reinterpret_cast<const float4 *>(qs + hs[u] * hd)[d4];
-                    acc[u] = __fmaf_rn(qq.x, kk.x, acc[u]);
-                    acc[u] = __fmaf_rn(qq.y, kk.y, acc[u]);
-                    acc[u] = __fmaf_rn(qq.z, kk.z, acc[u]);
-                    acc[u] = __fmaf_rn(qq.w, kk.w, acc[u]);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (hs[u] < group) ps[hs[u] * C + pp] = (start + pp <= (int)pos) ? acc[u] * scale : -INFINITY;
-        }
+    switch ((group + nthreads / C - 1) / (nthreads / C)) {
+        case 1: chunk_scores<1, C>(qs, ks4, row4, ps, hd, group, start, (int)pos, scale, tid, nthreads); break;
+        case 2: chunk_scores<2, C>(qs, ks4, row4, ps, hd, group, start, (int)pos, scale, tid, nthreads); break;
+        case 4: chunk_scores<4, C>(qs, ks4, row4, ps, hd, group, start, (int)pos, scale, tid, nthreads); break;
+        default: chunk_scores<8, C>(qs, ks4, row4, ps, hd, group, start, (int)pos, scale, tid, nthreads); break;
     }
     Sync::sync();
     const int warp = tid >> 5, lane = tid & 31;
@@ -405,22 +447,11 @@ __device__ void attention_chunk(const tg_params &p, const float *__restrict__ q,
         }
     }
     Sync::sync();
-    // Outputs: thread t takes dimension t % hd for heads t / hd, t / hd + nh, ...
-    {
-        const int nh = nthreads / hd, d = tid % hd;
-        for (int h0 = tid / hd; h0 < group; h0 += 4 * nh) {
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            const int hs[4] = {h0, h0 + nh, h0 + 2 * nh, h0 + 3 * nh};
-            for (int pp = 0; pp < C; pp++) {
-                const float v = vs[pp * hd + d];
-#pragma unroll
-                for (int u = 0; u < 4; u++)
-                    if (hs[u] < group) acc[u] = __fmaf_rn(ps[hs[u] * C + pp], v, acc[u]);
-            }
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (hs[u] < group) o_out[hs[u] * o_stride + d] = acc[u];
-        }
+    switch ((group + nthreads / hd - 1) / (nthreads / hd)) {
+        case 1: chunk_outputs<1, C>(vs, ps, hd, group, o_out, o_stride, tid, nthreads); break;
+        case 2: chunk_outputs<2, C>(vs, ps, hd, group, o_out, o_stride, tid, nthreads); break;
+        case 4: chunk_outputs<4, C>(vs, ps, hd, group, o_out, o_stride, tid, nthreads); break;
+        default: chunk_outputs<8, C>(vs, ps, hd, group, o_out, o_stride, tid, nthreads); break;
     }
 }
 
@@ -594,30 +625,43 @@ __global__ void __launch_bounds__(128)
 
 // ---- the persistent decode step ----------------------------------------------------------------
 //
-// One cooperative launch runs the whole step - every layer's q/k/v projection with RoPE and the
-// KV append, attention, the output projection, gate/up, down, and the final norm - with one block
-// per SM. Each block's producer warp streams the block's share of every weight matrix, in the
-// order the phases use them, through a ring of PS_SLOTS shared-memory slots with 1-D bulk copies
-// (TMA, no multicast), so that HBM keeps streaming the next phases' weights while the consumer
-// warps wait at the grid barriers between phases. The consumers take the same sums in the same
-// order as the per-kernel step (dot_smem, warp_rms_scale, attention_chunk, attention_combine's
-// join), so a row's results are the same bits on either path. Every wait is bounded in time: a
-// block that gives up sets the context's error word and a global abort word that ends the others'
-// waits, drains its copies in flight and returns.
+// One cooperative launch runs the whole step, one block per SM, as a dataflow over per-phase
+// arrival counters instead of grid-wide barriers. A layer is five phases: q/k/v (+ RMSNorm, RoPE,
+// KV append), attention over 64-position chunks, the join of the chunks with the output
+// projection (+ residual), gate/up (+ RMSNorm, SiLU-mul), and down (+ residual). Each block takes
+// a fixed share of every phase - a run of the projection's output units, and attention chunks dealt
+// from the last block down, to the blocks that q/k/v leaves idle - and bumps the phase's counter
+// once its share is written. A block with work in a phase first waits until every block has
+// bumped the counter of the phase before; a block without work bumps at once. Every counter is used
+// once per step (the launch zeroes them), so no barrier is reused and no block waits for one that
+// has nothing to give it.
+//
+// The producer warp streams the block's share of every weight matrix, in the order the phases use
+// them, into a byte ring in shared memory with 1-D bulk copies (TMA, no multicast): one copy per run
+// of consecutive weight rows, one to four runs of up to ~112 KB a projection - few large copies,
+// which is what lets each SM's copy engine take its share of HBM. It runs ahead of the consumers by
+// up to the ring, so the next phases' weights land while the consumer warps wait on a handoff.
+//
+// The consumers take the same sums in the same order as the six-kernels-a-layer step (dot_smem,
+// warp_rms_scale, attention_chunk, attention_combine's join, the epilogues), so a row comes out the
+// same bits on either path. Every wait is bounded in time: a block that gives up sets the context's
+// error word and an abort word that ends the other blocks' waits, waits (bounded) for its copies in
+// flight, and returns.
 
 constexpr int PS_CONSUMERS = 8;                 // consumer warps
 constexpr int PS_CTHREADS = PS_CONSUMERS * 32;  // consumer threads
 constexpr int PS_THREADS = PS_CTHREADS + 32;    // and one producer warp
-constexpr int PS_SLOTS = 6;
-constexpr uint32_t PS_SLOT_BYTES = 28 * 1024;
 constexpr int PS_ROWS = 2;                      // the most rows a persistent step takes
+constexpr int PS_NBAR = 16;                     // weight segments a block has in flight at most
+constexpr int PS_NCOUNT = 4;                    // a phase's arrivals, spread over this many words
+constexpr int PS_PHASES = 5;
 constexpr uint64_t PS_WAIT_NS = 2000000000ull;  // 2 s
+
+enum { PH_QKV = 0, PH_ATT = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4 };
 
 struct ConsumerSync {
     static TG_DEVICE void sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 };
-
-enum { PH_QKV = 0, PH_O = 1, PH_GU = 2, PH_DOWN = 3 };
 
 struct PersistArgs {
     tg_params p;
@@ -628,20 +672,102 @@ struct PersistArgs {
     const float *cosv, *sinv;
     const uint32_t *at;
     const float *x_in;
-    float *h, *mid, *mlp, *q, *out, *po, *pml;
+    float *h, *mid, *mlp, *q, *att, *out, *po, *pml;
     unsigned char *kcache, *vcache;
     uint64_t cache_layer;
-    uint32_t *sync;  // [0] grid-barrier arrivals, [1] abort; zero at launch
+    // [layers][PS_PHASES][PS_NCOUNT] arrivals, the abort word, then [layers][PS_ROWS][kv_heads] counts
+    // of the attention chunks written; zero at launch.
+    uint32_t *flags;
     uint32_t *err;
-    int units[4], per[4], seg[4], nseg[4], k[4];
-    int segs_per_layer;
-    uint32_t xs_floats, raw_floats;  // shared-memory layout after the slots
+    uint32_t ring;    // bytes of the weight ring at the start of dynamic shared memory
+    int prefetch;     // at the end, prefetch the block's first-layer weights into L2 for the next step
 };
 
-TG_DEVICE uint32_t ld_acquire(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
+TG_DEVICE uint32_t *abort_word(const PersistArgs &a) { return a.flags + (size_t)a.layers * PS_PHASES * PS_NCOUNT; }
+TG_DEVICE uint32_t *chunks_done(const PersistArgs &a, int l, int b, int kv) {
+    return abort_word(a) + 1 + ((size_t)l * PS_ROWS + b) * a.p.kv_heads + kv;
+}
+
+// The units, row length and rows per unit of weight phase wi (0 q/k/v, 1 o, 2 gate/up, 3 down).
+struct WPhase {
+    int units, k, R;
+};
+TG_DEVICE WPhase wphase(const tg_params &p, int wi) {
+    switch (wi) {
+        case 0: return {(int)((p.heads + 2 * p.kv_heads) * p.head_dim / 2), (int)p.hidden, 2};
+        case 1: return {(int)p.hidden, (int)(p.heads * p.head_dim), 1};
+        case 2: return {(int)p.inner, (int)p.hidden, 2};
+        default: return {(int)p.hidden, (int)p.inner, 1};
+    }
+}
+TG_DEVICE int wrow(const tg_params &p, int wi, int u, int r) {
+    if (wi == 0) return unit_row<EPI_QKV_ROPE>(p, u, r);
+    if (wi == 2) return unit_row<EPI_GATE_UP>(p, u, r);
+    return u;
+}
+// This block's units [ub, ue) of weight phase wi, dealt in runs of ceil(units / blocks) from block
+// 0 up. q/k/v leaves as many blocks at the top of the grid as the step can have attention items (at
+// most half of them), so that the blocks that take attention have no q/k/v to finish first.
+__host__ __device__ inline int phase_blocks(const tg_params &p, int wi, int grid) {
+    if (wi != 0) return grid;
+    const int most = (int)(p.rows * p.kv_heads * attn_chunks(p.capacity));
+    return grid - min(most, grid / 2);
+}
+TG_DEVICE void share(const tg_params &p, int wi, int units, int &ub, int &ue) {
+    const int blocks = phase_blocks(p, wi, gridDim.x);
+    const int per = (units + blocks - 1) / blocks;
+    ub = min(units, (int)blockIdx.x * per);
+    ue = min(units, ub + per);
+}
+// Places a segment of `bytes` at the next linear ring position from `lin` that is a multiple of
+// its row length: returns its linear start and moves lin past it. Producer and consumers place
+// alike. A segment may wrap around the ring's end; the ring is a multiple of every row length, so
+// no row is split by the wrap.
+TG_DEVICE uint32_t ring_place(uint32_t &lin, uint32_t bytes, uint32_t row_bytes) {
+    lin = (lin + row_bytes - 1) / row_bytes * row_bytes;
+    const uint32_t start = lin;
+    lin += bytes;
+    return start;
+}
+
+// A weight segment in the ring: row i (unit j's row r is row r nu + j) starts at linear position
+// start + i row_bytes, taken modulo the ring.
+struct SegRef {
+    const unsigned char *ring;
+    uint32_t start, size, row_bytes;
+    template <typename T>
+    TG_DEVICE const T *row(int i) const {
+        return reinterpret_cast<const T *>(ring + (start + (uint32_t)i * row_bytes) % size);
+    }
+};
+
+// The consumers' arrival at phase ph of layer l: every store of the phase issued (the barrier),
+// then one thread publishes them and bumps one of the phase's counters in one release (the
+// barrier orders the other threads' stores before it, as a grid barrier's fence does).
+TG_DEVICE void arrive(const PersistArgs &a, int l, int ph, int ctid) {
+    ConsumerSync::sync();
+    if (ctid == 0) {
+        uint32_t *c = a.flags + ((size_t)l * PS_PHASES + ph) * PS_NCOUNT + blockIdx.x % PS_NCOUNT;
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
+    }
+}
+
+// Waits until every block has arrived at phase ph of layer l (lanes 0 .. PS_NCOUNT - 1 of the first
+// consumer warp each watch one counter), then lets all consumer threads on. False when a wait gave
+// up or another block aborted.
+TG_DEVICE bool wait_phase(const PersistArgs &a, int l, int ph, int ctid, int *ok_s) {
+    if (ctid < 32) {
+        bool ok = true;
+        if (ctid < PS_NCOUNT) {
+            const uint32_t target = (gridDim.x - ctid + PS_NCOUNT - 1) / PS_NCOUNT;
+            ok = flag_wait_bounded(a.flags + ((size_t)l * PS_PHASES + ph) * PS_NCOUNT + ctid, target, a.err,
+                                   PS_WAIT_NS, abort_word(a));
+        }
+        ok = __all_sync(0xffffffffu, ok);
+        if (ctid == 0) *ok_s = ok;
+    }
+    ConsumerSync::sync();
+    return *ok_s != 0;
 }
 
 // Waits on an mbarrier phase, giving up at the time limit or when another block aborted.
@@ -651,230 +777,334 @@ TG_DEVICE bool mbar_wait_abortable(uint32_t bar, uint32_t parity, const PersistA
     for (uint32_t i = 0;; i++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63) == 0) {
-            if (*(volatile uint32_t *)(a.sync + 1)) return false;
+            if (*(volatile uint32_t *)abort_word(a)) return false;
             if (globaltimer() - t0 > PS_WAIT_NS) {
                 atomicExch(a.err, ERR_WAIT_TIMEOUT);
-                atomicExch(a.sync + 1, 1u);
+                atomicExch(abort_word(a), 1u);
                 return false;
             }
         }
     }
 }
 
-// The grid barrier of the consumer warps: every block adds its arrival (release), then waits
-// until all have (acquire). Returns false when the step was aborted.
-TG_DEVICE bool grid_barrier(const PersistArgs &a, uint32_t &count, int *ok_s) {
+// Rows of x ([rows][k] f32, other blocks' writes) into xs in Stage layout, normed when `norm` with
+// the gain staged in gs (stage_rows' arithmetic: the row's scale by warp_rms_scale's sums, then
+// x s g). Every thread loads its share of x at once (at most PS_STAGE float4s) while warp b takes
+// row b's scale straight from L2, so the staging costs one trip to L2.
+constexpr int PS_STAGE = 8;
+template <typename T, int NB>
+TG_DEVICE void flow_stage(const float *x, const float *gs, bool norm, int rows, int k, float eps, float *xs,
+                          float *scales, int ctid) {
+    const int quads = k / 4, n = NB * quads;
+    float4 v[PS_STAGE];
+#pragma unroll
+    for (int u = 0; u < PS_STAGE; u++) {
+        const int i = ctid + u * PS_CTHREADS, b = i / quads, c = i % quads;
+        v[u] = (i < n && b < rows) ? __ldcg(reinterpret_cast<const float4 *>(x + (size_t)b * k) + c)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    if (norm) {
+        const int warp = ctid >> 5;
+        if (warp < NB) {
+            const float sc = warp < rows ? warp_rms_scale_cg(x + (size_t)warp * k, k, eps) : 0.0f;
+            if ((ctid & 31) == 0) scales[warp] = sc;
+        }
+        ConsumerSync::sync();
+    }
+#pragma unroll
+    for (int u = 0; u < PS_STAGE; u++) {
+        const int i = ctid + u * PS_CTHREADS, b = i / quads, c = i % quads;
+        if (i >= n) continue;
+        float4 o = v[u];
+        if (norm) {
+            const float4 gg = reinterpret_cast<const float4 *>(gs)[c];
+            const float sc = scales[b];
+            o = make_float4(o.x * sc * gg.x, o.y * sc * gg.y, o.z * sc * gg.z, o.w * sc * gg.w);
+        }
+        *reinterpret_cast<float4 *>(xs + Stage<T>::index(k, b, 4 * c)) = o;
+    }
     ConsumerSync::sync();
-    count += gridDim.x;
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        __threadfence();
-        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
-        const uint64_t t0 = globaltimer();
-        for (uint32_t i = 0;; i++) {
-            if (ld_acquire(a.sync) >= count) break;
-            if ((i & 15) == 0) {
-                if (*(volatile uint32_t *)(a.sync + 1)) {
-                    ok = 0;
-                    break;
-                }
-                if (globaltimer() - t0 > PS_WAIT_NS) {
-                    atomicExch(a.err, ERR_WAIT_TIMEOUT);
-                    atomicExch(a.sync + 1, 1u);
-                    ok = 0;
-                    break;
+}
+
+// A gain ([k] f32, a weight: constant) into shared memory, before the wait it is needed after.
+TG_DEVICE void stage_gain(const float *g, int k, float *gs, int ctid) {
+    for (int i = ctid; i < k / 4; i += PS_CTHREADS)
+        reinterpret_cast<float4 *>(gs)[i] = __ldg(reinterpret_cast<const float4 *>(g) + i);
+}
+
+// attention_combine for the GROUP heads of kv head `kv` of row b (attention_combine.comp:29-58),
+// into att [rows][heads hd] f32: thread t takes four dimensions of one head, loads the head's chunk
+// maxima and sums and its four columns of every chunk's partial output in one batch (the first 16
+// chunks; longer caches continue chunk by chunk), and folds them in chunk order as
+// attention_combine_kernel does.
+TG_DEVICE void flow_join(const PersistArgs &a, int b, int kv, int n, int ctid) {
+    constexpr int B = 16;
+    const tg_params &p = a.p;
+    const int hd = p.head_dim, heads = p.heads, q4 = hd / 4, group = heads / p.kv_heads;
+    const int chunks = attn_chunks(p.capacity);
+    for (int i = ctid; i < group * q4; i += PS_CTHREADS) {
+        const int h = kv * group + i / q4, d4 = i % q4;
+        const float2 *ml = reinterpret_cast<const float2 *>(a.pml) + ((size_t)b * heads + h) * chunks;
+        const float4 *o = reinterpret_cast<const float4 *>(a.po) + ((size_t)b * heads + h) * chunks * q4 + d4;
+        float2 mv[B];
+        float4 ov[B];
+#pragma unroll
+        for (int c = 0; c < B; c++) {
+            mv[c] = c < n ? __ldcg(ml + c) : make_float2(-INFINITY, 0.f);
+            ov[c] = c < n ? __ldcg(o + (size_t)c * q4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        float m = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < B; c++)
+            if (c < n) m = fmaxf(m, mv[c].x);
+        for (int c = B; c < n; c++) m = fmaxf(m, __ldcg(ml + c).x);
+        float total = 0.0f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < B; c++) {
+            if (c >= n) continue;
+            const float w = expf(mv[c].x - m);
+            total = __fmaf_rn(mv[c].y, w, total);
+            acc.x = __fmaf_rn(ov[c].x, w, acc.x);
+            acc.y = __fmaf_rn(ov[c].y, w, acc.y);
+            acc.z = __fmaf_rn(ov[c].z, w, acc.z);
+            acc.w = __fmaf_rn(ov[c].w, w, acc.w);
+        }
+        for (int c = B; c < n; c++) {
+            const float2 v = __ldcg(ml + c);
+            const float4 oc = __ldcg(o + (size_t)c * q4);
+            const float w = expf(v.x - m);
+            total = __fmaf_rn(v.y, w, total);
+            acc.x = __fmaf_rn(oc.x, w, acc.x);
+            acc.y = __fmaf_rn(oc.y, w, acc.y);
+            acc.z = __fmaf_rn(oc.z, w, acc.z);
+            acc.w = __fmaf_rn(oc.w, w, acc.w);
+        }
+        reinterpret_cast<float4 *>(a.att + ((size_t)b * heads + h) * hd)[d4] =
+            make_float4(__fdiv_rn(acc.x, total), __fdiv_rn(acc.y, total), __fdiv_rn(acc.z, total),
+                        __fdiv_rn(acc.w, total));
+    }
+}
+
+// One weight segment's dot products and epilogues. Warp w takes units w, w + 8, ..., U of them at
+// once (their rows' sums interleaved, each in dot_smem's order), and lane u NB + b runs the epilogue
+// of the pass's unit u for row b; a residual is loaded before the sums that it waits behind.
+template <typename T, int NB, int EPI, int U>
+TG_DEVICE void flow_dots(const GemvArgs &ga, const SegRef &seg, int ub, int nu, int k, const float *xs, int rows,
+                         int ctid) {
+    constexpr int R = EPI == EPI_RESIDUAL ? 1 : 2;
+    static_assert(U * NB <= 32, "one lane per (unit, row)");
+    const int warp = ctid >> 5, lane = ctid & 31;
+    for (int j0 = warp; j0 < nu; j0 += PS_CONSUMERS * U) {
+        const int eu = lane / NB, eb = lane % NB, ej = j0 + PS_CONSUMERS * eu;
+        const bool mine = eu < U && eb < rows && ej < nu;
+        float res = 0.0f;
+        if constexpr (EPI == EPI_RESIDUAL)
+            if (mine) res = __ldcg(ga.res + (size_t)eb * ga.p.n + ub + ej);
+        const T *w[R * U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int j = min(j0 + PS_CONSUMERS * u, nu - 1);  // past the share: a row whose sums go unused
+#pragma unroll
+            for (int r = 0; r < R; r++) w[u * R + r] = seg.row<T>(r * nu + j);
+        }
+        float acc[NB][R * U];
+        dot_smem<T, NB, R * U>(w, k, xs, acc);
+        float y0 = 0.0f, y1 = 0.0f;
+#pragma unroll
+        for (int b = 0; b < NB; b++)
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const float s0 = warp_sum(acc[b][u * R]);
+                const float s1 = R == 2 ? warp_sum(acc[b][u * R + R - 1]) : s0;
+                if (u == eu && b == eb) {
+                    y0 = s0;
+                    y1 = s1;
                 }
             }
-        }
-        *ok_s = ok;
-    }
-    ConsumerSync::sync();
-    return *ok_s != 0;
-}
-
-TG_DEVICE int phase_rows(int ph) { return (ph == PH_QKV || ph == PH_GU) ? 2 : 1; }
-
-template <typename T>
-TG_DEVICE const T *phase_weights(const PersistArgs &a, int l, int ph) {
-    return reinterpret_cast<const T *>(a.weights + a.offs[l * 6 + ph]);
-}
-
-TG_DEVICE int weight_row(const tg_params &p, int ph, int u, int r) {
-    switch (ph) {
-        case PH_QKV: return unit_row<EPI_QKV_ROPE>(p, u, r);
-        case PH_GU: return unit_row<EPI_GATE_UP>(p, u, r);
-        default: return u;
-    }
-}
-
-// Segment g of the step: its layer, phase and index within the phase.
-TG_DEVICE void segment_of(const PersistArgs &a, int g, int &l, int &ph, int &s) {
-    l = g / a.segs_per_layer;
-    int r = g % a.segs_per_layer;
-    for (ph = 0; ph < 4; ph++) {
-        if (r < a.nseg[ph]) break;
-        r -= a.nseg[ph];
-    }
-    s = r;
-}
-
-// The units [ub, ue) of segment s of phase ph for this block.
-TG_DEVICE void segment_units(const PersistArgs &a, int ph, int s, int &ub, int &ue) {
-    const int b0 = blockIdx.x * a.per[ph];
-    const int b1 = min(b0 + a.per[ph], a.units[ph]);
-    ub = min(b0 + s * a.seg[ph], b1);
-    ue = min(ub + a.seg[ph], b1);
-}
-
-// rows of x ([rows][k] f32, other blocks' writes) into xs in Stage layout, normed with gain g when
-// given: the consumer-warp version of stage_rows.
-template <typename T>
-TG_DEVICE void persist_stage(const float *x, const float *g, int rows, int k, float eps, float *xs, float *raw,
-                             float *scales, int ctid) {
-    const int quads = k / 4;
-    for (int i = ctid; i < PS_ROWS * quads; i += PS_CTHREADS) {
-        const int b = i / quads, c = i % quads;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (b < rows) v = __ldcg(reinterpret_cast<const float4 *>(x + (size_t)b * k) + c);
-        if (g)
-            reinterpret_cast<float4 *>(raw)[i] = v;
-        else
-            *reinterpret_cast<float4 *>(xs + Stage<T>::index(k, b, 4 * c)) = v;
-    }
-    ConsumerSync::sync();
-    if (!g) return;
-    const int warp = ctid >> 5;
-    if (warp < PS_ROWS) {
-        const float sc = warp < rows ? warp_rms_scale(raw + (size_t)warp * k, k, eps) : 0.0f;
-        if ((ctid & 31) == 0) scales[warp] = sc;
-    }
-    ConsumerSync::sync();
-    for (int i = ctid; i < PS_ROWS * quads; i += PS_CTHREADS) {
-        const int b = i / quads, c = i % quads;
-        const float4 v = reinterpret_cast<const float4 *>(raw)[i];
-        const float4 gg = reinterpret_cast<const float4 *>(g)[c];
-        const float sc = scales[b];
-        *reinterpret_cast<float4 *>(xs + Stage<T>::index(k, b, 4 * c)) =
-            make_float4(v.x * sc * gg.x, v.y * sc * gg.y, v.z * sc * gg.z, v.w * sc * gg.w);
-    }
-    ConsumerSync::sync();
-}
-
-template <typename T, int EPI>
-TG_DEVICE void persist_gemv_segment(const PersistArgs &a, const GemvArgs &ga, const T *slot, int ub, int ue,
-                                    int k, const float *xs, int rows, int ctid) {
-    constexpr int R = EPI == EPI_RESIDUAL ? 1 : 2;
-    const int warp = ctid >> 5, lane = ctid & 31;
-    for (int j = warp; j < ue - ub; j += PS_CONSUMERS) {
-        const T *w[R];
-#pragma unroll
-        for (int r = 0; r < R; r++) w[r] = slot + (size_t)(j * R + r) * k;
-        float acc[PS_ROWS][R];
-        dot_smem<T, PS_ROWS, R>(w, k, xs, acc);
-        float y[PS_ROWS][R];
-#pragma unroll
-        for (int b = 0; b < PS_ROWS; b++)
-#pragma unroll
-            for (int r = 0; r < R; r++) y[b][r] = warp_sum(acc[b][r]);
-        if (lane < rows) {
-            float y0 = 0.0f, y1 = 0.0f;
-#pragma unroll
-            for (int b = 0; b < PS_ROWS; b++)
-                if (b == lane) {
-                    y0 = y[b][0];
-                    y1 = y[b][R - 1];
-                }
-            gemv_epilogue<T, EPI>(ga, ub + j, lane, y0, y1);
+        if (mine) {
+            if constexpr (EPI == EPI_RESIDUAL) {
+                const size_t at = (size_t)eb * ga.p.n + ub + ej;
+                ga.out[at] = __fmaf_rn(ga.p.residual_scale, y0, res);
+            } else {
+                gemv_epilogue<T, EPI>(ga, ub + ej, eb, y0, y1);
+            }
         }
     }
 }
 
-template <typename T>
+template <typename T, int NB>
 __global__ void __launch_bounds__(PS_THREADS, 1) decode_step_kernel(const __grid_constant__ PersistArgs a) {
     extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ __align__(8) uint64_t full[PS_SLOTS], empty[PS_SLOTS];
+    __shared__ __align__(8) uint64_t full[PS_NBAR];
+    // The consumers' release mark: bit 63 an abort, bits 32..62 the segments released, bits 0..31
+    // the linear ring end of the last one.
+    __shared__ volatile unsigned long long released;
+    __shared__ int ok_t;
+    __shared__ int last_s;
     __shared__ float scales[PS_ROWS];
     __shared__ int ok_s;
     const tg_params &p = a.p;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rows = p.rows;
-    T *slots = reinterpret_cast<T *>(smem);
-    float *scratch = reinterpret_cast<float *>(smem + (size_t)PS_SLOTS * PS_SLOT_BYTES);
-    float *xs = scratch;                      // [PS_ROWS][kmax], Stage layout
-    float *raw = scratch + a.xs_floats;       // [PS_ROWS][hidden]
-    float *comb = raw + a.raw_floats;         // the join's maxima, sums and weights
-    float *work = scratch;                    // attention's working space (aliases the above)
-    auto slot_ptr = [&](int g) { return slots + (size_t)(g % PS_SLOTS) * (PS_SLOT_BYTES / sizeof(T)); };
+    const int H = p.hidden;
+    const size_t es = sizeof(T);
+    unsigned char *ring = smem;
+    float *gs = reinterpret_cast<float *>(smem + a.ring);  // [hidden]: the RMSNorm gain in use
+    float *xs = gs + H;                                     // [NB][k], Stage layout
+    float *work = xs + (size_t)NB * H;                      // attention's working space (past q/k/v's xs)
     if (threadIdx.x == 0) {
-        for (int i = 0; i < PS_SLOTS; i++) {
-            mbar_init(smem_u32(&full[i]), 1);
-            mbar_init(smem_u32(&empty[i]), 1);
-        }
+        for (int i = 0; i < PS_NBAR; i++) mbar_init(smem_u32(&full[i]), 1);
+        released = 0ull;
         mbar_fence_init();
     }
     __syncthreads();
-    const int total = a.layers * a.segs_per_layer;
 
     if (warp == PS_CONSUMERS) {
-        // Producer: every segment in order, each into the next slot once its last use is released.
-        int issued = 0;
-        for (int g = 0; g < total; g++) {
-            const int slot = g % PS_SLOTS;
-            if (g >= PS_SLOTS && !mbar_wait_abortable(smem_u32(&empty[slot]), ((g / PS_SLOTS) - 1) & 1, a)) break;
-            int l, ph, sg, ub, ue;
-            segment_of(a, g, l, ph, sg);
-            segment_units(a, ph, sg, ub, ue);
-            const int R = phase_rows(ph);
-            const uint32_t row_bytes = (uint32_t)(a.k[ph] * sizeof(T));
-            const int n = (ue - ub) * R;
-            if (lane == 0) mbar_arrive_expect_tx(smem_u32(&full[slot]), (uint32_t)n * row_bytes);
-            __syncwarp();
-            const T *w = phase_weights<T>(a, l, ph);
-            T *dst = slot_ptr(g);
-            for (int j = lane; j < n; j += 32) {
-                const int row = weight_row(p, ph, ub + j / R, j % R);
-                bulk_load(smem_u32(dst + (size_t)j * a.k[ph]), w + (size_t)row * a.k[ph], row_bytes,
-                          smem_u32(&full[slot]));
+        // Producer: the block's segment of every weight phase of every layer, in the consumers' order.
+        uint32_t lin = 0;
+        int g = 0;
+        bool ok = true;
+        for (int l = 0; l < a.layers && ok; l++) {
+            for (int wi = 0; wi < 4 && ok; wi++) {
+                const WPhase ph = wphase(p, wi);
+                int ub, ue;
+                share(p, wi, ph.units, ub, ue);
+                if (ub >= ue) continue;
+                const int nu = ue - ub;
+                const uint32_t row_bytes = (uint32_t)(ph.k * es);
+                const uint32_t bytes = (uint32_t)nu * ph.R * row_bytes;
+                const uint32_t start = ring_place(lin, bytes, row_bytes);
+                const uint32_t end = start + bytes;
+                // The ring bytes it takes were last used by segments that start before end - ring
+                // (all of them released once every segment before it is, or once the released ones
+                // reach end - ring), and its barrier by segment g - PS_NBAR.
+                if (lane == 0) {
+                    const uint64_t t0 = globaltimer();
+                    for (uint32_t i = 0;; i++) {
+                        const unsigned long long rel = released;
+                        if (rel >> 63) {
+                            ok = false;
+                            break;
+                        }
+                        const int count = (int)(rel >> 32);
+                        if ((count >= g || (uint32_t)rel + a.ring >= end) && count >= g + 1 - PS_NBAR) break;
+                        if ((i & 63) == 0) {
+                            if (*(volatile uint32_t *)abort_word(a)) {
+                                ok = false;
+                                break;
+                            }
+                            if (globaltimer() - t0 > PS_WAIT_NS) {
+                                atomicExch(a.err, ERR_WAIT_TIMEOUT);
+                                atomicExch(abort_word(a), 1u);
+                                ok = false;
+                                break;
+                            }
+                        }
+                    }
+                    if (ok) {
+                        const uint32_t bar = smem_u32(&full[g % PS_NBAR]);
+                        mbar_arrive_expect_tx(bar, bytes);
+                        const unsigned char *w = a.weights + a.offs[l * 6 + wi];
+                        // Rows that follow each other in W go in one copy (unit j's row r at
+                        // segment row r nu + j), split in two where it wraps around the ring.
+                        for (int r = 0; r < ph.R; r++)
+                            for (int j0 = 0; j0 < nu;) {
+                                const int row0 = wrow(p, wi, ub + j0, r);
+                                int j1 = j0 + 1;
+                                while (j1 < nu && wrow(p, wi, ub + j1, r) == row0 + (j1 - j0)) j1++;
+                                const uint32_t at = (start + (uint32_t)(r * nu + j0) * row_bytes) % a.ring;
+                                const uint32_t n = (uint32_t)(j1 - j0) * row_bytes;
+                                const uint32_t first = min(n, a.ring - at);
+                                const unsigned char *src = w + (size_t)row0 * row_bytes;
+                                bulk_load(smem_u32(ring + at), src, first, bar);
+                                if (first < n) bulk_load(smem_u32(ring), src + first, n - first, bar);
+                                j0 = j1;
+                            }
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (ok) g++;
             }
-            issued = g + 1;
+        }
+        // The first layer's weights into L2 for the next step, while this step's last layers finish.
+        if (ok && lane == 0 && a.prefetch) {
+            for (int wi = 0; wi < 4; wi++) {
+                const WPhase ph = wphase(p, wi);
+                int ub, ue;
+                share(p, wi, ph.units, ub, ue);
+                const char *w = reinterpret_cast<const char *>(a.weights + a.offs[wi]);
+                for (int r = 0; r < ph.R && ub < ue; r++)
+                    for (int j0 = 0; j0 < ue - ub;) {
+                        const int row0 = wrow(p, wi, ub + j0, r);
+                        int j1 = j0 + 1;
+                        while (j1 < ue - ub && wrow(p, wi, ub + j1, r) == row0 + (j1 - j0)) j1++;
+                        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w + (size_t)row0 * ph.k * es),
+                                     "r"((uint32_t)((j1 - j0) * ph.k * es))
+                                     : "memory");
+                        j0 = j1;
+                    }
+            }
         }
         // Every copy issued has landed before the block ends.
-        for (int g = max(0, issued - PS_SLOTS); g < issued; g++)
-            mbar_wait_bounded(smem_u32(&full[g % PS_SLOTS]), (g / PS_SLOTS) & 1, a.err, 100000000ull);
+        if (lane == 0)
+            for (int s = max(0, g - PS_NBAR); s < g; s++)
+                mbar_wait_bounded(smem_u32(&full[s % PS_NBAR]), (s / PS_NBAR) & 1, a.err, 100000000ull);
         return;
     }
 
     // Consumers.
     const int ctid = threadIdx.x;
-    uint32_t count = 0;
-    bool ok = true;
-    int g = 0;
+    const int G = gridDim.x;
     const int hd = p.head_dim, heads = p.heads, kvh = p.kv_heads, group = heads / kvh;
-    const int chunks = attn_chunks(p.capacity), H = p.hidden;
+    const int chunks = attn_chunks(p.capacity);
     uint32_t pos[PS_ROWS], slotw[PS_ROWS];
-    int nchunks[PS_ROWS];
+    int nch[PS_ROWS];
     bool live[PS_ROWS];
+    int items = 0;
+#pragma unroll
     for (int b = 0; b < PS_ROWS; b++) {
         live[b] = b < rows && placed(a.at, rows, b, p.capacity, p.slots, pos[b], slotw[b]);
-        nchunks[b] = live[b] ? (int)(pos[b] / ATTN_CHUNK) + 1 : 0;
+        nch[b] = live[b] ? (int)(pos[b] / ATTN_CHUNK) + 1 : 0;
+        items += kvh * nch[b];
     }
-    auto take = [&](int gg) -> bool {
-        return mbar_wait_abortable(smem_u32(&full[gg % PS_SLOTS]), (gg / PS_SLOTS) & 1, a);
-    };
-    auto give = [&](int gg) {
+    uint32_t lin = 0;
+    int g = 0;
+    bool ok = true;
+    // Takes the block's next segment of weight phase wi: waits for it to land, returns its start.
+    // One thread waits (bounded); once it has seen the copies land, the phase stays complete until
+    // the segment is released, so every thread's own check of it passes at once.
+    auto take = [&](int wi, int nu) -> SegRef {
+        const WPhase ph = wphase(p, wi);
+        const uint32_t row_bytes = (uint32_t)(ph.k * es);
+        const uint32_t bytes = (uint32_t)nu * ph.R * row_bytes;
+        const uint32_t start = ring_place(lin, bytes, row_bytes);
+        const uint32_t bar = smem_u32(&full[g % PS_NBAR]), parity = (g / PS_NBAR) & 1;
+        if (ctid == 0) ok_t = ok && mbar_wait_abortable(bar, parity, a);
         ConsumerSync::sync();
-        if (ctid == 0) mbar_arrive(smem_u32(&empty[gg % PS_SLOTS]));
+        if (!ok_t) ok = false;
+        if (ok) mbar_wait_bounded(bar, parity, a.err, 1000000ull);
+        return SegRef{ring, start, a.ring, row_bytes};
     };
-    for (int l = 0; l < a.layers && ok; l++) {
-        const float *x = l == 0 ? a.x_in : a.h;
+    auto give = [&]() {
+        ConsumerSync::sync();
+        if (ctid == 0 && ok) released = ((unsigned long long)(g + 1) << 32) | lin;
+        g++;
+    };
+    const float *x = a.x_in;
+    for (int l = 0; l < a.layers; l++) {
         const float *g_in = reinterpret_cast<const float *>(a.weights + a.offs[l * 6 + 4]);
         const float *g_post = reinterpret_cast<const float *>(a.weights + a.offs[l * 6 + 5]);
         T *kc = reinterpret_cast<T *>(a.kcache + (size_t)l * a.cache_layer);
         T *vc = reinterpret_cast<T *>(a.vcache + (size_t)l * a.cache_layer);
+        int ub, ue;
         // q, k, v with RoPE and the KV append.
-        if (l > 0 && !(ok = grid_barrier(a, count, &ok_s))) break;
-        persist_stage<T>(x, g_in, rows, H, p.eps, xs, raw, scales, ctid);
-        {
+        share(p, 0, wphase(p, 0).units, ub, ue);
+        if (ub < ue) {
+            stage_gain(g_in, H, gs, ctid);
+            if (l > 0 && !wait_phase(a, l - 1, PH_DOWN, ctid, &ok_s)) ok = false;
+            flow_stage<T, NB>(x, gs, true, rows, H, p.eps, xs, scales, ctid);
+            const SegRef seg = take(0, ue - ub);
             GemvArgs ga{};
             ga.p = p;
             ga.cosv = a.cosv;
@@ -883,143 +1113,100 @@ __global__ void __launch_bounds__(PS_THREADS, 1) decode_step_kernel(const __grid
             ga.q = a.q;
             ga.kc = kc;
             ga.vc = vc;
-            for (int sg = 0; sg < a.nseg[PH_QKV] && ok; sg++, g++) {
-                int ub, ue;
-                segment_units(a, PH_QKV, sg, ub, ue);
-                if (!(ok = take(g))) break;
-                persist_gemv_segment<T, EPI_QKV_ROPE>(a, ga, slot_ptr(g), ub, ue, a.k[PH_QKV], xs, rows, ctid);
-                give(g);
+            if (ok) flow_dots<T, NB, EPI_QKV_ROPE, 1>(ga, seg, ub, ue - ub, H, xs, rows, ctid);
+            give();
+        }
+        if (!ok) break;
+        arrive(a, l, PH_QKV, ctid);
+        // Attention: items (row, kv head, chunk) dealt from the last block down. The keys and
+        // values before each row's position are staged before the wait on q/k/v.
+        {
+            bool waited = false;
+            auto wait_qkv = [&]() {
+                if (!waited && !wait_phase(a, l, PH_QKV, ctid, &ok_s)) ok = false;
+                waited = true;
+            };
+            for (int it = G - 1 - (int)blockIdx.x, first = it; it < items; it += G) {
+                // Item `it`: rows in order, then kv heads, then chunks.
+                int b = 0, rest = it;
+                while (b < PS_ROWS - 1 && rest >= kvh * nch[b]) {
+                    rest -= kvh * nch[b];
+                    b++;
+                }
+                const int kv = rest / nch[b], c = rest % nch[b];
+                const uint32_t pb = pos[b], sb = slotw[b];
+                if (it != first) ConsumerSync::sync();  // the previous item's reads of `work` are done
+                const size_t head0 = (size_t)b * heads + kv * group;
+                attention_chunk<T, ConsumerSync>(p, a.q, kc, vc, b, kv, c, pb, sb, a.po + (head0 * chunks + c) * hd,
+                                                 (size_t)chunks * hd, a.pml + (head0 * chunks + c) * 2,
+                                                 (size_t)chunks * 2, work, ctid, PS_CTHREADS, wait_qkv);
+                // The block that writes the last chunk of (row, kv head) joins them: every thread's
+                // partials published, then the count (the threadfence-reduction pattern).
+                __threadfence();
+                ConsumerSync::sync();
+                if (ctid == 0) {
+                    last_s = atomicAdd(chunks_done(a, l, b, kv), 1u) + 1 == (uint32_t)nch[b];
+                    __threadfence();
+                }
+                ConsumerSync::sync();
+                if (last_s) flow_join(a, b, kv, nch[b], ctid);
             }
         }
-        if (!ok || !(ok = grid_barrier(a, count, &ok_s))) break;
-        // Attention: items (row, kv head, chunk) dealt over the blocks.
-        {
-            int item = 0;
-            for (int b = 0; b < rows; b++)
-                for (int kv = 0; kv < kvh; kv++)
-                    for (int c = 0; c < nchunks[b]; c++, item++) {
-                        if (item % (int)gridDim.x != (int)blockIdx.x) continue;
-                        const size_t head0 = (size_t)b * heads + kv * group;
-                        attention_chunk<T, ConsumerSync, true>(p, a.q, kc, vc, b, kv, c, pos[b], slotw[b],
-                                                         a.po + (head0 * chunks + c) * hd, (size_t)chunks * hd,
-                                                         a.pml + (head0 * chunks + c) * 2, (size_t)chunks * 2,
-                                                         work, ctid, PS_CTHREADS);
-                        ConsumerSync::sync();
-                    }
-        }
-        if (!(ok = grid_barrier(a, count, &ok_s))) break;
-        // The join of every head's chunks (attention_combine's order), into xs as o_proj's input.
-        {
-            const int K = heads * hd;
-            float *cml = comb;                                   // [PS_ROWS][heads][chunks][2]
-            float *wts = cml + (size_t)PS_ROWS * heads * chunks * 2;  // [PS_ROWS][heads][chunks]
-            float *tot = wts + (size_t)PS_ROWS * heads * chunks;      // [PS_ROWS][heads]
-            for (int i = ctid; i < rows * heads * chunks * 2; i += PS_CTHREADS) {
-                const int b = i / (heads * chunks * 2);
-                const int c = (i / 2) % chunks;
-                if (c < nchunks[b]) cml[i] = __ldcg(a.pml + i);
-            }
-            ConsumerSync::sync();
-            for (int bh = ctid; bh < rows * heads; bh += PS_CTHREADS) {
-                const int b = bh / heads, n = nchunks[b];
-                const float *ml = cml + (size_t)bh * chunks * 2;
-                float m = -INFINITY;
-                for (int c = 0; c < n; c++) m = fmaxf(m, ml[2 * c]);
-                float total = 0.0f;
-                for (int c = 0; c < n; c++) total = __fmaf_rn(ml[2 * c + 1], expf(ml[2 * c] - m), total);
-                for (int c = 0; c < n; c++) wts[(size_t)bh * chunks + c] = expf(ml[2 * c] - m);
-                tot[bh] = total;
-            }
-            ConsumerSync::sync();
-            // Thread t takes outputs t, t + 256, t + 512, t + 768 of each pass; the first NC chunks
-            // of all four are loaded in one batch (static indices, so the loads stay independent
-            // in registers), then each output is folded in chunk order (later chunks, if any, by
-            // join_chunks, continuing the same fold).
-            constexpr int U = 4, NC = 16;
-            const int outs = PS_ROWS * K;
-            for (int i0 = 0; i0 < outs; i0 += PS_CTHREADS * U) {
-                float v[U][NC];
-                int n_u[U], bh_u[U];
-#pragma unroll
-                for (int u = 0; u < U; u++) {
-                    const int i = i0 + u * PS_CTHREADS + ctid;
-                    const int b = i / K, hdd = i % K, h = hdd / hd, d = hdd % hd;
-                    const int n = (i < outs && b < rows && live[b]) ? nchunks[b] : 0;
-                    n_u[u] = n;
-                    bh_u[u] = b * heads + h;
-                    const float *o = a.po + (size_t)(b * heads + h) * chunks * hd + d;
-#pragma unroll
-                    for (int c = 0; c < NC; c++) v[u][c] = c < n ? __ldcg(o + (size_t)c * hd) : 0.0f;
-                }
-#pragma unroll
-                for (int u = 0; u < U; u++) {
-                    const int i = i0 + u * PS_CTHREADS + ctid;
-                    if (i >= outs) continue;
-                    const int b = i / K, hdd = i % K, d = hdd % hd, n = n_u[u], bh = bh_u[u];
-                    float val = 0.0f;
-                    if (n > 0) {
-                        const float *w = wts + (size_t)bh * chunks;
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int c = 0; c < NC; c++)
-                            if (c < n) acc = __fmaf_rn(v[u][c], w[c], acc);
-                        if (n > NC)
-                            acc = join_chunks(a.po + (size_t)bh * chunks * hd + d + (size_t)NC * hd, hd, w + NC, n - NC, acc);
-                        val = __fdiv_rn(acc, tot[bh]);
-                    }
-                    xs[Stage<T>::index(K, b, hdd)] = val;
-                }
-            }
-            ConsumerSync::sync();
+        if (!ok) break;
+        arrive(a, l, PH_ATT, ctid);
+        // The join of every head's chunks, then the output projection with the residual.
+        share(p, 1, wphase(p, 1).units, ub, ue);
+        if (ub < ue) {
+            if (!wait_phase(a, l, PH_ATT, ctid, &ok_s)) ok = false;
+            flow_stage<T, NB>(a.att, nullptr, false, rows, heads * hd, p.eps, xs, scales, ctid);
+            const SegRef seg = take(1, ue - ub);
             GemvArgs ga{};
             ga.p = p;
             ga.p.n = H;
             ga.res = x;
             ga.out = a.mid;
-            for (int sg = 0; sg < a.nseg[PH_O] && ok; sg++, g++) {
-                int ub, ue;
-                segment_units(a, PH_O, sg, ub, ue);
-                if (!(ok = take(g))) break;
-                persist_gemv_segment<T, EPI_RESIDUAL>(a, ga, slot_ptr(g), ub, ue, a.k[PH_O], xs, rows, ctid);
-                give(g);
-            }
+            if (ok) flow_dots<T, NB, EPI_RESIDUAL, 1>(ga, seg, ub, ue - ub, heads * hd, xs, rows, ctid);
+            give();
         }
-        if (!ok || !(ok = grid_barrier(a, count, &ok_s))) break;
+        if (!ok) break;
+        arrive(a, l, PH_O, ctid);
         // gate/up with the post-attention norm, SiLU-mul.
-        persist_stage<T>(a.mid, g_post, rows, H, p.eps, xs, raw, scales, ctid);
-        {
+        share(p, 2, wphase(p, 2).units, ub, ue);
+        if (ub < ue) {
+            stage_gain(g_post, H, gs, ctid);
+            if (!wait_phase(a, l, PH_O, ctid, &ok_s)) ok = false;
+            flow_stage<T, NB>(a.mid, gs, true, rows, H, p.eps, xs, scales, ctid);
+            const SegRef seg = take(2, ue - ub);
             GemvArgs ga{};
             ga.p = p;
             ga.out = a.mlp;
-            for (int sg = 0; sg < a.nseg[PH_GU] && ok; sg++, g++) {
-                int ub, ue;
-                segment_units(a, PH_GU, sg, ub, ue);
-                if (!(ok = take(g))) break;
-                persist_gemv_segment<T, EPI_GATE_UP>(a, ga, slot_ptr(g), ub, ue, a.k[PH_GU], xs, rows, ctid);
-                give(g);
-            }
+            if (ok) flow_dots<T, NB, EPI_GATE_UP, 4>(ga, seg, ub, ue - ub, H, xs, rows, ctid);
+            give();
         }
-        if (!ok || !(ok = grid_barrier(a, count, &ok_s))) break;
+        if (!ok) break;
+        arrive(a, l, PH_GU, ctid);
         // down with the residual.
-        persist_stage<T>(a.mlp, nullptr, rows, p.inner, p.eps, xs, raw, scales, ctid);
-        {
+        share(p, 3, wphase(p, 3).units, ub, ue);
+        if (ub < ue) {
+            if (!wait_phase(a, l, PH_GU, ctid, &ok_s)) ok = false;
+            flow_stage<T, NB>(a.mlp, nullptr, false, rows, p.inner, p.eps, xs, scales, ctid);
+            const SegRef seg = take(3, ue - ub);
             GemvArgs ga{};
             ga.p = p;
             ga.p.n = H;
             ga.res = a.mid;
             ga.out = a.h;
-            for (int sg = 0; sg < a.nseg[PH_DOWN] && ok; sg++, g++) {
-                int ub, ue;
-                segment_units(a, PH_DOWN, sg, ub, ue);
-                if (!(ok = take(g))) break;
-                persist_gemv_segment<T, EPI_RESIDUAL>(a, ga, slot_ptr(g), ub, ue, a.k[PH_DOWN], xs, rows, ctid);
-                give(g);
-            }
+            if (ok) flow_dots<T, NB, EPI_RESIDUAL, 1>(ga, seg, ub, ue - ub, p.inner, xs, rows, ctid);
+            give();
         }
+        if (!ok) break;
+        arrive(a, l, PH_DOWN, ctid);
+        x = a.h;
     }
-    if (ok && (ok = grid_barrier(a, count, &ok_s)) && blockIdx.x == 0) {
+    if (ok && blockIdx.x == 0 && wait_phase(a, a.layers - 1, PH_DOWN, ctid, &ok_s)) {
         // The final norm (rmsnorm.comp), in f32.
         const float *gf = reinterpret_cast<const float *>(a.weights + a.final_norm);
+        float *raw = xs;  // [rows][hidden]
         for (int i = ctid; i < rows * (H / 4); i += PS_CTHREADS)
             reinterpret_cast<float4 *>(raw)[i] = __ldcg(reinterpret_cast<const float4 *>(a.h) + i);
         ConsumerSync::sync();
@@ -1034,9 +1221,11 @@ __global__ void __launch_bounds__(PS_THREADS, 1) decode_step_kernel(const __grid
             }
         }
     }
-    // An aborted step releases the slots it still holds, so that the producer is not left waiting.
-    if (!ok && ctid == 0)
-        for (int i = 0; i < PS_SLOTS; i++) mbar_arrive(smem_u32(&empty[i]));
+    // An aborted step tells the producer to stop issuing copies (it then waits for those in flight).
+    if (!ok && ctid == 0) {
+        atomicExch(abort_word(a), 1u);
+        released = released | (1ull << 63);
+    }
 }
 
 // stream_read.comp: reads the buffer once, 16 bytes per load, and writes one word per block of
@@ -1254,12 +1443,40 @@ cudaError_t launch_attention_decode(const tg_params &p, const void *q, const voi
                               : decode_attention_t<float>(p, q, kc, vc, at, out, s);
 }
 
-// The persistent step over a decoder's buffers: partitions each phase's units over the SMs and
-// its weight rows into slot-sized segments. Returns cudaErrorNotSupported for shapes or batches it
-// does not take (more than PS_ROWS rows, a unit's rows larger than a slot).
+// The persistent step over a decoder's buffers: one block per SM, the ring as large as shared
+// memory allows beside the block's staging space. Returns cudaErrorNotSupported for batches or
+// shapes it does not take (more than PS_ROWS rows; a block's share of a projection larger than
+// the ring).
+size_t decode_step_flag_bytes(int layers, int kv_heads) {
+    return ((size_t)layers * PS_PHASES * PS_NCOUNT + 1 + (size_t)layers * PS_ROWS * kv_heads) * sizeof(uint32_t);
+}
+
+template <typename T, int NB>
+static cudaError_t launch_step_t(const PersistArgs &a, int sms, size_t smem, size_t flag_bytes, cudaStream_t s) {
+    auto kern = decode_step_kernel<T, NB>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, PS_THREADS, smem)) != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorNotSupported;
+    if ((e = cudaMemsetAsync(a.flags, 0, flag_bytes, s)) != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sms);
+    cfg.blockDim = dim3(PS_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+
 cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s) {
     const tg_params &p = d.p;
     if (p.rows == 0 || p.rows > (uint32_t)PS_ROWS) return cudaErrorNotSupported;
+    const int NB = p.rows == 1 ? 1 : 2;
     const size_t es = p.dtype == TG_BF16 ? 2 : 4;
     PersistArgs a{};
     a.p = p;
@@ -1275,65 +1492,46 @@ cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s
     a.mid = d.mid;
     a.mlp = d.mlp;
     a.q = d.q;
+    a.att = d.att;
     a.out = d.out;
     a.po = d.po;
     a.pml = d.pml;
     a.kcache = d.kcache;
     a.vcache = d.vcache;
     a.cache_layer = d.cache_layer;
-    a.sync = d.sync;
+    a.flags = d.sync;
     a.err = d.err;
-    const int units[4] = {(int)((p.heads + 2 * p.kv_heads) * p.head_dim / 2), (int)p.hidden, (int)p.inner,
-                          (int)p.hidden};
-    const int ks[4] = {(int)p.hidden, (int)(p.heads * p.head_dim), (int)p.hidden, (int)p.inner};
-    const int G = sm_count;
-    a.segs_per_layer = 0;
-    for (int ph = 0; ph < 4; ph++) {
-        const int R = (ph == PH_QKV || ph == PH_GU) ? 2 : 1;
-        const size_t unit_bytes = (size_t)R * ks[ph] * es;
-        if (unit_bytes > PS_SLOT_BYTES) return cudaErrorNotSupported;
-        a.units[ph] = units[ph];
-        a.k[ph] = ks[ph];
-        a.per[ph] = (units[ph] + G - 1) / G;
-        a.seg[ph] = (int)(PS_SLOT_BYTES / unit_bytes);
-        a.nseg[ph] = (a.per[ph] + a.seg[ph] - 1) / a.seg[ph];
-        a.segs_per_layer += a.nseg[ph];
+    a.prefetch = 1;
+    // The largest share of a projection one block streams at once.
+    const uint64_t units[4] = {(uint64_t)(p.heads + 2 * p.kv_heads) * p.head_dim / 2, p.hidden, p.inner, p.hidden};
+    const uint64_t ks[4] = {p.hidden, (uint64_t)p.heads * p.head_dim, p.hidden, p.inner};
+    const uint64_t rs[4] = {2, 1, 2, 1};
+    uint64_t seg = 0;
+    for (int i = 0; i < 4; i++) {
+        const uint64_t blocks = (uint64_t)phase_blocks(p, i, sm_count);
+        seg = std::max(seg, (units[i] + blocks - 1) / blocks * rs[i] * ks[i] * es);
     }
-    const uint32_t kmax = std::max({p.hidden, p.inner, p.heads * p.head_dim});
-    a.xs_floats = PS_ROWS * kmax;
-    a.raw_floats = PS_ROWS * p.hidden;
-    const uint32_t chunks = attn_chunks(p.capacity);
-    const size_t comb_floats = (size_t)PS_ROWS * p.heads * chunks * 3 + PS_ROWS * p.heads;
-    const size_t scratch = std::max((size_t)(a.xs_floats + a.raw_floats) * 4 + comb_floats * 4, attention_smem(p));
-    const size_t smem = (size_t)PS_SLOTS * PS_SLOT_BYTES + scratch;
-    if (smem > 227 * 1024) return cudaErrorNotSupported;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(G);
-    cfg.blockDim = dim3(PS_THREADS);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e;
-    if (p.dtype == TG_BF16) {
-        auto kern = decode_step_kernel<bf16>;
-        if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
-        int per_sm = 0;
-        if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, PS_THREADS, smem)) != cudaSuccess) return e;
-        if (per_sm < 1) return cudaErrorNotSupported;
-        if ((e = cudaMemsetAsync(d.sync, 0, 8, s)) != cudaSuccess) return e;
-        return cudaLaunchKernelEx(&cfg, kern, a);
-    }
-    auto kern = decode_step_kernel<float>;
-    if ((e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
-    int per_sm = 0;
-    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, PS_THREADS, smem)) != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorNotSupported;
-    if ((e = cudaMemsetAsync(d.sync, 0, 8, s)) != cudaSuccess) return e;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    // The gain [hidden], then xs [NB][kmax] with attention's working space past q/k/v's part of it.
+    const uint64_t kmax = std::max({(uint64_t)p.hidden, (uint64_t)p.inner, (uint64_t)p.heads * p.head_dim});
+    if ((uint64_t)NB * kmax > (uint64_t)4 * PS_STAGE * PS_CTHREADS) return cudaErrorNotSupported;
+    const uint64_t scratch =
+        4 * (uint64_t)p.hidden + std::max<uint64_t>(4 * NB * kmax, 4 * (uint64_t)NB * p.hidden + attention_smem(p));
+    int dev = 0, optin = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    const int64_t room = (int64_t)optin - 1024 - (int64_t)scratch;  // 1 KiB for the static barriers
+    if (room < (int64_t)seg) return cudaErrorNotSupported;
+    const int64_t row_max = (int64_t)(kmax * es);
+    a.ring = (uint32_t)(room / row_max * row_max);  // a multiple of every phase's row length
+    if (a.ring < seg) return cudaErrorNotSupported;
+    const size_t smem = a.ring + scratch;
+    const size_t flag_bytes = decode_step_flag_bytes(d.layers, (int)p.kv_heads);
+    if (p.dtype == TG_BF16)
+        return NB == 1 ? launch_step_t<bf16, 1>(a, sm_count, smem, flag_bytes, s)
+                       : launch_step_t<bf16, 2>(a, sm_count, smem, flag_bytes, s);
+    return NB == 1 ? launch_step_t<float, 1>(a, sm_count, smem, flag_bytes, s)
+                   : launch_step_t<float, 2>(a, sm_count, smem, flag_bytes, s);
 }
 
 cudaError_t launch_stream_read(const tg_params &p, const uint32_t *data, uint32_t *out,

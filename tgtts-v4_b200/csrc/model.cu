@@ -83,7 +83,7 @@ static int check_shape(const tg_shape &s, tg_dtype dtype) {
     if (s.hidden % vec || s.inner % vec || (s.heads * s.head_dim) % vec)
         return fail(TG_ESHAPE, "%u hidden, %u inner and %u attention columns in steps of %u", s.hidden, s.inner,
                     s.heads * s.head_dim, vec);
-    if (s.heads % s.kv_heads || (s.head_dim != 64 && s.head_dim != 128))
+    if (s.heads % s.kv_heads || s.heads / s.kv_heads > MAX_GROUP || (s.head_dim != 64 && s.head_dim != 128))
         return fail(TG_ESHAPE, "%u heads over %u of %u", s.heads, s.kv_heads, s.head_dim);
     if (s.inner % GU_BLOCK) return fail(TG_ESHAPE, "inner %u is not a multiple of %u", s.inner, GU_BLOCK);
     if (s.capacity == 0 || s.capacity % CAPACITY_STEP)
@@ -129,6 +129,7 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
         st.mid = reinterpret_cast<float *>(d.mid.ptr());
         st.mlp = reinterpret_cast<float *>(d.mlp.ptr());
         st.q = reinterpret_cast<float *>(d.q.ptr());
+        st.att = reinterpret_cast<float *>(d.att.ptr());
         st.out = reinterpret_cast<float *>(d.out.ptr());
         st.po = reinterpret_cast<float *>(d.po.ptr());
         st.pml = reinterpret_cast<float *>(d.pml.ptr());
@@ -276,7 +277,7 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(d->words.alloc(ctx, 2 * R * 4));
     TG_TRY(d->po.alloc(ctx, R * s->heads * chunks * s->head_dim * F));
     TG_TRY(d->pml.alloc(ctx, R * s->heads * chunks * 2 * F));
-    TG_TRY(d->psync.alloc(ctx, 256));
+    TG_TRY(d->psync.alloc(ctx, decode_step_flag_bytes((int)s->layers, (int)s->kv_heads)));
     {
         std::vector<uint64_t> offs;
         for (const LayerOffsets &o : d->layer) {

@@ -45,7 +45,7 @@ extern "C" int tg_attention_decode_noalloc(const tg_params *p, const float *q, c
         if (reinterpret_cast<uintptr_t>(ptr) % 16)
             return fail(TG_EINVAL, "tg_attention_decode_noalloc: a pointer is not 16-byte aligned");
     if (p->dtype != TG_F32 && p->dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %u", p->dtype);
-    if (p->rows == 0 || p->slots == 0 || p->heads == 0 || p->kv_heads == 0 || p->heads % p->kv_heads ||
+    if (p->rows == 0 || p->slots == 0 || p->heads == 0 || p->kv_heads == 0 || p->heads % p->kv_heads || p->heads / p->kv_heads > MAX_GROUP ||
         (p->head_dim != 64 && p->head_dim != 128) || p->capacity == 0 || p->capacity % CAPACITY_STEP)
         return fail(TG_ESHAPE, "tg_attention_decode_noalloc: %u rows, %u heads over %u of %u, a cache of %u",
                     p->rows, p->heads, p->kv_heads, p->head_dim, p->capacity);

@@ -253,8 +253,8 @@ static int check_shape(const Launch &l) {
     if (p.dtype != TG_F32 && p.dtype != TG_BF16) return fail(TG_ESHAPE, "dtype %u", p.dtype);
     const uint32_t vec = p.dtype == TG_BF16 ? 256 : 128;  // a warp's 16-byte step over K
     auto heads_ok = [&] {
-        return p.kv_heads > 0 && p.heads % p.kv_heads == 0 && (p.head_dim == 64 || p.head_dim == 128) &&
-               p.capacity > 0 && p.capacity % CAPACITY_STEP == 0;
+        return p.kv_heads > 0 && p.heads % p.kv_heads == 0 && p.heads / p.kv_heads <= MAX_GROUP &&
+               (p.head_dim == 64 || p.head_dim == 128) && p.capacity > 0 && p.capacity % CAPACITY_STEP == 0;
     };
     switch (l.kernel) {
         case TG_KERNEL_RMSNORM:

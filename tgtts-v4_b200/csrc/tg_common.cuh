@@ -119,6 +119,30 @@ TG_DEVICE float warp_rms_scale(const float *row, int k, float eps) {
     return 1.0f / sqrtf(__fdiv_rn(s, (float)k) + eps);
 }
 
+// warp_rms_scale of a row in global memory that other blocks of the same launch wrote: the same
+// sums in the same order, its loads through L2 (ld.global.cg), eight chunks a lane in flight at once.
+TG_DEVICE float warp_rms_scale_cg(const float *row, int k, float eps) {
+    const int lane = threadIdx.x & 31;
+    const float4 *v = reinterpret_cast<const float4 *>(row);
+    const int n = k / 4;
+    float s = 0.0f;
+    for (int c0 = lane; c0 < n; c0 += 32 * 8) {
+        float4 q[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) q[u] = c0 + 32 * u < n ? __ldcg(v + c0 + 32 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            if (c0 + 32 * u >= n) continue;
+            s = __fmaf_rn(q[u].x, q[u].x, s);
+            s = __fmaf_rn(q[u].y, q[u].y, s);
+            s = __fmaf_rn(q[u].z, q[u].z, s);
+            s = __fmaf_rn(q[u].w, q[u].w, s);
+        }
+    }
+    s = warp_sum(s);
+    return 1.0f / sqrtf(__fdiv_rn(s, (float)k) + eps);
+}
+
 TG_DEVICE float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
 
 // Placement words (crates/graph/src/decode.rs:198-227, kernels/glsl/batch.glsl:9-14): positions

@@ -56,10 +56,10 @@ struct DecodeStep {
     const float *cosv, *sinv;
     const uint32_t *at;
     const float *x_in;
-    float *h, *mid, *mlp, *q, *out, *po, *pml;
+    float *h, *mid, *mlp, *q, *att, *out, *po, *pml;
     unsigned char *kcache, *vcache;
     uint64_t cache_layer;
-    uint32_t *sync;  // 8 bytes, zeroed by the launch
+    uint32_t *sync;  // decode_step_flag_bytes(layers, kv_heads): the step's counters, zeroed by the launch
     uint32_t *err;
 };
 // Kernel ids past the table's, for launches the library records itself.
@@ -181,8 +181,13 @@ cudaError_t launch_dtc_residual(const tg_params &p, const float *x, const void *
 // One cooperative launch for the whole step (batches of up to 2 rows); cudaErrorNotSupported when
 // the shape or batch is not one it takes.
 cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s);
+// The bytes of the persistent step's arrival counters for a stack of `layers` layers.
+size_t decode_step_flag_bytes(int layers, int kv_heads);
 // The decode constants: positions per attention chunk.
 constexpr uint32_t ATTN_CHUNK = 64;
+// The most query heads one KV head may serve: decode attention gives a thread at most 8 of a
+// group's heads (attention_chunk's chunk_scores / chunk_outputs).
+constexpr uint32_t MAX_GROUP = 8;
 // A cache's capacity is a multiple of this, as the reference's (decode.rs:28 CHUNK, :480); the
 // last attention chunk of a cache may then be half full.
 constexpr uint32_t CAPACITY_STEP = 32;
