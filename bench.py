@@ -11,7 +11,14 @@ output, every step). The weights (717 MB) are far larger than the 126 MB L2, so 
 needed between steps.
 
 Under torchrun (N > 1) each rank holds a full replica and decodes its own request (the path
-shards by request: no collective on the data path); the job's time is the max over ranks.
+shards by request: no collective on the data path); the job's time is the max over ranks. At N > 1
+the line also carries config 5, the request-sharded serving BASELINE names for 1/2/4/8 GPUs
+(`extras.serve_c5`: aggregate tokens/s, p50/p99 step latency, each rank's busy time).
+
+`roofline` is the decode step's: its algorithmic bytes (every weight once, the KV positions read)
+over its measured time against MEASURED_PEAKS.json's HBM rate; with the persistent step (the
+default at batch 1) the step is one launch, and `traffic` is that launch's DRAM bytes as the
+committed ncu summary under profiles/ records them.
 
 `--impl reference` times the reference's CPU path for the same workload: tgtts-v4 itself cannot
 run here (Rust toolchain absent; its GPU path is Vulkan), so it is the C restatement under
@@ -185,8 +192,6 @@ def run_ours(args, rank, world, local):
     stream = stream_ctx(ctx)
     H = cfg.hidden
 
-    launches_per_step = len(dec.labels())  # the recorded step's kernels (6 a layer + the final norm)
-
     # ---- value: device-resident decode steps, CUDA events on the runtime's stream ----
     x_dev = torch.from_numpy(pre_out[-1:].copy()).to(f"cuda:{local}")
     out_dev = torch.empty_like(x_dev)
@@ -231,13 +236,18 @@ def run_ours(args, rank, world, local):
 
     result = None
     extras = {}
+    labels = dec.labels()
+    # Config 5 (request-sharded serving) on the same GPUs: at N > 1 every rank takes part.
+    if world > 1 and not args.no_extras:
+        extras["serve_c5"] = serve_config5(pkg, syn, ctx, torch, rank, world, local, args.requests, weights)
     if rank == 0:
         hbm, tc, peak_kind = peaks()
-        roof = gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind)
-        step_bytes = shape.weight_bytes(2) + kv_bytes(shape, PREFILL + 15)
-        extras["step_hbm"] = {"bytes": step_bytes, "ms": round(ms_per_step, 4),
-                              "achieved_gbs": round(step_bytes / (ms_per_step * 1e6), 1),
-                              "frac": round(step_bytes / (ms_per_step * 1e6) / hbm, 4)}
+        # The steps timed ran from position PREFILL; a step at position p reads p + 1 positions.
+        mean_pos = PREFILL + (args.warmup + (args.steps - 1) / 2.0)
+        step_bytes = shape.weight_bytes(2) + kv_bytes(shape, int(round(mean_pos)))
+        roof = step_roofline(labels, step_bytes, ms_per_step, hbm, peak_kind)
+        if not args.no_extras and world == 1:
+            extras["gemv_gate_up_alone"] = gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind)
         # The side measurements and the CPU baseline are single-GPU numbers: at N > 1 they would
         # only hold the other GPUs.
         if not args.no_extras and world == 1:
@@ -258,7 +268,7 @@ def run_ours(args, rank, world, local):
                     "d2h_bytes_per_step": H * 4},
             "roofline": roof,
             "cpu_baseline": cpu,
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": len(labels) * args.steps,
             "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
             "extras": extras,
         }
@@ -268,8 +278,38 @@ def run_ours(args, rank, world, local):
     return result
 
 
-# DRAM bytes of one gemv_gate_up launch at config 2 from an ncu capture (read 16,824,832, written 0).
-GATE_UP_TRAFFIC = 16824832
+STEP_PROFILE = ROOT / "profiles" / "decode_step_persistent_config2.md"
+
+
+def profiled_traffic(path):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) as the committed ncu
+    summary `path` records them on its line "dram bytes per launch: N", with the summary's name;
+    None when there is no such summary. The summary is re-captured whenever the kernel changes."""
+    try:
+        for line in path.read_text().splitlines():
+            if line.lower().startswith("dram bytes per launch:"):
+                return int(line.split(":", 1)[1].strip().replace(",", "")), str(path.relative_to(ROOT))
+    except (OSError, ValueError):
+        pass
+    return None, None
+
+
+def step_roofline(labels, step_bytes, ms_per_step, hbm, peak_kind):
+    """The decode step against HBM: its algorithmic bytes (every weight once, the KV positions the
+    steps read) over its measured time. With the persistent step the whole step is one launch, so the
+    step is the dominant kernel; with six kernels a layer it names the chain."""
+    persistent = labels == ["decode_step"]
+    achieved = step_bytes / (ms_per_step * 1e6)
+    traffic, source = profiled_traffic(STEP_PROFILE) if persistent else (None, None)
+    return {"kernel": "decode_step (persistent: the whole step, 24 layers, in one launch)" if persistent
+            else f"the step's {len(labels)}-kernel chain",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "traffic": traffic,
+            "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "bytes_per_launch": step_bytes,
+            "launch_us": round(ms_per_step * 1e3, 2),
+            "traffic_source": (f"{source}: ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch"
+                               if source else None),
+            "how": "bytes = every weight once + the KV positions read; time = the timed steps' CUDA events"}
 
 
 def gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind, layers=24, reps=20):
@@ -300,7 +340,7 @@ def gate_up_roofline(pkg, ctx, shape, stream, torch, hbm, peak_kind, layers=24, 
     return {"kernel": "gemv_gate_up (fused RMSNorm + gate/up GEMV + SiLU-mul), batch 1", "bound": "hbm",
             "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)", "bytes_per_launch": algo,
-            "launch_us": round(ns / 1e3, 3), "traffic": GATE_UP_TRAFFIC, "traffic_source": "ncu --set full capture of one launch at config 2: dram__bytes_read.sum + dram__bytes_write.sum",
+            "launch_us": round(ns / 1e3, 3), "traffic": None,
             "how": f"one program of {n} back-to-back launches cycling over {layers} distinct weight buffers, "
                    "CUDA events at its ends"}
 
@@ -531,40 +571,32 @@ def run_reference(args, rank, world, local):
 SERVE_METRIC = "serving decode tokens/s, all GPUs (0.5B-shaped bf16 backbone, <= 128 requests per GPU)"
 
 
-def run_serve(args, rank, world, local):
-    """Config 5: `--requests` requests (prompts uniform 64-1024, decodes uniform 64-768, seed 3,
-    Poisson arrivals at 4096 a second, which keeps every GPU's 128 slots full), spread over the
-    GPUs by a least-loaded rule every rank computes alike; each rank serves its share with one
-    weight replica, continuous batching and no collective on the data path. Time: CUDA events on
-    the rank's stream from the first admission to the last step (prefills included), max over
-    ranks; per-step decode latency from events around each step, p50/p99 over all steps."""
-    import torch
-
-    import __graft_entry__ as entry
-
-    pkg = entry.load_package()
+def serve_config5(pkg, syn, ctx, torch, rank, world, local, requests, weights, clocks=None):
+    """Config 5 on this rank's GPU: `requests` requests (prompts uniform 64-1024, decodes uniform
+    64-768, seed 3, Poisson arrivals at 4096 a second, which keeps every GPU's 128 slots full),
+    spread over the GPUs by a least-loaded rule every rank computes alike; each rank serves its share
+    with one weight replica, continuous batching and no collective on the data path. Time: CUDA
+    events on the rank's stream from the first admission to the last step (prefills included), max
+    over ranks; per-step decode latency from events around each step, p50/p99 over all steps (max
+    over ranks); each rank's busy time. Every rank returns the same dict."""
     from tgtts_v4_b200 import serving
-    from tgtts_v4_b200 import synthetic as syn
 
-    torch.cuda.set_device(local)
-    ctx = pkg.Context(local)
     cfg = syn.S05B
     slots = 128
     shape = syn.shape_of(cfg, capacity=1024 + 768)
-    weights = syn.make_weights(cfg, seed=0, as_bits=True)
     dec = pkg.Decoder(ctx, shape, rows=slots, slots=slots, dtype="bf16")
     dec.load(weights)
     pre = pkg.Prefill(dec, max_rows=8192)
     server = pkg.Server(dec, pre)
     stream = stream_ctx(ctx)
-    reqs, pool = serving.poisson_requests(args.requests, cfg.hidden, seed=3)
+    reqs, pool = serving.poisson_requests(requests, cfg.hidden, seed=3)
     mine = serving.assign_least_loaded(reqs, world)[rank]
     drv = serving.Driver(server, pool, slots)
-    clocks = Clocks(local)
     barrier(world)
     torch.cuda.synchronize()
-    clocks.__enter__()
-    ev = lambda: torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.__enter__()
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
     e0 = ev()
     e0.record(stream)
     t0 = time.perf_counter()
@@ -589,45 +621,72 @@ def run_serve(args, rank, world, local):
     e1 = ev()
     e1.record(stream)
     e1.synchronize()
-    clocks.__exit__(None, None, None)
+    if clocks:
+        clocks.__exit__(None, None, None)
     ms = e0.elapsed_time(e1)
     step_ms = sorted(x.elapsed_time(y) for x, y in marks)
-    ms_max = max_over_ranks(ms, world)
-    decoded = drv.decoded
-    prefilled = drv.prefilled
+    busy = [ms]
+    decoded, prefilled, n_steps = drv.decoded, drv.prefilled, len(marks)
+    p50, p99 = step_ms[len(step_ms) // 2], step_ms[int(len(step_ms) * 0.99)]
     if world > 1:
         import torch.distributed as dist
 
-        t = torch.tensor([decoded, prefilled, len(marks)], dtype=torch.float64)
+        t = torch.tensor([decoded, prefilled, n_steps], dtype=torch.float64)
         dist.all_reduce(t)
         decoded, prefilled, n_steps = (int(v) for v in t.tolist())
-        lat = torch.tensor([step_ms[len(step_ms) // 2], step_ms[int(len(step_ms) * 0.99)]], dtype=torch.float64)
+        lat = torch.tensor([p50, p99], dtype=torch.float64)
         dist.all_reduce(lat, op=dist.ReduceOp.MAX)
         p50, p99 = lat.tolist()
-    else:
-        n_steps = len(marks)
-        p50, p99 = step_ms[len(step_ms) // 2], step_ms[int(len(step_ms) * 0.99)]
-    result = None
-    if rank == 0:
-        c = clocks.summary()
-        result = {
-            "metric": SERVE_METRIC, "value": round(decoded / (ms_max / 1e3), 1), "unit": "tokens/s",
-            "n_gpus": world, "steps": n_steps, "warmup": 0, "ms_per_step": round(ms_max / max(1, n_steps // world), 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: N(0,0.02) weights seed 0, N(0,1) bf16-valued prompt rows, request lengths seed 3",
-            "config": {"workload": "config 5: request-sharded serving, one weight replica per GPU, no collective",
-                       "requests": args.requests, "slots_per_gpu": slots, "prompt": "U[64,1024]",
-                       "decode": "U[64,768]", "arrivals": "Poisson 4096/s (saturating)",
-                       "parallelism": f"replicas x{world}, least-loaded assignment"},
-            "prefill_tokens": prefilled, "decode_tokens": decoded, "seconds": round(ms_max / 1e3, 3),
-            "step_latency_ms": {"p50": round(p50, 4), "p99": round(p99, 4), "max_over_ranks": world > 1},
-            # Decode steps only: the gather, the step's kernels, the scatter.
-            "gpu_launches": n_steps * (len(dec.labels()) + 2),
-            "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
-        }
+        per = torch.zeros(world, dtype=torch.float64)
+        per[rank] = ms
+        dist.all_reduce(per)
+        busy = per.tolist()
+    ms_max = max(busy)
+    launches = n_steps * (len(dec.labels()) + 2)  # a step's kernels, the gather and the scatter
     server.close()
     pre.close()
     dec.close()
+    return {"tokens_per_s": round(decoded / (ms_max / 1e3), 1), "decode_tokens": decoded,
+            "prefill_tokens": prefilled, "steps": n_steps, "seconds": round(ms_max / 1e3, 3),
+            "step_latency_ms": {"p50": round(p50, 4), "p99": round(p99, 4), "max_over_ranks": world > 1},
+            "busy_s_per_rank": [round(v / 1e3, 3) for v in busy], "gpu_launches": launches,
+            "requests": requests, "slots_per_gpu": slots,
+            "how": "least-loaded split by prompt + decode positions; device time max over ranks"}
+
+
+def run_serve(args, rank, world, local):
+    """Config 5's own line (serve_config5): aggregate decode tokens/s over all GPUs."""
+    import torch
+
+    import __graft_entry__ as entry
+
+    pkg = entry.load_package()
+    from tgtts_v4_b200 import synthetic as syn
+
+    torch.cuda.set_device(local)
+    ctx = pkg.Context(local)
+    weights = syn.make_weights(syn.S05B, seed=0, as_bits=True)
+    clocks = Clocks(local)
+    r = serve_config5(pkg, syn, ctx, torch, rank, world, local, args.requests, weights, clocks)
+    result = None
+    if rank == 0:
+        c = clocks.summary()
+        n_steps = r["steps"]
+        result = {
+            "metric": SERVE_METRIC, "value": r["tokens_per_s"], "unit": "tokens/s",
+            "n_gpus": world, "steps": n_steps, "warmup": 0,
+            "ms_per_step": round(r["seconds"] * 1e3 / max(1, n_steps // world), 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: N(0,0.02) weights seed 0, N(0,1) bf16-valued prompt rows, request lengths seed 3",
+            "config": {"workload": "config 5: request-sharded serving, one weight replica per GPU, no collective",
+                       "requests": args.requests, "slots_per_gpu": r["slots_per_gpu"], "prompt": "U[64,1024]",
+                       "decode": "U[64,768]", "arrivals": "Poisson 4096/s (saturating)",
+                       "parallelism": f"replicas x{world}, least-loaded assignment"},
+            "prefill_tokens": r["prefill_tokens"], "decode_tokens": r["decode_tokens"], "seconds": r["seconds"],
+            "step_latency_ms": r["step_latency_ms"], "busy_s_per_rank": r["busy_s_per_rank"],
+            "gpu_launches": r["gpu_launches"],
+            "clocks": {"sm_mhz": c["sm_mhz"], "sm_max_mhz": c["sm_max_mhz"], "reasons": c["reasons"]},
+        }
     ctx.close()
     return result
 

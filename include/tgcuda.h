@@ -138,10 +138,7 @@ typedef enum {
     TG_KERNEL_SILU_MUL_ROWS = 11,
     /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32) */
     TG_KERNEL_GEMM = 12,
-    /* q f32, k cache T, v cache T, at u32 -> out f32 [rows][heads hd]: ATTENTION_SPLIT and
-     * ATTENTION_COMBINE in one dispatch, a thread-block cluster per (row, kv head) whose blocks
-     * keep their chunks' partials in shared memory; the same results bit for bit */
-    TG_KERNEL_ATTENTION_DECODE = 13,
+    /* 13: not used (an earlier fused split + combine, measured slower than the two dispatches) */
     /* a bf16 [m][k], b bf16 [2 inner][k] with gate and up rows interleaved in blocks of 128
      * (gate rows i..i+127, then up rows i..i+127, i = 0, 128, ...) -> out bf16 [m][inner] =
      * SiLU(gate) up of a b^T, in the tcgen05 GEMM's epilogue     gemm.mlir + silu_mul_rows.comp */

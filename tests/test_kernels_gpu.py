@@ -90,7 +90,10 @@ def test_stream_read_reads_every_word(pkg, ctx):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
-def test_fused_decode_attention_equals_split_and_combine(pkg, ctx, syn, dtype):
+def test_decode_attention_split_and_combine_against_f64(pkg, ctx, syn, dtype):
+    """attention_split + attention_combine (attention_split.comp, attention_combine.comp) over
+    rows at chunk edges and a spare row: the same bits on a second run, and softmax attention in
+    f64 for a live row within 1e-5 (glsl.rs:617-649 holds its attention to a bound of that order)."""
     rows, cap = 5, 256
     shape = pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=1, capacity=cap)
     rng = np.random.default_rng(9)
@@ -108,28 +111,27 @@ def test_fused_decode_attention_equals_split_and_combine(pkg, ctx, syn, dtype):
     n = rows * heads * hd
     outs = []
     for _ in range(2):
-        a, b = pkg.Memory(ctx, n * 4), pkg.Memory(ctx, n * 4)
+        a = pkg.Memory(ctx, n * 4)
         a.write(np.zeros(n, np.float32))
-        b.write(np.zeros(n, np.float32))
         p = pkg.params(shape, dtype, rows=rows, slots=rows)
         common = [(mq, 0, q.nbytes), (mk, 0, k.nbytes), (mv, 0, v.nbytes), (mat, 0, words.nbytes),
                   (po, 0, po.nbytes), (pml, 0, pml.nbytes)]
         pkg.dispatch_once(ctx, "attention_split", p, common)
         pkg.dispatch_once(ctx, "attention_combine", p, [(mat, 0, words.nbytes), (po, 0, po.nbytes),
                                                         (pml, 0, pml.nbytes), (a, 0, n * 4)])
-        pkg.dispatch_once(ctx, "attention_decode", p, common[:4] + [(b, 0, n * 4)])
-        outs.append((a.read(np.float32, n), b.read(np.float32, n)))
-    for split_combine, fused in outs:
-        assert np.array_equal(split_combine, fused)
-    # Against softmax attention in f64 for a live row (row 2 at position 64, slot 2).
+        outs.append(a.read(np.float32, n))
+    assert np.array_equal(outs[0], outs[1])
+    # Against softmax attention in f64 for live rows at chunk edges: row 2 at position 64 (the first
+    # position of the second chunk), row 1 at 63 (the last of the first), slot = row.
     kf = syn.bf16_to_f32(k) if dtype == "bf16" else k
     vf = syn.bf16_to_f32(v) if dtype == "bf16" else v
-    got = outs[0][1].reshape(rows, heads, hd)
-    for h in (0, 9):
-        s = kf[2, h // 8, :65].astype(np.float64) @ q[2, h].astype(np.float64) / 8.0
-        e = np.exp(s - s.max())
-        want = (e / e.sum()) @ vf[2, h // 8, :65].astype(np.float64)
-        assert np.max(np.abs(got[2, h] - want)) < 1e-5
+    got = outs[0].reshape(rows, heads, hd)
+    for r, pos in ((2, 64), (1, 63), (4, 255)):
+        for h in (0, 9):
+            s = kf[r, h // 8, :pos + 1].astype(np.float64) @ q[r, h].astype(np.float64) / 8.0
+            e = np.exp(s - s.max())
+            want = (e / e.sum()) @ vf[r, h // 8, :pos + 1].astype(np.float64)
+            assert np.max(np.abs(got[r, h] - want)) < 1e-5, (r, pos, h)
 
 
 @pytest.mark.parametrize("m,inner,k", [(200, 256, 256), (512, 4096, 1024)])

@@ -94,7 +94,7 @@ RES_DEVICE, RES_UPLOAD, RES_READBACK = 0, 1, 2
 KERNELS = {
     "rmsnorm": 0, "gemv_qkv_rope": 1, "attention_split": 2, "attention_combine": 3,
     "gemv_residual": 4, "gemv_gate_up": 5, "stream_read": 6, "norm_rows": 7, "add_norm_rows": 8,
-    "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12, "attention_decode": 13,
+    "rope_rows": 9, "attention_rows": 10, "silu_mul_rows": 11, "gemm": 12,
     "gemm_silu": 14, "attention_rows_tc": 15, "gemm_qkv_rope": 16, "gemv_linear": 17,
     "local_norm": 18, "local_partial": 19, "local_gate_up": 20, "local_attention": 21,
     "local_add_norm": 22, "local_rows": 23, "local_embed": 24, "cfm_noise": 25, "dit_euler": 26,

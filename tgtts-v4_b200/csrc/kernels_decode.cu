@@ -8,7 +8,6 @@
 // the output takes the 16-byte vectors l, l + 32, ... in order, each element by one fused
 // multiply-add, then the xor butterfly joins the lanes - never on how many rows run beside it or
 // how the rows are cut over blocks. Norms are summed by tg::warp_rms_scale in every kernel.
-#include <cooperative_groups.h>
 
 #include <algorithm>
 
@@ -18,8 +17,6 @@
 namespace tg {
 
 constexpr int GEMV_WARPS = 8;
-// The blocks of a decode-attention cluster (the portable maximum).
-constexpr int ATTN_CLUSTER = 8;
 constexpr int GEMV_THREADS = GEMV_WARPS * 32;
 
 // The vectors of the batch a GEMV block multiplies are staged in shared memory in f32 (the
@@ -471,31 +468,6 @@ TG_DEVICE float join_chunks(const float *o, size_t stride, const float *w, int n
     return acc;
 }
 
-// attention_combine.comp:29-58 for `n_heads` heads from `first_head` of row b: joins chunks
-// 0 .. n - 1 in order - their largest maximum, the rescaled sums, and the division - into out (f32).
-TG_DEVICE void attention_join(const tg_params &p, const float *__restrict__ po, const float *__restrict__ pml,
-                              int b, int first_head, int n_heads, int n, float *__restrict__ out) {
-    constexpr int MAXC = 64;  // chunks joined per pass of the weights below
-    const int hd = p.head_dim, chunks = attn_chunks(p.capacity);
-    for (int i = threadIdx.x; i < n_heads * hd; i += blockDim.x) {
-        const int h = first_head + i / hd, d = i % hd;
-        const float *ml = pml + ((size_t)b * p.heads + h) * chunks * 2;
-        const float *o = po + ((size_t)b * p.heads + h) * chunks * hd;
-        float m = -INFINITY;
-        for (int c = 0; c < n; c++) m = fmaxf(m, __ldcg(ml + 2 * c));
-        float total = 0.0f;
-        for (int c = 0; c < n; c++) total = __fmaf_rn(__ldcg(ml + 2 * c + 1), expf(__ldcg(ml + 2 * c) - m), total);
-        float acc = 0.0f;
-        for (int c0 = 0; c0 < n; c0 += MAXC) {
-            float w[MAXC];
-            const int nc = min(MAXC, n - c0);
-            for (int c = 0; c < nc; c++) w[c] = expf(__ldcg(ml + 2 * (c0 + c)) - m);
-            acc = join_chunks(o + (size_t)c0 * hd + d, hd, w, nc, acc);
-        }
-        out[((size_t)b * p.heads + h) * hd + d] = __fdiv_rn(acc, total);
-    }
-}
-
 static size_t attention_smem(const tg_params &p) {
     const size_t group = p.heads / p.kv_heads, hd = p.head_dim, C = ATTN_CHUNK;
     return sizeof(float) * (group * hd + C * (hd + 4) + C * hd + group * C);
@@ -557,70 +529,6 @@ __global__ void __launch_bounds__(128)
     const float *o = po + ((size_t)b * p.heads + h) * chunks * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x)
         out[((size_t)b * p.heads + h) * hd + d] = __fdiv_rn(join_chunks(o + d, hd, w, n), total_s);
-}
-
-// Split and combine in one kernel, as a thread-block cluster: the ATTN_CLUSTER blocks of cluster
-// (b, kv) take chunks r, r + ATTN_CLUSTER, ... of row b's positions (block r), keep each chunk's
-// partials in their own shared memory, and after a cluster barrier block h < GROUP joins query
-// head h's chunks in chunk order, reading the other blocks' partials over distributed shared
-// memory. The same sums in the same order as attention_split + attention_combine, so the same bits.
-template <typename T>
-__global__ void __launch_bounds__(128)
-    attention_decode_kernel(tg_params p, const float *__restrict__ q, const T *__restrict__ kc,
-                            const T *__restrict__ vc, const uint32_t *__restrict__ at, float *__restrict__ out) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cluster = cg::this_cluster();
-    extern __shared__ __align__(128) unsigned char smem[];
-    pdl_launch_dependents();
-    const int r = (int)cluster.block_rank(), kv = blockIdx.y, b = blockIdx.z;
-    const int hd = p.head_dim, heads = p.heads, group = heads / p.kv_heads;
-    const int chunks = attn_chunks(p.capacity), mine = (chunks + ATTN_CLUSTER - 1) / ATTN_CLUSTER;
-    // This block's partials: [mine][group][hd] outputs, then [mine][group][2] maxima and sums, then
-    // (16-byte aligned) the chunk's working space.
-    float *my_o = reinterpret_cast<float *>(smem);
-    float *my_ml = my_o + (size_t)mine * group * hd;
-    float *work = my_o + ((size_t)mine * group * (hd + 2) + 3) / 4 * 4;
-    uint32_t pos = 0, slot = 0;
-    const bool live = placed(at, p.rows, b, p.capacity, p.slots, pos, slot);
-    const int n = live ? (int)(pos / ATTN_CHUNK) + 1 : 0;
-    bool waited = false;
-    for (int i = 0; i < mine; i++) {
-        const int c = r + i * ATTN_CLUSTER;
-        if (c >= n) break;
-        if (i > 0) __syncthreads();
-        attention_chunk<T>(p, q, kc, vc, b, kv, c, pos, slot, my_o + (size_t)i * group * hd, (size_t)hd,
-                           my_ml + (size_t)i * group * 2, 2, work, threadIdx.x, blockDim.x);
-        waited = true;
-    }
-    if (!waited) pdl_wait();
-    cluster.sync();
-    // Join: block r takes query heads r, r + ATTN_CLUSTER, ... It first gathers the head's chunk
-    // partials from their blocks into its own shared memory (all loads at once), then takes
-    // attention_combine's sums in chunk order.
-    float *go = work;                        // [n][hd]
-    float *gml = work + (size_t)chunks * hd;  // [n][2]
-    for (int h = r; live && h < group; h += ATTN_CLUSTER) {
-        for (int i = threadIdx.x; i < n * (hd + 2); i += blockDim.x) {
-            const int c = i / (hd + 2), e = i % (hd + 2);
-            const int owner = c % ATTN_CLUSTER, at_i = c / ATTN_CLUSTER;
-            if (e < hd)
-                go[(size_t)c * hd + e] = cluster.map_shared_rank(my_o, owner)[((size_t)at_i * group + h) * hd + e];
-            else
-                gml[(size_t)c * 2 + (e - hd)] = cluster.map_shared_rank(my_ml, owner)[((size_t)at_i * group + h) * 2 + (e - hd)];
-        }
-        __syncthreads();
-        float m = -INFINITY;
-        for (int c = 0; c < n; c++) m = fmaxf(m, gml[2 * c]);
-        float total = 0.0f;
-        for (int c = 0; c < n; c++) total = __fmaf_rn(gml[2 * c + 1], expf(gml[2 * c] - m), total);
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-            float acc = 0.0f;
-            for (int c = 0; c < n; c++) acc = __fmaf_rn(go[(size_t)c * hd + d], expf(gml[2 * c] - m), acc);
-            out[((size_t)b * heads + kv * group + h) * hd + d] = __fdiv_rn(acc, total);
-        }
-        __syncthreads();
-    }
-    cluster.sync();  // no block leaves while another may still read its partials
 }
 
 // ---- the persistent decode step ----------------------------------------------------------------
@@ -1404,43 +1312,6 @@ cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, c
 cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, const float *po,
                                      const float *pml, void *out, cudaStream_t s) {
     return launch_attention_combine_chunk(p, ATTN_CHUNK, at, po, pml, out, s);
-}
-
-static size_t cluster_attention_smem(const tg_params &p) {
-    const size_t group = p.heads / p.kv_heads, hd = p.head_dim;
-    const size_t chunks = attn_chunks(p.capacity), mine = (chunks + ATTN_CLUSTER - 1) / ATTN_CLUSTER;
-    const size_t gather = chunks * (hd + 2) * sizeof(float);  // the join's copy of one head's partials
-    return sizeof(float) * ((mine * group * (hd + 2) + 3) / 4 * 4) + std::max(attention_smem(p), gather);
-}
-
-template <typename T>
-static cudaError_t decode_attention_t(const tg_params &p, const void *q, const void *kc, const void *vc,
-                                      const uint32_t *at, void *out, cudaStream_t s) {
-    const size_t smem = cluster_attention_smem(p);
-    auto kern = attention_decode_kernel<T>;
-    cudaError_t e = with_smem(kern, smem);
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(ATTN_CLUSTER, p.kv_heads, p.rows);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = ATTN_CLUSTER;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, p, (const float *)q, (const T *)kc, (const T *)vc, at, (float *)out);
-}
-
-cudaError_t launch_attention_decode(const tg_params &p, const void *q, const void *kc, const void *vc,
-                                    const uint32_t *at, void *out, cudaStream_t s) {
-    return p.dtype == TG_BF16 ? decode_attention_t<bf16>(p, q, kc, vc, at, out, s)
-                              : decode_attention_t<float>(p, q, kc, vc, at, out, s);
 }
 
 // The persistent step over a decoder's buffers: one block per SM, the ring as large as shared

@@ -294,9 +294,10 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     // A decoder of DTC_MIN_ROWS rows or more runs its projections on tcgen05 in every bucket (so that
     // a row's bits do not depend on the bucket); smaller ones run the GEMVs.
     d->tensor = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && dtc_supported(d->params(rows));
-    // Six kernels a layer by default: at batch 1 on B200 they take ~690 us a step against the
-    // persistent launch's ~970 us (tg_decoder_retune selects either).
-    TG_TRY(record_step(*d, false));
+    // A bf16 decoder of one or two rows records its step as the one persistent launch (on B200
+    // 0.61-0.63 ms a step at config 2 against 0.67-0.70 ms for six kernels a layer, the same bits);
+    // anything else as six kernels a layer. tg_decoder_retune selects either.
+    TG_TRY(record_step(*d, dtype == TG_BF16 && rows <= 2 && !d->tensor));
     *out = d.release();
     return TG_OK;
 }

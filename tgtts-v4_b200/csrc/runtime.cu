@@ -133,10 +133,6 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
                    {"c", (uint64_t)p.m * p.n * F}};
             break;
-        case TG_KERNEL_ATTENTION_DECODE:
-            out = {{"q", rows * attn * F}, {"k_cache", cache}, {"v_cache", cache}, {"at", words},
-                   {"out", rows * attn * F}};
-            break;
         case TG_KERNEL_GEMM_SILU:
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
                    {"out", (uint64_t)p.m * (p.n / 2) * T}};
@@ -194,7 +190,7 @@ static const char *kernel_name(uint32_t k) {
     static const char *names[TG_KERNEL_COUNT] = {
         "rmsnorm", "gemv_qkv_rope", "attention_split", "attention_combine", "gemv_residual",
         "gemv_gate_up", "stream_read", "norm_rows", "add_norm_rows", "rope_rows", "attention_rows",
-        "silu_mul_rows", "gemm", "attention_decode", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope", "gemv_linear",
+        "silu_mul_rows", "gemm", "(unused)", "gemm_silu", "attention_rows_tc", "gemm_qkv_rope", "gemv_linear",
         "local_norm", "local_partial", "local_gate_up", "local_attention", "local_add_norm", "local_rows",
         "local_embed", "cfm_noise", "dit_euler"};
     return k < TG_KERNEL_COUNT ? names[k] : "?";
@@ -274,7 +270,6 @@ static int check_shape(const Launch &l) {
             break;
         case TG_KERNEL_ATTENTION_SPLIT:
         case TG_KERNEL_ATTENTION_COMBINE:
-        case TG_KERNEL_ATTENTION_DECODE:
         case TG_KERNEL_ROPE_ROWS:
         case TG_KERNEL_ATTENTION_ROWS:
             if (!heads_ok()) return fail(TG_ESHAPE, "%s: %u heads over %u of %u, capacity %u (multiple of %u)", kernel_name(l.kernel), p.heads, p.kv_heads, p.head_dim, p.capacity, CAPACITY_STEP);
@@ -382,7 +377,6 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case TG_KERNEL_SILU_MUL_ROWS: e = launch_silu_mul_rows(p, U(0), F(1), b[2], s); break;
         case TG_KERNEL_GEMM: e = launch_gemm(p, b[0], b[1], F(2), err, s); break;
         case TG_KERNEL_GEMM_SILU: e = launch_gemm_silu(p, b[0], b[1], b[2], err, s); break;
-        case TG_KERNEL_ATTENTION_DECODE: e = launch_attention_decode(p, b[0], b[1], b[2], U(3), b[4], s); break;
         case KERNEL_DECODE_STEP: e = launch_decode_step(l.step, sm_count, s); break;
         case KERNEL_DTC_QKV_ROPE: e = launch_dtc_qkv_rope(p, F(0), F(1), b[2], F(3), F(4), U(5), F(6), b[7], b[8], err, s); break;
         case KERNEL_DTC_GATE_UP: e = launch_dtc_gate_up(p, F(0), F(1), b[2], F(3), err, s); break;

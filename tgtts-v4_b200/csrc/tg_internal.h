@@ -145,8 +145,6 @@ cudaError_t launch_gemv_residual(const tg_params &p, const void *x, const void *
 cudaError_t launch_gemv_gate_up(const tg_params &p, const float *x, const float *g,
                                 const void *w, void *out, uint32_t *err, cudaStream_t s);
 // Split and combine in one kernel: a thread-block cluster per (row, kv head).
-cudaError_t launch_attention_decode(const tg_params &p, const void *q, const void *kc, const void *vc,
-                                    const uint32_t *at, void *out, cudaStream_t s);
 cudaError_t launch_stream_read(const tg_params &p, const uint32_t *data, uint32_t *out,
                                cudaStream_t s, int sm_count);
 cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
