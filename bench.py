@@ -165,6 +165,15 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def sustained_tflops():
+    """MEASURED_PEAKS.json's sustained bf16 rate (a seconds-long GEMM loop under the power cap): the
+    denominator for kernels timed inside a long program, such as the prefill's GEMMs."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()).get("bf16_tflops_sustained")
+    return None
+
+
 def stream_ctx(ctx):
     import torch
 
@@ -375,6 +384,8 @@ def side_measurements(pkg, syn, ctx, torch, tc_peak, peak_kind, weights):
     out["prefill_c4"] = {"rows": rows, "tokens_per_s": round(rows / (ns / 1e9), 1), "ms": round(ns / 1e6, 3),
                          "gemm_tflops": round(gemm_flops / gemm_ns / 1e3, 1),
                          "gemm_frac_of_peak": round(gemm_flops / gemm_ns / 1e3 / tc_peak, 4),
+                         "gemm_frac_of_sustained_peak": (round(gemm_flops / gemm_ns / 1e3 / sustained_tflops(), 4)
+                                                         if sustained_tflops() else None),
                          "gate_up_gemm_tflops": round(gu_flops / gu_ns / 1e3, 1),
                          "peak_tflops": tc_peak, "peak_source": peak_kind,
                          "share": {k: round(v / sum(per.values()), 4) for k, v in sorted(per.items(), key=lambda kv: -kv[1])}}
