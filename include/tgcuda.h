@@ -136,7 +136,9 @@ typedef enum {
     /* at u32, c f32 [rows][2 inner] (columns in gate_up's interleaved order) -> out T [rows][inner]
      *                                                                           silu_mul_rows.comp */
     TG_KERNEL_SILU_MUL_ROWS = 11,
-    /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32) */
+    /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32)
+     * params.flags bit 0: b is constant for the program (a weight), so that its first tiles may be
+     * loaded while the kernel before is still running (programmatic dependent launch) */
     TG_KERNEL_GEMM = 12,
     /* 13: not used (an earlier fused split + combine, measured slower than the two dispatches) */
     /* a bf16 [m][k], b bf16 [2 inner][k] with gate and up rows interleaved in blocks of 128
@@ -346,19 +348,22 @@ int tg_decoder_copy_out(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m,
 int tg_decoder_copy_in(tg_decoder *d, uint32_t slot, uint32_t count, tg_mem *m, uint64_t offset);
 /* Decoder::retuned (decode.rs:874-890): records the step again over the same weights and cache, as
  * one persistent launch (persistent != 0; batches of up to 2 rows) or as six kernels a layer, timed
- * per dispatch when `timed`. Both give the same results bit for bit. A new decoder starts recorded
- * as kernels. TG_ESHAPE when the persistent step does not take the decoder (it is then left
- * recorded as kernels). */
+ * per dispatch when `timed`. Both give the same results bit for bit. A new bf16 decoder of one or
+ * two rows starts recorded as the persistent launch, any other as kernels. TG_ESHAPE when the
+ * persistent step does not take the decoder (it is then left recorded as kernels). */
 int tg_decoder_retune(tg_decoder *d, int persistent, int timed);
 /* 1 when the decoder's step is the persistent launch. */
 int tg_decoder_persistent(const tg_decoder *d);
-/* 1 when the decoder's projections run on tcgen05 (bf16 decoders of 16 rows or more, in every row
- * bucket), 0 when they run as GEMVs on the CUDA cores. */
+/* How the decoder's projections run (bf16 decoders of 16 rows or more run on tcgen05 in every row
+ * bucket): 1 as the prefill's tcgen05 GEMMs over bf16 activations (the step the prefill chain of
+ * prefill.rs:318-411 over one-position runs, with the decode attention), 2 as tcgen05 split-K
+ * clusters over f32 activations split into bf16 hi and lo, 0 as GEMVs on the CUDA cores. */
 int tg_decoder_tensor(const tg_decoder *d);
-/* Records the step again with its projections on tcgen05 (tensor != 0) or as GEMVs, over the same
- * weights and cache. The two give results within their roundings of each other, not the same
- * bits: a decoder that checks a request against its run beside others uses the family those ran
- * in. TG_ESHAPE when tcgen05 does not take the decoder's dtype or shape. */
+/* Records the step again with its projections as `tensor` names (1: tcgen05 GEMMs, falling back to
+ * split-K clusters where the GEMMs do not take the shape; 2: split-K clusters; 0: GEMVs), over the
+ * same weights and cache. The families give results within their roundings of each other, not the
+ * same bits: a decoder that checks a request against its run beside others uses the family those
+ * ran in. TG_ESHAPE when the family asked for does not take the decoder's dtype or shape. */
 int tg_decoder_set_tensor(tg_decoder *d, int tensor);
 /* The weight bytes one step reads at this dtype (Shape::weight_bytes at its element size). */
 uint64_t tg_decoder_weight_bytes(const tg_decoder *d);

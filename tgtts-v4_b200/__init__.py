@@ -786,10 +786,17 @@ class Decoder:
         """True when the projections run on tcgen05 (bf16 decoders of 16 rows or more)."""
         return bool(library().tg_decoder_tensor(self.handle))
 
-    def with_tensor(self, on: bool = True) -> "Decoder":
-        """Records the step again with its projections on tcgen05 (or as GEMVs); returns self."""
-        check(library().tg_decoder_set_tensor(self.handle, int(on)))
+    def with_tensor(self, on: bool = True, split_k: bool = False) -> "Decoder":
+        """Records the step again with its projections on tcgen05 (or as GEMVs); returns self. On
+        tcgen05 they run as the prefill's GEMMs, or with `split_k` as split-K clusters over hi/lo
+        activations."""
+        check(library().tg_decoder_set_tensor(self.handle, 2 if (on and split_k) else int(on)))
         return self
+
+    @property
+    def split_k(self) -> bool:
+        """True when the tcgen05 projections run as split-K clusters (not as the prefill's GEMMs)."""
+        return bool(library().tg_decoder_tensor(self.handle) == 2)
 
     def _x(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)

@@ -13,6 +13,8 @@
 // warps (four consecutive chunks of one row and KV head); each warp streams its chunk's keys and
 // values into its own shared memory with cp.async: the positions before the row's (written by
 // earlier steps) before the wait on the kernel before, the row's own position after it.
+#include <type_traits>
+
 #include "mma_common.cuh"
 #include "tg_internal.h"
 
@@ -36,10 +38,11 @@ TG_DEVICE void split_pack(float x0, float x1, uint32_t &hi, uint32_t &lo) {
 
 // SUB sub-chunks of ATTN_CHUNK positions a warp (a partial covers ATTN_CHUNK SUB positions): the
 // warp walks them in order with an online softmax (the running maximum, the sum and the output
-// rescaled as the maximum grows), so the partial is the same as one chunk's would be.
-template <int SUB>
+// rescaled as the maximum grows), so the partial is the same as one chunk's would be. QT is q's
+// type: f32 (split into hi + lo) or bf16 (already a bf16 value: the hi part alone, one MMA a step).
+template <int SUB, typename QT>
 __global__ void __launch_bounds__(AM_WARPS * 32)
-    attention_split_mma_kernel(tg_params p, const float *__restrict__ q, const bf16 *__restrict__ kc,
+    attention_split_mma_kernel(tg_params p, const QT *__restrict__ q, const bf16 *__restrict__ kc,
                                const bf16 *__restrict__ vc, const uint32_t *__restrict__ at, float *__restrict__ po,
                                float *__restrict__ pml) {
     using namespace fa;
@@ -82,13 +85,26 @@ __global__ void __launch_bounds__(AM_WARPS * 32)
         cp_async_commit();
     }
     // q of the group's heads (rows g < group; rows g + 8 and past the group are zero), hi and lo.
+    constexpr bool QBF = std::is_same<QT, bf16>::value;
     uint32_t qh[4][4], ql[4][4];
-    const float *qg = q + ((size_t)b * heads + kv * group) * HD;
+    const QT *qg = q + ((size_t)b * heads + kv * group) * HD;
 #pragma unroll
     for (int s = 0; s < 4; s++) {
 #pragma unroll
         for (int r = 0; r < 4; r++) qh[s][r] = ql[s][r] = 0u;
         const int row0 = g, row1 = g + 8;
+        if constexpr (QBF) {
+            auto pair = [&](int row, int col) { return __ldcg(reinterpret_cast<const unsigned int *>(qg + row * HD + col)); };
+            if (row0 < group) {
+                qh[s][0] = pair(row0, 16 * s + 2 * t4);
+                qh[s][2] = pair(row0, 16 * s + 8 + 2 * t4);
+            }
+            if (row1 < group) {
+                qh[s][1] = pair(row1, 16 * s + 2 * t4);
+                qh[s][3] = pair(row1, 16 * s + 8 + 2 * t4);
+            }
+            continue;
+        }
         if (row0 < group) {
             const float2 x0 = __ldcg(reinterpret_cast<const float2 *>(qg + row0 * HD + 16 * s + 2 * t4));
             const float2 x2 = __ldcg(reinterpret_cast<const float2 *>(qg + row0 * HD + 16 * s + 8 + 2 * t4));
@@ -128,9 +144,9 @@ __global__ void __launch_bounds__(AM_WARPS * 32)
                 const int mi = lane >> 3, rr = lane & 7;
                 ldmatrix_x4(kb, ks + (8 * j + (mi >> 1) * 8 + rr) * AM_ROW + s * 16 + (mi & 1) * 8);
                 mma_bf16(sc[j], qh[s], kb[0], kb[1]);
-                mma_bf16(sc[j], ql[s], kb[0], kb[1]);
+                if (!QBF) mma_bf16(sc[j], ql[s], kb[0], kb[1]);
                 mma_bf16(sc[j + 1], qh[s], kb[2], kb[3]);
-                mma_bf16(sc[j + 1], ql[s], kb[2], kb[3]);
+                if (!QBF) mma_bf16(sc[j + 1], ql[s], kb[2], kb[3]);
             }
         }
         // The sub-chunk's maxima joined with the running ones; the running sums and outputs
@@ -215,11 +231,11 @@ bool attention_split_mma_supported(const tg_params &p) {
            p.heads / p.kv_heads <= 16 && p.capacity % CAPACITY_STEP == 0;
 }
 
-cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
-                                       const uint32_t *at, float *po, float *pml, cudaStream_t s) {
-    if (!attention_split_mma_supported(p)) return cudaErrorInvalidValue;
+template <typename QT>
+static cudaError_t split_mma_t(const tg_params &p, const void *q, const void *kc, const void *vc, const uint32_t *at,
+                               float *po, float *pml, cudaStream_t s) {
     constexpr int SUB = DECODE_WIDE_CHUNK / ATTN_CHUNK;
-    auto kern = attention_split_mma_kernel<SUB>;
+    auto kern = attention_split_mma_kernel<SUB, QT>;
     const size_t smem = (size_t)AM_WARPS * AM_WARP_SMEM;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -234,7 +250,13 @@ cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, p, (const float *)q, (const bf16 *)kc, (const bf16 *)vc, at, po, pml);
+    return cudaLaunchKernelEx(&cfg, kern, p, (const QT *)q, (const bf16 *)kc, (const bf16 *)vc, at, po, pml);
+}
+
+cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
+                                       const uint32_t *at, float *po, float *pml, cudaStream_t s, bool q_bf16) {
+    if (!attention_split_mma_supported(p)) return cudaErrorInvalidValue;
+    return q_bf16 ? split_mma_t<bf16>(p, q, kc, vc, at, po, pml, s) : split_mma_t<float>(p, q, kc, vc, at, po, pml, s);
 }
 
 }  // namespace tg

@@ -97,7 +97,8 @@ constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
 template <int BN, int EPI = TC_EPI_F32>
 __global__ void __launch_bounds__(TC_PTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ RopeEpi re) {
+                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ RopeEpi re,
+                   int b_const) {
     using L = TcLayout<BN>;
     constexpr int S = L::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -114,6 +115,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int mt = (M + TC_BM - 1) / TC_BM, tiles = mt * (N / BN);
     const int nk = K / TC_BK;
+    pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
         gave_up = 0;
@@ -144,12 +146,24 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
     if (warp == 0) {
         if (lane == 0) {
             // Producer: k-block g (over all this block's tiles) into stage g % S once its MMAs
-            // have released it.
+            // have released it. When B is a weight (constant for the program), the first tile's
+            // first stages of B are loaded before the wait on the kernel before it, so that they
+            // stream while that kernel finishes; A, that kernel's output, after the wait.
+            const int pre = b_const ? (nk < S ? nk : S) : 0;
+            for (int kb = 0; kb < pre; kb++) {
+                mbar_arrive_expect_tx(full(kb), L::STAGE);
+                tma_load_2d(base + kb * L::STAGE + TC_A_BYTES, &map_b, kb * TC_BK, (blockIdx.x / mt) * BN, full(kb));
+            }
+            pdl_wait();
             int g = 0;
             for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
                 const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
                 for (int kb = 0; kb < nk; kb++, g++) {
                     const int s = g % S;
+                    if (g < pre) {  // B is in flight already
+                        tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
+                        continue;
+                    }
                     mbar_wait(empty(s), ((g / S) & 1) ^ 1, err, &gave_up);
                     mbar_arrive_expect_tx(full(s), L::STAGE);
                     tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
@@ -321,7 +335,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
 
 template <int BN, int EPI = TC_EPI_F32>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
-                             cudaStream_t s, const RopeEpi &re = RopeEpi{}) {
+                             cudaStream_t s, bool b_const, const RopeEpi &re = RopeEpi{}) {
     CUtensorMap ma, mb;
     if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, BN))
         return cudaErrorInvalidValue;
@@ -332,8 +346,8 @@ static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN);
-    kern<<<tiles < sms ? tiles : sms, TC_PTHREADS, TcLayout<BN>::SMEM, s>>>(ma, mb, c, M, N, K, err, re);
-    return cudaGetLastError();
+    return launch_pdl(kern, dim3(tiles < sms ? tiles : sms), dim3(TC_PTHREADS), (size_t)TcLayout<BN>::SMEM, s, ma, mb, c,
+                      M, N, K, err, re, (int)b_const);
 }
 
 cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c, uint32_t *err,
@@ -346,9 +360,18 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
         return cudaGetLastError();
     }
     if (K % TC_BK != 0) return cudaErrorInvalidValue;
-    if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s);
-    if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s);
-    if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s);
+    const bool b_const = (p.flags & 1) != 0;
+    // The widest tile that still gives the SMs work: a few rows (a batched decode step) take
+    // narrower tiles, so that more blocks stream the weights.
+    int sms = 148, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int mt = (M + TC_BM - 1) / TC_BM;
+    if (N % 256 == 0 && mt * (N / 256) * 4 >= sms) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
+    if (N % 128 == 0 && mt * (N / 128) * 4 >= sms) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
+    if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const);
+    if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
+    if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
     return cudaErrorInvalidValue;
 }
 
@@ -360,14 +383,14 @@ cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *
         N != (int)((p.heads + 2 * p.kv_heads) * p.head_dim) || p.rows != p.m)
         return cudaErrorInvalidValue;
     RopeEpi re{p, at, cosv, sinv, (bf16 *)q, (bf16 *)kc, (bf16 *)vc};
-    return launch_tc<256, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, re);
+    return launch_tc<256, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
 }
 
 cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,
                              cudaStream_t s) {
     const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
     if (p.dtype != TG_BF16 || M <= 0 || N % 256 || K % TC_BK) return cudaErrorInvalidValue;
-    return launch_tc<256, TC_EPI_SILU>(a, b, out, M, N, K, err, s);
+    return launch_tc<256, TC_EPI_SILU>(a, b, out, M, N, K, err, s, true);
 }
 
 }  // namespace tg

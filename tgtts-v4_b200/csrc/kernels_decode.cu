@@ -496,11 +496,13 @@ __global__ void __launch_bounds__(128)
 }
 
 // attention_combine.comp as a kernel of its own: block (h, b). The chunks' maxima and sums are
-// staged in shared memory in one parallel load, then folded in chunk order as attention_join does.
+// staged in shared memory in one parallel load, then folded in chunk order. The output in f32, or
+// rounded to bf16 (OT) for a tcgen05 GEMM's operand.
+template <typename OT>
 __global__ void __launch_bounds__(128)
     attention_combine_kernel(tg_params p, const uint32_t *__restrict__ at,
                              const float *__restrict__ po, const float *__restrict__ pml,
-                             float *__restrict__ out, uint32_t width) {
+                             OT *__restrict__ out, uint32_t width) {
     extern __shared__ __align__(128) unsigned char smem[];
     pdl_launch_dependents();
     pdl_wait();
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(128)
     __syncthreads();
     const float *o = po + ((size_t)b * p.heads + h) * chunks * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x)
-        out[((size_t)b * p.heads + h) * hd + d] = __fdiv_rn(join_chunks(o + d, hd, w, n), total_s);
+        out[((size_t)b * p.heads + h) * hd + d] = from_f32<OT>(__fdiv_rn(join_chunks(o + d, hd, w, n), total_s));
 }
 
 // ---- the persistent decode step ----------------------------------------------------------------
@@ -1302,11 +1304,13 @@ cudaError_t launch_attention_split(const tg_params &p, const void *q, const void
 }
 
 cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, const uint32_t *at, const float *po,
-                                           const float *pml, void *out, cudaStream_t s) {
+                                           const float *pml, void *out, cudaStream_t s, bool out_bf16) {
     dim3 grid(p.heads, p.rows);
     const int threads = p.head_dim < 128 ? p.head_dim : 128;
     const size_t smem = (size_t)3 * (attn_chunks(p.capacity)) * sizeof(float);
-    return launch_pdl(attention_combine_kernel, grid, dim3(threads), smem, s, p, at, po, pml, (float *)out, chunk);
+    if (out_bf16)
+        return launch_pdl(attention_combine_kernel<bf16>, grid, dim3(threads), smem, s, p, at, po, pml, (bf16 *)out, chunk);
+    return launch_pdl(attention_combine_kernel<float>, grid, dim3(threads), smem, s, p, at, po, pml, (float *)out, chunk);
 }
 
 cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, const float *po,

@@ -14,6 +14,8 @@ template <typename T>
 __global__ void __launch_bounds__(128)
     norm_rows_kernel(tg_params p, const uint32_t *__restrict__ at, const float *__restrict__ x,
                      const float *__restrict__ g, T *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= (int)p.rows) return;
     const int k = p.hidden;
@@ -37,6 +39,8 @@ __global__ void __launch_bounds__(128)
     add_norm_rows_kernel(tg_params p, const uint32_t *__restrict__ at, const float *__restrict__ c,
                          const float *__restrict__ res, const float *__restrict__ g,
                          float *__restrict__ sum, void *__restrict__ normed) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= (int)p.rows) return;
     const int k = p.hidden;
@@ -430,11 +434,8 @@ __global__ void __launch_bounds__(128)
 cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
                              const float *g, void *out, cudaStream_t s) {
     const dim3 grid((p.rows + 3) / 4);
-    if (p.dtype == TG_BF16)
-        norm_rows_kernel<bf16><<<grid, 128, 0, s>>>(p, at, x, g, (bf16 *)out);
-    else
-        norm_rows_kernel<float><<<grid, 128, 0, s>>>(p, at, x, g, (float *)out);
-    return cudaGetLastError();
+    if (p.dtype == TG_BF16) return launch_pdl(norm_rows_kernel<bf16>, grid, dim3(128), 0, s, p, at, x, g, (bf16 *)out);
+    return launch_pdl(norm_rows_kernel<float>, grid, dim3(128), 0, s, p, at, x, g, (float *)out);
 }
 
 cudaError_t launch_add_norm_rows(const tg_params &p, const uint32_t *at, const float *c,
@@ -442,12 +443,10 @@ cudaError_t launch_add_norm_rows(const tg_params &p, const uint32_t *at, const f
                                  cudaStream_t s) {
     const dim3 grid((p.rows + 3) / 4);
     if (p.normed_f32)
-        add_norm_rows_kernel<float, true><<<grid, 128, 0, s>>>(p, at, c, res, g, sum, normed);
-    else if (p.dtype == TG_BF16)
-        add_norm_rows_kernel<bf16, false><<<grid, 128, 0, s>>>(p, at, c, res, g, sum, normed);
-    else
-        add_norm_rows_kernel<float, false><<<grid, 128, 0, s>>>(p, at, c, res, g, sum, normed);
-    return cudaGetLastError();
+        return launch_pdl(add_norm_rows_kernel<float, true>, grid, dim3(128), 0, s, p, at, c, res, g, sum, normed);
+    if (p.dtype == TG_BF16)
+        return launch_pdl(add_norm_rows_kernel<bf16, false>, grid, dim3(128), 0, s, p, at, c, res, g, sum, normed);
+    return launch_pdl(add_norm_rows_kernel<float, false>, grid, dim3(128), 0, s, p, at, c, res, g, sum, normed);
 }
 
 cudaError_t launch_rope_rows(const tg_params &p, const uint32_t *at, const float *c,

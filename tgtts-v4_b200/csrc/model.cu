@@ -105,6 +105,80 @@ static void push(std::vector<Launch> &v, uint32_t kernel, const tg_params &p, co
     v.push_back(std::move(l));
 }
 
+// The GEMM family's step for R rows (bf16, R >= DTC_MIN_ROWS): the prefill's chain of kernels
+// (prefill.rs:318-411) over rows that are each a run of one position in its own slot, with the
+// decode attention in place of attention_rows: per layer the q/k/v GEMM with RoPE and the cache
+// append in its epilogue, attention_split (mma.sync) and attention_combine, the o GEMM, the
+// residual add with the post-attention norm, the gate/up GEMM with SiLU-mul in its epilogue, the
+// down GEMM, and the residual add with the next layer's input norm (the last layer's with the final
+// norm, in f32). Activations between them are bf16 where a GEMM reads them, the residual stream f32.
+// Every GEMM's B is a weight, so its first tiles stream while the kernel before it finishes.
+static std::vector<Launch> decode_gemm_launches(tg_decoder &d, uint32_t R) {
+    const tg_params base = d.params(R);
+    const tg_shape &s = d.shape;
+    const uint64_t T = d.esize, F = 4, H = s.hidden, I = s.inner, hd = s.head_dim, heads = s.heads;
+    const uint64_t W = d.width(), A = d.attn(), chunks = attn_chunks(s.capacity);
+    const uint64_t words = (d.slots > 1 ? 2 : 1) * (uint64_t)R * 4;
+    const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
+    std::vector<Launch> v;
+    auto gemm = [&](uint32_t kernel, const char *label, void *a, void *b, void *c, uint64_t c_bytes, uint64_t n,
+                    uint64_t k) {
+        tg_params g = base;
+        g.m = R;
+        g.n = (uint32_t)n;
+        g.k = (uint32_t)k;
+        g.flags = 1;
+        push(v, kernel, g, label, {{a, R * k * T}, {b, n * k * T}, {c, c_bytes}});
+    };
+    push(v, TG_KERNEL_NORM_ROWS, base, "input_norm",
+         {{d.words.ptr(), words}, {d.x_in.ptr(), R * H * F}, {d.w(d.layer[0].in_norm), H * F}, {d.g_normed.ptr(), R * H * T}});
+    for (uint32_t l = 0; l < s.layers; l++) {
+        const LayerOffsets &o = d.layer[l];
+        char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
+        {
+            tg_params g = base;
+            g.m = R;
+            g.n = (uint32_t)W;
+            g.k = (uint32_t)H;
+            push(v, TG_KERNEL_GEMM_QKV_ROPE, g, "qkv_proj",
+                 {{d.g_normed.ptr(), R * H * T}, {d.w(o.qkv), W * H * T}, {d.words.ptr(), words}, {d.cos.ptr(), table},
+                  {d.sin.ptr(), table}, {d.g_q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
+        }
+        push(v, KERNEL_ATTN_SPLIT_MMA_BQ, base, "attention_split",
+             {{d.g_q.ptr(), R * A * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}, {d.words.ptr(), words},
+              {d.po.ptr(), R * heads * chunks * hd * F}, {d.pml.ptr(), R * heads * chunks * 2 * F}});
+        push(v, KERNEL_ATTN_COMBINE_WIDE_BF, base, "attention_combine",
+             {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
+              {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.g_att.ptr(), R * A * F}});
+        gemm(TG_KERNEL_GEMM, "o_proj", d.g_att.ptr(), d.w(o.o), d.g_proj.ptr(), R * H * F, H, A);
+        push(v, TG_KERNEL_ADD_NORM_ROWS, base, "add_norm",
+             {{d.words.ptr(), words}, {d.g_proj.ptr(), R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
+              {d.mid.ptr(), R * H * F}, {d.g_normed.ptr(), R * H * T}});
+        gemm(TG_KERNEL_GEMM_SILU, "gate_up", d.g_normed.ptr(), d.w(o.gate_up), d.g_mlp.ptr(), R * I * T, 2 * I, H);
+        gemm(TG_KERNEL_GEMM, "down_proj", d.g_mlp.ptr(), d.w(o.down), d.g_proj.ptr(), R * H * F, H, I);
+        const bool last = l + 1 == s.layers;
+        tg_params an = base;
+        an.normed_f32 = last ? 1 : 0;
+        push(v, TG_KERNEL_ADD_NORM_ROWS, an, last ? "final_norm" : "add_norm",
+             {{d.words.ptr(), words}, {d.g_proj.ptr(), R * H * F}, {d.mid.ptr(), R * H * F},
+              {d.w(last ? d.final_norm : d.layer[l + 1].in_norm), H * F}, {d.h.ptr(), R * H * F},
+              {last ? d.out.ptr() : d.g_normed.ptr(), R * H * (last ? F : T)}});
+    }
+    return v;
+}
+
+// Decoders of at least this many rows run the GEMM family by default.
+constexpr uint32_t GEMM_MIN_ROWS = 128;
+
+// Whether a decoder's shape and rows take the GEMM family (the prefill GEMMs' tiles and epilogues,
+// the batched attention).
+static bool gemm_family_supported(const tg_decoder &d) {
+    const tg_shape &s = d.shape;
+    return d.dtype == TG_BF16 && d.rows >= DTC_MIN_ROWS && d.width() % 256 == 0 && (2 * (uint64_t)s.inner) % 256 == 0 &&
+           s.hidden % 64 == 0 && s.inner % 64 == 0 && d.attn() % 64 == 0 && 256 % s.head_dim == 0 &&
+           attention_split_mma_supported(d.params(d.rows));
+}
+
 // decode_batch_graph (decode.rs:457-736): per layer qkv_rope, attention_split, attention_combine,
 // o_proj (+ residual), gate_up (+ norm, SiLU), down_proj (+ residual); then the final norm.
 static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
@@ -147,6 +221,7 @@ static std::vector<Launch> decode_launches(tg_decoder &d, uint32_t R) {
     const uint64_t chunks = attn_chunks(s.capacity);
     const uint64_t words = (d.slots > 1 ? 2 : 1) * (uint64_t)R * 4;
     const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
+    if (d.tensor && d.gemm) return decode_gemm_launches(d, R);
     for (uint32_t l = 0; l < s.layers; l++) {
         const LayerOffsets &o = d.layer[l];
         char *in = l == 0 ? d.x_in.ptr() : d.h.ptr();
@@ -293,7 +368,20 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
     // A decoder of DTC_MIN_ROWS rows or more runs its projections on tcgen05 in every bucket (so that
     // a row's bits do not depend on the bucket); smaller ones run the GEMVs.
-    d->tensor = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && dtc_supported(d->params(rows));
+    // Both tcgen05 forms are recorded on request; by default a decoder of GEMM_MIN_ROWS rows or
+    // more runs the GEMMs (on B200 a 128-row step: 2.41 ms against 3.30 as split-K clusters) and a
+    // smaller one the split-K clusters (16 rows: 1.21 ms against 1.85; 64 rows: 2.00 against 2.07).
+    const bool gemm_ok = gemm_family_supported(*d);
+    const bool dtc_ok = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && dtc_supported(d->params(rows));
+    d->gemm = gemm_ok && (rows >= GEMM_MIN_ROWS || !dtc_ok);
+    d->tensor = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && (gemm_ok || dtc_ok);
+    if (gemm_ok) {
+        TG_TRY(d->g_normed.alloc(ctx, R * H * 2));
+        TG_TRY(d->g_q.alloc(ctx, R * d->attn() * F));  // bf16 values, sized as the checks size f32 q
+        TG_TRY(d->g_att.alloc(ctx, R * d->attn() * F));
+        TG_TRY(d->g_proj.alloc(ctx, R * H * F));
+        TG_TRY(d->g_mlp.alloc(ctx, R * I * 2));
+    }
     // A bf16 decoder of one or two rows records its step as the one persistent launch (on B200
     // 0.61-0.63 ms a step at config 2 against 0.67-0.70 ms for six kernels a layer, the same bits);
     // anything else as six kernels a layer. tg_decoder_retune selects either.
@@ -342,14 +430,18 @@ extern "C" int tg_decoder_retune(tg_decoder *d, int persistent, int timed) {
 
 extern "C" int tg_decoder_persistent(const tg_decoder *d) { return d && d->persistent ? 1 : 0; }
 
-extern "C" int tg_decoder_tensor(const tg_decoder *d) { return d && d->tensor ? 1 : 0; }
+extern "C" int tg_decoder_tensor(const tg_decoder *d) { return d && d->tensor ? (d->gemm ? 1 : 2) : 0; }
 
 extern "C" int tg_decoder_set_tensor(tg_decoder *d, int tensor) {
     if (!d) return fail(TG_EINVAL, "null decoder");
-    if (tensor && !(d->dtype == TG_BF16 && dtc_supported(d->params(d->rows))))
+    if (tensor < 0 || tensor > 2) return fail(TG_EINVAL, "tg_decoder_set_tensor: %d", tensor);
+    if (tensor == 1 && !(d->g_normed.m || (d->dtype == TG_BF16 && dtc_supported(d->params(d->rows)))))
         return fail(TG_ESHAPE, "no tcgen05 projections for this decoder's dtype or shape");
+    if (tensor == 2 && !(d->dtype == TG_BF16 && dtc_supported(d->params(d->rows))))
+        return fail(TG_ESHAPE, "no split-K tcgen05 projections for this decoder's dtype or shape");
     TG_CUDA(cudaSetDevice(d->ctx->device));
     d->tensor = tensor != 0;
+    d->gemm = tensor == 1 && d->g_normed.m != nullptr;
     return record_step(*d, d->persistent && !d->tensor);
 }
 
@@ -677,6 +769,7 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
         g.m = rows;
         g.n = (uint32_t)n;
         g.k = (uint32_t)k;
+        g.flags = 1;  // b is a weight: its first tiles stream while the kernel before finishes
         push(v, TG_KERNEL_GEMM, g, label, {{a, R * k * T}, {b, n * k * T}, {c, R * n * F}});
     };
     for (uint32_t l = 0; l < s.layers; l++) {

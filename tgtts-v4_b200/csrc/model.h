@@ -109,6 +109,10 @@ struct tg_decoder {
     tg::Owned po, pml, psync, offs;  // the persistent step's attention partials, barrier words, weight offsets
     bool persistent = false;         // the step is one persistent launch (rows <= 2), else six kernels a layer
     bool tensor = false;             // the projections run on tcgen05 (rows >= DTC_MIN_ROWS, bf16)
+    // With `tensor`: the projections as the prefill's tcgen05 GEMMs (a weight tile a block over the
+    // whole of K, bf16 activations), else as split-K clusters over f32 activations split into hi/lo.
+    bool gemm = false;
+    tg::Owned g_normed, g_q, g_att, g_proj, g_mlp;  // the GEMM family's activations
     tg::Owned stage_x, stage_out;  // pinned host staging
     cudaEvent_t out_done = nullptr;  // recorded after a step's output copy (tg_decoder_step_rows_n)
     tg::StageRing word_ring;                    // placements of device-resident steps

@@ -325,8 +325,10 @@ static uint32_t table_kernel(uint32_t k) {
         case KERNEL_DTC_QKV_ROPE: return TG_KERNEL_GEMV_QKV_ROPE;
         case KERNEL_DTC_GATE_UP: return TG_KERNEL_GEMV_GATE_UP;
         case KERNEL_DTC_RESIDUAL: return TG_KERNEL_GEMV_RESIDUAL;
-        case KERNEL_ATTN_SPLIT_MMA: return TG_KERNEL_ATTENTION_SPLIT;
-        case KERNEL_ATTN_COMBINE_WIDE: return TG_KERNEL_ATTENTION_COMBINE;
+        case KERNEL_ATTN_SPLIT_MMA:
+        case KERNEL_ATTN_SPLIT_MMA_BQ: return TG_KERNEL_ATTENTION_SPLIT;
+        case KERNEL_ATTN_COMBINE_WIDE:
+        case KERNEL_ATTN_COMBINE_WIDE_BF: return TG_KERNEL_ATTENTION_COMBINE;
         default: return k;
     }
 }
@@ -335,7 +337,8 @@ int check_launch(const Launch &l0) {
     if (l0.kernel == KERNEL_DECODE_STEP) return TG_OK;  // recorded by the decoder over its own buffers
     Launch l = l0;
     l.kernel = table_kernel(l0.kernel);
-    const bool wide = l0.kernel == KERNEL_ATTN_SPLIT_MMA || l0.kernel == KERNEL_ATTN_COMBINE_WIDE;
+    const bool wide = l0.kernel == KERNEL_ATTN_SPLIT_MMA || l0.kernel == KERNEL_ATTN_COMBINE_WIDE ||
+                      l0.kernel == KERNEL_ATTN_SPLIT_MMA_BQ || l0.kernel == KERNEL_ATTN_COMBINE_WIDE_BF;
     if (wide ? !attention_split_mma_supported(l.p) : (l.kernel != l0.kernel && !dtc_supported(l.p)))
         return fail(TG_ESHAPE, "%s: no tcgen05 plan for %u rows of this shape", l0.label.c_str(), l.p.rows);
     int st = check_shape(l);
@@ -382,6 +385,10 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case KERNEL_DTC_GATE_UP: e = launch_dtc_gate_up(p, F(0), F(1), b[2], F(3), err, s); break;
         case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
         case KERNEL_ATTN_SPLIT_MMA: e = launch_attention_split_mma(p, b[0], b[1], b[2], U(3), F(4), F(5), s); break;
+        case KERNEL_ATTN_SPLIT_MMA_BQ: e = launch_attention_split_mma(p, b[0], b[1], b[2], U(3), F(4), F(5), s, true); break;
+        case KERNEL_ATTN_COMBINE_WIDE_BF:
+            e = launch_attention_combine_chunk(p, DECODE_WIDE_CHUNK, U(0), F(1), F(2), b[3], s, true);
+            break;
         case KERNEL_ATTN_COMBINE_WIDE:
             e = launch_attention_combine_chunk(p, DECODE_WIDE_CHUNK, U(0), F(1), F(2), b[3], s);
             break;

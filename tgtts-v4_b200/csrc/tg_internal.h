@@ -74,14 +74,18 @@ constexpr uint32_t KERNEL_DTC_RESIDUAL = 1003;
 // each partial over DECODE_WIDE_CHUNK positions; and attention_combine over such partials.
 constexpr uint32_t KERNEL_ATTN_SPLIT_MMA = 1004;
 constexpr uint32_t KERNEL_ATTN_COMBINE_WIDE = 1005;
+// The same two for the GEMM-family decoder: q in bf16 (as the q/k/v GEMM's epilogue stores it; its
+// binding still sized as f32 q), the joined output in bf16 (the o GEMM's A operand; sized as f32).
+constexpr uint32_t KERNEL_ATTN_SPLIT_MMA_BQ = 1006;
+constexpr uint32_t KERNEL_ATTN_COMBINE_WIDE_BF = 1007;
 // 64: wider partials (a warp walking sub-chunks) measured slower on B200 at 16-128 rows: 2.15 ms
 // a step at 64 rows with 256 against 2.00 ms with 64.
 constexpr uint32_t DECODE_WIDE_CHUNK = 64;
 cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, const uint32_t *at, const float *po,
-                                           const float *pml, void *out, cudaStream_t s);
+                                           const float *pml, void *out, cudaStream_t s, bool out_bf16 = false);
 bool attention_split_mma_supported(const tg_params &p);
 cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
-                                       const uint32_t *at, float *po, float *pml, cudaStream_t s);
+                                       const uint32_t *at, float *po, float *pml, cudaStream_t s, bool q_bf16 = false);
 // Decoders of at least this many rows run their projections on tcgen05 (every bucket of them).
 constexpr uint32_t DTC_MIN_ROWS = 16;
 
