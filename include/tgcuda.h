@@ -138,7 +138,8 @@ typedef enum {
     TG_KERNEL_SILU_MUL_ROWS = 11,
     /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32)
      * params.flags bit 0: b is constant for the program (a weight), so that its first tiles may be
-     * loaded while the kernel before is still running (programmatic dependent launch) */
+     * loaded while the kernel before is still running (programmatic dependent launch); bit 1:
+     * narrow tiles (64 columns; GEMM_QKV_ROPE: one head), for launches of few rows */
     TG_KERNEL_GEMM = 12,
     /* 13: not used (an earlier fused split + combine, measured slower than the two dispatches) */
     /* a bf16 [m][k], b bf16 [2 inner][k] with gate and up rows interleaved in blocks of 128

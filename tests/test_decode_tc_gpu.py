@@ -19,8 +19,7 @@ def _filled(pkg, ctx, syn, rows, layers, capacity, seed, split_k=False):
     shape = syn.shape_of(cfg, capacity=capacity, layers=layers)
     w = syn.make_weights(cfg, seed=0, layers=layers, jitter_gains=True, as_bits=True)
     dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
-    if split_k:
-        dec.with_tensor(True, split_k=True)
+    dec.with_tensor(True, split_k=split_k)  # the default is the GEMMs from 128 rows, split-K below
     assert dec.tensor and dec.split_k == split_k
     dec.load(w)
     pre = pkg.Prefill(dec, max_rows=1024)
@@ -88,8 +87,7 @@ def test_tensor_and_gemv_decoders_agree(pkg, ctx, syn, split_k):
     shape = syn.shape_of(cfg, capacity=128, layers=2)
     w = syn.make_weights(cfg, seed=0, layers=2, jitter_gains=True, as_bits=True)
     big = pkg.Decoder(ctx, shape, rows=16, slots=16, dtype="bf16")
-    if split_k:
-        big.with_tensor(True, split_k=True)
+    big.with_tensor(True, split_k=split_k)
     small = pkg.Decoder(ctx, shape, rows=1, slots=16, dtype="bf16")
     assert big.tensor and big.split_k == split_k and not small.tensor
     rng = np.random.default_rng(5)
@@ -105,3 +103,13 @@ def test_tensor_and_gemv_decoders_agree(pkg, ctx, syn, split_k):
         assert m < 1e-2 and cos > 0.99999, (m, rel, cos)
     else:
         assert m <= BF16_MAX_ABS and cos >= BF16_COS, (m, rel, cos)
+
+
+def test_the_default_family_by_rows(pkg, ctx, syn):
+    """bf16 decoders of 128 rows or more run the prefill's GEMMs, of 16-127 rows split-K clusters
+    (each where it measured faster on B200), of fewer rows the GEMVs."""
+    shape = syn.shape_of(syn.S05B, capacity=128, layers=1)
+    for rows, tensor, split_k in ((1, False, False), (16, True, True), (64, True, True), (128, True, False)):
+        dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
+        assert (dec.tensor, dec.split_k) == (tensor, split_k), rows
+        dec.close()

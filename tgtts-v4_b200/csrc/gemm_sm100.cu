@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             const int row = m0 + q * 32 + lane;
             const uint32_t lane_base = tmem + lane_off + (uint32_t)(acc * BN);
             if constexpr (EPI == TC_EPI_ROPE) {
-                static_assert(BN == 256, "whole heads a tile");
+                static_assert(BN % 64 == 0, "whole heads a tile");
                 const tg_params &p = re.p;
                 const int hd = p.head_dim, half = hd / 2, heads = p.heads, kvh = p.kv_heads;
                 uint32_t pos = 0, slot = 0;
@@ -361,17 +361,16 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
     }
     if (K % TC_BK != 0) return cudaErrorInvalidValue;
     const bool b_const = (p.flags & 1) != 0;
-    // The widest tile that still gives the SMs work: a few rows (a batched decode step) take
-    // narrower tiles, so that more blocks stream the weights.
-    int sms = 148, dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int mt = (M + TC_BM - 1) / TC_BM;
-    if (N % 256 == 0 && mt * (N / 256) * 4 >= sms) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
-    if (N % 128 == 0 && mt * (N / 128) * 4 >= sms) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
-    if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const);
-    if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
+    // Narrow tiles (flags bit 1, a batched decode step's few rows): more blocks stream the weights.
+    // The tile width is the caller's choice, not the rows': a row's sums do not depend on how many
+    // rows a launch takes.
+    if (p.flags & 2) {
+        if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const);
+        return cudaErrorInvalidValue;
+    }
     if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
+    if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
+    if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const);
     return cudaErrorInvalidValue;
 }
 
@@ -383,6 +382,9 @@ cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *
         N != (int)((p.heads + 2 * p.kv_heads) * p.head_dim) || p.rows != p.m)
         return cudaErrorInvalidValue;
     RopeEpi re{p, at, cosv, sinv, (bf16 *)q, (bf16 *)kc, (bf16 *)vc};
+    // A tile holds whole heads; narrow tiles (flags bit 1, a batched decode step) one head each, so
+    // that more blocks stream the weights.
+    if ((p.flags & 2) && p.head_dim == 64) return launch_tc<64, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
     return launch_tc<256, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
 }
 

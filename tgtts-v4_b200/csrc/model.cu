@@ -127,7 +127,7 @@ static std::vector<Launch> decode_gemm_launches(tg_decoder &d, uint32_t R) {
         g.m = R;
         g.n = (uint32_t)n;
         g.k = (uint32_t)k;
-        g.flags = 1;
+        g.flags = 1 | 2;  // b a weight; narrow tiles
         push(v, kernel, g, label, {{a, R * k * T}, {b, n * k * T}, {c, c_bytes}});
     };
     push(v, TG_KERNEL_NORM_ROWS, base, "input_norm",
@@ -140,6 +140,7 @@ static std::vector<Launch> decode_gemm_launches(tg_decoder &d, uint32_t R) {
             g.m = R;
             g.n = (uint32_t)W;
             g.k = (uint32_t)H;
+            g.flags = 2;  // narrow tiles: one head a tile
             push(v, TG_KERNEL_GEMM_QKV_ROPE, g, "qkv_proj",
                  {{d.g_normed.ptr(), R * H * T}, {d.w(o.qkv), W * H * T}, {d.words.ptr(), words}, {d.cos.ptr(), table},
                   {d.sin.ptr(), table}, {d.g_q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
