@@ -59,6 +59,7 @@ def parse():
                          "serving; sweep: decode step time by batch rows; gemm: config 4's four "
                          "projection GEMMs alone; local: VoxCPM2's patch sampler and local encoder")
     ap.add_argument("--rows", type=int, default=32768, help="gemm: rows (M)")
+    ap.add_argument("--sweep-rows", default="1,16,64,128", help="sweep: the decoders' rows, comma-separated")
     ap.add_argument("--requests", type=int, default=2048, help="serve: requests over all GPUs")
     return ap.parse_args()
 
@@ -363,17 +364,28 @@ def side_measurements(pkg, syn, ctx, torch, tc_peak, peak_kind, weights):
     dec = pkg.Decoder(ctx, shape, rows=16, slots=16, dtype="bf16")
     dec.load(weights)
     rows = 16 * 2048
-    pre = pkg.Prefill(dec, max_rows=rows, timed=True)
     x = torch.randn(rows, cfg.hidden, device=f"cuda:{ctx.device}").to(torch.bfloat16).float()
     o = torch.empty_like(x)
     runs = [(0, 2048, s) for s in range(16)]
+    # The prefill's time from a program recorded without per-dispatch events (events between the
+    # dispatches would keep each kernel from starting under the one before); its shares from one
+    # recorded with them.
+    plain = pkg.Prefill(dec, max_rows=rows)
+    plain.run_batch_device(runs, x.data_ptr(), o.data_ptr())
+    ctx.synchronize()
+    times = []
+    for _ in range(3):
+        plain.run_batch_device(runs, x.data_ptr(), o.data_ptr())
+        ctx.synchronize()
+        times.append(plain.elapsed_ns())
+    plain.close()
+    pre = pkg.Prefill(dec, max_rows=rows, timed=True)
     pre.run_batch_device(runs, x.data_ptr(), o.data_ptr())
     ctx.synchronize()
-    times, per = [], {}
+    per = {}
     for _ in range(3):
         pre.run_batch_device(runs, x.data_ptr(), o.data_ptr())
         ctx.synchronize()
-        times.append(pre.elapsed_ns())
         for label, ns in pre.timings():
             per[label] = per.get(label, 0.0) + ns / 3
     ns = min(times)
@@ -703,7 +715,7 @@ def run_serve(args, rank, world, local):
 
 
 def run_sweep(args, rank, world, local):
-    """Decode step time by batch rows (1, 16, 64, 128): one decoder per size (rows = slots,
+    """Decode step time by batch rows (`--sweep-rows`, default 1, 16, 64, 128): one decoder per size (rows = slots,
     capacity 2560, positions uniform 64-2048), `--steps` device-resident steps timed with CUDA
     events on the runtime's stream after `--warmup`; the projections' family as the decoder picks
     it (GEMVs below 16 rows, tcgen05 from 16)."""
@@ -723,7 +735,7 @@ def run_sweep(args, rank, world, local):
     weights = syn.make_weights(cfg, seed=0, as_bits=True)
     stream = stream_ctx(ctx)
     out = {}
-    for rows in (1, 16, 64, 128):
+    for rows in (int(v) for v in args.sweep_rows.split(",")):
         dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
         dec.load(weights)
         pos = np.random.default_rng(2).integers(64, 2049, rows)
@@ -742,7 +754,8 @@ def run_sweep(args, rank, world, local):
         ms = e0.elapsed_time(e1) / args.steps
         kv = sum(kv_bytes(shape, int(p)) for p in pos)
         out[str(rows)] = {"ms": round(ms, 4), "tokens_per_s": round(rows / ms * 1e3, 1),
-                          "projections": "tcgen05" if dec.tensor else "gemv",
+                          "projections": ("tcgen05 split-K" if dec.split_k else "tcgen05 GEMM") if dec.tensor
+                          else "gemv",
                           "hbm_gbs": round((shape.weight_bytes(2) + kv) / (ms * 1e6), 1)}
         dec.close()
     ctx.close()

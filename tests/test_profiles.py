@@ -35,8 +35,8 @@ def test_a_summary_quotes_commands_that_run(path, monkeypatch):
     text = path.read_text()
     assert "ncu " in text or "python " in text, "no command"
     for args in _bench_commands(text):
-        if args and args[-1].startswith(">"):
-            args = args[:-1]
+        ends = [i for i, a in enumerate(args) if a in ("&&", "||", "|", ";")]
+        args = args[:ends[0]] if ends else args
         monkeypatch.setattr(sys, "argv", ["bench.py", *[a for a in args if not a.startswith(">")]])
         bench.parse()  # exits on an argument bench.py does not take
     joined = re.sub(r"\\\n\s*", " ", text)
