@@ -125,8 +125,10 @@ typedef enum {
     TG_KERNEL_STREAM_READ = 6,
     /* at u32 [2 rows], x f32, gain f32 -> out T                                   norm_rows.comp */
     TG_KERNEL_NORM_ROWS = 7,
-    /* at u32, c f32 [rows][hidden], residual f32, gain f32 -> sum f32, normed (T, or f32 when
-     * params.normed_f32)                                                      add_norm_rows.comp */
+    /* at u32, c f32 [parts][rows][hidden], residual f32, gain f32 -> sum f32, normed (T, or f32
+     * when params.normed_f32); c's parts (params.parts, 0 or 1: one; at most 16) are a GEMM's
+     * partial sums, added in part order; hidden at most 4096. params.flags bit 1: few rows (a
+     * block to a row rather than a warp; the same sums in another order)    add_norm_rows.comp */
     TG_KERNEL_ADD_NORM_ROWS = 8,
     /* at u32, c f32 [rows][(heads+2kv)hd], cos f32, sin f32 -> q T, k cache T, v cache T
      *                                                                             rope_rows.comp */
@@ -139,7 +141,9 @@ typedef enum {
     /* a T [m][k], b T [n][k] -> c f32 [m][n] = a b^T        gemm.mlir (tcgen05 for bf16, SIMT f32)
      * params.flags bit 0: b is constant for the program (a weight), so that its first tiles may be
      * loaded while the kernel before is still running (programmatic dependent launch); bit 1:
-     * narrow tiles (64 columns; GEMM_QKV_ROPE: one head), for launches of few rows */
+     * narrow tiles (64 columns; GEMM_QKV_ROPE: one head), for launches of few rows.
+     * params.parts > 1 (bf16): K in that many equal parts (k a multiple of 64 parts), c f32
+     * [parts][m][n] the partial sum over each, for ADD_NORM_ROWS to add in part order */
     TG_KERNEL_GEMM = 12,
     /* 13: not used (an earlier fused split + combine, measured slower than the two dispatches) */
     /* a bf16 [m][k], b bf16 [2 inner][k] with gate and up rows interleaved in blocks of 128
@@ -357,8 +361,9 @@ int tg_decoder_retune(tg_decoder *d, int persistent, int timed);
 int tg_decoder_persistent(const tg_decoder *d);
 /* How the decoder's projections run (bf16 decoders of 16 rows or more run on tcgen05 in every row
  * bucket): 1 as the prefill's tcgen05 GEMMs over bf16 activations (the step the prefill chain of
- * prefill.rs:318-411 over one-position runs, with the decode attention), 2 as tcgen05 split-K
- * clusters over f32 activations split into bf16 hi and lo, 0 as GEMVs on the CUDA cores. */
+ * prefill.rs:318-411 over one-position runs, with the decode attention; the default where the
+ * shape takes it), 2 as tcgen05 split-K clusters over f32 activations split into bf16 hi and lo,
+ * 0 as GEMVs on the CUDA cores. */
 int tg_decoder_tensor(const tg_decoder *d);
 /* Records the step again with its projections as `tensor` names (1: tcgen05 GEMMs, falling back to
  * split-K clusters where the GEMMs do not take the shape; 2: split-K clusters; 0: GEMVs), over the

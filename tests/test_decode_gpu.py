@@ -118,7 +118,7 @@ def test_a_row_comes_out_bit_for_bit_as_it_does_alone(pkg, ctx, syn, dtype):
                 assert np.array_equal(batched[:, i], alone[r]), (rows, r)
     if dtype == "bf16":
         # The tcgen05 projections (a 64-row decoder's own): alone and beside 63 others alike.
-        alone_tc = {r: run(1, 1, [r], tensor=True)[:, 0] for r in (0, 17, 63)}
+        alone_tc = {r: run(64, 64, [r], tensor=True)[:, 0] for r in (0, 17, 63)}
         batched = run(64, 64, list(range(64)), tensor=True)
         for r, want in alone_tc.items():
             assert np.array_equal(batched[:, r], want), ("tensor", r)

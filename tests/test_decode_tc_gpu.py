@@ -19,7 +19,7 @@ def _filled(pkg, ctx, syn, rows, layers, capacity, seed, split_k=False):
     shape = syn.shape_of(cfg, capacity=capacity, layers=layers)
     w = syn.make_weights(cfg, seed=0, layers=layers, jitter_gains=True, as_bits=True)
     dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
-    dec.with_tensor(True, split_k=split_k)  # the default is the GEMMs from 128 rows, split-K below
+    dec.with_tensor(True, split_k=split_k)  # the default is the GEMMs
     assert dec.tensor and dec.split_k == split_k
     dec.load(w)
     pre = pkg.Prefill(dec, max_rows=1024)
@@ -41,9 +41,12 @@ def _filled(pkg, ctx, syn, rows, layers, capacity, seed, split_k=False):
 
 
 @pytest.mark.parametrize("split_k", [False, True], ids=["gemm", "split_k"])
-@pytest.mark.parametrize("rows", [16, 64, 128])
-def test_tensor_decoder_rows_are_the_same_bits_in_every_bucket(pkg, ctx, syn, rows, split_k):
-    cfg, shape, w, dec, pre, lens, _ = _filled(pkg, ctx, syn, rows, layers=2, capacity=256, seed=rows, split_k=split_k)
+@pytest.mark.parametrize("rows,capacity", [(16, 256), (64, 256), (128, 256), (64, 1280)])
+def test_tensor_decoder_rows_are_the_same_bits_in_every_bucket(pkg, ctx, syn, rows, capacity, split_k):
+    """Contexts up to half the capacity: at 1280 the attention joins up to three blocks of 256
+    positions a row, whichever arrives last."""
+    cfg, shape, w, dec, pre, lens, _ = _filled(pkg, ctx, syn, rows, layers=2, capacity=capacity, seed=rows,
+                                               split_k=split_k)
     assert dec.tensor
     rng = np.random.default_rng(1)
     x = rng.standard_normal((rows, cfg.hidden), dtype=np.float32)
@@ -57,9 +60,11 @@ def test_tensor_decoder_rows_are_the_same_bits_in_every_bucket(pkg, ctx, syn, ro
         np.testing.assert_array_equal(alone[0], full[b], err_msg=f"row {b} alone")
 
 
-@pytest.mark.parametrize("rows,layers,split_k", [(64, 2, False), (128, 24, False), (64, 2, True), (128, 24, True)])
-def test_tensor_decoder_matches_the_oracle(pkg, ctx, syn, rows, layers, split_k):
-    cfg, shape, w, dec, pre, lens, prompts = _filled(pkg, ctx, syn, rows, layers=layers, capacity=192, seed=3,
+@pytest.mark.parametrize("rows,layers,capacity,split_k", [(64, 2, 192, False), (128, 24, 192, False),
+                                                        (64, 2, 1280, False), (64, 2, 192, True),
+                                                        (128, 24, 192, True)])
+def test_tensor_decoder_matches_the_oracle(pkg, ctx, syn, rows, layers, capacity, split_k):
+    cfg, shape, w, dec, pre, lens, prompts = _filled(pkg, ctx, syn, rows, layers=layers, capacity=capacity, seed=3,
                                                      split_k=split_k)
     check = [0, rows // 2, rows - 1]
     ref = oracle.OracleStack(shape, syn.as_f32(w), slots=len(check))
@@ -106,10 +111,11 @@ def test_tensor_and_gemv_decoders_agree(pkg, ctx, syn, split_k):
 
 
 def test_the_default_family_by_rows(pkg, ctx, syn):
-    """bf16 decoders of 128 rows or more run the prefill's GEMMs, of 16-127 rows split-K clusters
-    (each where it measured faster on B200), of fewer rows the GEMVs."""
+    """bf16 decoders of 16 rows or more run the prefill's GEMMs (faster than split-K clusters on
+    B200 at every size from 16 rows), of fewer rows the GEMVs."""
     shape = syn.shape_of(syn.S05B, capacity=128, layers=1)
-    for rows, tensor, split_k in ((1, False, False), (16, True, True), (64, True, True), (128, True, False)):
+    for rows, tensor, split_k in ((1, False, False), (15, False, False), (16, True, False), (64, True, False),
+                                  (128, True, False)):
         dec = pkg.Decoder(ctx, shape, rows=rows, slots=rows, dtype="bf16")
         assert (dec.tensor, dec.split_k) == (tensor, split_k), rows
         dec.close()

@@ -39,6 +39,59 @@ def test_tcgen05_gemm_matches_f64(pkg, ctx, syn, m, n, k):
     assert np.mean(np.abs(short - want) > bound) > 0.5
 
 
+@pytest.mark.parametrize("m,n,k,parts,flags", [(128, 1024, 1024, 8, 3), (64, 1024, 4096, 8, 3), (200, 256, 512, 2, 0),
+                                                (128, 512, 1024, 4, 1)])
+def test_gemm_in_parts_then_add_norm_rows(pkg, ctx, syn, m, n, k, parts, flags):
+    """A GEMM in parts of K stores, for each part, exactly what the whole GEMM computes over that
+    part's columns alone; add_norm_rows (a warp to a row, or with flags bit 1 a block) adds the
+    parts in part order (f32, bit for bit as numpy's left-to-right sum) before the residual and the
+    norm."""
+    rng = np.random.default_rng(m + n + parts)
+    a = rng.standard_normal((m, k), dtype=np.float32)
+    b = rng.standard_normal((n, k), dtype=np.float32) * 0.02
+    ab, bb = syn.bf16_bits(a), syn.bf16_bits(b)
+    ma, mb = _mem(pkg, ctx, ab), _mem(pkg, ctx, bb)
+    shape = pkg.Shape(hidden=n, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    mc = pkg.Memory(ctx, parts * m * n * 4)
+    p = pkg.params(shape, "bf16", rows=m, m=m, n=n, k=k, parts=parts, flags=flags)
+    pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, ab.nbytes), (mb, 0, bb.nbytes), (mc, 0, parts * m * n * 4)])
+    got = mc.read(np.float32, parts * m * n).reshape(parts, m, n)
+    w = k // parts
+    for j in sorted({0, parts - 1, parts // 2}):
+        a_j, b_j = np.ascontiguousarray(ab[:, j * w:(j + 1) * w]), np.ascontiguousarray(bb[:, j * w:(j + 1) * w])
+        one = pkg.Memory(ctx, m * n * 4)
+        q = pkg.params(shape, "bf16", rows=m, m=m, n=n, k=w, flags=flags)
+        pkg.dispatch_once(ctx, "gemm", q, [(_mem(pkg, ctx, a_j), 0, a_j.nbytes), (_mem(pkg, ctx, b_j), 0, b_j.nbytes),
+                                           (one, 0, m * n * 4)])
+        np.testing.assert_array_equal(got[j], one.read(np.float32, m * n).reshape(m, n), err_msg=f"part {j}")
+    # Too few bytes for the parts, and a K the parts do not divide, are refused.
+    with pytest.raises(pkg.ShapeError):
+        pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, ab.nbytes), (mb, 0, bb.nbytes), (mc, 0, m * n * 4)])
+    bad = pkg.params(shape, "bf16", rows=m, m=m, n=n, k=k, parts=3 if k % 192 else 5, flags=flags)
+    with pytest.raises(pkg.ShapeError):
+        pkg.dispatch_once(ctx, "gemm", bad, [(ma, 0, ab.nbytes), (mb, 0, bb.nbytes), (mc, 0, parts * m * n * 4)])
+
+    res = rng.standard_normal((m, n), dtype=np.float32)
+    gain = (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    words = _mem(pkg, ctx, np.zeros(m, np.uint32))
+    msum, mnorm = pkg.Memory(ctx, m * n * 4), pkg.Memory(ctx, m * n * 2)
+    pa = pkg.params(shape, "bf16", rows=m, parts=parts, flags=flags & 2)
+    pkg.dispatch_once(ctx, "add_norm_rows", pa, [(words, 0, m * 4), (mc, 0, parts * m * n * 4), (_mem(pkg, ctx, res), 0, res.nbytes),
+                                                 (_mem(pkg, ctx, gain), 0, gain.nbytes), (msum, 0, m * n * 4),
+                                                 (mnorm, 0, m * n * 2)])
+    c = got[0].copy()
+    for j in range(1, parts):
+        c = c + got[j]
+    np.testing.assert_array_equal(msum.read(np.float32, m * n).reshape(m, n), res + c)
+    s64 = (res + c).astype(np.float64)
+    want = s64 / np.sqrt(np.mean(s64 * s64, axis=1, keepdims=True) + shape.eps) * gain
+    assert distance(syn.bf16_to_f32(mnorm.read(np.uint16, m * n).reshape(m, n)), want)[1] < 1e-2
+    with pytest.raises(pkg.ShapeError):  # at most 16 parts
+        pkg.dispatch_once(ctx, "add_norm_rows", pkg.params(shape, "bf16", rows=m, parts=17),
+                          [(words, 0, m * 4), (mc, 0, parts * m * n * 4), (msum, 0, m * n * 4), (msum, 0, m * n * 4),
+                           (msum, 0, m * n * 4), (mnorm, 0, m * n * 2)])
+
+
 def test_simt_gemm_f32(pkg, ctx):
     rng = np.random.default_rng(1)
     m, n, k = 100, 72, 48

@@ -87,7 +87,10 @@ struct RopeEpi {
 };
 
 // Persistent: one block per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m fastest, so the
-// blocks at work share B tiles in L2). Warp 0 streams A and B tiles into a ring of stages with
+// blocks at work share B tiles in L2, then n, then the part of K). With `parts` > 1 (f32 epilogue
+// only) K is cut into that many equal ranges and tile (m, n, part) stores its partial sum at
+// C[part][m][n]; the kernel that reads C adds the parts in part order, so a row's sums depend on
+// the shape and the part count, never on how many rows a launch takes. Warp 0 streams A and B tiles into a ring of stages with
 // TMA; warp 1 owns TMEM (two accumulators of BN columns) and issues the MMAs; warps 2-5 drain an
 // accumulator (tcgen05.ld) and store it while the MMAs fill the other, so that a tile's epilogue
 // overlaps the next tile's main loop.
@@ -98,7 +101,7 @@ template <int BN, int EPI = TC_EPI_F32>
 __global__ void __launch_bounds__(TC_PTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ RopeEpi re,
-                   int b_const) {
+                   int b_const, int parts) {
     using L = TcLayout<BN>;
     constexpr int S = L::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -113,8 +116,10 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
     __shared__ int gave_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = (M + TC_BM - 1) / TC_BM, tiles = mt * (N / BN);
-    const int nk = K / TC_BK;
+    const int mt = (M + TC_BM - 1) / TC_BM, per = mt * (N / BN), tiles = per * parts;
+    const int nk = K / TC_BK / parts;  // k-blocks a tile
+    auto n0_of = [&](int t) { return ((t % per) / mt) * BN; };
+    auto kb0_of = [&](int t) { return (t / per) * nk; };  // the tile's first k-block
     pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
@@ -152,22 +157,23 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             const int pre = b_const ? (nk < S ? nk : S) : 0;
             for (int kb = 0; kb < pre; kb++) {
                 mbar_arrive_expect_tx(full(kb), L::STAGE);
-                tma_load_2d(base + kb * L::STAGE + TC_A_BYTES, &map_b, kb * TC_BK, (blockIdx.x / mt) * BN, full(kb));
+                tma_load_2d(base + kb * L::STAGE + TC_A_BYTES, &map_b, (kb0_of(blockIdx.x) + kb) * TC_BK,
+                            n0_of(blockIdx.x), full(kb));
             }
             pdl_wait();
             int g = 0;
             for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-                const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+                const int m0 = (t % mt) * TC_BM, n0 = n0_of(t), kb0 = kb0_of(t);
                 for (int kb = 0; kb < nk; kb++, g++) {
-                    const int s = g % S;
+                    const int s = g % S, kx = (kb0 + kb) * TC_BK;
                     if (g < pre) {  // B is in flight already
-                        tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
+                        tma_load_2d(base + s * L::STAGE, &map_a, kx, m0, full(s));
                         continue;
                     }
                     mbar_wait(empty(s), ((g / S) & 1) ^ 1, err, &gave_up);
                     mbar_arrive_expect_tx(full(s), L::STAGE);
-                    tma_load_2d(base + s * L::STAGE, &map_a, kb * TC_BK, m0, full(s));
-                    tma_load_2d(base + s * L::STAGE + TC_A_BYTES, &map_b, kb * TC_BK, n0, full(s));
+                    tma_load_2d(base + s * L::STAGE, &map_a, kx, m0, full(s));
+                    tma_load_2d(base + s * L::STAGE + TC_A_BYTES, &map_b, kx, n0, full(s));
                 }
             }
             // Every copy this thread started has landed before the block can end.
@@ -205,7 +211,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
         int i = 0;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
             const int acc = i & 1;
-            const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+            const int m0 = (t % mt) * TC_BM, n0 = n0_of(t);
             mbar_wait(acc_full(acc), (i >> 1) & 1, err, &gave_up);
             tc_fence_after();
             const int row = m0 + q * 32 + lane;
@@ -302,7 +308,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                     }
                 }
             } else {
-                float *C = static_cast<float *>(Cout);
+                float *C = static_cast<float *>(Cout) + (size_t)(t / per) * M * N;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 32) {
                     uint32_t v[2][16];
@@ -335,7 +341,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
 
 template <int BN, int EPI = TC_EPI_F32>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
-                             cudaStream_t s, bool b_const, const RopeEpi &re = RopeEpi{}) {
+                             cudaStream_t s, bool b_const, const RopeEpi &re = RopeEpi{}, int parts = 1) {
     CUtensorMap ma, mb;
     if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, BN))
         return cudaErrorInvalidValue;
@@ -345,9 +351,9 @@ static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN);
+    const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN) * parts;
     return launch_pdl(kern, dim3(tiles < sms ? tiles : sms), dim3(TC_PTHREADS), (size_t)TcLayout<BN>::SMEM, s, ma, mb, c,
-                      M, N, K, err, re, (int)b_const);
+                      M, N, K, err, re, (int)b_const, parts);
 }
 
 cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c, uint32_t *err,
@@ -355,18 +361,26 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
     const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
     if (M <= 0 || N <= 0 || K <= 0) return cudaErrorInvalidValue;
     if (p.dtype != TG_BF16) {
+        if (p.parts > 1) return cudaErrorInvalidValue;
         dim3 grid((N + 63) / 64, (M + 63) / 64);
         gemm_f32_kernel<<<grid, 256, 0, s>>>(M, N, K, (const float *)a, (const float *)b, c);
         return cudaGetLastError();
     }
     if (K % TC_BK != 0) return cudaErrorInvalidValue;
     const bool b_const = (p.flags & 1) != 0;
-    // Narrow tiles (flags bit 1, a batched decode step's few rows): more blocks stream the weights.
-    // The tile width is the caller's choice, not the rows': a row's sums do not depend on how many
-    // rows a launch takes.
+    const int parts = p.parts > 1 ? (int)p.parts : 1;
+    if (K % (TC_BK * parts) != 0) return cudaErrorInvalidValue;
+    // Narrow tiles (flags bit 1, a batched decode step's few rows) and parts of K: more blocks
+    // stream the weights. Both are the caller's choice, not the rows': a row's sums do not depend
+    // on how many rows a launch takes.
     if (p.flags & 2) {
-        if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const);
+        if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
         return cudaErrorInvalidValue;
+    }
+    if (parts > 1) {
+        if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
+        if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
+        return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
     }
     if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
     if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);

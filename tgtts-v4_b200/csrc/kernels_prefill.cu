@@ -33,7 +33,9 @@ __global__ void __launch_bounds__(128)
 }
 
 // add_norm_rows.comp:21-45: sum = residual + s c in f32, normed = RMSNorm(sum) g (from the f32
-// sum), rounded to T, or kept in f32 for the final norm; a warp to a row.
+// sum), rounded to T, or kept in f32 for the final norm. With p.parts > 1, c is a GEMM's partial
+// sums over parts of K, [parts][rows][hidden], added in part order first. A warp to a row (the
+// prefill's many rows).
 template <typename T, bool NORMED_F32>
 __global__ void __launch_bounds__(128)
     add_norm_rows_kernel(tg_params p, const uint32_t *__restrict__ at, const float *__restrict__ c,
@@ -44,10 +46,15 @@ __global__ void __launch_bounds__(128)
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= (int)p.rows) return;
     const int k = p.hidden;
-    const size_t base = (size_t)row * k;
+    const size_t base = (size_t)row * k, part = (size_t)p.rows * k;
+    const int parts = p.parts > 1 ? (int)p.parts : 1;
     const float sc = p.residual_scale;
     for (int q = lane; q < k / 4; q += 32) {
-        const float4 cv = reinterpret_cast<const float4 *>(c + base)[q];
+        float4 cv = reinterpret_cast<const float4 *>(c + base)[q];
+        for (int j = 1; j < parts; j++) {
+            const float4 v = reinterpret_cast<const float4 *>(c + j * part + base)[q];
+            cv = make_float4(cv.x + v.x, cv.y + v.y, cv.z + v.z, cv.w + v.w);
+        }
         const float4 rv = reinterpret_cast<const float4 *>(res + base)[q];
         reinterpret_cast<float4 *>(sum + base)[q] =
             make_float4(__fmaf_rn(sc, cv.x, rv.x), __fmaf_rn(sc, cv.y, rv.y),
@@ -67,6 +74,55 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
             for (int e = 0; e < 4; e++) n[e] = from_f32<T>(o[e]);
         }
+    }
+}
+
+// add_norm_rows for few rows (a batched decode step's): a block to a row and a thread to 4
+// columns, so that all of a row's loads are in flight at once; the sum of squares is each thread's
+// 4 in column order, then each warp's (butterfly), then the warps' in order.
+template <typename T, bool NORMED_F32>
+__global__ void __launch_bounds__(1024)
+    add_norm_rows_block_kernel(tg_params p, const uint32_t *__restrict__ at, const float *__restrict__ c,
+                         const float *__restrict__ res, const float *__restrict__ g,
+                         float *__restrict__ sum, void *__restrict__ normed) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ float warp_ss[32];
+    const int row = blockIdx.x, t = threadIdx.x;
+    const int k = p.hidden;
+    const size_t base = (size_t)row * k, part = (size_t)p.rows * k;
+    const int parts = p.parts > 1 ? (int)p.parts : 1;
+    float4 v[ADD_NORM_MAX_PARTS];
+#pragma unroll
+    for (int j = 0; j < ADD_NORM_MAX_PARTS; j++)
+        if (j < parts) v[j] = reinterpret_cast<const float4 *>(c + j * part + base)[t];
+    const float4 rv = reinterpret_cast<const float4 *>(res + base)[t];
+    const float4 gg = reinterpret_cast<const float4 *>(g)[t];
+    float4 cv = v[0];
+#pragma unroll
+    for (int j = 1; j < ADD_NORM_MAX_PARTS; j++)
+        if (j < parts) cv = make_float4(cv.x + v[j].x, cv.y + v[j].y, cv.z + v[j].z, cv.w + v[j].w);
+    const float sc = p.residual_scale;
+    const float4 sv = make_float4(__fmaf_rn(sc, cv.x, rv.x), __fmaf_rn(sc, cv.y, rv.y), __fmaf_rn(sc, cv.z, rv.z),
+                                  __fmaf_rn(sc, cv.w, rv.w));
+    reinterpret_cast<float4 *>(sum + base)[t] = sv;
+    float ss = __fmul_rn(sv.x, sv.x);
+    ss = __fmaf_rn(sv.y, sv.y, ss);
+    ss = __fmaf_rn(sv.z, sv.z, ss);
+    ss = __fmaf_rn(sv.w, sv.w, ss);
+    ss = warp_sum(ss);
+    if ((t & 31) == 0) warp_ss[t >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); w++) tot += warp_ss[w];
+    const float s = 1.0f / sqrtf(__fdiv_rn(tot, (float)k) + p.eps);
+    const float o[4] = {sv.x * s * gg.x, sv.y * s * gg.y, sv.z * s * gg.z, sv.w * s * gg.w};
+    if (NORMED_F32) {
+        reinterpret_cast<float4 *>(static_cast<float *>(normed) + base)[t] = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+        T *n = static_cast<T *>(normed) + base + 4 * t;
+#pragma unroll
+        for (int e = 0; e < 4; e++) n[e] = from_f32<T>(o[e]);
     }
 }
 
@@ -441,6 +497,15 @@ cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float
 cudaError_t launch_add_norm_rows(const tg_params &p, const uint32_t *at, const float *c,
                                  const float *res, const float *g, float *sum, void *normed,
                                  cudaStream_t s) {
+    if (p.hidden % 128 || p.hidden > 4 * 1024 || p.parts > (uint32_t)ADD_NORM_MAX_PARTS) return cudaErrorInvalidValue;
+    if (p.flags & 2) {  // few rows: a block to a row
+        const dim3 grid(p.rows), block(p.hidden / 4);
+        if (p.normed_f32)
+            return launch_pdl(add_norm_rows_block_kernel<float, true>, grid, block, 0, s, p, at, c, res, g, sum, normed);
+        if (p.dtype == TG_BF16)
+            return launch_pdl(add_norm_rows_block_kernel<bf16, false>, grid, block, 0, s, p, at, c, res, g, sum, normed);
+        return launch_pdl(add_norm_rows_block_kernel<float, false>, grid, block, 0, s, p, at, c, res, g, sum, normed);
+    }
     const dim3 grid((p.rows + 3) / 4);
     if (p.normed_f32)
         return launch_pdl(add_norm_rows_kernel<float, true>, grid, dim3(128), 0, s, p, at, c, res, g, sum, normed);

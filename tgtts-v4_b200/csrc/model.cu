@@ -113,6 +113,15 @@ static void push(std::vector<Launch> &v, uint32_t kernel, const tg_params &p, co
 // down GEMM, and the residual add with the next layer's input norm (the last layer's with the final
 // norm, in f32). Activations between them are bf16 where a GEMM reads them, the residual stream f32.
 // Every GEMM's B is a weight, so its first tiles stream while the kernel before it finishes.
+// The parts of K a batched decode step's o and down GEMMs are cut into (n outputs of k): the most,
+// a power of two, that keeps the 64-column tiles within one wave of B200's 148 SMs. The shape
+// alone fixes it, so a row's sums do not depend on the bucket.
+static uint32_t decode_gemm_parts(uint64_t n, uint64_t k) {
+    uint32_t parts = 1;
+    while ((n / 64) * parts * 2 <= 148 && (k / 64) % (parts * 2) == 0) parts *= 2;
+    return parts;
+}
+
 static std::vector<Launch> decode_gemm_launches(tg_decoder &d, uint32_t R) {
     const tg_params base = d.params(R);
     const tg_shape &s = d.shape;
@@ -121,12 +130,14 @@ static std::vector<Launch> decode_gemm_launches(tg_decoder &d, uint32_t R) {
     const uint64_t words = (d.slots > 1 ? 2 : 1) * (uint64_t)R * 4;
     const uint64_t table = (uint64_t)s.capacity * (hd / 2) * F;
     std::vector<Launch> v;
+    const uint32_t o_parts = decode_gemm_parts(H, A), down_parts = decode_gemm_parts(H, I);
     auto gemm = [&](uint32_t kernel, const char *label, void *a, void *b, void *c, uint64_t c_bytes, uint64_t n,
-                    uint64_t k) {
+                    uint64_t k, uint32_t parts = 1) {
         tg_params g = base;
         g.m = R;
         g.n = (uint32_t)n;
         g.k = (uint32_t)k;
+        g.parts = parts;
         g.flags = 1 | 2;  // b a weight; narrow tiles
         push(v, kernel, g, label, {{a, R * k * T}, {b, n * k * T}, {c, c_bytes}});
     };
@@ -145,31 +156,34 @@ static std::vector<Launch> decode_gemm_launches(tg_decoder &d, uint32_t R) {
                  {{d.g_normed.ptr(), R * H * T}, {d.w(o.qkv), W * H * T}, {d.words.ptr(), words}, {d.cos.ptr(), table},
                   {d.sin.ptr(), table}, {d.g_q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}});
         }
-        push(v, KERNEL_ATTN_SPLIT_MMA_BQ, base, "attention_split",
+        // attention_split and attention_combine in one launch.
+        push(v, KERNEL_ATTN_SPLIT_JOIN, base, "attention",
              {{d.g_q.ptr(), R * A * F}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer}, {d.words.ptr(), words},
-              {d.po.ptr(), R * heads * chunks * hd * F}, {d.pml.ptr(), R * heads * chunks * 2 * F}});
-        push(v, KERNEL_ATTN_COMBINE_WIDE_BF, base, "attention_combine",
-             {{d.words.ptr(), words}, {d.po.ptr(), R * heads * chunks * hd * F},
-              {d.pml.ptr(), R * heads * chunks * 2 * F}, {d.g_att.ptr(), R * A * F}});
-        gemm(TG_KERNEL_GEMM, "o_proj", d.g_att.ptr(), d.w(o.o), d.g_proj.ptr(), R * H * F, H, A);
-        push(v, TG_KERNEL_ADD_NORM_ROWS, base, "add_norm",
-             {{d.words.ptr(), words}, {d.g_proj.ptr(), R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
+              {d.po.ptr(), R * heads * chunks * hd * F}, {d.pml.ptr(), R * heads * chunks * 2 * F},
+              {d.g_att.ptr(), R * A * 2}, {d.g_counts.ptr(), R * s.kv_heads * 4}});
+        // o and down in parts of K, each part's sums added by the add_norm after it.
+        gemm(TG_KERNEL_GEMM, "o_proj", d.g_att.ptr(), d.w(o.o), d.g_proj.ptr(), o_parts * R * H * F, H, A, o_parts);
+        tg_params on = base;
+        on.parts = o_parts;
+        on.flags = 2;  // few rows: a block to a row
+        push(v, TG_KERNEL_ADD_NORM_ROWS, on, "add_norm",
+             {{d.words.ptr(), words}, {d.g_proj.ptr(), o_parts * R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
               {d.mid.ptr(), R * H * F}, {d.g_normed.ptr(), R * H * T}});
         gemm(TG_KERNEL_GEMM_SILU, "gate_up", d.g_normed.ptr(), d.w(o.gate_up), d.g_mlp.ptr(), R * I * T, 2 * I, H);
-        gemm(TG_KERNEL_GEMM, "down_proj", d.g_mlp.ptr(), d.w(o.down), d.g_proj.ptr(), R * H * F, H, I);
+        gemm(TG_KERNEL_GEMM, "down_proj", d.g_mlp.ptr(), d.w(o.down), d.g_proj.ptr(), down_parts * R * H * F, H, I,
+             down_parts);
         const bool last = l + 1 == s.layers;
         tg_params an = base;
         an.normed_f32 = last ? 1 : 0;
+        an.parts = down_parts;
+        an.flags = 2;
         push(v, TG_KERNEL_ADD_NORM_ROWS, an, last ? "final_norm" : "add_norm",
-             {{d.words.ptr(), words}, {d.g_proj.ptr(), R * H * F}, {d.mid.ptr(), R * H * F},
+             {{d.words.ptr(), words}, {d.g_proj.ptr(), down_parts * R * H * F}, {d.mid.ptr(), R * H * F},
               {d.w(last ? d.final_norm : d.layer[l + 1].in_norm), H * F}, {d.h.ptr(), R * H * F},
               {last ? d.out.ptr() : d.g_normed.ptr(), R * H * (last ? F : T)}});
     }
     return v;
 }
-
-// Decoders of at least this many rows run the GEMM family by default.
-constexpr uint32_t GEMM_MIN_ROWS = 128;
 
 // Whether a decoder's shape and rows take the GEMM family (the prefill GEMMs' tiles and epilogues,
 // the batched attention).
@@ -369,19 +383,21 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(tg_mem_fill(d->words.m, 0, TG_SPARE, 2 * R * 4));
     // A decoder of DTC_MIN_ROWS rows or more runs its projections on tcgen05 in every bucket (so that
     // a row's bits do not depend on the bucket); smaller ones run the GEMVs.
-    // Both tcgen05 forms are recorded on request; by default a decoder of GEMM_MIN_ROWS rows or
-    // more runs the GEMMs (on B200 a 128-row step: 2.41 ms against 3.30 as split-K clusters) and a
-    // smaller one the split-K clusters (16 rows: 1.21 ms against 1.85; 64 rows: 2.00 against 2.07).
+    // Both tcgen05 forms are recorded on request; by default the GEMMs, where they take the shape
+    // (on B200 a step at 16 / 64 / 128 rows: 1.16 / 1.44 / 1.77 ms against 1.25 / 1.99 / 3.29 ms as
+    // split-K clusters).
     const bool gemm_ok = gemm_family_supported(*d);
     const bool dtc_ok = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && dtc_supported(d->params(rows));
-    d->gemm = gemm_ok && (rows >= GEMM_MIN_ROWS || !dtc_ok);
+    d->gemm = gemm_ok;
     d->tensor = dtype == TG_BF16 && rows >= DTC_MIN_ROWS && (gemm_ok || dtc_ok);
     if (gemm_ok) {
         TG_TRY(d->g_normed.alloc(ctx, R * H * 2));
         TG_TRY(d->g_q.alloc(ctx, R * d->attn() * F));  // bf16 values, sized as the checks size f32 q
         TG_TRY(d->g_att.alloc(ctx, R * d->attn() * F));
-        TG_TRY(d->g_proj.alloc(ctx, R * H * F));
+        const uint64_t parts = std::max(decode_gemm_parts(H, d->attn()), decode_gemm_parts(H, I));
+        TG_TRY(d->g_proj.alloc(ctx, parts * R * H * F));
         TG_TRY(d->g_mlp.alloc(ctx, R * I * 2));
+        TG_TRY(d->g_counts.alloc(ctx, R * s->kv_heads * 4));
     }
     // A bf16 decoder of one or two rows records its step as the one persistent launch (on B200
     // 0.61-0.63 ms a step at config 2 against 0.67-0.70 ms for six kernels a layer, the same bits);

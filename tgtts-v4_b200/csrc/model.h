@@ -113,6 +113,7 @@ struct tg_decoder {
     // whole of K, bf16 activations), else as split-K clusters over f32 activations split into hi/lo.
     bool gemm = false;
     tg::Owned g_normed, g_q, g_att, g_proj, g_mlp;  // the GEMM family's activations
+    tg::Owned g_counts;  // its attention's arrival counters, [rows][kv_heads], zero between launches
     tg::Owned stage_x, stage_out;  // pinned host staging
     cudaEvent_t out_done = nullptr;  // recorded after a step's output copy (tg_decoder_step_rows_n)
     tg::StageRing word_ring;                    // placements of device-resident steps

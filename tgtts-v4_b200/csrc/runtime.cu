@@ -114,7 +114,7 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"at", words}, {"x", rows * H * F}, {"gain", H * F}, {"out", rows * H * T}};
             break;
         case TG_KERNEL_ADD_NORM_ROWS:
-            out = {{"at", words}, {"c", rows * H * F}, {"residual", rows * H * F}, {"gain", H * F},
+            out = {{"at", words}, {"c", (p.parts > 1 ? p.parts : 1) * rows * H * F}, {"residual", rows * H * F}, {"gain", H * F},
                    {"sum", rows * H * F}, {"normed", rows * H * (p.normed_f32 ? F : T)}};
             break;
         case TG_KERNEL_ROPE_ROWS:
@@ -131,7 +131,7 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             break;
         case TG_KERNEL_GEMM:
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
-                   {"c", (uint64_t)p.m * p.n * F}};
+                   {"c", (uint64_t)(p.parts > 1 ? p.parts : 1) * p.m * p.n * F}};
             break;
         case TG_KERNEL_GEMM_SILU:
             out = {{"a", (uint64_t)p.m * p.k * T}, {"b", (uint64_t)p.n * p.k * T},
@@ -255,8 +255,12 @@ static int check_shape(const Launch &l) {
     switch (l.kernel) {
         case TG_KERNEL_RMSNORM:
         case TG_KERNEL_NORM_ROWS:
-        case TG_KERNEL_ADD_NORM_ROWS:
             if (p.hidden == 0 || p.hidden % 128) return fail(TG_ESHAPE, "%s: hidden %u is not a multiple of 128", kernel_name(l.kernel), p.hidden);
+            break;
+        case TG_KERNEL_ADD_NORM_ROWS:
+            if (p.hidden == 0 || p.hidden % 128 || p.hidden > 4096 || p.parts > (uint32_t)ADD_NORM_MAX_PARTS)
+                return fail(TG_ESHAPE, "add_norm_rows: hidden %u (a multiple of 128, at most 4096), %u parts (at most %u)",
+                            p.hidden, p.parts, ADD_NORM_MAX_PARTS);
             break;
         case TG_KERNEL_GEMV_QKV_ROPE:
             if (p.hidden % vec || !heads_ok()) return fail(TG_ESHAPE, "gemv_qkv_rope: hidden %u (multiple of %u), %u heads over %u of %u, capacity %u", p.hidden, vec, p.heads, p.kv_heads, p.head_dim, p.capacity);
@@ -308,6 +312,8 @@ static int check_shape(const Launch &l) {
             if (p.m == 0 || p.n == 0 || p.k == 0) return fail(TG_ESHAPE, "gemm %ux%ux%u", p.m, p.n, p.k);
             if (p.dtype == TG_BF16 && (p.k % 64 || p.n % 64))
                 return fail(TG_ESHAPE, "gemm %ux%ux%u: bf16 needs n and k multiples of 64", p.m, p.n, p.k);
+            if (p.parts > 1 && (p.dtype != TG_BF16 || p.k % (64 * p.parts)))
+                return fail(TG_ESHAPE, "gemm %ux%ux%u in %u parts: bf16 with k a multiple of 64 parts", p.m, p.n, p.k, p.parts);
             break;
         default:
             return fail(TG_EINVAL, "no kernel %u", l.kernel);
@@ -326,7 +332,8 @@ static uint32_t table_kernel(uint32_t k) {
         case KERNEL_DTC_GATE_UP: return TG_KERNEL_GEMV_GATE_UP;
         case KERNEL_DTC_RESIDUAL: return TG_KERNEL_GEMV_RESIDUAL;
         case KERNEL_ATTN_SPLIT_MMA:
-        case KERNEL_ATTN_SPLIT_MMA_BQ: return TG_KERNEL_ATTENTION_SPLIT;
+        case KERNEL_ATTN_SPLIT_MMA_BQ:
+        case KERNEL_ATTN_SPLIT_JOIN: return TG_KERNEL_ATTENTION_SPLIT;
         case KERNEL_ATTN_COMBINE_WIDE:
         case KERNEL_ATTN_COMBINE_WIDE_BF: return TG_KERNEL_ATTENTION_COMBINE;
         default: return k;
@@ -338,13 +345,18 @@ int check_launch(const Launch &l0) {
     Launch l = l0;
     l.kernel = table_kernel(l0.kernel);
     const bool wide = l0.kernel == KERNEL_ATTN_SPLIT_MMA || l0.kernel == KERNEL_ATTN_COMBINE_WIDE ||
-                      l0.kernel == KERNEL_ATTN_SPLIT_MMA_BQ || l0.kernel == KERNEL_ATTN_COMBINE_WIDE_BF;
+                      l0.kernel == KERNEL_ATTN_SPLIT_MMA_BQ || l0.kernel == KERNEL_ATTN_COMBINE_WIDE_BF ||
+                      l0.kernel == KERNEL_ATTN_SPLIT_JOIN;
     if (wide ? !attention_split_mma_supported(l.p) : (l.kernel != l0.kernel && !dtc_supported(l.p)))
         return fail(TG_ESHAPE, "%s: no tcgen05 plan for %u rows of this shape", l0.label.c_str(), l.p.rows);
     int st = check_shape(l);
     if (st) return st;
     std::vector<Need> need;
     if ((st = needs(l, need))) return st;
+    if (l0.kernel == KERNEL_ATTN_SPLIT_JOIN) {
+        need.push_back({"out", (uint64_t)l.p.rows * l.p.heads * l.p.head_dim * 2});
+        need.push_back({"counts", (uint64_t)l.p.rows * l.p.kv_heads * 4});
+    }
     if (l.ptr.size() != need.size() || l.bytes.size() != need.size())
         return fail(TG_EINVAL, "%s: %zu bindings, takes %zu", kernel_name(l.kernel), l.ptr.size(), need.size());
     for (size_t i = 0; i < need.size(); i++) {
@@ -386,6 +398,9 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
         case KERNEL_ATTN_SPLIT_MMA: e = launch_attention_split_mma(p, b[0], b[1], b[2], U(3), F(4), F(5), s); break;
         case KERNEL_ATTN_SPLIT_MMA_BQ: e = launch_attention_split_mma(p, b[0], b[1], b[2], U(3), F(4), F(5), s, true); break;
+        case KERNEL_ATTN_SPLIT_JOIN:
+            e = launch_attention_split_join(p, b[0], b[1], b[2], U(3), F(4), F(5), b[6], U(7), s);
+            break;
         case KERNEL_ATTN_COMBINE_WIDE_BF:
             e = launch_attention_combine_chunk(p, DECODE_WIDE_CHUNK, U(0), F(1), F(2), b[3], s, true);
             break;

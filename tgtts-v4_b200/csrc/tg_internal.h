@@ -78,6 +78,9 @@ constexpr uint32_t KERNEL_ATTN_COMBINE_WIDE = 1005;
 // binding still sized as f32 q), the joined output in bf16 (the o GEMM's A operand; sized as f32).
 constexpr uint32_t KERNEL_ATTN_SPLIT_MMA_BQ = 1006;
 constexpr uint32_t KERNEL_ATTN_COMBINE_WIDE_BF = 1007;
+// The two of the GEMM-family decoder in one launch (the split's bindings, then out bf16 [rows][heads
+// hd] and counts u32 [rows][kv_heads], zero before the first launch and after each).
+constexpr uint32_t KERNEL_ATTN_SPLIT_JOIN = 1008;
 // 64: wider partials (a warp walking sub-chunks) measured slower on B200 at 16-128 rows: 2.15 ms
 // a step at 64 rows with 256 against 2.00 ms with 64.
 constexpr uint32_t DECODE_WIDE_CHUNK = 64;
@@ -86,6 +89,9 @@ cudaError_t launch_attention_combine_chunk(const tg_params &p, uint32_t chunk, c
 bool attention_split_mma_supported(const tg_params &p);
 cudaError_t launch_attention_split_mma(const tg_params &p, const void *q, const void *kc, const void *vc,
                                        const uint32_t *at, float *po, float *pml, cudaStream_t s, bool q_bf16 = false);
+cudaError_t launch_attention_split_join(const tg_params &p, const void *q, const void *kc, const void *vc,
+                                        const uint32_t *at, float *po, float *pml, void *out, uint32_t *counts,
+                                        cudaStream_t s);
 // Decoders of at least this many rows run their projections on tcgen05 (every bucket of them).
 constexpr uint32_t DTC_MIN_ROWS = 16;
 
@@ -153,6 +159,8 @@ cudaError_t launch_stream_read(const tg_params &p, const uint32_t *data, uint32_
                                cudaStream_t s, int sm_count);
 cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
                              const float *g, void *out, cudaStream_t s);
+// The most parts of K an add_norm_rows dispatch adds (tg_params.parts).
+constexpr int ADD_NORM_MAX_PARTS = 16;
 cudaError_t launch_add_norm_rows(const tg_params &p, const uint32_t *at, const float *c,
                                  const float *res, const float *g, float *sum, void *normed,
                                  cudaStream_t s);
