@@ -187,10 +187,13 @@ def test_decode_attention_split_and_combine_against_f64(pkg, ctx, syn, dtype):
             assert np.max(np.abs(got[r, h] - want)) < 1e-5, (r, pos, h)
 
 
-@pytest.mark.parametrize("m,inner,k", [(200, 256, 256), (512, 4096, 1024)])
-def test_gemm_silu_epilogue_equals_gemm_then_silu_mul_rows(pkg, ctx, syn, m, inner, k):
+@pytest.mark.parametrize("m,inner,k,flags", [(200, 256, 256, 0), (512, 4096, 1024, 0), (128, 4096, 1024, 2),
+                                             (40, 256, 256, 2)])
+def test_gemm_silu_epilogue_equals_gemm_then_silu_mul_rows(pkg, ctx, syn, m, inner, k, flags):
     """The fused epilogue takes SiLU(gate) up of the same f32 accumulators the plain GEMM stores, so
-    it matches gemm + silu_mul_rows bit for bit; gate and up rows are interleaved in blocks of 128."""
+    it matches gemm + silu_mul_rows bit for bit, in 256-column tiles and in narrow ones (flags bit
+    1: each tile's gate and up rows loaded as two boxes of 32); gate and up rows are interleaved in
+    blocks of 128."""
     rng = np.random.default_rng(m + inner)
     a = rng.standard_normal((m, k), dtype=np.float32)
     gate = rng.standard_normal((inner, k), dtype=np.float32) * 0.05
@@ -201,7 +204,8 @@ def test_gemm_silu_epilogue_equals_gemm_then_silu_mul_rows(pkg, ctx, syn, m, inn
     shape = pkg.Shape(hidden=256, inner=inner, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
     p = pkg.params(shape, "bf16", rows=m, m=m, n=2 * inner, k=k)
     fused = pkg.Memory(ctx, m * inner * 2)
-    pkg.dispatch_once(ctx, "gemm_silu", p, [(ma, 0, ab.nbytes), (mw, 0, wb.nbytes), (fused, 0, m * inner * 2)])
+    pf = pkg.params(shape, "bf16", rows=m, m=m, n=2 * inner, k=k, flags=flags)
+    pkg.dispatch_once(ctx, "gemm_silu", pf, [(ma, 0, ab.nbytes), (mw, 0, wb.nbytes), (fused, 0, m * inner * 2)])
     c = pkg.Memory(ctx, m * 2 * inner * 4)
     pkg.dispatch_once(ctx, "gemm", p, [(ma, 0, ab.nbytes), (mw, 0, wb.nbytes), (c, 0, m * 2 * inner * 4)])
     words = _mem(pkg, ctx, np.zeros(m, np.uint32))

@@ -73,8 +73,10 @@ struct TcLayout {
     static constexpr int SMEM = BARRIERS + 256 + 1024;                        // + barriers + alignment slack
 };
 
-// Epilogues: C in f32, or (BN = 256, B's rows in gate_up_row's order) SiLU(gate) up in bf16, the
-// tile's columns 0..127 the gate and 128..255 the up of the same 128 outputs, or (BN = 256, B the
+// Epilogues: C in f32, or (B's rows in gate_up_row's order: blocks of 128 gate rows, then the same
+// outputs' 128 up rows) SiLU(gate) up in bf16, a tile's B loaded as two boxes of BN / 2 rows — the
+// gate rows of BN / 2 outputs, then their up rows — so that columns c and BN / 2 + c of the
+// accumulator are one output's gate and up, or (B the
 // q/k/v projection) rope_rows.comp's work: RoPE on each head's column pairs (i, i + hd/2), q rows
 // stored bf16, k and v rows appended to the cache at the row's position and slot.
 enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1, TC_EPI_ROPE = 2 };
@@ -120,6 +122,17 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
     const int nk = K / TC_BK / parts;  // k-blocks a tile
     auto n0_of = [&](int t) { return ((t % per) / mt) * BN; };
     auto kb0_of = [&](int t) { return (t / per) * nk; };  // the tile's first k-block
+    // A stage's B tile: BN rows from n0, or (SiLU) the gate rows of outputs n0 / 2 .. + BN / 2 and
+    // then their up rows.
+    auto load_b = [&](uint32_t dst, int kx, int n0, uint32_t bar) {
+        if constexpr (EPI == TC_EPI_SILU) {
+            const int o0 = n0 / 2, gate = (o0 / 128) * 256 + o0 % 128;
+            tma_load_2d(dst, &map_b, kx, gate, bar);
+            tma_load_2d(dst + (BN / 2) * TC_BK * 2, &map_b, kx, gate + 128, bar);
+        } else {
+            tma_load_2d(dst, &map_b, kx, n0, bar);
+        }
+    };
     pdl_launch_dependents();
 
     if (threadIdx.x == 0) {
@@ -157,8 +170,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             const int pre = b_const ? (nk < S ? nk : S) : 0;
             for (int kb = 0; kb < pre; kb++) {
                 mbar_arrive_expect_tx(full(kb), L::STAGE);
-                tma_load_2d(base + kb * L::STAGE + TC_A_BYTES, &map_b, (kb0_of(blockIdx.x) + kb) * TC_BK,
-                            n0_of(blockIdx.x), full(kb));
+                load_b(base + kb * L::STAGE + TC_A_BYTES, (kb0_of(blockIdx.x) + kb) * TC_BK, n0_of(blockIdx.x), full(kb));
             }
             pdl_wait();
             int g = 0;
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                     mbar_wait(empty(s), ((g / S) & 1) ^ 1, err, &gave_up);
                     mbar_arrive_expect_tx(full(s), L::STAGE);
                     tma_load_2d(base + s * L::STAGE, &map_a, kx, m0, full(s));
-                    tma_load_2d(base + s * L::STAGE + TC_A_BYTES, &map_b, kx, n0, full(s));
+                    load_b(base + s * L::STAGE + TC_A_BYTES, kx, n0, full(s));
                 }
             }
             // Every copy this thread started has landed before the block can end.
@@ -284,14 +296,14 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                     }
                 }
             } else if constexpr (EPI == TC_EPI_SILU) {
-                static_assert(BN == 256, "the SiLU epilogue pairs columns c and c + 128 of a 256-wide tile");
+                static_assert(BN % 32 == 0 && 128 % (BN / 2) == 0, "gate and up halves of whole 16-column loads");
                 bf16 *out = static_cast<bf16 *>(Cout);
                 const int inner = N / 2;
 #pragma unroll 1
-                for (int c0 = 0; c0 < 128; c0 += 16) {
+                for (int c0 = 0; c0 < BN / 2; c0 += 16) {
                     uint32_t g[16], u[16];
                     tmem_ld16_nowait(lane_base + c0, g);
-                    tmem_ld16_nowait(lane_base + 128 + c0, u);
+                    tmem_ld16_nowait(lane_base + BN / 2 + c0, u);
                     tmem_wait_ld();
                     if (row < M) {
                         uint32_t packed[8];
@@ -343,7 +355,8 @@ template <int BN, int EPI = TC_EPI_F32>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
                              cudaStream_t s, bool b_const, const RopeEpi &re = RopeEpi{}, int parts = 1) {
     CUtensorMap ma, mb;
-    if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, BN))
+    const int b_box = EPI == TC_EPI_SILU ? BN / 2 : BN;  // the SiLU tile's B is two boxes
+    if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, b_box))
         return cudaErrorInvalidValue;
     auto kern = gemm_tc_kernel<BN, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<BN>::SMEM);
@@ -406,6 +419,8 @@ cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, v
                              cudaStream_t s) {
     const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
     if (p.dtype != TG_BF16 || M <= 0 || N % 256 || K % TC_BK) return cudaErrorInvalidValue;
+    // Narrow tiles (flags bit 1, a batched decode step): 32 outputs a tile, four times the blocks.
+    if (p.flags & 2) return launch_tc<64, TC_EPI_SILU>(a, b, out, M, N, K, err, s, true);
     return launch_tc<256, TC_EPI_SILU>(a, b, out, M, N, K, err, s, true);
 }
 
