@@ -8,12 +8,13 @@
 //   warp 0     TMA: the two Q tiles once, then K and V tiles into two stages (128-byte swizzle,
 //              no multicast);
 //   warp 1     TMEM (per head: S, 128 columns, and O, 64) and the MMAs: S_j = Q K_j^T
-//              (M = 128, N = 128, K = 64) and PV_j = P_j V_j (M = 128, N = 64, K = 128, V read
+//              (M = 128, N = 128, K = 64) and O += P_j V_j (M = 128, N = 64, K = 128, V read
 //              MN-major), each head's S_{j+1} issued as soon as its PV_j is;
 //   warps 2-5  head 2g, warps 6-9 head 2g + 1: a thread to a query row: S_j from TMEM (the mask,
-//              the row maximum, then the base-2 exponentials with the scale folded in), P_j as
-//              bf16 into shared memory as PV's A operand, and PV_{j-1} from TMEM folded into the
-//              row's f32 output in registers.
+//              the row maximum, then the base-2 exponentials with the scale folded in) and P_j as
+//              bf16 into shared memory as PV's A operand, against a reference maximum that moves
+//              only when a tile's passes it by more than 2^FA_RESCALE, O in TMEM then rescaled
+//              in place (as in FlashAttention-4); O / l at the end.
 // The two heads' softmax warps run while the other head's MMAs do. Every wait on an mbarrier is
 // bounded (the context's error word, then the block runs out).
 #include "tc_common.cuh"
@@ -27,6 +28,8 @@ constexpr uint32_t FA_TILE = 128 * 64 * 2;  // a 128-row x 64-column bf16 box
 // Shared memory: Q of the two heads, K and V in two stages, P of the two heads (two boxes each).
 constexpr uint32_t FA_Q = 0, FA_K = 2 * FA_TILE, FA_V = 4 * FA_TILE, FA_P = 6 * FA_TILE;
 constexpr uint32_t FA_SMEM = 10 * FA_TILE + 1024;
+// How far (base 2) a tile's maximum may pass a row's reference before O and l are rescaled.
+constexpr float FA_RESCALE = 8.0f;
 
 // 2^x by the hardware's approximate base-2 exponential (PTX ex2.approx.ftz.f32: relative error
 // about 2^-22, far below the bf16 rounding the probabilities take next); 2^-inf = 0.
@@ -34,6 +37,29 @@ TG_DEVICE float fa_exp2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// Two-wide f32 arithmetic (sm_100's fma/add .f32x2: each lane the scalar IEEE operation, so the
+// same bits as two scalar instructions, in one issue) and the three-input maximum.
+TG_DEVICE float2 fa_fma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<const uint64_t *>(&a)), "l"(*reinterpret_cast<const uint64_t *>(&b)),
+          "l"(*reinterpret_cast<const uint64_t *>(&c)));
+    return *reinterpret_cast<const float2 *>(&d);
+}
+TG_DEVICE float2 fa_add2(float2 a, float2 b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<const uint64_t *>(&a)), "l"(*reinterpret_cast<const uint64_t *>(&b)));
+    return *reinterpret_cast<const float2 *>(&d);
+}
+TG_DEVICE float fa_max3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
 }
 
 TG_DEVICE uint32_t fa_sw128(int n, int c) {
@@ -181,7 +207,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++)
                         tc_mma(tmem + o_col(h), sw128_desc(base + FA_P + (2 * h + kk / 4) * FA_TILE + (kk % 4) * 32),
-                               fa_desc_mn(v + kk * 2048), idesc_o, kk > 0 ? 1u : 0u);
+                               fa_desc_mn(v + kk * 2048), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
                     tc_commit(B(bo_full[h]));
                     if (j + 1 < n) issue_s(j + 1, h);
                 }
@@ -195,20 +221,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         const uint32_t lanes = tmem + ((uint32_t)(q * 32) << 16);
         const int pos = pos_s[m];
         const float scale2 = 1.4426950408889634f / sqrtf((float)p.head_dim);  // log2(e) / sqrt(hd)
-        float o[64];
-#pragma unroll
-        for (int d = 0; d < 64; d++) o[d] = 0.0f;
-        float mrow = -INFINITY, l = 0.0f, a_pend = 0.0f;
-        auto fold_pv = [&](int j) {  // o = o a_pend + PV_j, PV_j from TMEM
-            mbar_wait(B(bo_full[h]), j & 1, err, &gave_up);
-            tc_fence_after();
-            uint32_t v[4][16];
-#pragma unroll
-            for (int c = 0; c < 4; c++) tmem_ld16_nowait(lanes + o_col(h) + c * 16, v[c]);
-            tmem_wait_ld();
-#pragma unroll
-            for (int d = 0; d < 64; d++) o[d] = __fmaf_rn(o[d], a_pend, __uint_as_float(v[d / 16][d % 16]));
-        };
+        // P_j = 2^(S_j scale2 - mref) against the row's reference maximum mref (base 2, scaled), and
+        // the running sum l against the same; O accumulates P_j V_j in TMEM over the tiles. mref
+        // moves up to a tile's maximum only when that passes it by more than FA_RESCALE (so P stays
+        // below 2^FA_RESCALE), and then O (in TMEM, once PV_{j-1} is in it) and l are rescaled to
+        // it; the output is O / l after the last tile.
+        float mref = -INFINITY, l = 0.0f;
         // Half c2 (64 keys) of S_j as the raw scores, masked past the row's position (-inf) only in
         // a half that reaches past it: the scale to base 2 is folded into the exponential's FMA, so
         // that a score costs a max, an FMA, an exponential and an add.
@@ -238,21 +256,41 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 float sv[64];
                 load_half(j, c2, sv);
 #pragma unroll
-                for (int c = 0; c < 64; c++) mx8[c % 8] = fmaxf(mx8[c % 8], sv[c]);
+                for (int e = 0; e < 8; e++)
+#pragma unroll
+                    for (int t = 0; t < 8; t += 2) mx8[e] = fa_max3(mx8[e], sv[e + 8 * t], sv[e + 8 * t + 8]);
             }
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-            const float m_new = fmaxf(mrow, mx * scale2);  // the scale is positive: max, then scale
-            const bool live = m_new != -INFINITY;  // false only for a spare row
-            const float a = live ? fa_exp2(mrow - m_new) : 1.0f;
+            const float m_tile = mx * scale2;  // the scale is positive: max, then scale
+            const bool move = m_tile != -INFINITY && (mref == -INFINITY || m_tile > mref + FA_RESCALE);
+            const float a = move && mref != -INFINITY ? fa_exp2(mref - m_tile) : 1.0f;
+            if (move) mref = m_tile;
+            const bool live = mref != -INFINITY;  // false only for a spare row
             if (j > 0) {
-                fold_pv(j - 1);  // PV_{j-1} is done: this head's P buffer is free, O holds PV_{j-1}
+                // PV_{j-1} is in O: rescale it where the reference moved (the warp's 32 rows
+                // together, a row that keeps its reference times 1), then PV_j may add to it.
+                mbar_wait(B(bo_full[h]), (j - 1) & 1, err, &gave_up);
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, a != 1.0f)) {
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        uint32_t v[16];
+                        tmem_ld16_nowait(lanes + o_col(h) + c * 16, v);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 16; e++) v[e] = __float_as_uint(__uint_as_float(v[e]) * a);
+                        tmem_st16(lanes + o_col(h) + c * 16, v);
+                    }
+                    tmem_wait_st();
+                }
                 tc_fence_before();
                 mbar_arrive(B(bo_empty[h]));
             }
-            float sum8[8];
+            float2 sum4[4];  // the running sums of columns c % 8 = 2 e and 2 e + 1
 #pragma unroll
-            for (int e = 0; e < 8; e++) sum8[e] = 0.0f;
+            for (int e = 0; e < 4; e++) sum4[e] = make_float2(0.0f, 0.0f);
+            const float2 scale22 = make_float2(scale2, scale2), neg_m = make_float2(-mref, -mref);
 #pragma unroll
             for (int c2 = 0; c2 < 2; c2++) {
                 float sv[64];
@@ -260,10 +298,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 uint32_t pk[32];
 #pragma unroll
                 for (int c = 0; c < 64; c += 2) {
-                    const float p0 = live ? fa_exp2(__fmaf_rn(sv[c], scale2, -m_new)) : 0.0f;
-                    const float p1 = live ? fa_exp2(__fmaf_rn(sv[c + 1], scale2, -m_new)) : 0.0f;
-                    sum8[c % 8] += p0;
-                    sum8[(c + 1) % 8] += p1;
+                    const float2 x = fa_fma2(make_float2(sv[c], sv[c + 1]), scale22, neg_m);
+                    const float p0 = live ? fa_exp2(x.x) : 0.0f;
+                    const float p1 = live ? fa_exp2(x.y) : 0.0f;
+                    sum4[(c % 8) / 2] = fa_add2(sum4[(c % 8) / 2], make_float2(p0, p1));
                     const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
                     pk[c / 2] = *reinterpret_cast<const uint32_t *>(&pp);
                 }
@@ -276,14 +314,19 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             }
             tc_fence_before();
             mbar_arrive(B(bs_empty[h]));  // S_j is read: the MMAs may write S_{j+1}
-            const float sum = ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+            const float sum = ((sum4[0].x + sum4[0].y) + (sum4[1].x + sum4[1].y)) +
+                              ((sum4[2].x + sum4[2].y) + (sum4[3].x + sum4[3].y));
             l = __fmaf_rn(l, a, sum);
-            mrow = m_new;
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(B(bp_full[h]));
-            a_pend = a;
         }
-        fold_pv(n - 1);
+        // The output: O / l, once PV_{n-1} is in O.
+        mbar_wait(B(bo_full[h]), (n - 1) & 1, err, &gave_up);
+        tc_fence_after();
+        uint32_t v[4][16];
+#pragma unroll
+        for (int c = 0; c < 4; c++) tmem_ld16_nowait(lanes + o_col(h) + c * 16, v[c]);
+        tmem_wait_ld();
         if (pos >= 0) {
             const float inv = 1.0f / l;
             uint4 *dst = reinterpret_cast<uint4 *>(out + ((size_t)(r0 + m) * heads + head0 + h) * 64);
@@ -292,8 +335,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                 uint32_t w[4];
 #pragma unroll
                 for (int e = 0; e < 4; e++) {
-                    const __nv_bfloat162 pp =
-                        __floats2bfloat162_rn(o[8 * c + 2 * e] * inv, o[8 * c + 2 * e + 1] * inv);
+                    const int d = 8 * c + 2 * e;
+                    const __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(v[d / 16][d % 16]) * inv,
+                                                                    __uint_as_float(v[d / 16][d % 16 + 1]) * inv);
                     w[e] = *reinterpret_cast<const uint32_t *>(&pp);
                 }
                 dst[c] = make_uint4(w[0], w[1], w[2], w[3]);

@@ -92,6 +92,17 @@ TG_DEVICE void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
 }
 TG_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Stores 16 consecutive f32 columns of this warp's 32 TMEM lanes (lane i of the warp to row
+// (warp % 4) * 32 + i); tmem_wait_st before anything else reads or writes them.
+TG_DEVICE void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+TG_DEVICE void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // 16 consecutive f32 columns of this warp's 32 TMEM lanes: lane i of the warp gets row
 // (warp % 4) * 32 + i.
 TG_DEVICE void tmem_ld16(uint32_t taddr, float (&v)[16]) {
