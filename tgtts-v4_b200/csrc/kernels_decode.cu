@@ -594,9 +594,6 @@ struct PersistArgs {
 };
 
 TG_DEVICE uint32_t *abort_word(const PersistArgs &a) { return a.flags + (size_t)a.layers * PS_PHASES * PS_NCOUNT; }
-TG_DEVICE uint32_t *chunks_done(const PersistArgs &a, int l, int b, int kv) {
-    return abort_word(a) + 1 + ((size_t)l * PS_ROWS + b) * a.p.kv_heads + kv;
-}
 
 // The units, row length and rows per unit of weight phase wi (0 q/k/v, 1 o, 2 gate/up, 3 down).
 struct WPhase {
@@ -742,18 +739,23 @@ TG_DEVICE void stage_gain(const float *g, int k, float *gs, int ctid) {
         reinterpret_cast<float4 *>(gs)[i] = __ldg(reinterpret_cast<const float4 *>(g) + i);
 }
 
-// attention_combine for the GROUP heads of kv head `kv` of row b (attention_combine.comp:29-58),
-// into att [rows][heads hd] f32: thread t takes four dimensions of one head, loads the head's chunk
-// maxima and sums and its four columns of every chunk's partial output in one batch (the first 16
-// chunks; longer caches continue chunk by chunk), and folds them in chunk order as
-// attention_combine_kernel does.
-TG_DEVICE void flow_join(const PersistArgs &a, int b, int kv, int n, int ctid) {
+// attention_combine (attention_combine.comp:29-58) as the output projection's staging: every
+// head of every row joined from the attention phase's chunk partials straight into xs (Stage
+// layout, as flow_stage would stage att [rows][heads hd]). Thread t takes four dimensions of one
+// head, loads the head's chunk maxima and sums and its four columns of every chunk's partial output
+// in one batch (the first 16 chunks; longer caches continue chunk by chunk), and folds them in
+// chunk order as attention_combine_kernel does, so the staged values are its bits. Each block joins
+// for itself: one round trip through L2 after the attention phase, instead of a join by one block,
+// a store and a second round trip. A spare row stages zeros.
+template <typename T, int NB>
+TG_DEVICE void flow_stage_join(const PersistArgs &a, int rows, const int (&nch)[PS_ROWS], float *xs, int ctid) {
     constexpr int B = 16;
     const tg_params &p = a.p;
-    const int hd = p.head_dim, heads = p.heads, q4 = hd / 4, group = heads / p.kv_heads;
+    const int hd = p.head_dim, heads = p.heads, q4 = hd / 4, k = heads * hd;
     const int chunks = attn_chunks(p.capacity);
-    for (int i = ctid; i < group * q4; i += PS_CTHREADS) {
-        const int h = kv * group + i / q4, d4 = i % q4;
+    for (int i = ctid; i < NB * heads * q4; i += PS_CTHREADS) {
+        const int b = i / (heads * q4), h = (i / q4) % heads, d4 = i % q4;
+        const int n = b < rows ? nch[b] : 0;
         const float2 *ml = reinterpret_cast<const float2 *>(a.pml) + ((size_t)b * heads + h) * chunks;
         const float4 *o = reinterpret_cast<const float4 *>(a.po) + ((size_t)b * heads + h) * chunks * q4 + d4;
         float2 mv[B];
@@ -790,10 +792,12 @@ TG_DEVICE void flow_join(const PersistArgs &a, int b, int kv, int n, int ctid) {
             acc.z = __fmaf_rn(oc.z, w, acc.z);
             acc.w = __fmaf_rn(oc.w, w, acc.w);
         }
-        reinterpret_cast<float4 *>(a.att + ((size_t)b * heads + h) * hd)[d4] =
-            make_float4(__fdiv_rn(acc.x, total), __fdiv_rn(acc.y, total), __fdiv_rn(acc.z, total),
-                        __fdiv_rn(acc.w, total));
+        const float4 v = n > 0 ? make_float4(__fdiv_rn(acc.x, total), __fdiv_rn(acc.y, total),
+                                             __fdiv_rn(acc.z, total), __fdiv_rn(acc.w, total))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(xs + Stage<T>::index(k, b, 4 * (h * q4 + d4))) = v;
     }
+    ConsumerSync::sync();
 }
 
 // One weight segment's dot products and epilogues. Warp w takes units w, w + 8, ..., U of them at
@@ -851,7 +855,6 @@ __global__ void __launch_bounds__(PS_THREADS, 1) decode_step_kernel(const __grid
     // the linear ring end of the last one.
     __shared__ volatile unsigned long long released;
     __shared__ int ok_t;
-    __shared__ int last_s;
     __shared__ float scales[PS_ROWS];
     __shared__ int ok_s;
     const tg_params &p = a.p;
@@ -1050,25 +1053,16 @@ __global__ void __launch_bounds__(PS_THREADS, 1) decode_step_kernel(const __grid
                 attention_chunk<T, ConsumerSync>(p, a.q, kc, vc, b, kv, c, pb, sb, a.po + (head0 * chunks + c) * hd,
                                                  (size_t)chunks * hd, a.pml + (head0 * chunks + c) * 2,
                                                  (size_t)chunks * 2, work, ctid, PS_CTHREADS, wait_qkv);
-                // The block that writes the last chunk of (row, kv head) joins them: every thread's
-                // partials published, then the count (the threadfence-reduction pattern).
-                __threadfence();
-                ConsumerSync::sync();
-                if (ctid == 0) {
-                    last_s = atomicAdd(chunks_done(a, l, b, kv), 1u) + 1 == (uint32_t)nch[b];
-                    __threadfence();
-                }
-                ConsumerSync::sync();
-                if (last_s) flow_join(a, b, kv, nch[b], ctid);
             }
         }
         if (!ok) break;
         arrive(a, l, PH_ATT, ctid);
-        // The join of every head's chunks, then the output projection with the residual.
+        // The join of every head's chunks (each block its own), then the output projection with the
+        // residual.
         share(p, 1, wphase(p, 1).units, ub, ue);
         if (ub < ue) {
             if (!wait_phase(a, l, PH_ATT, ctid, &ok_s)) ok = false;
-            flow_stage<T, NB>(a.att, nullptr, false, rows, heads * hd, p.eps, xs, scales, ctid);
+            flow_stage_join<T, NB>(a, rows, nch, xs, ctid);
             const SegRef seg = take(1, ue - ub);
             GemvArgs ga{};
             ga.p = p;
@@ -1322,8 +1316,8 @@ cudaError_t launch_attention_combine(const tg_params &p, const uint32_t *at, con
 // memory allows beside the block's staging space. Returns cudaErrorNotSupported for batches or
 // shapes it does not take (more than PS_ROWS rows; a block's share of a projection larger than
 // the ring).
-size_t decode_step_flag_bytes(int layers, int kv_heads) {
-    return ((size_t)layers * PS_PHASES * PS_NCOUNT + 1 + (size_t)layers * PS_ROWS * kv_heads) * sizeof(uint32_t);
+size_t decode_step_flag_bytes(int layers) {
+    return ((size_t)layers * PS_PHASES * PS_NCOUNT + 1) * sizeof(uint32_t);
 }
 
 template <typename T, int NB>
@@ -1401,7 +1395,7 @@ cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s
     a.ring = (uint32_t)(room / row_max * row_max);  // a multiple of every phase's row length
     if (a.ring < seg) return cudaErrorNotSupported;
     const size_t smem = a.ring + scratch;
-    const size_t flag_bytes = decode_step_flag_bytes(d.layers, (int)p.kv_heads);
+    const size_t flag_bytes = decode_step_flag_bytes(d.layers);
     if (p.dtype == TG_BF16)
         return NB == 1 ? launch_step_t<bf16, 1>(a, sm_count, smem, flag_bytes, s)
                        : launch_step_t<bf16, 2>(a, sm_count, smem, flag_bytes, s);

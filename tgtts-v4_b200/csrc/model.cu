@@ -367,7 +367,7 @@ extern "C" int tg_decoder_create(tg_ctx *ctx, const tg_shape *s, uint32_t rows, 
     TG_TRY(d->words.alloc(ctx, 2 * R * 4));
     TG_TRY(d->po.alloc(ctx, R * s->heads * chunks * s->head_dim * F));
     TG_TRY(d->pml.alloc(ctx, R * s->heads * chunks * 2 * F));
-    TG_TRY(d->psync.alloc(ctx, decode_step_flag_bytes((int)s->layers, (int)s->kv_heads)));
+    TG_TRY(d->psync.alloc(ctx, decode_step_flag_bytes((int)s->layers)));
     {
         std::vector<uint64_t> offs;
         for (const LayerOffsets &o : d->layer) {

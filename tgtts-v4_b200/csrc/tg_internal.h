@@ -59,7 +59,7 @@ struct DecodeStep {
     float *h, *mid, *mlp, *q, *att, *out, *po, *pml;
     unsigned char *kcache, *vcache;
     uint64_t cache_layer;
-    uint32_t *sync;  // decode_step_flag_bytes(layers, kv_heads): the step's counters, zeroed by the launch
+    uint32_t *sync;  // decode_step_flag_bytes(layers): the step's counters, zeroed by the launch
     uint32_t *err;
 };
 // Kernel ids past the table's, for launches the library records itself.
@@ -192,7 +192,7 @@ cudaError_t launch_dtc_residual(const tg_params &p, const float *x, const void *
 // the shape or batch is not one it takes.
 cudaError_t launch_decode_step(const DecodeStep &d, int sm_count, cudaStream_t s);
 // The bytes of the persistent step's arrival counters for a stack of `layers` layers.
-size_t decode_step_flag_bytes(int layers, int kv_heads);
+size_t decode_step_flag_bytes(int layers);
 // The decode constants: positions per attention chunk.
 constexpr uint32_t ATTN_CHUNK = 64;
 // The most query heads one KV head may serve: decode attention gives a thread at most 8 of a
