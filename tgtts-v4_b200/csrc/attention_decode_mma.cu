@@ -26,13 +26,7 @@ constexpr int AM_WARPS = 4;
 constexpr int AM_ROW = 64 + fa::PAD;  // bf16 per shared row
 constexpr int AM_WARP_SMEM = 2 * (int)ATTN_CHUNK * AM_ROW * 2;  // K and V of one chunk
 
-TG_DEVICE void split_pack(float x0, float x1, uint32_t &hi, uint32_t &lo) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
-    const float h0 = __low2float(h), h1 = __high2float(h);
-    hi = *reinterpret_cast<const uint32_t *>(&h);
-    const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
-    lo = *reinterpret_cast<const uint32_t *>(&l);
-}
+using fa::split_pack;
 
 }  // namespace
 

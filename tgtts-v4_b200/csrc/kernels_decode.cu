@@ -10,7 +10,9 @@
 // how the rows are cut over blocks. Norms are summed by tg::warp_rms_scale in every kernel.
 
 #include <algorithm>
+#include <type_traits>
 
+#include "mma_common.cuh"
 #include "tg_common.cuh"
 #include "tg_internal.h"
 
@@ -368,11 +370,157 @@ TG_DEVICE void chunk_outputs(const float *vs, const float *ps, int hd, int group
     }
 }
 
+// The chunk's softmax (attention_split.comp:84-94) over scaled scores ps [group][C] (masked
+// positions -inf): m = the largest, e = exp(s - m) in place, l = sum e, a warp to a head; m and l
+// stored.
+template <typename Sync>
+TG_DEVICE void chunk_softmax(float *ps, int group, float *__restrict__ ml_out, size_t ml_stride, int tid,
+                             int nthreads) {
+    constexpr int C = ATTN_CHUNK;
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int h = warp; h < group; h += nthreads / 32) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int t = 0; t < C / 32; t++) m = fmaxf(m, ps[h * C + t * 32 + lane]);
+        m = warp_max(m);
+        float l = 0.0f;
+#pragma unroll
+        for (int t = 0; t < C / 32; t++) {
+            const float e = expf(ps[h * C + t * 32 + lane] - m);
+            ps[h * C + t * 32 + lane] = e;
+            l += e;
+        }
+        l = warp_sum(l);
+        if (lane == 0) {
+            ml_out[h * ml_stride] = m;
+            ml_out[h * ml_stride + 1] = l;
+        }
+    }
+}
+
+// attention_chunk for bf16 caches and a head dimension of 64, on the tensor cores: the chunk's keys
+// and values stay bf16 in shared memory (rows padded for ldmatrix), the group's query heads are
+// the rows of mma.sync.m16n8k16 (rows past the group zero): S = q K^T with q split into bf16 hi +
+// lo (two MMAs a step, so the scores carry 16 bits of each query value), then chunk_softmax, then
+// O = e V with e split the same way and V^T fragments by ldmatrix.trans. Warp w takes the 16-column
+// tile pairs w, w + warps, ... of S and of O, so an element's MMAs and their order are the same
+// for any thread count.
+template <typename Sync, typename Wait>
+__device__ void attention_chunk_mma(const tg_params &p, const float *__restrict__ q, const bf16 *__restrict__ kc,
+                                    const bf16 *__restrict__ vc, int b, int kv, int c, uint32_t pos, uint32_t slot,
+                                    float *__restrict__ o_out, size_t o_stride, float *__restrict__ ml_out,
+                                    size_t ml_stride, float *smem, int tid, int nthreads, const Wait &wait) {
+    constexpr int C = ATTN_CHUNK, HD = 64, ROW = HD + fa::PAD;
+    static_assert(C == 64, "four 16-position k-steps and four tile pairs a chunk");
+    const int heads = p.heads, kvh = p.kv_heads, group = heads / kvh;
+    const int start = c * C, first_head = kv * group;
+    bf16 *ks = reinterpret_cast<bf16 *>(smem);  // [C][ROW]
+    bf16 *vs = ks + C * ROW;                    // [C][ROW]
+    float *qs = reinterpret_cast<float *>(vs + C * ROW);  // [group][HD]
+    float *ps = qs + group * HD;                          // [group][C]
+    const size_t base = (((size_t)slot * kvh + kv) * p.capacity + start) * HD;
+    const uint4 *ksrc = reinterpret_cast<const uint4 *>(kc + base);
+    const uint4 *vsrc = reinterpret_cast<const uint4 *>(vc + base);
+    // Keys and values, 8 bf16 at a time: the positions before the row's before the wait, the row's
+    // own (which the kernel before appends) after it; past it zero.
+    for (int pass = 0; pass < 2; pass++) {
+        if (pass == 1) wait();  // a no-op after the first wait of the block
+        for (int i = tid; i < C * (HD / 8); i += nthreads) {
+            const int pp = i / (HD / 8), j = i % (HD / 8);
+            const int at_pos = start + pp;
+            if ((pass == 0) != (at_pos < (int)pos)) continue;
+            uint4 kk = make_uint4(0u, 0u, 0u, 0u), vv = kk;
+            if (at_pos <= (int)pos) {
+                kk = __ldcg(ksrc + i);
+                vv = __ldcg(vsrc + i);
+            }
+            *reinterpret_cast<uint4 *>(ks + pp * ROW + j * 8) = kk;
+            *reinterpret_cast<uint4 *>(vs + pp * ROW + j * 8) = vv;
+        }
+    }
+    {
+        const float4 *src = reinterpret_cast<const float4 *>(q + ((size_t)b * heads + first_head) * HD);
+        for (int i = tid; i < group * HD / 4; i += nthreads) reinterpret_cast<float4 *>(qs)[i] = __ldcg(src + i);
+    }
+    Sync::sync();
+    const int warp = tid >> 5, lane = tid & 31, warps = nthreads >> 5, g = lane >> 2, t4 = lane & 3;
+    const int mi = lane >> 3, rr = lane & 7;
+    const float scale = 1.0f / sqrtf((float)HD);
+    // Row r's columns k0 + 2 t4 and + 1 of a [group][ld] f32 matrix, as hi and lo bf16 pairs.
+    auto frag = [&](const float *m, int ld, int r, int k0, uint32_t &hi, uint32_t &lo) {
+        hi = lo = 0u;
+        if (r < group) {
+            const float2 x = *reinterpret_cast<const float2 *>(m + r * ld + k0 + 2 * t4);
+            fa::split_pack(x.x, x.y, hi, lo);
+        }
+    };
+    // S = q K^T: tile pair t covers positions 16 t .. 16 t + 15.
+    for (int t = warp; t < C / 16; t += warps) {
+        float sc[2][4] = {};
+#pragma unroll
+        for (int s = 0; s < HD / 16; s++) {
+            uint32_t qh[4], ql[4], kb[4];
+            frag(qs, HD, g, 16 * s, qh[0], ql[0]);
+            frag(qs, HD, g + 8, 16 * s, qh[1], ql[1]);
+            frag(qs, HD, g, 16 * s + 8, qh[2], ql[2]);
+            frag(qs, HD, g + 8, 16 * s + 8, qh[3], ql[3]);
+            fa::ldmatrix_x4(kb, ks + (16 * t + (mi >> 1) * 8 + rr) * ROW + 16 * s + (mi & 1) * 8);
+            fa::mma_bf16(sc[0], qh, kb[0], kb[1]);
+            fa::mma_bf16(sc[0], ql, kb[0], kb[1]);
+            fa::mma_bf16(sc[1], qh, kb[2], kb[3]);
+            fa::mma_bf16(sc[1], ql, kb[2], kb[3]);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 2; jj++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int h = g + 8 * (e >> 1), col = 16 * t + 8 * jj + 2 * t4 + (e & 1);
+                if (h < group) ps[h * C + col] = start + col <= (int)pos ? sc[jj][e] * scale : -INFINITY;
+            }
+    }
+    Sync::sync();
+    chunk_softmax<Sync>(ps, group, ml_out, ml_stride, tid, nthreads);
+    Sync::sync();
+    // O = e V: tile pair t covers dimensions 16 t .. 16 t + 15.
+    for (int t = warp; t < HD / 16; t += warps) {
+        float o[2][4] = {};
+#pragma unroll
+        for (int s = 0; s < C / 16; s++) {
+            uint32_t ph[4], pl[4], vb[4];
+            frag(ps, C, g, 16 * s, ph[0], pl[0]);
+            frag(ps, C, g + 8, 16 * s, ph[1], pl[1]);
+            frag(ps, C, g, 16 * s + 8, ph[2], pl[2]);
+            frag(ps, C, g + 8, 16 * s + 8, ph[3], pl[3]);
+            fa::ldmatrix_x4_trans(vb, vs + (16 * s + (mi & 1) * 8 + rr) * ROW + 16 * t + (mi >> 1) * 8);
+            fa::mma_bf16(o[0], ph, vb[0], vb[1]);
+            fa::mma_bf16(o[0], pl, vb[0], vb[1]);
+            fa::mma_bf16(o[1], ph, vb[2], vb[3]);
+            fa::mma_bf16(o[1], pl, vb[2], vb[3]);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 2; jj++)
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const int h = g + 8 * i;
+                if (h < group)
+                    *reinterpret_cast<float2 *>(o_out + h * o_stride + 16 * t + 8 * jj + 2 * t4) =
+                        make_float2(o[jj][2 * i], o[jj][2 * i + 1]);
+            }
+    }
+}
+
 template <typename T, typename Sync = BlockSync, typename Wait = PdlWait>
 __device__ void attention_chunk(const tg_params &p, const float *__restrict__ q, const T *__restrict__ kc,
                                 const T *__restrict__ vc, int b, int kv, int c, uint32_t pos, uint32_t slot,
                                 float *__restrict__ o_out, size_t o_stride, float *__restrict__ ml_out,
                                 size_t ml_stride, float *smem, int tid, int nthreads, const Wait &wait = Wait()) {
+    if constexpr (std::is_same<T, bf16>::value) {
+        if (p.head_dim == 64) {
+            attention_chunk_mma<Sync>(p, q, kc, vc, b, kv, c, pos, slot, o_out, o_stride, ml_out, ml_stride, smem, tid,
+                                      nthreads, wait);
+            return;
+        }
+    }
     constexpr int C = ATTN_CHUNK;
     using VT = Vec<T>;
     using Raw = typename VT::Raw;
@@ -424,25 +572,7 @@ __device__ void attention_chunk(const tg_params &p, const float *__restrict__ q,
         default: chunk_scores<8, C>(qs, ks4, row4, ps, hd, group, start, (int)pos, scale, tid, nthreads); break;
     }
     Sync::sync();
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int h = warp; h < group; h += nthreads / 32) {
-        float m = -INFINITY;
-#pragma unroll
-        for (int t = 0; t < C / 32; t++) m = fmaxf(m, ps[h * C + t * 32 + lane]);
-        m = warp_max(m);
-        float l = 0.0f;
-#pragma unroll
-        for (int t = 0; t < C / 32; t++) {
-            const float e = expf(ps[h * C + t * 32 + lane] - m);
-            ps[h * C + t * 32 + lane] = e;
-            l += e;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            ml_out[h * ml_stride] = m;
-            ml_out[h * ml_stride + 1] = l;
-        }
-    }
+    chunk_softmax<Sync>(ps, group, ml_out, ml_stride, tid, nthreads);
     Sync::sync();
     switch ((group + nthreads / hd - 1) / (nthreads / hd)) {
         case 1: chunk_outputs<1, C>(vs, ps, hd, group, o_out, o_stride, tid, nthreads); break;
@@ -470,6 +600,8 @@ TG_DEVICE float join_chunks(const float *o, size_t stride, const float *w, int n
 
 static size_t attention_smem(const tg_params &p) {
     const size_t group = p.heads / p.kv_heads, hd = p.head_dim, C = ATTN_CHUNK;
+    if (p.dtype == TG_BF16 && hd == 64)  // attention_chunk_mma: bf16 keys and values, f32 q and scores
+        return 2 * C * (64 + fa::PAD) * sizeof(bf16) + sizeof(float) * (group * hd + group * C);
     return sizeof(float) * (group * hd + C * (hd + 4) + C * hd + group * C);
 }
 

@@ -37,6 +37,14 @@ TG_DEVICE void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// x0, x1 as bf16 pairs hi and lo with hi + lo = x to about 16 bits (hi rounded, lo the rest rounded).
+TG_DEVICE void split_pack(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float h0 = __low2float(h), h1 = __high2float(h);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(__fsub_rn(x0, h0), __fsub_rn(x1, h1));
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
 TG_DEVICE uint32_t pack_bf16(float lo, float hi) {
     const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<const uint32_t *>(&v);
