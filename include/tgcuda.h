@@ -123,7 +123,7 @@ typedef enum {
     TG_KERNEL_GEMV_GATE_UP = 5,
     /* data u32 -> out u32 (one word per block)                                  stream_read.comp */
     TG_KERNEL_STREAM_READ = 6,
-    /* at u32 [2 rows], x f32, gain f32 -> out T                                   norm_rows.comp */
+    /* at u32 [2 rows], x f32, gain f32 -> out T (f32 when params.normed_f32)     norm_rows.comp */
     TG_KERNEL_NORM_ROWS = 7,
     /* at u32, c f32 [parts][rows][hidden], residual f32, gain f32 -> sum f32, normed (T, or f32
      * when params.normed_f32); c's parts (params.parts, 0 or 1: one; at most 16) are a GEMM's

@@ -79,13 +79,16 @@ struct TcLayout {
 // accumulator are one output's gate and up, or (B the
 // q/k/v projection) rope_rows.comp's work: RoPE on each head's column pairs (i, i + hd/2), q rows
 // stored bf16, k and v rows appended to the cache at the row's position and slot.
-enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1, TC_EPI_ROPE = 2 };
+// TC_EPI_RES: C = residual + s C in f32, add_norm_rows.comp's sum (the same fused multiply-add),
+// stored in place of C.
+enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1, TC_EPI_ROPE = 2, TC_EPI_RES = 3 };
 
-struct RopeEpi {
+struct EpiArgs {
     tg_params p;
     const uint32_t *at;
     const float *cosv, *sinv;
     bf16 *q, *kc, *vc;
+    const float *res;  // TC_EPI_RES: [M][N] f32, scaled by p.residual_scale
 };
 
 // Persistent: one block per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m fastest, so the
@@ -102,7 +105,7 @@ constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
 template <int BN, int EPI = TC_EPI_F32>
 __global__ void __launch_bounds__(TC_PTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ RopeEpi re,
+                   void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ EpiArgs re,
                    int b_const, int parts) {
     using L = TcLayout<BN>;
     constexpr int S = L::STAGES;
@@ -321,8 +324,17 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                 }
             } else {
                 float *C = static_cast<float *>(Cout) + (size_t)(t / per) * M * N;
+                const float sc = re.p.residual_scale;
 #pragma unroll 1
                 for (int c0 = 0; c0 < BN; c0 += 32) {
+                    float4 r[8];
+                    if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
+                        if (row < M) {
+#pragma unroll
+                            for (int e = 0; e < 8; e++)
+                                r[e] = __ldg(reinterpret_cast<const float4 *>(re.res + (size_t)row * N + n0 + c0) + e);
+                        }
+                    }
                     uint32_t v[2][16];
                     tmem_ld16_nowait(lane_base + c0, v[0]);
                     tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
@@ -330,9 +342,14 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                     if (row < M) {
                         float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
 #pragma unroll
-                        for (int e = 0; e < 8; e++)
-                            dst[e] = make_float4(__uint_as_float(v[e / 4][4 * (e % 4)]), __uint_as_float(v[e / 4][4 * (e % 4) + 1]),
-                                                 __uint_as_float(v[e / 4][4 * (e % 4) + 2]), __uint_as_float(v[e / 4][4 * (e % 4) + 3]));
+                        for (int e = 0; e < 8; e++) {
+                            float4 o = make_float4(__uint_as_float(v[e / 4][4 * (e % 4)]), __uint_as_float(v[e / 4][4 * (e % 4) + 1]),
+                                                   __uint_as_float(v[e / 4][4 * (e % 4) + 2]), __uint_as_float(v[e / 4][4 * (e % 4) + 3]));
+                            if constexpr (EPI == TC_EPI_RES)
+                                o = make_float4(__fmaf_rn(sc, o.x, r[e].x), __fmaf_rn(sc, o.y, r[e].y),
+                                                __fmaf_rn(sc, o.z, r[e].z), __fmaf_rn(sc, o.w, r[e].w));
+                            dst[e] = o;
+                        }
                     }
                 }
             }
@@ -353,7 +370,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
 
 template <int BN, int EPI = TC_EPI_F32>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
-                             cudaStream_t s, bool b_const, const RopeEpi &re = RopeEpi{}, int parts = 1) {
+                             cudaStream_t s, bool b_const, const EpiArgs &re = EpiArgs{}, int parts = 1) {
     CUtensorMap ma, mb;
     const int b_box = EPI == TC_EPI_SILU ? BN / 2 : BN;  // the SiLU tile's B is two boxes
     if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, b_box))
@@ -387,13 +404,13 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
     // stream the weights. Both are the caller's choice, not the rows': a row's sums do not depend
     // on how many rows a launch takes.
     if (p.flags & 2) {
-        if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
+        if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, EpiArgs{}, parts);
         return cudaErrorInvalidValue;
     }
     if (parts > 1) {
-        if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
-        if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
-        return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, RopeEpi{}, parts);
+        if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const, EpiArgs{}, parts);
+        if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const, EpiArgs{}, parts);
+        return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, EpiArgs{}, parts);
     }
     if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
     if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
@@ -408,11 +425,24 @@ cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *
     if (p.dtype != TG_BF16 || M <= 0 || N % 256 || K % TC_BK || 256 % p.head_dim ||
         N != (int)((p.heads + 2 * p.kv_heads) * p.head_dim) || p.rows != p.m)
         return cudaErrorInvalidValue;
-    RopeEpi re{p, at, cosv, sinv, (bf16 *)q, (bf16 *)kc, (bf16 *)vc};
+    EpiArgs re{p, at, cosv, sinv, (bf16 *)q, (bf16 *)kc, (bf16 *)vc, nullptr};
     // A tile holds whole heads; narrow tiles (flags bit 1, a batched decode step) one head each, so
     // that more blocks stream the weights.
     if ((p.flags & 2) && p.head_dim == 64) return launch_tc<64, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
     return launch_tc<256, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
+}
+
+cudaError_t launch_gemm_residual(const tg_params &p, const void *a, const void *b, const float *res, float *out,
+                                 uint32_t *err, cudaStream_t s) {
+    const int M = (int)p.m, N = (int)p.n, K = (int)p.k;
+    if (p.dtype != TG_BF16 || M <= 0 || N % 64 || K % TC_BK || p.parts > 1) return cudaErrorInvalidValue;
+    EpiArgs re{};
+    re.p = p;
+    re.res = res;
+    const bool b_const = (p.flags & 1) != 0;
+    if (N % 256 == 0) return launch_tc<256, TC_EPI_RES>(a, b, out, M, N, K, err, s, b_const, re);
+    if (N % 128 == 0) return launch_tc<128, TC_EPI_RES>(a, b, out, M, N, K, err, s, b_const, re);
+    return launch_tc<64, TC_EPI_RES>(a, b, out, M, N, K, err, s, b_const, re);
 }
 
 cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, void *out, uint32_t *err,

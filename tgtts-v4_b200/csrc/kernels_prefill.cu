@@ -490,7 +490,8 @@ __global__ void __launch_bounds__(128)
 cudaError_t launch_norm_rows(const tg_params &p, const uint32_t *at, const float *x,
                              const float *g, void *out, cudaStream_t s) {
     const dim3 grid((p.rows + 3) / 4);
-    if (p.dtype == TG_BF16) return launch_pdl(norm_rows_kernel<bf16>, grid, dim3(128), 0, s, p, at, x, g, (bf16 *)out);
+    if (p.dtype == TG_BF16 && !p.normed_f32)
+        return launch_pdl(norm_rows_kernel<bf16>, grid, dim3(128), 0, s, p, at, x, g, (bf16 *)out);
     return launch_pdl(norm_rows_kernel<float>, grid, dim3(128), 0, s, p, at, x, g, (float *)out);
 }
 

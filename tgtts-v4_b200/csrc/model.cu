@@ -789,6 +789,23 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
         g.flags = 1;  // b is a weight: its first tiles stream while the kernel before finishes
         push(v, TG_KERNEL_GEMM, g, label, {{a, R * k * T}, {b, n * k * T}, {c, R * n * F}});
     };
+    // bf16: the residual added in the GEMM's epilogue (sum = residual + s a b^T), then norm_rows
+    // over the sum - add_norm_rows' sums and norm, without the GEMM's f32 rows going through memory.
+    const bool fused_res = d.dtype == TG_BF16;
+    auto gemm_res = [&](const char *label, void *a, void *b, void *sum, void *res, uint64_t n, uint64_t k) {
+        tg_params g = base;
+        g.m = rows;
+        g.n = (uint32_t)n;
+        g.k = (uint32_t)k;
+        g.flags = 1;
+        push(v, KERNEL_GEMM_RESIDUAL, g, label, {{a, R * k * T}, {b, n * k * T}, {sum, R * n * F}, {res, R * n * F}});
+    };
+    auto norm = [&](const char *label, void *x, uint64_t gain, void *out, bool f32_out) {
+        tg_params nr = base;
+        nr.normed_f32 = f32_out ? 1 : 0;
+        push(v, TG_KERNEL_NORM_ROWS, nr, label,
+             {{p.words.ptr(), words}, {x, R * H * F}, {d.w(gain), H * F}, {out, R * H * (f32_out ? F : T)}});
+    };
     for (uint32_t l = 0; l < s.layers; l++) {
         const LayerOffsets &o = d.layer[l];
         char *in = l == 0 ? p.x_in.ptr() : p.h.ptr();
@@ -810,10 +827,15 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
         push(v, attention_tc_supported(base) ? TG_KERNEL_ATTENTION_ROWS_TC : TG_KERNEL_ATTENTION_ROWS, base, "attention_rows",
              {{p.words.ptr(), words}, {p.q.ptr(), R * A * T}, {d.kc(l), d.cache_layer}, {d.vc(l), d.cache_layer},
               {p.att.ptr(), R * A * T}});
-        gemm("o_proj", p.att.ptr(), d.w(o.o), p.proj.ptr(), H, A);
-        push(v, TG_KERNEL_ADD_NORM_ROWS, base, "add_norm_rows",
-             {{p.words.ptr(), words}, {p.proj.ptr(), R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
-              {p.mid.ptr(), R * H * F}, {p.normed.ptr(), R * H * T}});
+        if (fused_res) {
+            gemm_res("o_proj", p.att.ptr(), d.w(o.o), p.mid.ptr(), in, H, A);
+            norm("norm_rows", p.mid.ptr(), o.post_norm, p.normed.ptr(), false);
+        } else {
+            gemm("o_proj", p.att.ptr(), d.w(o.o), p.proj.ptr(), H, A);
+            push(v, TG_KERNEL_ADD_NORM_ROWS, base, "add_norm_rows",
+                 {{p.words.ptr(), words}, {p.proj.ptr(), R * H * F}, {in, R * H * F}, {d.w(o.post_norm), H * F},
+                  {p.mid.ptr(), R * H * F}, {p.normed.ptr(), R * H * T}});
+        }
         if (d.dtype == TG_BF16) {
             // SiLU-mul in the GEMM's epilogue: the f32 gate/up rows never reach memory.
             tg_params g = base;
@@ -827,8 +849,14 @@ static std::vector<Launch> prefill_launches(tg_prefill &p, uint32_t rows) {
             push(v, TG_KERNEL_SILU_MUL_ROWS, base, "silu_mul_rows",
                  {{p.words.ptr(), words}, {p.gu.ptr(), R * 2 * I * F}, {p.mlp.ptr(), R * I * T}});
         }
-        gemm("down_proj", p.mlp.ptr(), d.w(o.down), p.proj.ptr(), H, I);
         const bool last = l + 1 == s.layers;
+        if (fused_res) {
+            gemm_res("down_proj", p.mlp.ptr(), d.w(o.down), p.h.ptr(), p.mid.ptr(), H, I);
+            norm("norm_rows", p.h.ptr(), last ? d.final_norm : d.layer[l + 1].in_norm, last ? p.out.ptr() : p.normed.ptr(),
+                 last);
+            continue;
+        }
+        gemm("down_proj", p.mlp.ptr(), d.w(o.down), p.proj.ptr(), H, I);
         tg_params an = base;
         an.normed_f32 = last ? 1 : 0;
         push(v, TG_KERNEL_ADD_NORM_ROWS, an, "add_norm_rows",

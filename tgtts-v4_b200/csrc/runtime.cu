@@ -111,7 +111,7 @@ static int needs(const Launch &l, std::vector<Need> &out) {
             out = {{"data", (uint64_t)p.k * 4}, {"out", (uint64_t)p.n * 4}};
             break;
         case TG_KERNEL_NORM_ROWS:
-            out = {{"at", words}, {"x", rows * H * F}, {"gain", H * F}, {"out", rows * H * T}};
+            out = {{"at", words}, {"x", rows * H * F}, {"gain", H * F}, {"out", rows * H * (p.normed_f32 ? F : T)}};
             break;
         case TG_KERNEL_ADD_NORM_ROWS:
             out = {{"at", words}, {"c", (p.parts > 1 ? p.parts : 1) * rows * H * F}, {"residual", rows * H * F}, {"gain", H * F},
@@ -334,6 +334,7 @@ static uint32_t table_kernel(uint32_t k) {
         case KERNEL_ATTN_SPLIT_MMA:
         case KERNEL_ATTN_SPLIT_MMA_BQ:
         case KERNEL_ATTN_SPLIT_JOIN: return TG_KERNEL_ATTENTION_SPLIT;
+        case KERNEL_GEMM_RESIDUAL: return TG_KERNEL_GEMM;
         case KERNEL_ATTN_COMBINE_WIDE:
         case KERNEL_ATTN_COMBINE_WIDE_BF: return TG_KERNEL_ATTENTION_COMBINE;
         default: return k;
@@ -347,12 +348,13 @@ int check_launch(const Launch &l0) {
     const bool wide = l0.kernel == KERNEL_ATTN_SPLIT_MMA || l0.kernel == KERNEL_ATTN_COMBINE_WIDE ||
                       l0.kernel == KERNEL_ATTN_SPLIT_MMA_BQ || l0.kernel == KERNEL_ATTN_COMBINE_WIDE_BF ||
                       l0.kernel == KERNEL_ATTN_SPLIT_JOIN;
-    if (wide ? !attention_split_mma_supported(l.p) : (l.kernel != l0.kernel && !dtc_supported(l.p)))
+    if (wide ? !attention_split_mma_supported(l.p) : (l.kernel != l0.kernel && l0.kernel != KERNEL_GEMM_RESIDUAL && !dtc_supported(l.p)))
         return fail(TG_ESHAPE, "%s: no tcgen05 plan for %u rows of this shape", l0.label.c_str(), l.p.rows);
     int st = check_shape(l);
     if (st) return st;
     std::vector<Need> need;
     if ((st = needs(l, need))) return st;
+    if (l0.kernel == KERNEL_GEMM_RESIDUAL) need.push_back({"residual", (uint64_t)l.p.m * l.p.n * 4});
     if (l0.kernel == KERNEL_ATTN_SPLIT_JOIN) {
         need.push_back({"out", (uint64_t)l.p.rows * l.p.heads * l.p.head_dim * 2});
         need.push_back({"counts", (uint64_t)l.p.rows * l.p.kv_heads * 4});
@@ -398,6 +400,7 @@ int enqueue_launch(const Launch &l, uint32_t *err, cudaStream_t s, int sm_count)
         case KERNEL_DTC_RESIDUAL: e = launch_dtc_residual(p, F(0), b[1], F(2), F(3), err, s); break;
         case KERNEL_ATTN_SPLIT_MMA: e = launch_attention_split_mma(p, b[0], b[1], b[2], U(3), F(4), F(5), s); break;
         case KERNEL_ATTN_SPLIT_MMA_BQ: e = launch_attention_split_mma(p, b[0], b[1], b[2], U(3), F(4), F(5), s, true); break;
+        case KERNEL_GEMM_RESIDUAL: e = launch_gemm_residual(p, b[0], b[1], F(3), F(2), err, s); break;
         case KERNEL_ATTN_SPLIT_JOIN:
             e = launch_attention_split_join(p, b[0], b[1], b[2], U(3), F(4), F(5), b[6], U(7), s);
             break;

@@ -81,6 +81,11 @@ constexpr uint32_t KERNEL_ATTN_COMBINE_WIDE_BF = 1007;
 // The two of the GEMM-family decoder in one launch (the split's bindings, then out bf16 [rows][heads
 // hd] and counts u32 [rows][kv_heads], zero before the first launch and after each).
 constexpr uint32_t KERNEL_ATTN_SPLIT_JOIN = 1008;
+// The prefill's o and down projections with the residual add in the GEMM's epilogue: GEMM's
+// bindings (a, b, c: the sum) and then the residual f32 [m][n] (scaled by params.residual_scale).
+constexpr uint32_t KERNEL_GEMM_RESIDUAL = 1009;
+cudaError_t launch_gemm_residual(const tg_params &p, const void *a, const void *b, const float *res, float *out,
+                                 uint32_t *err, cudaStream_t s);
 // 64: wider partials (a warp walking sub-chunks) measured slower on B200 at 16-128 rows: 2.15 ms
 // a step at 64 rows with 256 against 2.00 ms with 64.
 constexpr uint32_t DECODE_WIDE_CHUNK = 64;
