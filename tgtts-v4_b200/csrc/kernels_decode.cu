@@ -717,8 +717,7 @@ struct PersistArgs {
     float *h, *mid, *mlp, *q, *att, *out, *po, *pml;
     unsigned char *kcache, *vcache;
     uint64_t cache_layer;
-    // [layers][PS_PHASES][PS_NCOUNT] arrivals, the abort word, then [layers][PS_ROWS][kv_heads] counts
-    // of the attention chunks written; zero at launch.
+    // [layers][PS_PHASES][PS_NCOUNT] arrivals, then the abort word; zero at launch.
     uint32_t *flags;
     uint32_t *err;
     uint32_t ring;    // bytes of the weight ring at the start of dynamic shared memory

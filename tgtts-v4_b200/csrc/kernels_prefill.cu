@@ -9,7 +9,9 @@
 
 namespace tg {
 
-// norm_rows.comp: out = RMSNorm(x) g, rounded to T; a warp to a row.
+// norm_rows.comp: out = RMSNorm(x) g, rounded to T; a warp to a row. A row of up to 1024 values is
+// read once into registers (lane l holding its 16-byte vectors l, l + 32, ...) and its sum of squares
+// taken from them in warp_rms_scale's order, so the same bits as warp_rms_scale over memory.
 template <typename T>
 __global__ void __launch_bounds__(128)
     norm_rows_kernel(tg_params p, const uint32_t *__restrict__ at, const float *__restrict__ x,
@@ -20,6 +22,37 @@ __global__ void __launch_bounds__(128)
     if (row >= (int)p.rows) return;
     const int k = p.hidden;
     const float *xr = x + (size_t)row * k;
+    if (k <= 1024) {
+        constexpr int NV = 1024 / 128;  // vectors a lane at most
+        float4 v[NV];
+        const int nv = k / 128;
+#pragma unroll
+        for (int i = 0; i < NV; i++)
+            if (i < nv) v[i] = reinterpret_cast<const float4 *>(xr)[lane + 32 * i];
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            if (i >= nv) continue;
+            ss = __fmaf_rn(v[i].x, v[i].x, ss);
+            ss = __fmaf_rn(v[i].y, v[i].y, ss);
+            ss = __fmaf_rn(v[i].z, v[i].z, ss);
+            ss = __fmaf_rn(v[i].w, v[i].w, ss);
+        }
+        ss = warp_sum(ss);
+        const float s = 1.0f / sqrtf(__fdiv_rn(ss, (float)k) + p.eps);
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            if (i >= nv) continue;
+            const int c = lane + 32 * i;
+            const float4 gg = reinterpret_cast<const float4 *>(g)[c];
+            T *o = out + (size_t)row * k + 4 * c;
+            o[0] = from_f32<T>(v[i].x * s * gg.x);
+            o[1] = from_f32<T>(v[i].y * s * gg.y);
+            o[2] = from_f32<T>(v[i].z * s * gg.z);
+            o[3] = from_f32<T>(v[i].w * s * gg.w);
+        }
+        return;
+    }
     const float s = warp_rms_scale(xr, k, p.eps);
     for (int c = lane; c < k / 4; c += 32) {
         const float4 v = reinterpret_cast<const float4 *>(xr)[c];
