@@ -64,9 +64,10 @@ constexpr int TC_BM = 128, TC_BK = 64;
 constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;  // 16 KiB per stage
 
 
-template <int BN>
+// A stage: the tile's A (128 rows) and B (BN rows, or with CG = 2 this CTA's half of them).
+template <int BN, int CG = 1>
 struct TcLayout {
-    static constexpr int B_BYTES = BN * TC_BK * 2;
+    static constexpr int B_BYTES = BN / CG * TC_BK * 2;
     static constexpr int STAGE = TC_A_BYTES + B_BYTES;
     static constexpr int STAGES = (4 * (TC_A_BYTES + 256 * TC_BK * 2)) / STAGE;  // 192 KiB of stages
     static constexpr int BARRIERS = STAGES * STAGE;                           // offset of the mbarriers
@@ -102,12 +103,21 @@ struct EpiArgs {
 constexpr int TC_EPI_WARPS = 4;
 constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
 
-template <int BN, int EPI = TC_EPI_F32>
+//
+// CG = 2: the grid is pairs of CTAs (clusters of two), a pair taking tiles of 256 rows: each CTA
+// loads its 128 rows of A and half of B's BN rows (for SiLU, CTA 0 the gate rows and CTA 1 the up
+// rows of the tile's outputs), all the copies completing on the leader's (rank 0) barrier, which
+// expects both CTAs' bytes; the leader's MMA thread issues tcgen05.mma.cta_group::2 (M = 256) and
+// commits to the barriers of both CTAs; each CTA's epilogue drains its own TMEM rows as with
+// CG = 1 and releases the accumulator on the leader's barrier. Per stage an SM then reads
+// 128 + BN / 2 rows of K for 128 x BN outputs instead of 128 + BN.
+template <int BN, int EPI = TC_EPI_F32, int CG = 1>
 __global__ void __launch_bounds__(TC_PTHREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ EpiArgs re,
                    int b_const, int parts) {
-    using L = TcLayout<BN>;
+    static_assert(CG == 1 || CG == 2, "one CTA or a pair");
+    using L = TcLayout<BN, CG>;
     constexpr int S = L::STAGES;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -121,14 +131,32 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
     __shared__ int gave_up;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = (M + TC_BM - 1) / TC_BM, per = mt * (N / BN), tiles = per * parts;
+    const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+    const int cta = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // the pair's (or the CTA's) index
+    const int ctas = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+    constexpr int TM = TC_BM * CG;  // rows a tile
+    const int mt = (M + TM - 1) / TM, per = mt * (N / BN), tiles = per * parts;
     const int nk = K / TC_BK / parts;  // k-blocks a tile
+    auto m0_of = [&](int t) { return (t % mt) * TM + (int)rank * TC_BM; };  // this CTA's first row
     auto n0_of = [&](int t) { return ((t % per) / mt) * BN; };
     auto kb0_of = [&](int t) { return (t / per) * nk; };  // the tile's first k-block
+    auto load_a = [&](uint32_t dst, int kx, int m0, uint32_t bar) {
+        if constexpr (CG == 2)
+            tma_load_2d_pair(dst, &map_a, kx, m0, bar);
+        else
+            tma_load_2d(dst, &map_a, kx, m0, bar);
+    };
     // A stage's B tile: BN rows from n0, or (SiLU) the gate rows of outputs n0 / 2 .. + BN / 2 and
-    // then their up rows.
+    // then their up rows; with CG = 2 this CTA's half of them.
     auto load_b = [&](uint32_t dst, int kx, int n0, uint32_t bar) {
-        if constexpr (EPI == TC_EPI_SILU) {
+        if constexpr (CG == 2) {
+            int row = n0 + (int)rank * (BN / 2);
+            if constexpr (EPI == TC_EPI_SILU) {
+                static_assert(BN == 256, "a pair's SiLU tile: 128 gate rows in one CTA, their 128 up rows in the other");
+                row = (n0 / 2 / 128) * 256 + (int)rank * 128;
+            }
+            tma_load_2d_pair(dst, &map_b, kx, row, bar);
+        } else if constexpr (EPI == TC_EPI_SILU) {
             const int o0 = n0 / 2, gate = (o0 / 128) * 256 + o0 % 128;
             tma_load_2d(dst, &map_b, kx, gate, bar);
             tma_load_2d(dst + (BN / 2) * TC_BK * 2, &map_b, kx, gate + 128, bar);
@@ -146,7 +174,8 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(acc_full(a), 1);
-            mbar_init(acc_empty(a), TC_EPI_WARPS * 32);
+            // CG = 1: every epilogue thread; CG = 2: one thread of each CTA's epilogue, on the leader's.
+            mbar_init(acc_empty(a), CG == 2 ? 2 : TC_EPI_WARPS * 32);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -154,13 +183,23 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
         asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_b)) : "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"((uint32_t)(2 * BN))
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if constexpr (CG == 2) {  // warp 1 of both CTAs
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"((uint32_t)(2 * BN))
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                         "r"((uint32_t)(2 * BN))
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
     }
     tc_fence_before();
-    __syncthreads();
+    if constexpr (CG == 2)
+        cluster_sync();  // both CTAs' barriers are initialised before either's copies or commits reach them
+    else
+        __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
@@ -170,36 +209,48 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             // have released it. When B is a weight (constant for the program), the first tile's
             // first stages of B are loaded before the wait on the kernel before it, so that they
             // stream while that kernel finishes; A, that kernel's output, after the wait.
-            const int pre = b_const ? (nk < S ? nk : S) : 0;
+            // With CG = 2 only the leader expects (both CTAs' bytes, on its barrier).
+            auto expect = [&](int s) {
+                if (rank == 0) mbar_arrive_expect_tx(full(s), CG * L::STAGE);
+            };
+            const int pre = b_const && cta < tiles ? (nk < S ? nk : S) : 0;
             for (int kb = 0; kb < pre; kb++) {
-                mbar_arrive_expect_tx(full(kb), L::STAGE);
-                load_b(base + kb * L::STAGE + TC_A_BYTES, (kb0_of(blockIdx.x) + kb) * TC_BK, n0_of(blockIdx.x), full(kb));
+                expect(kb);
+                load_b(base + kb * L::STAGE + TC_A_BYTES, (kb0_of(cta) + kb) * TC_BK, n0_of(cta), full(kb));
             }
             pdl_wait();
             int g = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-                const int m0 = (t % mt) * TC_BM, n0 = n0_of(t), kb0 = kb0_of(t);
+            for (int t = cta; t < tiles; t += ctas) {
+                const int m0 = m0_of(t), n0 = n0_of(t), kb0 = kb0_of(t);
                 for (int kb = 0; kb < nk; kb++, g++) {
                     const int s = g % S, kx = (kb0 + kb) * TC_BK;
                     if (g < pre) {  // B is in flight already
-                        tma_load_2d(base + s * L::STAGE, &map_a, kx, m0, full(s));
+                        load_a(base + s * L::STAGE, kx, m0, full(s));
                         continue;
                     }
                     mbar_wait(empty(s), ((g / S) & 1) ^ 1, err, &gave_up);
-                    mbar_arrive_expect_tx(full(s), L::STAGE);
-                    tma_load_2d(base + s * L::STAGE, &map_a, kx, m0, full(s));
+                    expect(s);
+                    load_a(base + s * L::STAGE, kx, m0, full(s));
                     load_b(base + s * L::STAGE + TC_A_BYTES, kx, n0, full(s));
                 }
             }
-            // Every copy this thread started has landed before the block can end.
-            for (int h = g > S ? g - S : 0; h < g; h++) mbar_wait(full(h % S), (h / S) & 1, err, &gave_up);
+            // Every copy this thread started has landed before the block can end: on the leader's
+            // full barriers, or (the other CTA of a pair) once the MMAs that read them released
+            // this CTA's stages.
+            for (int h = g > S ? g - S : 0; h < g; h++) {
+                if (rank == 0)
+                    mbar_wait(full(h % S), (h / S) & 1, err, &gave_up);
+                else
+                    mbar_wait(empty(h % S), (h / S) & 1, err, &gave_up);
+            }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // MMA issuer: tile i into accumulator i % 2 once the epilogue has drained it.
-            constexpr uint32_t idesc = bf16_idesc(TC_BM, BN);
+        if (lane == 0 && rank == 0) {
+            // MMA issuer (the leader of a pair): tile i into accumulator i % 2 once the epilogue
+            // (both CTAs' with CG = 2) has drained it.
+            constexpr uint32_t idesc = bf16_idesc(TM, BN);
             int g = 0, i = 0;
-            for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
+            for (int t = cta; t < tiles; t += ctas, i++) {
                 const int acc = i & 1;
                 mbar_wait(acc_empty(acc), ((i >> 1) & 1) ^ 1, err, &gave_up);
                 tc_fence_after();
@@ -211,12 +262,23 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                     const uint32_t a_addr = base + s * L::STAGE;
                     const uint32_t b_addr = a_addr + TC_A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < TC_BK / 16; k++)
-                        tc_mma(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
-                               (kb > 0 || k > 0) ? 1u : 0u);
-                    tc_commit(empty(s));
+                    for (int k = 0; k < TC_BK / 16; k++) {
+                        if constexpr (CG == 2)
+                            tc_mma2(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
+                                    (kb > 0 || k > 0) ? 1u : 0u);
+                        else
+                            tc_mma(d, sw128_desc(a_addr + k * 32), sw128_desc(b_addr + k * 32), idesc,
+                                   (kb > 0 || k > 0) ? 1u : 0u);
+                    }
+                    if constexpr (CG == 2)
+                        tc_commit2(empty(s));
+                    else
+                        tc_commit(empty(s));
                 }
-                tc_commit(acc_full(acc));
+                if constexpr (CG == 2)
+                    tc_commit2(acc_full(acc));
+                else
+                    tc_commit(acc_full(acc));
             }
         }
     } else {
@@ -224,9 +286,9 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
         const int q = warp & 3;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int i = 0;
-        for (int t = blockIdx.x; t < tiles; t += gridDim.x, i++) {
+        for (int t = cta; t < tiles; t += ctas, i++) {
             const int acc = i & 1;
-            const int m0 = (t % mt) * TC_BM, n0 = n0_of(t);
+            const int m0 = m0_of(t), n0 = n0_of(t);
             mbar_wait(acc_full(acc), (i >> 1) & 1, err, &gave_up);
             tc_fence_after();
             const int row = m0 + q * 32 + lane;
@@ -355,36 +417,66 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             }
             // The accumulator is drained: the MMAs may fill it again.
             tc_fence_before();
-            mbar_arrive(acc_empty(acc));
+            if constexpr (CG == 2) {  // the epilogue warps together, then one arrival for the CTA
+                asm volatile("bar.sync 2, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
+                if (warp == 2 && lane == 0) mbar_arrive_remote(acc_empty(acc), 0);
+            } else {
+                mbar_arrive(acc_empty(acc));
+            }
         }
     }
     tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
-                     : "memory");
+    if constexpr (CG == 2) {
+        cluster_sync();  // the pair's MMAs and copies into either CTA are done
+        if (warp == 1)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
+                         : "memory");
+    } else {
+        __syncthreads();
+        if (warp == 1)
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(2 * BN))
+                         : "memory");
     }
 }
 
 // ---- host -------------------------------------------------------------------------------------
 
-template <int BN, int EPI = TC_EPI_F32>
+template <int BN, int EPI = TC_EPI_F32, int CG = 1>
 static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N, int K, uint32_t *err,
                              cudaStream_t s, bool b_const, const EpiArgs &re = EpiArgs{}, int parts = 1) {
+    using L = TcLayout<BN, CG>;
     CUtensorMap ma, mb;
-    const int b_box = EPI == TC_EPI_SILU ? BN / 2 : BN;  // the SiLU tile's B is two boxes
+    // The SiLU tile's B is two boxes (gate rows, up rows), one in each CTA of a pair.
+    const int b_box = (EPI == TC_EPI_SILU || CG == 2) ? BN / 2 : BN;
     if (!make_map_bf16(&ma, a, (uint64_t)M, (uint64_t)K, TC_BM) || !make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, b_box))
         return cudaErrorInvalidValue;
-    auto kern = gemm_tc_kernel<BN, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcLayout<BN>::SMEM);
+    auto kern = gemm_tc_kernel<BN, EPI, CG>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int tiles = ((M + TC_BM - 1) / TC_BM) * (N / BN) * parts;
-    return launch_pdl(kern, dim3(tiles < sms ? tiles : sms), dim3(TC_PTHREADS), (size_t)TcLayout<BN>::SMEM, s, ma, mb, c,
-                      M, N, K, err, re, (int)b_const, parts);
+    const int tiles = ((M + TC_BM * CG - 1) / (TC_BM * CG)) * (N / BN) * parts;
+    const int units = sms / CG;  // CTAs, or pairs of them
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CG * (tiles < units ? tiles : units));
+    cfg.blockDim = dim3(TC_PTHREADS);
+    cfg.dynamicSmemBytes = (size_t)L::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = CG;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CG == 2 ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, kern, ma, mb, c, M, N, K, err, re, (int)b_const, parts);
 }
+
+// Tiles of 256 rows for a pair of CTAs when the launch has the rows for it (the prefill's).
+constexpr int TC_PAIR_MIN_ROWS = 256;
 
 cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float *c, uint32_t *err,
                         cudaStream_t s) {
@@ -412,6 +504,7 @@ cudaError_t launch_gemm(const tg_params &p, const void *a, const void *b, float 
         if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const, EpiArgs{}, parts);
         return launch_tc<64>(a, b, c, M, N, K, err, s, b_const, EpiArgs{}, parts);
     }
+    if (N % 256 == 0 && M >= TC_PAIR_MIN_ROWS) return launch_tc<256, TC_EPI_F32, 2>(a, b, c, M, N, K, err, s, b_const);
     if (N % 256 == 0) return launch_tc<256>(a, b, c, M, N, K, err, s, b_const);
     if (N % 128 == 0) return launch_tc<128>(a, b, c, M, N, K, err, s, b_const);
     if (N % 64 == 0) return launch_tc<64>(a, b, c, M, N, K, err, s, b_const);
@@ -429,6 +522,7 @@ cudaError_t launch_gemm_qkv_rope(const tg_params &p, const void *a, const void *
     // A tile holds whole heads; narrow tiles (flags bit 1, a batched decode step) one head each, so
     // that more blocks stream the weights.
     if ((p.flags & 2) && p.head_dim == 64) return launch_tc<64, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
+    if (M >= TC_PAIR_MIN_ROWS) return launch_tc<256, TC_EPI_ROPE, 2>(a, b, nullptr, M, N, K, err, s, true, re);
     return launch_tc<256, TC_EPI_ROPE>(a, b, nullptr, M, N, K, err, s, true, re);
 }
 
@@ -440,6 +534,7 @@ cudaError_t launch_gemm_residual(const tg_params &p, const void *a, const void *
     re.p = p;
     re.res = res;
     const bool b_const = (p.flags & 1) != 0;
+    if (N % 256 == 0 && M >= TC_PAIR_MIN_ROWS) return launch_tc<256, TC_EPI_RES, 2>(a, b, out, M, N, K, err, s, b_const, re);
     if (N % 256 == 0) return launch_tc<256, TC_EPI_RES>(a, b, out, M, N, K, err, s, b_const, re);
     if (N % 128 == 0) return launch_tc<128, TC_EPI_RES>(a, b, out, M, N, K, err, s, b_const, re);
     return launch_tc<64, TC_EPI_RES>(a, b, out, M, N, K, err, s, b_const, re);
@@ -451,6 +546,7 @@ cudaError_t launch_gemm_silu(const tg_params &p, const void *a, const void *b, v
     if (p.dtype != TG_BF16 || M <= 0 || N % 256 || K % TC_BK) return cudaErrorInvalidValue;
     // Narrow tiles (flags bit 1, a batched decode step): 32 outputs a tile, four times the blocks.
     if (p.flags & 2) return launch_tc<64, TC_EPI_SILU>(a, b, out, M, N, K, err, s, true);
+    if (M >= TC_PAIR_MIN_ROWS) return launch_tc<256, TC_EPI_SILU, 2>(a, b, out, M, N, K, err, s, true);
     return launch_tc<256, TC_EPI_SILU>(a, b, out, M, N, K, err, s, true);
 }
 

@@ -77,6 +77,52 @@ TG_DEVICE void tc_commit(uint32_t bar) {
                  : "memory");
 }
 
+// ---- pairs of CTAs (a cluster of two on one TPC, tcgen05 cta_group::2) ----------------------------
+// The MMA issued by the pair's leader (rank 0) reads A's 128 rows and half of B's N from each CTA's
+// shared memory at the same offsets and writes each CTA's 128 rows of D into its own TMEM.
+
+TG_DEVICE uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Every thread of both CTAs: the pair's barriers, shared memory and TMEM are past this point in both.
+TG_DEVICE void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+TG_DEVICE void tc_mma2(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// The leader's MMAs so far done: one arrival on the barrier at `bar`'s offset in each CTA of the
+// pair (a commit to each: the leader's own, and the peer's through its cluster address).
+TG_DEVICE void tc_commit2(uint32_t bar) {
+    uint32_t peer;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 1;" : "=r"(peer) : "r"(bar));
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(peer) : "memory");
+}
+// A 2-D TMA load into this CTA's shared memory whose bytes complete on the leader CTA's barrier at
+// `bar`'s offset (no multicast).
+TG_DEVICE void tma_load_2d_pair(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar & 0xFEFFFFFFu)
+        : "memory");
+}
+// One arrival on the barrier at `bar`'s offset in CTA `rank` of the cluster.
+TG_DEVICE void mbar_arrive_remote(uint32_t bar, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(bar), "r"(rank));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(r) : "memory");
+}
+
 TG_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 TG_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
