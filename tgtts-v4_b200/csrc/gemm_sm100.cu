@@ -100,7 +100,9 @@ struct EpiArgs {
 // TMA; warp 1 owns TMEM (two accumulators of BN columns) and issues the MMAs; warps 2-5 drain an
 // accumulator (tcgen05.ld) and store it while the MMAs fill the other, so that a tile's epilogue
 // overlaps the next tile's main loop.
-constexpr int TC_EPI_WARPS = 4;
+// Eight epilogue warps: two to each quadrant of TMEM lanes, one to each half of the tile's columns
+// (a short main loop, as gate/up's K = 1024, would otherwise wait on SiLU's epilogue).
+constexpr int TC_EPI_WARPS = 8;
 constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
 
 //
@@ -282,8 +284,9 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
             }
         }
     } else {
-        // Epilogue: warp w drains TMEM lanes (w % 4) * 32 .. + 31, i.e. rows m0 + that of the tile.
-        const int q = warp & 3;
+        // Epilogue: warp w drains TMEM lanes (w % 4) * 32 .. + 31, i.e. rows m0 + that of the tile,
+        // columns of half eh of the tile (for RoPE: half of its heads, or of a head's pair columns).
+        const int q = warp & 3, eh = (warp - 2) / 4;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int i = 0;
         for (int t = cta; t < tiles; t += ctas, i++) {
@@ -301,8 +304,11 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                 const bool ok = row < M && placed(re.at, p.rows, row, p.capacity, p.slots, pos, slot);
                 // 16 pair columns at a time: the row's cos and sin for them once (every head of the
                 // tile shares the position), then each head's pairs.
+                const bool by_heads = BN / hd >= 2;  // else one head: the halves split its pair columns
+                const int c_lo = by_heads ? 0 : eh * (half / 2), c_hi = by_heads ? half : c_lo + half / 2;
+                const int h_lo = by_heads ? eh * (BN / 2) : 0, h_hi = by_heads ? h_lo + BN / 2 : BN;
 #pragma unroll 1
-                for (int c0 = 0; c0 < half; c0 += 16) {
+                for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                     float cs[16], sn[16];
                     if (ok && p.rope) {
                         const float4 *c4 = reinterpret_cast<const float4 *>(re.cosv + (size_t)pos * half + c0);
@@ -315,7 +321,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                         }
                     }
 #pragma unroll 1
-                    for (int hb = 0; hb < BN; hb += hd) {
+                    for (int hb = h_lo; hb < h_hi; hb += hd) {
                         const int head = (n0 + hb) / hd;
                         uint32_t va[16], vb[16];
                         tmem_ld16_nowait(lane_base + hb + c0, va);
@@ -365,7 +371,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                 bf16 *out = static_cast<bf16 *>(Cout);
                 const int inner = N / 2;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN / 2; c0 += 16) {
+                for (int c0 = eh * (BN / 4); c0 < (eh + 1) * (BN / 4); c0 += 16) {
                     uint32_t g[16], u[16];
                     tmem_ld16_nowait(lane_base + c0, g);
                     tmem_ld16_nowait(lane_base + BN / 2 + c0, u);
@@ -388,7 +394,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                 float *C = static_cast<float *>(Cout) + (size_t)(t / per) * M * N;
                 const float sc = re.p.residual_scale;
 #pragma unroll 1
-                for (int c0 = 0; c0 < BN; c0 += 32) {
+                for (int c0 = eh * (BN / 2); c0 < (eh + 1) * (BN / 2); c0 += 32) {
                     float4 r[8];
                     if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
                         if (row < M) {
