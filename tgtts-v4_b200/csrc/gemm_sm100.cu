@@ -71,7 +71,12 @@ struct TcLayout {
     static constexpr int STAGE = TC_A_BYTES + B_BYTES;
     static constexpr int STAGES = (4 * (TC_A_BYTES + 256 * TC_BK * 2)) / STAGE;  // 192 KiB of stages
     static constexpr int BARRIERS = STAGES * STAGE;                           // offset of the mbarriers
-    static constexpr int SMEM = BARRIERS + 256 + 1024;                        // + barriers + alignment slack
+    // A pair's f32 epilogue's [warp][32][32] transposes (a single CTA has none: its block stays small
+    // enough to be resident beside the kernel before it, under programmatic dependent launch).
+    static constexpr int XPOSE = BARRIERS + 256;
+    static constexpr int SMEM = XPOSE + (CG == 2 ? 8 * 32 * 32 * 4 : 0) + 1024;  // + alignment slack
+    // (with the 1 KiB of static shared memory the kernel also takes)
+    static_assert(SMEM + 1024 <= 227 * 1024, "the stages, barriers and transposes fit a block's shared memory");
 };
 
 // Epilogues: C in f32, or (B's rows in gate_up_row's order: blocks of 128 gate rows, then the same
@@ -100,10 +105,14 @@ struct EpiArgs {
 // TMA; warp 1 owns TMEM (two accumulators of BN columns) and issues the MMAs; warps 2-5 drain an
 // accumulator (tcgen05.ld) and store it while the MMAs fill the other, so that a tile's epilogue
 // overlaps the next tile's main loop.
-// Eight epilogue warps: two to each quadrant of TMEM lanes, one to each half of the tile's columns
-// (a short main loop, as gate/up's K = 1024, would otherwise wait on SiLU's epilogue).
-constexpr int TC_EPI_WARPS = 8;
-constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
+// Epilogue warps: four (one to each quadrant of TMEM lanes) for a single CTA - the batched
+// decoder's narrow, latency-bound tiles - and eight for a pair (two to each quadrant, one to each
+// half of the tile's columns: a short main loop, as the prefill gate/up's K = 1024, would
+// otherwise wait on SiLU's epilogue).
+template <int CG>
+constexpr int tc_epi_warps() { return 4 * CG; }
+template <int CG>
+constexpr int tc_threads() { return (2 + tc_epi_warps<CG>()) * 32; }
 
 //
 // CG = 2: the grid is pairs of CTAs (clusters of two), a pair taking tiles of 256 rows: each CTA
@@ -114,7 +123,7 @@ constexpr int TC_PTHREADS = (2 + TC_EPI_WARPS) * 32;
 // CG = 1 and releases the accumulator on the leader's barrier. Per stage an SM then reads
 // 128 + BN / 2 rows of K for 128 x BN outputs instead of 128 + BN.
 template <int BN, int EPI = TC_EPI_F32, int CG = 1>
-__global__ void __launch_bounds__(TC_PTHREADS, 1)
+__global__ void __launch_bounds__(tc_threads<CG>(), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    void *__restrict__ Cout, int M, int N, int K, uint32_t *err, const __grid_constant__ EpiArgs re,
                    int b_const, int parts) {
@@ -177,7 +186,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
         for (int a = 0; a < 2; a++) {
             mbar_init(acc_full(a), 1);
             // CG = 1: every epilogue thread; CG = 2: one thread of each CTA's epilogue, on the leader's.
-            mbar_init(acc_empty(a), CG == 2 ? 2 : TC_EPI_WARPS * 32);
+            mbar_init(acc_empty(a), CG == 2 ? 2 : tc_epi_warps<CG>() * 32);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -286,6 +295,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
     } else {
         // Epilogue: warp w drains TMEM lanes (w % 4) * 32 .. + 31, i.e. rows m0 + that of the tile,
         // columns of half eh of the tile (for RoPE: half of its heads, or of a head's pair columns).
+        constexpr int EH = tc_epi_warps<CG>() / 4;  // column parts: each a warp per TMEM lane quadrant
         const int q = warp & 3, eh = (warp - 2) / 4;
         const uint32_t lane_off = (uint32_t)(q * 32) << 16;
         int i = 0;
@@ -305,8 +315,8 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                 // 16 pair columns at a time: the row's cos and sin for them once (every head of the
                 // tile shares the position), then each head's pairs.
                 const bool by_heads = BN / hd >= 2;  // else one head: the halves split its pair columns
-                const int c_lo = by_heads ? 0 : eh * (half / 2), c_hi = by_heads ? half : c_lo + half / 2;
-                const int h_lo = by_heads ? eh * (BN / 2) : 0, h_hi = by_heads ? h_lo + BN / 2 : BN;
+                const int c_lo = by_heads ? 0 : eh * (half / EH), c_hi = by_heads ? half : c_lo + half / EH;
+                const int h_lo = by_heads ? eh * (BN / EH) : 0, h_hi = by_heads ? h_lo + BN / EH : BN;
 #pragma unroll 1
                 for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
                     float cs[16], sn[16];
@@ -371,7 +381,7 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                 bf16 *out = static_cast<bf16 *>(Cout);
                 const int inner = N / 2;
 #pragma unroll 1
-                for (int c0 = eh * (BN / 4); c0 < (eh + 1) * (BN / 4); c0 += 16) {
+                for (int c0 = eh * (BN / 2 / EH); c0 < (eh + 1) * (BN / 2 / EH); c0 += 16) {
                     uint32_t g[16], u[16];
                     tmem_ld16_nowait(lane_base + c0, g);
                     tmem_ld16_nowait(lane_base + BN / 2 + c0, u);
@@ -391,40 +401,90 @@ __global__ void __launch_bounds__(TC_PTHREADS, 1)
                     }
                 }
             } else {
+                // A pair's tile whose main loop is long (K of 2048 or more a tile, as down's) sends each
+                // 32 x 32 chunk (lane = row) through the warp's buffer in shared memory (16-byte piece
+                // j of row r at piece j ^ (r % 8)), written a row a lane and read back a quarter row a
+                // lane, so that every store - and, for the residual, every load - of the warp is 4
+                // rows' 128 consecutive bytes (down 6.2 -> 5.9 ms in config 4's prefill). A short one
+                // (K = 1024, as o's) stores a row a lane: its main loop cannot hide the buffer's round
+                // trip (o 2.95 -> 3.25 ms that way).
                 float *C = static_cast<float *>(Cout) + (size_t)(t / per) * M * N;
-                const float sc = re.p.residual_scale;
+                if (CG == 1 || nk * TC_BK < 2048) {
+                    const float sc = re.p.residual_scale;
 #pragma unroll 1
-                for (int c0 = eh * (BN / 2); c0 < (eh + 1) * (BN / 2); c0 += 32) {
-                    float4 r[8];
-                    if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
-                        if (row < M) {
+                    for (int c0 = eh * (BN / EH); c0 < (eh + 1) * (BN / EH); c0 += 32) {
+                        float4 r[8];
+                        if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
+                            if (row < M) {
 #pragma unroll
-                            for (int e = 0; e < 8; e++)
-                                r[e] = __ldg(reinterpret_cast<const float4 *>(re.res + (size_t)row * N + n0 + c0) + e);
+                                for (int e = 0; e < 8; e++)
+                                    r[e] = __ldg(reinterpret_cast<const float4 *>(re.res + (size_t)row * N + n0 + c0) + e);
+                            }
+                        }
+                        uint32_t v[2][16];
+                        tmem_ld16_nowait(lane_base + c0, v[0]);
+                        tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
+                        tmem_wait_ld();
+                        if (row < M) {
+                            float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+#pragma unroll
+                            for (int e = 0; e < 8; e++) {
+                                float4 o = make_float4(__uint_as_float(v[e / 4][4 * (e % 4)]), __uint_as_float(v[e / 4][4 * (e % 4) + 1]),
+                                                       __uint_as_float(v[e / 4][4 * (e % 4) + 2]),
+                                                       __uint_as_float(v[e / 4][4 * (e % 4) + 3]));
+                                if constexpr (EPI == TC_EPI_RES)
+                                    o = make_float4(__fmaf_rn(sc, o.x, r[e].x), __fmaf_rn(sc, o.y, r[e].y),
+                                                    __fmaf_rn(sc, o.z, r[e].z), __fmaf_rn(sc, o.w, r[e].w));
+                                dst[e] = o;
+                            }
                         }
                     }
-                    uint32_t v[2][16];
-                    tmem_ld16_nowait(lane_base + c0, v[0]);
-                    tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
-                    tmem_wait_ld();
-                    if (row < M) {
-                        float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
+                } else {
+                    float4 *xp = reinterpret_cast<float4 *>(smem + L::XPOSE) + (warp - 2) * 32 * 8;
+                    const int row0 = m0 + q * 32;
+                    const float sc = re.p.residual_scale;
+                    const int rq = lane >> 3, jq = lane & 7;  // this lane's row of 4 and piece
+#pragma unroll 1
+                    for (int c0 = eh * (BN / EH); c0 < (eh + 1) * (BN / EH); c0 += 32) {
+                        float4 rv[8];  // the residual's pieces this lane adds, loaded under the TMEM loads
+                        if constexpr (EPI == TC_EPI_RES) {
 #pragma unroll
-                        for (int e = 0; e < 8; e++) {
-                            float4 o = make_float4(__uint_as_float(v[e / 4][4 * (e % 4)]), __uint_as_float(v[e / 4][4 * (e % 4) + 1]),
-                                                   __uint_as_float(v[e / 4][4 * (e % 4) + 2]), __uint_as_float(v[e / 4][4 * (e % 4) + 3]));
-                            if constexpr (EPI == TC_EPI_RES)
-                                o = make_float4(__fmaf_rn(sc, o.x, r[e].x), __fmaf_rn(sc, o.y, r[e].y),
-                                                __fmaf_rn(sc, o.z, r[e].z), __fmaf_rn(sc, o.w, r[e].w));
-                            dst[e] = o;
+                            for (int i = 0; i < 8; i++) {
+                                const int r = 4 * i + rq;
+                                rv[i] = row0 + r < M ? __ldg(reinterpret_cast<const float4 *>(re.res + (size_t)(row0 + r) * N + n0 +
+                                                                                              c0 + 4 * jq))
+                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                            }
                         }
+                        uint32_t v[2][16];
+                        tmem_ld16_nowait(lane_base + c0, v[0]);
+                        tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 8; j++)
+                            xp[lane * 8 + (j ^ (lane & 7))] =
+                                make_float4(__uint_as_float(v[j / 4][4 * (j % 4)]), __uint_as_float(v[j / 4][4 * (j % 4) + 1]),
+                                            __uint_as_float(v[j / 4][4 * (j % 4) + 2]), __uint_as_float(v[j / 4][4 * (j % 4) + 3]));
+                        __syncwarp();
+#pragma unroll
+                        for (int i = 0; i < 8; i++) {
+                            const int r = 4 * i + rq;
+                            if (row0 + r < M) {
+                                float4 o = xp[r * 8 + (jq ^ (r & 7))];
+                                if constexpr (EPI == TC_EPI_RES)
+                                    o = make_float4(__fmaf_rn(sc, o.x, rv[i].x), __fmaf_rn(sc, o.y, rv[i].y),
+                                                    __fmaf_rn(sc, o.z, rv[i].z), __fmaf_rn(sc, o.w, rv[i].w));
+                                *reinterpret_cast<float4 *>(C + (size_t)(row0 + r) * N + n0 + c0 + 4 * jq) = o;
+                            }
+                        }
+                        __syncwarp();  // every lane is done with the buffer before the next chunk
                     }
                 }
             }
             // The accumulator is drained: the MMAs may fill it again.
             tc_fence_before();
             if constexpr (CG == 2) {  // the epilogue warps together, then one arrival for the CTA
-                asm volatile("bar.sync 2, %0;" ::"n"(TC_EPI_WARPS * 32) : "memory");
+                asm volatile("bar.sync 2, %0;" ::"n"(tc_epi_warps<CG>() * 32) : "memory");
                 if (warp == 2 && lane == 0) mbar_arrive_remote(acc_empty(acc), 0);
             } else {
                 mbar_arrive(acc_empty(acc));
@@ -466,7 +526,7 @@ static cudaError_t launch_tc(const void *a, const void *b, void *c, int M, int N
     const int units = sms / CG;  // CTAs, or pairs of them
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(CG * (tiles < units ? tiles : units));
-    cfg.blockDim = dim3(TC_PTHREADS);
+    cfg.blockDim = dim3(tc_threads<CG>());
     cfg.dynamicSmemBytes = (size_t)L::SMEM;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
