@@ -97,8 +97,11 @@ struct EpiArgs {
     const float *res;  // TC_EPI_RES: [M][N] f32, scaled by p.residual_scale
 };
 
-// Persistent: one block per SM walks tiles t = blockIdx.x, + gridDim.x, ... (m fastest, so the
-// blocks at work share B tiles in L2, then n, then the part of K). With `parts` > 1 (f32 epilogue
+// Persistent: one block per SM walks tiles t = blockIdx.x, + gridDim.x, ... within a part of K,
+// over the smaller operand fastest: the tiles at work at one time then share the few row panels
+// of the larger operand, which streams from HBM once, and re-read the smaller from L2 (n fastest
+// when N <= M, as every prefill projection's weights against its 32,768 rows: m fastest read
+// down's 268 MB of A four times from HBM, once for each 256-wide column of tiles). With `parts` > 1 (f32 epilogue
 // only) K is cut into that many equal ranges and tile (m, n, part) stores its partial sum at
 // C[part][m][n]; the kernel that reads C adds the parts in part order, so a row's sums depend on
 // the shape and the part count, never on how many rows a launch takes. Warp 0 streams A and B tiles into a ring of stages with
@@ -146,10 +149,12 @@ __global__ void __launch_bounds__(tc_threads<CG>(), 1)
     const int cta = CG == 2 ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;  // the pair's (or the CTA's) index
     const int ctas = CG == 2 ? (int)(gridDim.x >> 1) : (int)gridDim.x;
     constexpr int TM = TC_BM * CG;  // rows a tile
-    const int mt = (M + TM - 1) / TM, per = mt * (N / BN), tiles = per * parts;
+    const int mt = (M + TM - 1) / TM, nt = N / BN, per = mt * nt, tiles = per * parts;
     const int nk = K / TC_BK / parts;  // k-blocks a tile
-    auto m0_of = [&](int t) { return (t % mt) * TM + (int)rank * TC_BM; };  // this CTA's first row
-    auto n0_of = [&](int t) { return ((t % per) / mt) * BN; };
+    const bool n_fast = N <= M;
+    auto m_of = [&](int t) { return n_fast ? (t % per) / nt : t % mt; };
+    auto m0_of = [&](int t) { return m_of(t) * TM + (int)rank * TC_BM; };  // this CTA's first row
+    auto n0_of = [&](int t) { return (n_fast ? (t % per) % nt : (t % per) / mt) * BN; };
     auto kb0_of = [&](int t) { return (t / per) * nk; };  // the tile's first k-block
     auto load_a = [&](uint32_t dst, int kx, int m0, uint32_t bar) {
         if constexpr (CG == 2)
