@@ -5,16 +5,22 @@
 // Block (t, g) takes query rows [128 t, 128 t + 128) of the launch (one run's rows: runs start on
 // multiples of 128) for query heads 2g and 2g + 1 (one KV head's), and walks its slot's cache from
 // position 0 to the tile's last position in tiles of 128 keys, shared by the two heads. Ten warps:
-//   warp 0     TMA: the two Q tiles once, then K and V tiles into two stages (128-byte swizzle,
-//              no multicast);
-//   warp 1     TMEM (per head: S, 128 columns, and O, 64) and the MMAs: S_j = Q K_j^T
-//              (M = 128, N = 128, K = 64) and O += P_j V_j (M = 128, N = 64, K = 128, V read
-//              MN-major), each head's S_{j+1} issued as soon as its PV_j is;
+//   warp 0     TMA: the two Q tiles once, then K and V tiles into FA_STAGES stages (128-byte
+//              swizzle, no multicast);
+//   warp 1     TMEM (per head: S, 128 columns; P, 64; O, 64: all 512) and the MMAs:
+//              S_j = Q K_j^T (M = 128, N = 128, K = 64; Q and K in shared memory) and
+//              O += P_j V_j (M = 128, N = 64, K = 128; P in TMEM, V in shared memory read
+//              MN-major). Once a head's P_j is in, its S_{j+1} is issued ahead of its PV_j, so
+//              that the head's next softmax starts after the four MMAs of S (an M = 128, K = 16
+//              MMA of N up to 128 takes ~95 clocks here, measured), with PV_j under it; PV_j
+//              waits for no later tile's copies;
 //   warps 2-5  head 2g, warps 6-9 head 2g + 1: a thread to a query row: S_j from TMEM (the mask,
-//              the row maximum, then the base-2 exponentials with the scale folded in) and P_j as
-//              bf16 into shared memory as PV's A operand, against a reference maximum that moves
-//              only when a tile's passes it by more than 2^FA_RESCALE, O in TMEM then rescaled
-//              in place (as in FlashAttention-4); O / l at the end.
+//              the row maximum, then the base-2 exponentials with the scale folded in) and P_j
+//              as bf16 into TMEM, once PV_{j-1} has read P_{j-1}, against a reference maximum
+//              that moves only when a tile's passes it by more than 2^FA_RESCALE, O in TMEM then
+//              rescaled in place (as in FlashAttention-4); O / l at the end.
+// With P in shared memory PV read 192 bytes a tensor clock (P and V) against the SM's 128, and
+// the softmax's P stores met those reads there.
 // The two heads' softmax warps run while the other head's MMAs do. Every wait on an mbarrier is
 // bounded (the context's error word, then the block runs out).
 #include "tc_common.cuh"
@@ -25,9 +31,10 @@ namespace {
 
 constexpr int FA_THREADS = 320;
 constexpr uint32_t FA_TILE = 128 * 64 * 2;  // a 128-row x 64-column bf16 box
-// Shared memory: Q of the two heads, K and V in two stages, P of the two heads (two boxes each).
-constexpr uint32_t FA_Q = 0, FA_K = 2 * FA_TILE, FA_V = 4 * FA_TILE, FA_P = 6 * FA_TILE;
-constexpr uint32_t FA_SMEM = 10 * FA_TILE + 1024;
+constexpr int FA_STAGES = 4;                  // K and V tiles in flight
+// Shared memory: Q of the two heads, K and V stages.
+constexpr uint32_t FA_Q = 0, FA_K = 2 * FA_TILE, FA_V = FA_K + FA_STAGES * FA_TILE;
+constexpr uint32_t FA_SMEM = FA_V + FA_STAGES * FA_TILE + 1024;
 // How far (base 2) a tile's maximum may pass a row's reference before O and l are rescaled.
 constexpr float FA_RESCALE = 8.0f;
 
@@ -62,10 +69,6 @@ TG_DEVICE float fa_max3(float a, float b, float c) {
     return d;
 }
 
-TG_DEVICE uint32_t fa_sw128(int n, int c) {
-    return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4));
-}
-
 // The same bytes as a K-major SW128 tile read MN-major: V's tile [keys][64] is B = V^T with N = 64
 // along a row and K = keys down the rows, in atoms of 8 keys x 128 bytes, 1024 bytes apart along K.
 TG_DEVICE uint64_t fa_desc_mn(uint32_t addr) {
@@ -82,8 +85,8 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t base = smem_u32(smem);
-    __shared__ __align__(8) uint64_t bq, bkv_full[2], bkv_empty[2];
-    __shared__ __align__(8) uint64_t bs_full[2], bs_empty[2], bp_full[2], bo_full[2], bo_empty[2];  // by head
+    __shared__ __align__(8) uint64_t bq, bkv_full[FA_STAGES], bkv_empty[FA_STAGES];
+    __shared__ __align__(8) uint64_t bs_full[2], bp_full[2], bo_full[2];  // by head
     __shared__ __align__(8) uint64_t bv_clear;  // V_{n-1}'s rows past the tile's last position are zero
     __shared__ uint32_t tmem_slot, t_last, t_slot, t_slot_max;
     __shared__ int gave_up;
@@ -101,14 +104,14 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         t_slot = 0xffffffffu;
         t_slot_max = 0;
         mbar_init(B(bq), 1);
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < FA_STAGES; i++) {
             mbar_init(B(bkv_full[i]), 1);
             mbar_init(B(bkv_empty[i]), 1);
+        }
+        for (int i = 0; i < 2; i++) {
             mbar_init(B(bs_full[i]), 1);
-            mbar_init(B(bs_empty[i]), 128);
-            mbar_init(B(bp_full[i]), 128);
+            mbar_init(B(bp_full[i]), 128);  // P_j in TMEM, S_j read and O rescaled
             mbar_init(B(bo_full[i]), 1);
-            mbar_init(B(bo_empty[i]), 128);
         }
         mbar_init(B(bv_clear), 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -145,9 +148,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     // slot, or the next cache range's) would still make 0 x v NaN in PV. When the last key tile
     // reaches past it, warp 0 clears those rows of V_{n-1} before PV_{n-1} is issued.
     const bool clear_v = n > 0 && t_last % 128 != 127;
-    // TMEM columns: head h's S at 256 h, its O at 256 h + 128.
+    // TMEM columns: head h's S at 256 h, P (bf16 pairs) at 256 h + 128, O at 256 h + 192.
     auto s_col = [](int h) { return (uint32_t)(256 * h); };
-    auto o_col = [](int h) { return (uint32_t)(256 * h + 128); };
+    auto p_col = [](int h) { return (uint32_t)(256 * h + 128); };
+    auto o_col = [](int h) { return (uint32_t)(256 * h + 192); };
 
     if (warp == 0) {
         if (lane == 0 && n > 0) {
@@ -156,19 +160,20 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             tma_load_2d(base + FA_Q + FA_TILE, &qmap, (head0 + 1) * 64, r0, B(bq));
             const int row0 = (int)((t_slot * (uint32_t)kvh + kv) * p.capacity);
             for (int j = 0; j < n; j++) {
-                const int b = j & 1;
-                mbar_wait(B(bkv_empty[b]), ((j >> 1) & 1) ^ 1, err, &gave_up);
+                const int b = j % FA_STAGES;
+                mbar_wait(B(bkv_empty[b]), ((j / FA_STAGES) & 1) ^ 1, err, &gave_up);
                 mbar_arrive_expect_tx(B(bkv_full[b]), 2 * FA_TILE);
                 tma_load_2d(base + FA_K + b * FA_TILE, &kmap, 0, row0 + j * 128, B(bkv_full[b]));
                 tma_load_2d(base + FA_V + b * FA_TILE, &vmap, 0, row0 + j * 128, B(bkv_full[b]));
             }
             // Every copy this thread started has landed before the block can end.
-            for (int j = n > 2 ? n - 2 : 0; j < n; j++) mbar_wait(B(bkv_full[j & 1]), (j >> 1) & 1, err, &gave_up);
+            for (int j = n > FA_STAGES ? n - FA_STAGES : 0; j < n; j++)
+                mbar_wait(B(bkv_full[j % FA_STAGES]), (j / FA_STAGES) & 1, err, &gave_up);
         }
         if (clear_v) {
             __syncwarp();
-            mbar_wait(B(bkv_full[(n - 1) & 1]), ((n - 1) >> 1) & 1, err, &gave_up);
-            uint8_t *vt = smem + FA_V + ((n - 1) & 1) * FA_TILE;
+            mbar_wait(B(bkv_full[(n - 1) % FA_STAGES]), ((n - 1) / FA_STAGES) & 1, err, &gave_up);
+            uint8_t *vt = smem + FA_V + ((n - 1) % FA_STAGES) * FA_TILE;
             const int keep = (int)(t_last % 128) + 1;
             for (int i = lane; i < (128 - keep) * 8; i += 32) {
                 const int r = keep + i / 8;  // a row of the swizzled tile is 128 whole bytes
@@ -182,36 +187,39 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         if (lane == 0 && n > 0) {
             constexpr uint32_t idesc_s = bf16_idesc(128, 128);
             constexpr uint32_t idesc_o = bf16_idesc(128, 64) | (1u << 16);  // B (V) MN-major
-            mbar_wait(B(bq), 0, err, &gave_up);
-            auto issue_s = [&](int j, int h) {  // S_j of head h (K_j landed, S_{j-1} read)
-                if (j > 0) mbar_wait(B(bs_empty[h]), (j - 1) & 1, err, &gave_up);
-                tc_fence_after();
-                const uint32_t kt = base + FA_K + (j & 1) * FA_TILE;
+            // S_j of head h (Q and K_j in shared memory), issued once the head's S_{j-1} is read
+            // and K_j has landed.
+            auto issue_s = [&](int j, int h) {
+                const uint32_t kt = base + FA_K + (j % FA_STAGES) * FA_TILE;
 #pragma unroll
                 for (int k = 0; k < 4; k++)
                     tc_mma(tmem + s_col(h), sw128_desc(base + FA_Q + h * FA_TILE + k * 32), sw128_desc(kt + k * 32),
                            idesc_s, k > 0 ? 1u : 0u);
                 tc_commit(B(bs_full[h]));
             };
+            mbar_wait(B(bq), 0, err, &gave_up);
             mbar_wait(B(bkv_full[0]), 0, err, &gave_up);
+            tc_fence_after();
             issue_s(0, 0);
             issue_s(0, 1);
             for (int j = 0; j < n; j++) {
-                if (j + 1 < n) mbar_wait(B(bkv_full[(j + 1) & 1]), ((j + 1) >> 1) & 1, err, &gave_up);
-                const uint32_t v = base + FA_V + (j & 1) * FA_TILE;
+                const int b = j % FA_STAGES;
+                const uint32_t v = base + FA_V + b * FA_TILE;
                 if (clear_v && j == n - 1) mbar_wait(B(bv_clear), 0, err, &gave_up);
                 for (int h = 0; h < 2; h++) {
+                    // P_j in TMEM, S_j read, and O rescaled to the row's reference.
                     mbar_wait(B(bp_full[h]), j & 1, err, &gave_up);
-                    if (j > 0) mbar_wait(B(bo_empty[h]), (j - 1) & 1, err, &gave_up);
+                    if (j + 1 < n && h == 0)
+                        mbar_wait(B(bkv_full[(j + 1) % FA_STAGES]), ((j + 1) / FA_STAGES) & 1, err, &gave_up);
                     tc_fence_after();
+                    if (j + 1 < n) issue_s(j + 1, h);
 #pragma unroll
                     for (int kk = 0; kk < 8; kk++)
-                        tc_mma(tmem + o_col(h), sw128_desc(base + FA_P + (2 * h + kk / 4) * FA_TILE + (kk % 4) * 32),
-                               fa_desc_mn(v + kk * 2048), idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+                        tc_mma_ts(tmem + o_col(h), tmem + p_col(h) + 8 * kk, fa_desc_mn(v + kk * 2048), idesc_o,
+                                  (j > 0 || kk > 0) ? 1u : 0u);
                     tc_commit(B(bo_full[h]));
-                    if (j + 1 < n) issue_s(j + 1, h);
+                    if (h == 1) tc_commit(B(bkv_empty[b]));  // K_j and V_j are read by every MMA issued so far
                 }
-                tc_commit(B(bkv_empty[j & 1]));  // K_j and V_j are read by every MMA issued so far
             }
         }
     } else if (n > 0) {
@@ -268,8 +276,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             if (move) mref = m_tile;
             const bool live = mref != -INFINITY;  // false only for a spare row
             if (j > 0) {
-                // PV_{j-1} is in O: rescale it where the reference moved (the warp's 32 rows
-                // together, a row that keeps its reference times 1), then PV_j may add to it.
+                // PV_{j-1} is in O (and has read P_{j-1}, which P_j replaces): rescale O where
+                // the reference moved (the warp's 32 rows together, a row that keeps its
+                // reference times 1), then PV_j may add to it (P_j's arrival below says both).
                 mbar_wait(B(bo_full[h]), (j - 1) & 1, err, &gave_up);
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, a != 1.0f)) {
@@ -284,8 +293,6 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     }
                     tmem_wait_st();
                 }
-                tc_fence_before();
-                mbar_arrive(B(bo_empty[h]));
             }
             float2 sum4[4];  // the running sums of columns c % 8 = 2 e and 2 e + 1
 #pragma unroll
@@ -295,7 +302,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             for (int c2 = 0; c2 < 2; c2++) {
                 float sv[64];
                 load_half(j, c2, sv);
-                uint32_t pk[32];
+                uint32_t pk[2][16];
 #pragma unroll
                 for (int c = 0; c < 64; c += 2) {
                     const float2 x = fa_fma2(make_float2(sv[c], sv[c + 1]), scale22, neg_m);
@@ -303,21 +310,17 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     const float p1 = live ? fa_exp2(x.y) : 0.0f;
                     sum4[(c % 8) / 2] = fa_add2(sum4[(c % 8) / 2], make_float2(p0, p1));
                     const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                    pk[c / 2] = *reinterpret_cast<const uint32_t *>(&pp);
+                    pk[c / 32][(c / 2) % 16] = *reinterpret_cast<const uint32_t *>(&pp);
                 }
-                // Keys 64 c2 .. 64 c2 + 63 of row m: box c2 of this head's P, swizzled.
-#pragma unroll
-                for (int ch = 0; ch < 8; ch++) {
-                    uint8_t *dst = smem + FA_P + (2 * h + c2) * FA_TILE + fa_sw128(m, ch);
-                    *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-                }
+                // Keys 64 c2 .. 64 c2 + 63 of row m: P's columns 32 c2 .. 32 c2 + 31, bf16 pairs.
+                tmem_st16(lanes + p_col(h) + 32 * c2, pk[0]);
+                tmem_st16(lanes + p_col(h) + 32 * c2 + 16, pk[1]);
             }
+            tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(B(bs_empty[h]));  // S_j is read: the MMAs may write S_{j+1}
             const float sum = ((sum4[0].x + sum4[0].y) + (sum4[1].x + sum4[1].y)) +
                               ((sum4[2].x + sum4[2].y) + (sum4[3].x + sum4[3].y));
             l = __fmaf_rn(l, a, sum);
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(B(bp_full[h]));
         }
         // The output: O / l, once PV_{n-1} is in O.

@@ -72,6 +72,18 @@ TG_DEVICE void tc_mma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, u
         : "memory");
 }
 
+// The same MMA with A read from TMEM (tmem_a: lane 0 and the first column; row i of A in lane i,
+// its K values two to a 32-bit column, the lower-indexed in the low half): no shared-memory read
+// for A.
+TG_DEVICE void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 TG_DEVICE void tc_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                  : "memory");
