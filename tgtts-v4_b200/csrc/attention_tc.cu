@@ -255,32 +255,59 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         for (int j = 0; j < n; j++) {
             mbar_wait(B(bs_full[h]), j & 1, err, &gave_up);
             tc_fence_after();
-            // The row maximum: eight running maxima (column c to c % 8) over both halves.
-            float mx8[8];
+            // P_j against mref, the tile's maximum taken in the same pass and checked after it:
+            // where it passes mref by more than FA_RESCALE (always on the first tile, where mref
+            // is -inf and P_0 comes out 0) the reference moves, O is rescaled (PV_{j-1} is in it),
+            // and the warp's pass runs again from S_j, still in TMEM - the same P and l as taking
+            // the maximum first, without a pass over S_j on the critical path of later tiles.
+            // One pass: P_j of the warp's rows against mref into TMEM, their sum; the tile's raw
+            // maximum into mx. P_j replaces P_{j-1} once PV_{j-1} has read it (and is in O): the
+            // first pass waits for that just before its first store, after half 0's exponentials.
+            auto p_pass = [&](float &mx, bool first) {
+                float2 sum4[4];  // the running sums of columns c % 8 = 2 e and 2 e + 1
 #pragma unroll
-            for (int e = 0; e < 8; e++) mx8[e] = -INFINITY;
+                for (int e = 0; e < 4; e++) sum4[e] = make_float2(0.0f, 0.0f);
+                float mxs[2] = {-INFINITY, -INFINITY};
+                // A spare row (mref -inf, every score masked to -inf) takes -inf for -mref, so that
+                // its exponentials are 2^-inf = 0 with no select in the loop.
+                const float nm = mref != -INFINITY ? -mref : -INFINITY;
+                const float2 scale22 = make_float2(scale2, scale2), neg_m = make_float2(nm, nm);
 #pragma unroll
-            for (int c2 = 0; c2 < 2; c2++) {
-                float sv[64];
-                load_half(j, c2, sv);
+                for (int c2 = 0; c2 < 2; c2++) {
+                    float sv[64];
+                    load_half(j, c2, sv);
+                    uint32_t pk[2][16];
 #pragma unroll
-                for (int e = 0; e < 8; e++)
-#pragma unroll
-                    for (int t = 0; t < 8; t += 2) mx8[e] = fa_max3(mx8[e], sv[e + 8 * t], sv[e + 8 * t + 8]);
-            }
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+                    for (int c = 0; c < 64; c += 2) {
+                        mxs[(c / 2) % 2] = fa_max3(mxs[(c / 2) % 2], sv[c], sv[c + 1]);
+                        const float2 x = fa_fma2(make_float2(sv[c], sv[c + 1]), scale22, neg_m);
+                        const float p0 = fa_exp2(x.x), p1 = fa_exp2(x.y);
+                        sum4[(c % 8) / 2] = fa_add2(sum4[(c % 8) / 2], make_float2(p0, p1));
+                        const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+                        pk[c / 32][(c / 2) % 16] = *reinterpret_cast<const uint32_t *>(&pp);
+                    }
+                    if (c2 == 0 && first && j > 0) {
+                        mbar_wait(B(bo_full[h]), (j - 1) & 1, err, &gave_up);
+                        tc_fence_after();
+                    }
+                    // Keys 64 c2 .. 64 c2 + 63 of row m: P's columns 32 c2 .. 32 c2 + 31, bf16 pairs.
+                    tmem_st16(lanes + p_col(h) + 32 * c2, pk[0]);
+                    tmem_st16(lanes + p_col(h) + 32 * c2 + 16, pk[1]);
+                }
+                mx = fmaxf(mxs[0], mxs[1]);
+                return ((sum4[0].x + sum4[0].y) + (sum4[1].x + sum4[1].y)) +
+                       ((sum4[2].x + sum4[2].y) + (sum4[3].x + sum4[3].y));
+            };
+            float a = 1.0f, mx;
+            float sum = p_pass(mx, true);
             const float m_tile = mx * scale2;  // the scale is positive: max, then scale
             const bool move = m_tile != -INFINITY && (mref == -INFINITY || m_tile > mref + FA_RESCALE);
-            const float a = move && mref != -INFINITY ? fa_exp2(mref - m_tile) : 1.0f;
-            if (move) mref = m_tile;
-            const bool live = mref != -INFINITY;  // false only for a spare row
-            if (j > 0) {
-                // PV_{j-1} is in O (and has read P_{j-1}, which P_j replaces): rescale O where
-                // the reference moved (the warp's 32 rows together, a row that keeps its
-                // reference times 1), then PV_j may add to it (P_j's arrival below says both).
-                mbar_wait(B(bo_full[h]), (j - 1) & 1, err, &gave_up);
-                tc_fence_after();
+            if (__any_sync(0xffffffffu, move)) {
+                // A row of the warp moves: rescale O where the reference moved (a row that keeps
+                // its reference times 1), then the warp's P_j again.
+                a = move && mref != -INFINITY ? fa_exp2(mref - m_tile) : 1.0f;
+                if (move) mref = m_tile;
+                tmem_wait_st();
                 if (__any_sync(0xffffffffu, a != 1.0f)) {
 #pragma unroll
                     for (int c = 0; c < 4; c++) {
@@ -293,33 +320,10 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
                     }
                     tmem_wait_st();
                 }
-            }
-            float2 sum4[4];  // the running sums of columns c % 8 = 2 e and 2 e + 1
-#pragma unroll
-            for (int e = 0; e < 4; e++) sum4[e] = make_float2(0.0f, 0.0f);
-            const float2 scale22 = make_float2(scale2, scale2), neg_m = make_float2(-mref, -mref);
-#pragma unroll
-            for (int c2 = 0; c2 < 2; c2++) {
-                float sv[64];
-                load_half(j, c2, sv);
-                uint32_t pk[2][16];
-#pragma unroll
-                for (int c = 0; c < 64; c += 2) {
-                    const float2 x = fa_fma2(make_float2(sv[c], sv[c + 1]), scale22, neg_m);
-                    const float p0 = live ? fa_exp2(x.x) : 0.0f;
-                    const float p1 = live ? fa_exp2(x.y) : 0.0f;
-                    sum4[(c % 8) / 2] = fa_add2(sum4[(c % 8) / 2], make_float2(p0, p1));
-                    const __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-                    pk[c / 32][(c / 2) % 16] = *reinterpret_cast<const uint32_t *>(&pp);
-                }
-                // Keys 64 c2 .. 64 c2 + 63 of row m: P's columns 32 c2 .. 32 c2 + 31, bf16 pairs.
-                tmem_st16(lanes + p_col(h) + 32 * c2, pk[0]);
-                tmem_st16(lanes + p_col(h) + 32 * c2 + 16, pk[1]);
+                sum = p_pass(mx, false);
             }
             tmem_wait_st();
             tc_fence_before();
-            const float sum = ((sum4[0].x + sum4[0].y) + (sum4[1].x + sum4[1].y)) +
-                              ((sum4[2].x + sum4[2].y) + (sum4[3].x + sum4[3].y));
             l = __fmaf_rn(l, a, sum);
             mbar_arrive(B(bp_full[h]));
         }
