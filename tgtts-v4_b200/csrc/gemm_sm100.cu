@@ -415,34 +415,47 @@ __global__ void __launch_bounds__(tc_threads<CG>(), 1)
                 // trip (o 2.95 -> 3.25 ms that way).
                 float *C = static_cast<float *>(Cout) + (size_t)(t / per) * M * N;
                 if (CG == 1 || nk * TC_BK < 2048) {
+                    // The warp's 32 rows in two 16-row halves by TMEM's 16x256b shape (a row's 8
+                    // columns of a group over 4 lanes): each 8-byte store - and residual load - of the
+                    // warp covers 8 rows' 32 consecutive bytes, whole sectors, where a row a lane's
+                    // float4 touched 32 rows' half sectors.
                     const float sc = re.p.residual_scale;
+                    const int rt = lane >> 2, ct = 2 * (lane & 3), rbase = m0 + q * 32;
 #pragma unroll 1
                     for (int c0 = eh * (BN / EH); c0 < (eh + 1) * (BN / EH); c0 += 32) {
-                        float4 r[8];
+                        float2 r[2][2][4];  // [half][row of the lane's two][column group]
                         if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
-                            if (row < M) {
 #pragma unroll
-                                for (int e = 0; e < 8; e++)
-                                    r[e] = __ldg(reinterpret_cast<const float4 *>(re.res + (size_t)row * N + n0 + c0) + e);
-                            }
+                            for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                                for (int s = 0; s < 2; s++) {
+                                    const int rr = rbase + 16 * hh + 8 * s + rt;
+#pragma unroll
+                                    for (int k = 0; k < 4; k++)
+                                        r[hh][s][k] = rr < M ? __ldg(reinterpret_cast<const float2 *>(re.res + (size_t)rr * N + n0 + c0 +
+                                                                                                      8 * k + ct))
+                                                             : make_float2(0.f, 0.f);
+                                }
                         }
                         uint32_t v[2][16];
-                        tmem_ld16_nowait(lane_base + c0, v[0]);
-                        tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
+                        tmem_ld16x256_nowait(lane_base + c0, v[0]);
+                        tmem_ld16x256_nowait(lane_base + (16u << 16) + c0, v[1]);
                         tmem_wait_ld();
-                        if (row < M) {
-                            float4 *dst = reinterpret_cast<float4 *>(C + (size_t)row * N + n0 + c0);
 #pragma unroll
-                            for (int e = 0; e < 8; e++) {
-                                float4 o = make_float4(__uint_as_float(v[e / 4][4 * (e % 4)]), __uint_as_float(v[e / 4][4 * (e % 4) + 1]),
-                                                       __uint_as_float(v[e / 4][4 * (e % 4) + 2]),
-                                                       __uint_as_float(v[e / 4][4 * (e % 4) + 3]));
-                                if constexpr (EPI == TC_EPI_RES)
-                                    o = make_float4(__fmaf_rn(sc, o.x, r[e].x), __fmaf_rn(sc, o.y, r[e].y),
-                                                    __fmaf_rn(sc, o.z, r[e].z), __fmaf_rn(sc, o.w, r[e].w));
-                                dst[e] = o;
+                        for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                            for (int s = 0; s < 2; s++) {
+                                const int rr = rbase + 16 * hh + 8 * s + rt;
+                                if (rr >= M) continue;
+                                float *dst = C + (size_t)rr * N + n0 + c0 + ct;
+#pragma unroll
+                                for (int k = 0; k < 4; k++) {
+                                    float2 o = make_float2(__uint_as_float(v[hh][4 * k + 2 * s]), __uint_as_float(v[hh][4 * k + 2 * s + 1]));
+                                    if constexpr (EPI == TC_EPI_RES)
+                                        o = make_float2(__fmaf_rn(sc, o.x, r[hh][s][k].x), __fmaf_rn(sc, o.y, r[hh][s][k].y));
+                                    *reinterpret_cast<float2 *>(dst + 8 * k) = o;
+                                }
                             }
-                        }
                     }
                 } else {
                     float4 *xp = reinterpret_cast<float4 *>(smem + L::XPOSE) + (warp - 2) * 32 * 8;

@@ -150,6 +150,16 @@ TG_DEVICE void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
 }
 TG_DEVICE void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 TMEM lanes x 32 columns (taddr's lane and up): lane t of the warp gets, of column group k
+// (columns 8 k .. 8 k + 7), r[4 k], r[4 k + 1] = row t / 4, columns 8 k + 2 (t % 4) and the next,
+// and r[4 k + 2], r[4 k + 3] = row t / 4 + 8, the same columns (mma.sync's accumulator layout).
+TG_DEVICE void tmem_ld16x256_nowait(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile("tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+                   "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+                 : "r"(taddr));
+}
+
 // Stores 16 consecutive f32 columns of this warp's 32 TMEM lanes (lane i of the warp to row
 // (warp % 4) * 32 + i); tmem_wait_st before anything else reads or writes them.
 TG_DEVICE void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
