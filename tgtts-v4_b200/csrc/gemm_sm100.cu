@@ -71,12 +71,9 @@ struct TcLayout {
     static constexpr int STAGE = TC_A_BYTES + B_BYTES;
     static constexpr int STAGES = (4 * (TC_A_BYTES + 256 * TC_BK * 2)) / STAGE;  // 192 KiB of stages
     static constexpr int BARRIERS = STAGES * STAGE;                           // offset of the mbarriers
-    // A pair's f32 epilogue's [warp][32][32] transposes (a single CTA has none: its block stays small
-    // enough to be resident beside the kernel before it, under programmatic dependent launch).
-    static constexpr int XPOSE = BARRIERS + 256;
-    static constexpr int SMEM = XPOSE + (CG == 2 ? 8 * 32 * 32 * 4 : 0) + 1024;  // + alignment slack
+    static constexpr int SMEM = BARRIERS + 256 + 1024;                        // + alignment slack
     // (with the 1 KiB of static shared memory the kernel also takes)
-    static_assert(SMEM + 1024 <= 227 * 1024, "the stages, barriers and transposes fit a block's shared memory");
+    static_assert(SMEM + 1024 <= 227 * 1024, "the stages and barriers fit a block's shared memory");
 };
 
 // Epilogues: C in f32, or (B's rows in gate_up_row's order: blocks of 128 gate rows, then the same
@@ -406,97 +403,49 @@ __global__ void __launch_bounds__(tc_threads<CG>(), 1)
                     }
                 }
             } else {
-                // A pair's tile whose main loop is long (K of 2048 or more a tile, as down's) sends each
-                // 32 x 32 chunk (lane = row) through the warp's buffer in shared memory (16-byte piece
-                // j of row r at piece j ^ (r % 8)), written a row a lane and read back a quarter row a
-                // lane, so that every store - and, for the residual, every load - of the warp is 4
-                // rows' 128 consecutive bytes (down 6.2 -> 5.9 ms in config 4's prefill). A short one
-                // (K = 1024, as o's) stores a row a lane: its main loop cannot hide the buffer's round
-                // trip (o 2.95 -> 3.25 ms that way).
+                // The warp's 32 rows in two 16-row halves by TMEM's 16x256b shape (a row's 8 columns
+                // of a group over 4 lanes): each 8-byte store - and residual load - of the warp covers
+                // 8 rows' 32 consecutive bytes, whole sectors, where a row a lane's float4 touched 32
+                // rows' half sectors (config 4's prefill: o 3.1 -> 2.2 ms; down 4.9 -> 4.8 ms against
+                // a transpose through shared memory, which o's short main loop could not hide).
                 float *C = static_cast<float *>(Cout) + (size_t)(t / per) * M * N;
-                if (CG == 1 || nk * TC_BK < 2048) {
-                    // The warp's 32 rows in two 16-row halves by TMEM's 16x256b shape (a row's 8
-                    // columns of a group over 4 lanes): each 8-byte store - and residual load - of the
-                    // warp covers 8 rows' 32 consecutive bytes, whole sectors, where a row a lane's
-                    // float4 touched 32 rows' half sectors.
-                    const float sc = re.p.residual_scale;
-                    const int rt = lane >> 2, ct = 2 * (lane & 3), rbase = m0 + q * 32;
+                const float sc = re.p.residual_scale;
+                const int rt = lane >> 2, ct = 2 * (lane & 3), rbase = m0 + q * 32;
 #pragma unroll 1
-                    for (int c0 = eh * (BN / EH); c0 < (eh + 1) * (BN / EH); c0 += 32) {
-                        float2 r[2][2][4];  // [half][row of the lane's two][column group]
-                        if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
-#pragma unroll
-                            for (int hh = 0; hh < 2; hh++)
-#pragma unroll
-                                for (int s = 0; s < 2; s++) {
-                                    const int rr = rbase + 16 * hh + 8 * s + rt;
-#pragma unroll
-                                    for (int k = 0; k < 4; k++)
-                                        r[hh][s][k] = rr < M ? __ldg(reinterpret_cast<const float2 *>(re.res + (size_t)rr * N + n0 + c0 +
-                                                                                                      8 * k + ct))
-                                                             : make_float2(0.f, 0.f);
-                                }
-                        }
-                        uint32_t v[2][16];
-                        tmem_ld16x256_nowait(lane_base + c0, v[0]);
-                        tmem_ld16x256_nowait(lane_base + (16u << 16) + c0, v[1]);
-                        tmem_wait_ld();
+                for (int c0 = eh * (BN / EH); c0 < (eh + 1) * (BN / EH); c0 += 32) {
+                    float2 r[2][2][4];  // [half][row of the lane's two][column group]
+                    if constexpr (EPI == TC_EPI_RES) {  // the residual's columns, loaded under the TMEM loads
 #pragma unroll
                         for (int hh = 0; hh < 2; hh++)
 #pragma unroll
                             for (int s = 0; s < 2; s++) {
                                 const int rr = rbase + 16 * hh + 8 * s + rt;
-                                if (rr >= M) continue;
-                                float *dst = C + (size_t)rr * N + n0 + c0 + ct;
 #pragma unroll
-                                for (int k = 0; k < 4; k++) {
-                                    float2 o = make_float2(__uint_as_float(v[hh][4 * k + 2 * s]), __uint_as_float(v[hh][4 * k + 2 * s + 1]));
-                                    if constexpr (EPI == TC_EPI_RES)
-                                        o = make_float2(__fmaf_rn(sc, o.x, r[hh][s][k].x), __fmaf_rn(sc, o.y, r[hh][s][k].y));
-                                    *reinterpret_cast<float2 *>(dst + 8 * k) = o;
-                                }
+                                for (int k = 0; k < 4; k++)
+                                    r[hh][s][k] = rr < M ? __ldg(reinterpret_cast<const float2 *>(re.res + (size_t)rr * N + n0 + c0 +
+                                                                                                  8 * k + ct))
+                                                         : make_float2(0.f, 0.f);
                             }
                     }
-                } else {
-                    float4 *xp = reinterpret_cast<float4 *>(smem + L::XPOSE) + (warp - 2) * 32 * 8;
-                    const int row0 = m0 + q * 32;
-                    const float sc = re.p.residual_scale;
-                    const int rq = lane >> 3, jq = lane & 7;  // this lane's row of 4 and piece
-#pragma unroll 1
-                    for (int c0 = eh * (BN / EH); c0 < (eh + 1) * (BN / EH); c0 += 32) {
-                        float4 rv[8];  // the residual's pieces this lane adds, loaded under the TMEM loads
-                        if constexpr (EPI == TC_EPI_RES) {
+                    uint32_t v[2][16];
+                    tmem_ld16x256_nowait(lane_base + c0, v[0]);
+                    tmem_ld16x256_nowait(lane_base + (16u << 16) + c0, v[1]);
+                    tmem_wait_ld();
 #pragma unroll
-                            for (int i = 0; i < 8; i++) {
-                                const int r = 4 * i + rq;
-                                rv[i] = row0 + r < M ? __ldg(reinterpret_cast<const float4 *>(re.res + (size_t)(row0 + r) * N + n0 +
-                                                                                              c0 + 4 * jq))
-                                                     : make_float4(0.f, 0.f, 0.f, 0.f);
-                            }
-                        }
-                        uint32_t v[2][16];
-                        tmem_ld16_nowait(lane_base + c0, v[0]);
-                        tmem_ld16_nowait(lane_base + c0 + 16, v[1]);
-                        tmem_wait_ld();
+                    for (int hh = 0; hh < 2; hh++)
 #pragma unroll
-                        for (int j = 0; j < 8; j++)
-                            xp[lane * 8 + (j ^ (lane & 7))] =
-                                make_float4(__uint_as_float(v[j / 4][4 * (j % 4)]), __uint_as_float(v[j / 4][4 * (j % 4) + 1]),
-                                            __uint_as_float(v[j / 4][4 * (j % 4) + 2]), __uint_as_float(v[j / 4][4 * (j % 4) + 3]));
-                        __syncwarp();
+                        for (int s = 0; s < 2; s++) {
+                            const int rr = rbase + 16 * hh + 8 * s + rt;
+                            if (rr >= M) continue;
+                            float *dst = C + (size_t)rr * N + n0 + c0 + ct;
 #pragma unroll
-                        for (int i = 0; i < 8; i++) {
-                            const int r = 4 * i + rq;
-                            if (row0 + r < M) {
-                                float4 o = xp[r * 8 + (jq ^ (r & 7))];
+                            for (int k = 0; k < 4; k++) {
+                                float2 o = make_float2(__uint_as_float(v[hh][4 * k + 2 * s]), __uint_as_float(v[hh][4 * k + 2 * s + 1]));
                                 if constexpr (EPI == TC_EPI_RES)
-                                    o = make_float4(__fmaf_rn(sc, o.x, rv[i].x), __fmaf_rn(sc, o.y, rv[i].y),
-                                                    __fmaf_rn(sc, o.z, rv[i].z), __fmaf_rn(sc, o.w, rv[i].w));
-                                *reinterpret_cast<float4 *>(C + (size_t)(row0 + r) * N + n0 + c0 + 4 * jq) = o;
+                                    o = make_float2(__fmaf_rn(sc, o.x, r[hh][s][k].x), __fmaf_rn(sc, o.y, r[hh][s][k].y));
+                                *reinterpret_cast<float2 *>(dst + 8 * k) = o;
                             }
                         }
-                        __syncwarp();  // every lane is done with the buffer before the next chunk
-                    }
                 }
             }
             // The accumulator is drained: the MMAs may fill it again.
