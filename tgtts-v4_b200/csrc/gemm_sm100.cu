@@ -86,6 +86,20 @@ struct TcLayout {
 // stored in place of C.
 enum { TC_EPI_F32 = 0, TC_EPI_SILU = 1, TC_EPI_ROPE = 2, TC_EPI_RES = 3 };
 
+// 32 bytes of a lane's row at dst (global memory): one 256-bit store, a whole sector, where dst is
+// 32-byte aligned, else two 16-byte stores (a binding need only be 16-byte aligned). A warp of such
+// stores, a row a lane, then asks L2 for 32 whole sectors rather than 64 halves.
+TG_DEVICE void st_row32(void *dst, uint4 a, uint4 b) {
+    if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+        asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w),
+                     "r"(b.x), "r"(b.y), "r"(b.z), "r"(b.w)
+                     : "memory");
+    } else {
+        reinterpret_cast<uint4 *>(dst)[0] = a;
+        reinterpret_cast<uint4 *>(dst)[1] = b;
+    }
+}
+
 struct EpiArgs {
     tg_params p;
     const uint32_t *at;
@@ -371,11 +385,8 @@ __global__ void __launch_bounds__(tc_threads<CG>(), 1)
                             wa[e] = *reinterpret_cast<const uint32_t *>(&x);
                             wb[e] = *reinterpret_cast<const uint32_t *>(&y);
                         }
-                        uint4 *da = reinterpret_cast<uint4 *>(dst + c0), *db = reinterpret_cast<uint4 *>(dst + half + c0);
-                        da[0] = make_uint4(wa[0], wa[1], wa[2], wa[3]);
-                        da[1] = make_uint4(wa[4], wa[5], wa[6], wa[7]);
-                        db[0] = make_uint4(wb[0], wb[1], wb[2], wb[3]);
-                        db[1] = make_uint4(wb[4], wb[5], wb[6], wb[7]);
+                        st_row32(dst + c0, make_uint4(wa[0], wa[1], wa[2], wa[3]), make_uint4(wa[4], wa[5], wa[6], wa[7]));
+                        st_row32(dst + half + c0, make_uint4(wb[0], wb[1], wb[2], wb[3]), make_uint4(wb[4], wb[5], wb[6], wb[7]));
                     }
                 }
             } else if constexpr (EPI == TC_EPI_SILU) {
@@ -397,9 +408,8 @@ __global__ void __launch_bounds__(tc_threads<CG>(), 1)
                                 silu_mul(__uint_as_float(g[2 * e + 1]), __uint_as_float(u[2 * e + 1])));
                             packed[e] = *reinterpret_cast<const uint32_t *>(&v);
                         }
-                        uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)row * inner + n0 / 2 + c0);
-                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                        st_row32(out + (size_t)row * inner + n0 / 2 + c0, make_uint4(packed[0], packed[1], packed[2], packed[3]),
+                                 make_uint4(packed[4], packed[5], packed[6], packed[7]));
                     }
                 }
             } else {
