@@ -9,6 +9,22 @@
 
 namespace tg {
 
+// Four consecutive values rounded to T in one store (o is 4 T-aligned within a 16-byte aligned
+// row): 16 bytes of f32, or 8 of bf16 where four 2-byte stores left a warp's 256 bytes in partial
+// sectors.
+template <typename T>
+TG_DEVICE void store4(T *o, float a, float b, float c, float d);
+template <>
+TG_DEVICE void store4<float>(float *o, float a, float b, float c, float d) {
+    *reinterpret_cast<float4 *>(o) = make_float4(a, b, c, d);
+}
+template <>
+TG_DEVICE void store4<bf16>(bf16 *o, float a, float b, float c, float d) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    *reinterpret_cast<uint2 *>(o) =
+        make_uint2(*reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+}
+
 // norm_rows.comp: out = RMSNorm(x) g, rounded to T; a warp to a row. A row of up to 1024 values is
 // read once into registers (lane l holding its 16-byte vectors l, l + 32, ...) and its sum of squares
 // taken from them in warp_rms_scale's order, so the same bits as warp_rms_scale over memory.
@@ -45,11 +61,8 @@ __global__ void __launch_bounds__(128)
             if (i >= nv) continue;
             const int c = lane + 32 * i;
             const float4 gg = reinterpret_cast<const float4 *>(g)[c];
-            T *o = out + (size_t)row * k + 4 * c;
-            o[0] = from_f32<T>(v[i].x * s * gg.x);
-            o[1] = from_f32<T>(v[i].y * s * gg.y);
-            o[2] = from_f32<T>(v[i].z * s * gg.z);
-            o[3] = from_f32<T>(v[i].w * s * gg.w);
+            store4<T>(out + (size_t)row * k + 4 * c, v[i].x * s * gg.x, v[i].y * s * gg.y, v[i].z * s * gg.z,
+                      v[i].w * s * gg.w);
         }
         return;
     }
@@ -57,11 +70,7 @@ __global__ void __launch_bounds__(128)
     for (int c = lane; c < k / 4; c += 32) {
         const float4 v = reinterpret_cast<const float4 *>(xr)[c];
         const float4 gg = reinterpret_cast<const float4 *>(g)[c];
-        T *o = out + (size_t)row * k + 4 * c;
-        o[0] = from_f32<T>(v.x * s * gg.x);
-        o[1] = from_f32<T>(v.y * s * gg.y);
-        o[2] = from_f32<T>(v.z * s * gg.z);
-        o[3] = from_f32<T>(v.w * s * gg.w);
+        store4<T>(out + (size_t)row * k + 4 * c, v.x * s * gg.x, v.y * s * gg.y, v.z * s * gg.z, v.w * s * gg.w);
     }
 }
 
@@ -103,9 +112,7 @@ __global__ void __launch_bounds__(128)
             reinterpret_cast<float4 *>(static_cast<float *>(normed) + base)[q] =
                 make_float4(o[0], o[1], o[2], o[3]);
         } else {
-            T *n = static_cast<T *>(normed) + base + 4 * q;
-#pragma unroll
-            for (int e = 0; e < 4; e++) n[e] = from_f32<T>(o[e]);
+            store4<T>(static_cast<T *>(normed) + base + 4 * q, o[0], o[1], o[2], o[3]);
         }
     }
 }
@@ -153,9 +160,7 @@ __global__ void __launch_bounds__(1024)
     if (NORMED_F32) {
         reinterpret_cast<float4 *>(static_cast<float *>(normed) + base)[t] = make_float4(o[0], o[1], o[2], o[3]);
     } else {
-        T *n = static_cast<T *>(normed) + base + 4 * t;
-#pragma unroll
-        for (int e = 0; e < 4; e++) n[e] = from_f32<T>(o[e]);
+        store4<T>(static_cast<T *>(normed) + base + 4 * t, o[0], o[1], o[2], o[3]);
     }
 }
 
