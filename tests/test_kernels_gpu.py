@@ -221,6 +221,25 @@ def test_gemm_silu_epilogue_equals_gemm_then_silu_mul_rows(pkg, ctx, syn, m, inn
     assert distance(syn.bf16_to_f32(got), want)[1] < 1e-2
 
 
+@pytest.mark.parametrize("m,flags", [(256, 0), (64, 2)])
+def test_gemm_silu_output_16_byte_aligned_gives_the_same_bits(pkg, ctx, syn, m, flags):
+    """The bf16 epilogues store a lane's 32 bytes of a row as one 256-bit store only at a 32-byte
+    aligned address; an output binding that is 16- but not 32-byte aligned (the runtime asks for 16)
+    takes two 16-byte stores and gives the same bits, in CTA pairs (256 rows) and narrow tiles."""
+    inner, k = 256, 128
+    rng = np.random.default_rng(m + 7)
+    a = syn.bf16_bits(rng.standard_normal((m, k), dtype=np.float32))
+    w = syn.bf16_bits(rng.standard_normal((2 * inner, k), dtype=np.float32) * 0.05)
+    ma, mw = _mem(pkg, ctx, a), _mem(pkg, ctx, w)
+    shape = pkg.Shape(hidden=256, inner=inner, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
+    p = pkg.params(shape, "bf16", rows=m, m=m, n=2 * inner, k=k, flags=flags)
+    nb = m * inner * 2
+    out0, out16 = pkg.Memory(ctx, nb), pkg.Memory(ctx, nb + 16)
+    pkg.dispatch_once(ctx, "gemm_silu", p, [(ma, 0, a.nbytes), (mw, 0, w.nbytes), (out0, 0, nb)])
+    pkg.dispatch_once(ctx, "gemm_silu", p, [(ma, 0, a.nbytes), (mw, 0, w.nbytes), (out16, 16, nb)])
+    np.testing.assert_array_equal(out16.read(np.uint16, m * inner, offset=16), out0.read(np.uint16, m * inner))
+
+
 def test_gemm_silu_refuses_a_width_it_does_not_tile(pkg, ctx):
     shape = pkg.Shape(hidden=256, inner=256, heads=4, kv_heads=1, head_dim=64, layers=1, capacity=64)
     p = pkg.params(shape, "bf16", rows=128, m=128, n=384, k=64)
