@@ -393,12 +393,18 @@ def side_measurements(pkg, syn, ctx, torch, tc_peak, peak_kind, weights):
     gemm_ns = sum(v for k, v in per.items() if k.endswith("_proj"))
     gu_ns = per.get("gate_up_proj", 0.0)
     gu_flops = 2 * rows * 8192 * 1024 * 24
+    # Causal attention: S = q k^T and P v over each row's positions 0..p, 2 x 2 x (p + 1) x hd
+    # flops a head a row, summed over the runs' rows: 2 x S (S + 1) x hd x heads a run a layer.
+    att_ns = per.get("attention_rows", 0.0)
+    att_flops = 2 * 2048 * 2049 * cfg.head_dim * cfg.heads * 16 * 24
     out["prefill_c4"] = {"rows": rows, "tokens_per_s": round(rows / (ns / 1e9), 1), "ms": round(ns / 1e6, 3),
                          "gemm_tflops": round(gemm_flops / gemm_ns / 1e3, 1),
                          "gemm_frac_of_peak": round(gemm_flops / gemm_ns / 1e3 / tc_peak, 4),
                          "gemm_frac_of_sustained_peak": (round(gemm_flops / gemm_ns / 1e3 / sustained_tflops(), 4)
                                                          if sustained_tflops() else None),
                          "gate_up_gemm_tflops": round(gu_flops / gu_ns / 1e3, 1),
+                         "attention_tflops": round(att_flops / att_ns / 1e3, 1) if att_ns else None,
+                         "attention_frac_of_peak": round(att_flops / att_ns / 1e3 / tc_peak, 4) if att_ns else None,
                          "peak_tflops": tc_peak, "peak_source": peak_kind,
                          "share": {k: round(v / sum(per.values()), 4) for k, v in sorted(per.items(), key=lambda kv: -kv[1])}}
     pre.close()
