@@ -141,6 +141,50 @@ def test_tcgen05_attention_matches_the_mma_sync_kernel_within_rounding(pkg, ctx,
     assert np.all(outs[1][~live] == 0)  # spare rows are not written
 
 
+def test_tcgen05_attention_moves_its_reference_on_later_tiles(pkg, ctx, syn):
+    """Keys that grow with their position (x (1 + p / 32)) make each later 128-key tile's largest
+    score pass the row's reference by ~14 (base 2, scaled) against the 8 that lets it stay, for
+    rows with unit queries: their reference moves on every tile, O is rescaled in TMEM and the
+    tile's pass runs again; rows with queries 0.02 as large, in the same warps, keep theirs. Against
+    the mma.sync kernel within rounding, as above."""
+    import numpy as np
+
+    from conftest import distance
+
+    shape = pkg.Shape(hidden=1024, inner=4096, heads=16, kv_heads=2, head_dim=64, layers=1, capacity=512)
+    rows, heads, hd, kvh, cap, slots = 512, 16, 64, 2, 512, 2
+    rng = np.random.default_rng(21)
+    row_scale = np.where(np.arange(rows) % 2 == 0, 1.0, 0.02).astype(np.float32)
+    q = syn.bf16_bits(rng.standard_normal((rows, heads, hd), dtype=np.float32) * row_scale[:, None, None])
+    grow = (1.0 + np.arange(cap, dtype=np.float32) / 32.0)[None, None, :, None]
+    k = syn.bf16_bits(rng.standard_normal((slots, kvh, cap, hd), dtype=np.float32) * grow)
+    v = syn.bf16_bits(rng.standard_normal((slots, kvh, cap, hd), dtype=np.float32))
+    # Runs: 384 rows of slot 1 from position 0, 100 rows of slot 0 from 300.
+    words = np.full(2 * rows, 0xFFFFFFFF, np.uint32)
+    for first, n, start, slot in ((0, 384, 0, 1), (384, 100, 300, 0)):
+        words[first:first + n] = np.arange(start, start + n)
+        words[rows + first:rows + first + n] = slot
+
+    def mem(a):
+        m = pkg.Memory(ctx, a.nbytes)
+        m.write(np.ascontiguousarray(a))
+        return m
+
+    mw, mq, mk, mv = mem(words), mem(q), mem(k), mem(v)
+    p = pkg.params(shape, "bf16", rows=rows, slots=slots)
+    outs = []
+    for kernel in ("attention_rows", "attention_rows_tc"):
+        o = pkg.Memory(ctx, rows * heads * hd * 2)
+        o.fill(0)
+        pkg.dispatch_once(ctx, kernel, p, [(mw, 0, words.nbytes), (mq, 0, q.nbytes), (mk, 0, k.nbytes),
+                                           (mv, 0, v.nbytes), (o, 0, rows * heads * hd * 2)])
+        outs.append(syn.bf16_to_f32(o.read(np.uint16, rows * heads * hd)).reshape(rows, heads, hd))
+    live = words[:rows] != 0xFFFFFFFF
+    assert np.all(np.isfinite(outs[1][live]))
+    m, rel, cos = distance(outs[1][live], outs[0][live])
+    assert rel < 1e-2 and cos > 0.9999, (m, rel, cos)
+
+
 @pytest.mark.parametrize("dtype", ["f32", "bf16"])
 def test_nan_in_the_cache_past_a_run_changes_no_bit(pkg, ctx, syn, dtype):
     """attention_rows.comp reads the keys past a tile's last position as zero (:77-83), so what a
