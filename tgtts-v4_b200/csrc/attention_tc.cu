@@ -15,10 +15,11 @@
 //              MMA of N up to 128 takes ~95 clocks here, measured), with PV_j under it; PV_j
 //              waits for no later tile's copies;
 //   warps 2-5  head 2g, warps 6-9 head 2g + 1: a thread to a query row: S_j from TMEM (the mask,
-//              the row maximum, then the base-2 exponentials with the scale folded in) and P_j
-//              as bf16 into TMEM, once PV_{j-1} has read P_{j-1}, against a reference maximum
-//              that moves only when a tile's passes it by more than 2^FA_RESCALE, O in TMEM then
-//              rescaled in place (as in FlashAttention-4); O / l at the end.
+//              the base-2 exponentials with the scale folded in, the tile's maximum alongside)
+//              and P_j as bf16 into TMEM, once PV_{j-1} has read P_{j-1}, against a reference
+//              maximum that moves only when a tile's passes it by more than 2^FA_RESCALE - O in
+//              TMEM then rescaled in place (as in FlashAttention-4) and the tile's pass run again
+//              from S_j; O / l at the end.
 // With P in shared memory PV read 192 bytes a tensor clock (P and V) against the SM's 128, and
 // the softmax's P stores met those reads there.
 // The two heads' softmax warps run while the other head's MMAs do. Every wait on an mbarrier is
